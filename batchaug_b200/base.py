@@ -1,0 +1,103 @@
+"""Transform base classes with the reference's API (batchaug/base.py:6-76).
+
+``BatchTransform.sample_params(batch_size, shape, device) -> dict`` and
+``apply(tensor, params) -> tensor`` keep the reference's names, argument
+meaning and params keys (``mask`` first).  Parameters are drawn on the host
+(see ``_rng``) and uploaded in one copy; the host copies ride along under the
+private key ``"_host"`` so ``Compose`` can fuse transforms without reading
+anything back from the GPU.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _rng
+
+
+def upload(arrays: dict, device) -> dict:
+    """Copy a dict of small numpy arrays to ``device`` in one transfer per
+    dtype group (float32 arrays packed together; bool arrays together)."""
+    device = torch.device(device)
+    out = {}
+    floats = {k: np.ascontiguousarray(v, dtype=np.float32) for k, v in arrays.items()
+              if v.dtype != np.bool_ and v.dtype.kind == "f"}
+    others = {k: v for k, v in arrays.items() if k not in floats}
+    if floats:
+        flat = np.concatenate([v.ravel() for v in floats.values()])
+        dev = torch.from_numpy(flat).to(device, non_blocking=False)
+        pos = 0
+        for k, v in floats.items():
+            n = v.size
+            out[k] = dev[pos:pos + n].view(v.shape)
+            pos += n
+    for k, v in others.items():
+        if v.dtype == np.bool_:
+            out[k] = torch.from_numpy(np.ascontiguousarray(v)).to(device)
+        else:
+            out[k] = torch.from_numpy(np.ascontiguousarray(v)).to(device)
+    return out
+
+
+class BatchTransform:
+    """Base class for tensor-level batched transforms on (B, C, H, W, D).
+
+    Random parameters are sampled independently per batch element and shared
+    by all channels of an element (batchaug/base.py:6-52).
+    """
+
+    _stream = _rng.S_MASK_ONLY
+
+    def __init__(self, prob: float = 1.0):
+        self.prob = prob
+
+    # -- parameter sampling ------------------------------------------------
+    def _n_uniforms(self, shape) -> int:
+        """Uniforms per element this transform draws (the mask's included)."""
+        return 1
+
+    def _host_params(self, batch_size: int, shape, u: np.ndarray, seed: int) -> dict:
+        """Host parameters from the (batch_size, n) uniforms; column 0 is the
+        Bernoulli mask draw (base.py:35: rand < prob)."""
+        return {"mask": u[:, 0] < self.prob}
+
+    def sample_host(self, batch_size: int, shape) -> dict:
+        seed = _rng.draw_seed()
+        u = _rng.uniforms(seed, self._stream, batch_size, self._n_uniforms(shape))
+        return self._host_params(batch_size, tuple(shape), u, seed)
+
+    def _device_params(self, host: dict, shape, device) -> dict:
+        """Device tensors of the params dict (reference keys)."""
+        return upload({"mask": host["mask"]}, device)
+
+    def sample_params(self, batch_size: int, shape, device) -> dict:
+        """Sample random parameters; returns at least ``mask`` (B,) bool."""
+        host = self.sample_host(batch_size, shape)
+        params = self._device_params(host, tuple(shape), device)
+        params["_host"] = host
+        return params
+
+    def apply(self, tensor: torch.Tensor, params: dict) -> torch.Tensor:
+        raise NotImplementedError
+
+    def __call__(self, tensor: torch.Tensor) -> torch.Tensor:
+        params = self.sample_params(tensor.shape[0], tensor.shape, tensor.device)
+        return self.apply(tensor, params)
+
+
+class BatchDictTransform:
+    """Dict wrapper: samples parameters once from the first key's tensor and
+    applies them to every listed key (batchaug/base.py:55-76)."""
+
+    def __init__(self, keys: list[str], transform: BatchTransform):
+        self.keys = keys
+        self.transform = transform
+
+    def __call__(self, data: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
+        d = dict(data)
+        first = d[self.keys[0]]
+        params = self.transform.sample_params(first.shape[0], first.shape, first.device)
+        for key in self.keys:
+            if key in d:
+                d[key] = self.transform.apply(d[key], params)
+        return d

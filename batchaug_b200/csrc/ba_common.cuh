@@ -1,0 +1,106 @@
+// Shared device helpers for the batchaug_b200 kernels (sm_100a).
+//
+// Every file of this library is compiled with -fmad=false: each float
+// multiply and add rounds on its own, as in torch's scalar CPU kernels that
+// the reference results come from.  Fused multiply-adds appear only where
+// written explicitly (__fmaf_rn), at the places where torch's own CPU path
+// fuses (MKL's bmm inside affine_grid, linspace, the einsum of the bias field).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/batchaug_b200.h"
+
+namespace ba {
+
+// ---------------------------------------------------------------------------
+// Host-side error reporting (thread-local message + status).
+// ---------------------------------------------------------------------------
+void set_error(const char* fmt, ...);
+void clear_error();
+ba_status check_launch(const char* what);
+
+#define BA_REQUIRE(cond, ...)        \
+  do {                               \
+    if (!(cond)) {                   \
+      ::ba::set_error(__VA_ARGS__);  \
+      return BA_EINVAL;              \
+    }                                \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// Element access.  bf16 is stored as the upper half of an fp32 and rounded
+// to nearest even on store, which is what c10::BFloat16 does.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) {
+  return __uint_as_float(((uint32_t)h) << 16);
+}
+
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+  if (f != f) return (uint16_t)0x7FC0;  // canonical NaN, as c10::BFloat16
+  uint32_t u = __float_as_uint(f);
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+// Round an fp32 value to the nearest bf16 and back (one torch bf16 op's
+// rounding of its fp32 result).
+__device__ __forceinline__ float round_bf16(float f) {
+  return bf16_bits_to_f32(f32_to_bf16_bits(f));
+}
+
+template <int DT>
+__device__ __forceinline__ float round_dt(float f) {
+  return DT == BA_BF16 ? round_bf16(f) : f;
+}
+
+__device__ __forceinline__ float load_f(const void* p, int dtype, int64_t i) {
+  if (dtype == BA_BF16) return bf16_bits_to_f32(__ldg((const uint16_t*)p + i));
+  return __ldg((const float*)p + i);
+}
+
+__device__ __forceinline__ void store_f(void* p, int dtype, int64_t i, float v) {
+  if (dtype == BA_BF16)
+    ((uint16_t*)p)[i] = f32_to_bf16_bits(v);
+  else
+    ((float*)p)[i] = v;
+}
+
+// ---------------------------------------------------------------------------
+// torch.linspace(start, end, n)[i]: step = fl((end - start) / (n - 1)),
+// first half fma(step, i, start), second half fma(-step, n-1-i, end).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float linspace_at(float start, float end, float step, int64_t i,
+                                             int64_t n) {
+  if (n == 1) return start;
+  if (i < n / 2) return __fmaf_rn(step, (float)i, start);
+  return __fmaf_rn(-step, (float)(n - 1 - i), end);
+}
+
+// ---------------------------------------------------------------------------
+// Order-preserving int32 keys for float min/max with atomics.  NaN maps to
+// the extreme key in each direction so that a NaN anywhere wins both the
+// min and the max, as torch.min / torch.max propagate NaN.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int32_t fkey(float f) {
+  int32_t k = __float_as_int(f);
+  return k >= 0 ? k : (k ^ 0x7FFFFFFF);
+}
+__device__ __forceinline__ float fkey_inv(int32_t k) {
+  return __int_as_float(k >= 0 ? k : (k ^ 0x7FFFFFFF));
+}
+constexpr int32_t KEY_MIN_NAN = (int32_t)0x80000000;  // below key(-inf)
+constexpr int32_t KEY_MAX_NAN = (int32_t)0x7FFFFFFF;  // above key(+inf)
+constexpr int32_t KEY_POS_INF = (int32_t)0x7F800000;
+constexpr int32_t KEY_NEG_INF = (int32_t)(0xFF800000u ^ 0x7FFFFFFFu);
+
+__device__ __forceinline__ float decode_min_key(int32_t k) {
+  return k == KEY_MIN_NAN ? __int_as_float(0x7FC00000) : fkey_inv(k);
+}
+__device__ __forceinline__ float decode_max_key(int32_t k) {
+  return k == KEY_MAX_NAN ? __int_as_float(0x7FC00000) : fkey_inv(k);
+}
+
+}  // namespace ba

@@ -1,0 +1,765 @@
+// Fused intensity chain and min/max reduction.
+//
+// Reference semantics (batchaug PyTorch backend, op by op in the tensor
+// dtype):
+//   RandGaussianNoise.apply     batchaug/pytorch/intensity/noise.py:62-66
+//   RandAdjustContrast.apply    batchaug/pytorch/intensity/contrast.py:116-131
+//   RandScaleIntensity.apply    batchaug/pytorch/intensity/scale_shift.py:51-56
+//   RandShiftIntensity.apply    batchaug/pytorch/intensity/scale_shift.py:106-113
+//   RandBiasField.apply         batchaug/pytorch/intensity/bias_field.py:99-112
+//   ScaleIntensity.apply        batchaug/pytorch/intensity/contrast.py:35-68
+// replacing the Triton kernels batchaug/triton/kernels/{reduce,elementwise,
+// scale_shift,bias_field}.py.
+//
+// Design (B200): a chain of these transforms is one kernel per "segment".
+// CONTRAST and RESCALE need the min/max of their own input, so the chain is
+// cut in front of each of them; a segment streams 16-byte vectors, applies its
+// ops in registers (rounding to the tensor dtype after every op, as torch
+// does), writes the result and folds its min/max into per-group int32 keys
+// with one atomic per CTA and group.  The next segment re-reads that result.
+// The host walks the batch in slices whose working set fits in L2, running
+// every segment on a slice before moving on, so the re-reads hit L2 and HBM
+// sees the input once and the output once.  Gaussian noise is generated in
+// registers (Philox4x32-10 + Box-Muller) instead of being materialised.
+#include <stdio.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "ba_common.cuh"
+#include "philox.cuh"
+
+namespace ba {
+namespace {
+
+constexpr int CHAIN_THREADS = 256;
+
+struct OpArgs {
+  int32_t kind;
+  int32_t flags;
+  const uint8_t* mask;
+  const float* param;
+  const float* param2;
+  const float* noise;
+  const int32_t* stats_in;  // keys (groups, 2) the op reads (CONTRAST, RESCALE)
+  int32_t stats_per_channel;
+  int32_t degree;
+  uint32_t seed_lo, seed_hi;
+  uint64_t elem_offset;
+  float minv, span, factor1p;  // RESCALE constants as the reference rounds them
+};
+
+struct ChainArgs {
+  const void* src;
+  void* dst;
+  int64_t C, H, W, D, HWD;
+  int32_t b0;       // first element of this launch
+  int32_t n_ops;
+  int32_t stats_mode;  // 0: none, 1: per element, 2: per (element, channel)
+  int64_t tile;        // spatial positions per CTA (multiple of VEC)
+  int32_t* stats_out;  // keys (groups, 2)
+  OpArgs ops[BA_MAX_OPS];
+};
+
+// ---------------------------------------------------------------------------
+// Bias field: Legendre values along one axis with the reference recurrence
+// p_n = ((2n-1) * c * p_{n-1} - (n-1) * p_{n-2}) / n  (bias_field.py:38-43).
+// ---------------------------------------------------------------------------
+template <int DEG>
+__device__ __forceinline__ void legendre(float c, float* p) {
+  p[0] = 1.0f;
+  if (DEG >= 1) p[1] = c;
+#pragma unroll
+  for (int n = 2; n <= DEG; ++n) {
+    float a = ((float)(2 * n - 1) * c) * p[n - 1];
+    float s = (float)(n - 1) * p[n - 2];
+    p[n] = (a - s) / (float)n;
+  }
+}
+
+__device__ __forceinline__ float axis_coord(int64_t i, int64_t n) {
+  if (n == 1) return -1.0f;
+  return linspace_at(-1.0f, 1.0f, 2.0f / (float)(n - 1), i, n);
+}
+
+// exp(sum_t c_t * L_i(x) L_j(y) L_k(z)) over (i,j,k), i+j+k <= DEG, in the
+// reference's triplet order (bias_field.py:24-28); the sum is the fused chain
+// torch's CPU einsum produces and each basis value is (Li*Lj)*Lk.
+template <int DEG>
+__device__ __forceinline__ float bias_multiplier(const float* coeffs, const float* lx,
+                                                 const float* ly, const float* lz) {
+  float acc = 0.0f;
+  int t = 0;
+#pragma unroll
+  for (int i = 0; i <= DEG; ++i)
+#pragma unroll
+    for (int j = 0; j <= DEG - i; ++j) {
+      const float pij = lx[i] * ly[j];
+#pragma unroll
+      for (int k = 0; k <= DEG - i - j; ++k) {
+        const float basis = pij * lz[k];
+        const float c = __ldg(coeffs + t);
+        acc = (t == 0) ? c * basis : __fmaf_rn(c, basis, acc);
+        ++t;
+      }
+    }
+  return expf(acc);
+}
+
+template <int DEG, int VEC>
+__device__ __forceinline__ void bias_run(const OpArgs& op, int64_t b, int64_t s0, int n,
+                                         const ChainArgs& a, float* v) {
+  constexpr int NC = (DEG + 1) * (DEG + 2) * (DEG + 3) / 6;
+  const float* coeffs = op.param + b * NC;
+  int64_t h = s0 / (a.W * a.D);
+  int64_t rem = s0 - h * a.W * a.D;
+  int64_t w = rem / a.D;
+  int64_t z = rem - w * a.D;
+  float lx[DEG + 1], ly[DEG + 1], lz[DEG + 1];
+  legendre<DEG>(axis_coord(h, a.H), lx);
+  legendre<DEG>(axis_coord(w, a.W), ly);
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    if (i < n) {
+      legendre<DEG>(axis_coord(z, a.D), lz);
+      v[i] = v[i] * bias_multiplier<DEG>(coeffs, lx, ly, lz);
+      if (++z == a.D) {
+        z = 0;
+        if (++w == a.W) {
+          w = 0;
+          ++h;
+          legendre<DEG>(axis_coord(h, a.H), lx);
+        }
+        legendre<DEG>(axis_coord(w, a.W), ly);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Apply ops to n consecutive values of one channel (positions s0..s0+n-1).
+// ---------------------------------------------------------------------------
+template <int DT, int VEC>
+__device__ __forceinline__ void apply_ops(const ChainArgs& a, int64_t b, int64_t c, int64_t s0,
+                                          int n, float* v) {
+  for (int oi = 0; oi < a.n_ops; ++oi) {
+    const OpArgs& op = a.ops[oi];
+    const bool on = op.mask == nullptr || op.mask[b] != 0;
+    switch (op.kind) {
+      case BA_OP_NOISE: {
+        // x + dt(noise) * dt(mask): computed for masked elements too (adds 0).
+        const float m = on ? 1.0f : 0.0f;
+        float nz[VEC];
+        if (op.flags & BA_NOISE_PHILOX) {
+          // Noise of flat position p = c*HWD + s of element b is normal
+          // (p & 3) of Philox block (seed; p >> 2, element, NOISE stream),
+          // times std plus mean in fp32 as torch.randn(...) * std + mean.
+          const float sd = __ldg(op.param + b), mu = __ldg(op.param2 + b);
+          const uint64_t eb = op.elem_offset + (uint64_t)b;
+          const int64_t first = c * a.HWD + s0;
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) nz[i] = 0.0f;
+          if (on) {
+            if (VEC >= 4) {
+              // vector path: first is a multiple of 4 (HWD % VEC == 0)
+#pragma unroll
+              for (int base = 0; base < VEC; base += 4) {
+                const uint64_t q = (uint64_t)(first + base) >> 2;
+                const U4 ctr = {(uint32_t)q, (uint32_t)eb, (uint32_t)(eb >> 32),
+                                STREAM_NOISE | (uint32_t)(q >> 32)};
+                float z4[4];
+                normal4(philox4x32_10(ctr, op.seed_lo, op.seed_hi), z4);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  if (base + i < VEC) nz[base + i] = z4[i] * sd + mu;
+              }
+            } else {
+              const uint64_t q = (uint64_t)first >> 2;
+              const U4 ctr = {(uint32_t)q, (uint32_t)eb, (uint32_t)(eb >> 32),
+                              STREAM_NOISE | (uint32_t)(q >> 32)};
+              float z4[4];
+              normal4(philox4x32_10(ctr, op.seed_lo, op.seed_hi), z4);
+              const int l = (int)(first & 3);
+              const float z = l == 0 ? z4[0] : (l == 1 ? z4[1] : (l == 2 ? z4[2] : z4[3]));
+              nz[0] = z * sd + mu;
+            }
+          }
+        } else {
+          const float* np = op.noise + (b * a.C + c) * a.HWD + s0;
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) nz[i] = (i < n) ? __ldg(np + i) : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          const float nm = round_dt<DT>(round_dt<DT>(nz[i]) * m);
+          v[i] = round_dt<DT>(v[i] + nm);
+        }
+        break;
+      }
+      case BA_OP_CONTRAST: {
+        if (!on) break;
+        const float mn = decode_min_key(op.stats_in[2 * b]);
+        const float mx = decode_max_key(op.stats_in[2 * b + 1]);
+        const float g = __ldg(op.param + b);
+        const float rng = mx - mn;
+        const float den = rng + 1e-7f;
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          float nrm = (v[i] - mn) / den;
+          nrm = (nrm < 0.0f) ? 0.0f : nrm;
+          v[i] = round_dt<DT>(powf(nrm, g) * rng + mn);
+        }
+        break;
+      }
+      case BA_OP_SCALE: {
+        if (!on) break;
+        const float s = round_dt<DT>(1.0f + round_dt<DT>(__ldg(op.param + b)));
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) v[i] = round_dt<DT>(v[i] * s);
+        break;
+      }
+      case BA_OP_SHIFT: {
+        if (!on) break;
+        const float o = round_dt<DT>(__ldg(op.param + b));
+        const bool safe = op.flags & BA_SHIFT_SAFE;
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          float r = round_dt<DT>(v[i] + o);
+          if (safe) r = (r < 0.0f) ? 0.0f : ((r > 1.0f) ? 1.0f : r);
+          v[i] = r;
+        }
+        break;
+      }
+      case BA_OP_BIAS_FIELD: {
+        if (!on) break;
+        float t[VEC];
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) t[i] = v[i];
+        switch (op.degree) {
+          case 1: bias_run<1, VEC>(op, b, s0, n, a, t); break;
+          case 2: bias_run<2, VEC>(op, b, s0, n, a, t); break;
+          case 3: bias_run<3, VEC>(op, b, s0, n, a, t); break;
+          case 4: bias_run<4, VEC>(op, b, s0, n, a, t); break;
+          case 5: bias_run<5, VEC>(op, b, s0, n, a, t); break;
+          default: bias_run<6, VEC>(op, b, s0, n, a, t); break;
+        }
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) v[i] = round_dt<DT>(t[i]);
+        break;
+      }
+      case BA_OP_RESCALE: {
+        if (op.flags & BA_RESCALE_FACTOR) {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) v[i] = round_dt<DT>(v[i] * op.factor1p);
+          break;
+        }
+        const bool has_min = op.flags & BA_RESCALE_MINV, has_max = op.flags & BA_RESCALE_MAXV;
+        if (!has_min && !has_max) break;
+        const int64_t g = op.stats_per_channel ? b * a.C + c : b;
+        const float mn = decode_min_key(op.stats_in[2 * g]);
+        const float mx = decode_max_key(op.stats_in[2 * g + 1]);
+        float den = round_dt<DT>(mx - mn);
+        const bool is_const = den == 0.0f;
+        if (is_const) den = 1.0f;
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          const float nrm = round_dt<DT>(round_dt<DT>(v[i] - mn) / den);
+          float r = nrm;
+          if (has_min && has_max) r = round_dt<DT>(round_dt<DT>(nrm * op.span) + op.minv);
+          if (has_min && is_const) r = round_dt<DT>(v[i] * op.minv);
+          v[i] = r;
+        }
+        break;
+      }
+      default:
+        break;
+    }
+  }
+}
+
+template <int DT, int VEC>
+__device__ __forceinline__ void load_run(const void* p, int64_t idx, int n, float* v) {
+  if (DT == BA_F32) {
+    const float* q = (const float*)p + idx;
+    if (VEC == 4 && n == 4) {
+      const float4 t = *(const float4*)q;
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) v[i] = (i < n) ? q[i] : 0.0f;
+    }
+  } else {
+    const uint16_t* q = (const uint16_t*)p + idx;
+    if (VEC == 8 && n == 8) {
+      const uint4 t = *(const uint4*)q;
+      const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) v[i] = (i < n) ? bf16_bits_to_f32(q[i]) : 0.0f;
+    }
+  }
+}
+
+template <int DT, int VEC>
+__device__ __forceinline__ void store_run(void* p, int64_t idx, int n, const float* v) {
+  if (DT == BA_F32) {
+    float* q = (float*)p + idx;
+    if (VEC == 4 && n == 4) {
+      *(float4*)q = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+      for (int i = 0; i < n; ++i) q[i] = v[i];
+    }
+  } else {
+    uint16_t* q = (uint16_t*)p + idx;
+    if (VEC == 8 && n == 8) {
+      uint4 t;
+      t.x = (uint32_t)f32_to_bf16_bits(v[0]) | ((uint32_t)f32_to_bf16_bits(v[1]) << 16);
+      t.y = (uint32_t)f32_to_bf16_bits(v[2]) | ((uint32_t)f32_to_bf16_bits(v[3]) << 16);
+      t.z = (uint32_t)f32_to_bf16_bits(v[4]) | ((uint32_t)f32_to_bf16_bits(v[5]) << 16);
+      t.w = (uint32_t)f32_to_bf16_bits(v[6]) | ((uint32_t)f32_to_bf16_bits(v[7]) << 16);
+      *(uint4*)q = t;
+    } else {
+      for (int i = 0; i < n; ++i) q[i] = f32_to_bf16_bits(v[i]);
+    }
+  }
+}
+
+// Block-wide min/max of (mn, mx, nan) followed by one atomic pair.
+__device__ __forceinline__ void block_minmax_commit(float mn, float mx, bool nan, int32_t* keys) {
+  __shared__ int32_t s_min[CHAIN_THREADS / 32], s_max[CHAIN_THREADS / 32];
+  int32_t kmin = nan ? KEY_MIN_NAN : fkey(mn);
+  int32_t kmax = nan ? KEY_MAX_NAN : fkey(mx);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    kmin = min(kmin, __shfl_xor_sync(0xFFFFFFFFu, kmin, o));
+    kmax = max(kmax, __shfl_xor_sync(0xFFFFFFFFu, kmax, o));
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  __syncthreads();  // s_min/s_max may still be read by a previous commit
+  if (lane == 0) {
+    s_min[warp] = kmin;
+    s_max[warp] = kmax;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < CHAIN_THREADS / 32; ++i) {
+      kmin = min(kmin, s_min[i]);
+      kmax = max(kmax, s_max[i]);
+    }
+    if (kmin != fkey(INFINITY)) atomicMin(keys, kmin);
+    if (kmax != fkey(-INFINITY)) atomicMax(keys + 1, kmax);
+  }
+}
+
+template <int VEC>
+__device__ __forceinline__ void fold_minmax(const float* v, int n, float& mn, float& mx,
+                                            bool& nan) {
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    if (i < n) {
+      // a NaN compares false both ways and only raises the flag
+      nan |= (v[i] != v[i]);
+      mn = v[i] < mn ? v[i] : mn;
+      mx = v[i] > mx ? v[i] : mx;
+    }
+  }
+}
+
+// One segment of the chain over elements [b0, b0 + gridDim.y), spatial
+// positions [blockIdx.x * tile, +tile) of every channel.
+template <int DT, int VEC, bool WRITE>
+__global__ void __launch_bounds__(CHAIN_THREADS)
+    chain_kernel(const __grid_constant__ ChainArgs a) {
+  const int64_t b = a.b0 + blockIdx.y;
+  const int64_t s_begin = (int64_t)blockIdx.x * a.tile;
+  const int64_t s_end = min(s_begin + a.tile, a.HWD);
+  if (a.stats_mode == 2) {
+    // statistics per (element, channel): channel-outer, one commit each
+    for (int64_t c = 0; c < a.C; ++c) {
+      float mn = INFINITY, mx = -INFINITY;
+      bool nan = false;
+      for (int64_t s = s_begin + (int64_t)threadIdx.x * VEC; s < s_end;
+           s += CHAIN_THREADS * VEC) {
+        const int n = (int)min((int64_t)VEC, s_end - s);
+        const int64_t idx = (b * a.C + c) * a.HWD + s;
+        float v[VEC];
+        load_run<DT, VEC>(a.src, idx, n, v);
+        apply_ops<DT, VEC>(a, b, c, s, n, v);
+        if (WRITE) store_run<DT, VEC>(a.dst, idx, n, v);
+        fold_minmax<VEC>(v, n, mn, mx, nan);
+      }
+      block_minmax_commit(mn, mx, nan, a.stats_out + 2 * (b * a.C + c));
+    }
+    return;
+  }
+  float mn = INFINITY, mx = -INFINITY;
+  bool nan = false;
+  for (int64_t s = s_begin + (int64_t)threadIdx.x * VEC; s < s_end; s += CHAIN_THREADS * VEC) {
+    const int n = (int)min((int64_t)VEC, s_end - s);
+    for (int64_t c = 0; c < a.C; ++c) {
+      const int64_t idx = (b * a.C + c) * a.HWD + s;
+      float v[VEC];
+      load_run<DT, VEC>(a.src, idx, n, v);
+      apply_ops<DT, VEC>(a, b, c, s, n, v);
+      if (WRITE) store_run<DT, VEC>(a.dst, idx, n, v);
+      if (a.stats_mode == 1) fold_minmax<VEC>(v, n, mn, mx, nan);
+    }
+  }
+  if (a.stats_mode == 1) block_minmax_commit(mn, mx, nan, a.stats_out + 2 * b);
+}
+
+__global__ void init_keys_kernel(int32_t* keys, int64_t n_groups) {
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < n_groups;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    keys[2 * g] = fkey(INFINITY);
+    keys[2 * g + 1] = fkey(-INFINITY);
+  }
+}
+
+__global__ void decode_keys_kernel(float* stats, int64_t n_groups) {
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < n_groups;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    const int32_t* k = (const int32_t*)stats;
+    const float mn = decode_min_key(k[2 * g]);
+    const float mx = decode_max_key(k[2 * g + 1]);
+    stats[2 * g] = mn;
+    stats[2 * g + 1] = mx;
+  }
+}
+
+// Plain per-group min/max over a (n_groups, group_size) view.
+template <int DT, int VEC>
+__global__ void __launch_bounds__(CHAIN_THREADS)
+    minmax_kernel(const void* x, int64_t group_size, int64_t tile, int32_t* keys) {
+  const int64_t g = blockIdx.y;
+  const int64_t s_begin = (int64_t)blockIdx.x * tile;
+  const int64_t s_end = min(s_begin + tile, group_size);
+  float mn = INFINITY, mx = -INFINITY;
+  bool nan = false;
+  for (int64_t s = s_begin + (int64_t)threadIdx.x * VEC; s < s_end; s += CHAIN_THREADS * VEC) {
+    const int n = (int)min((int64_t)VEC, s_end - s);
+    float v[VEC];
+    load_run<DT, VEC>(x, g * group_size + s, n, v);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i)
+      if (i < n) {
+        nan |= (v[i] != v[i]);
+        mn = v[i] < mn ? v[i] : mn;
+        mx = v[i] > mx ? v[i] : mx;
+      }
+  }
+  block_minmax_commit(mn, mx, nan, keys + 2 * g);
+}
+
+int sm_count() {
+  static int cached = 0;
+  if (cached == 0) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+      cached = n;
+    else
+      cached = 148;
+  }
+  return cached;
+}
+
+int64_t l2_bytes() {
+  static int64_t cached = 0;
+  if (cached == 0) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&n, cudaDevAttrL2CacheSize, dev) == cudaSuccess && n > 0)
+      cached = n;
+    else
+      cached = 126ll << 20;
+  }
+  return cached;
+}
+
+// Spatial positions per CTA: aim for ~4 CTAs per SM over the launch.
+int64_t pick_tile(int64_t positions, int64_t n_blocks_y, int vec) {
+  const int64_t target_blocks = (int64_t)sm_count() * 4;
+  int64_t per_y = std::max<int64_t>(1, target_blocks / std::max<int64_t>(1, n_blocks_y));
+  int64_t tile = (positions + per_y - 1) / per_y;
+  const int64_t quantum = (int64_t)CHAIN_THREADS * vec;
+  tile = std::max<int64_t>(quantum, (tile + quantum - 1) / quantum * quantum);
+  return tile;
+}
+
+bool needs_stats(const ba_op& op) {
+  if (op.kind == BA_OP_CONTRAST) return true;
+  if (op.kind == BA_OP_RESCALE)
+    return !(op.flags & BA_RESCALE_FACTOR) && (op.flags & (BA_RESCALE_MINV | BA_RESCALE_MAXV));
+  return false;
+}
+
+int64_t stats_groups(const ba_op& op, int64_t B, int64_t C) {
+  if (op.kind == BA_OP_RESCALE && (op.flags & BA_RESCALE_CHANNEL)) return B * C;
+  return B;
+}
+
+struct Segment {
+  int first, last;      // ops [first, last)
+  int stats_for;        // op index whose stats this segment produces, -1 none
+  int64_t stats_offset;  // int32 offset of those keys in the workspace
+};
+
+ba_status validate_chain(const ba_chain_desc* d) {
+  BA_REQUIRE(d != nullptr, "ba_intensity_chain: desc is NULL");
+  BA_REQUIRE(d->batch >= 0 && d->channels >= 0 && d->H > 0 && d->W > 0 && d->D > 0,
+             "ba_intensity_chain: bad shape");
+  BA_REQUIRE(d->batch <= 65535, "ba_intensity_chain: batch exceeds 65535");
+  BA_REQUIRE(d->dtype == BA_F32 || d->dtype == BA_BF16, "ba_intensity_chain: bad dtype %d",
+             d->dtype);
+  BA_REQUIRE(d->n_ops >= 1 && d->n_ops <= BA_MAX_OPS, "ba_intensity_chain: n_ops=%d not in 1..%d",
+             d->n_ops, BA_MAX_OPS);
+  for (int i = 0; i < d->n_ops; ++i) {
+    const ba_op& op = d->ops[i];
+    BA_REQUIRE(op.kind >= BA_OP_NOISE && op.kind <= BA_OP_RESCALE,
+               "ba_intensity_chain: op %d unknown kind %d", i, op.kind);
+    switch (op.kind) {
+      case BA_OP_NOISE:
+        if (op.flags & BA_NOISE_PHILOX)
+          BA_REQUIRE(op.param && op.param2, "ba_intensity_chain: op %d NOISE needs std and mean",
+                     i);
+        else
+          BA_REQUIRE(op.noise, "ba_intensity_chain: op %d NOISE needs an injected noise tensor",
+                     i);
+        break;
+      case BA_OP_CONTRAST:
+      case BA_OP_SCALE:
+      case BA_OP_SHIFT:
+        BA_REQUIRE(op.param, "ba_intensity_chain: op %d needs its per-element parameter", i);
+        break;
+      case BA_OP_BIAS_FIELD:
+        BA_REQUIRE(op.param, "ba_intensity_chain: op %d BIAS_FIELD needs coefficients", i);
+        if (op.degree < 1 || op.degree > 6) {
+          set_error("ba_intensity_chain: op %d BIAS_FIELD degree %d not in 1..6", i, op.degree);
+          return BA_EUNSUPPORTED;
+        }
+        break;
+      default:
+        break;
+    }
+  }
+  const int64_t n = d->batch * d->channels * d->H * d->W * d->D;
+  if (n > 0) {
+    BA_REQUIRE(d->src && d->dst, "ba_intensity_chain: NULL src or dst");
+    const size_t esz = d->dtype == BA_BF16 ? 2 : 4;
+    const char* s = (const char*)d->src;
+    const char* t = (const char*)d->dst;
+    BA_REQUIRE(s == t || s + n * esz <= t || t + n * esz <= s,
+               "ba_intensity_chain: dst partially overlaps src");
+    BA_REQUIRE((uintptr_t)s % esz == 0 && (uintptr_t)t % esz == 0,
+               "ba_intensity_chain: pointers not aligned to the element size");
+  }
+  return BA_OK;
+}
+
+void plan_segments(const ba_chain_desc* d, std::vector<Segment>& segs, int64_t& ws_ints) {
+  segs.clear();
+  ws_ints = 0;
+  int first = 0;
+  for (int i = 0; i <= d->n_ops; ++i) {
+    const bool cut = (i == d->n_ops) || needs_stats(d->ops[i]);
+    if (!cut) continue;
+    Segment s;
+    s.first = first;
+    s.last = i;
+    s.stats_for = (i < d->n_ops) ? i : -1;
+    s.stats_offset = 0;
+    if (s.stats_for >= 0) {
+      s.stats_offset = ws_ints;
+      ws_ints += 2 * stats_groups(d->ops[i], d->batch, d->channels);
+    }
+    segs.push_back(s);
+    first = i;
+  }
+}
+
+template <int DT, int VEC>
+ba_status launch_segment(ChainArgs& a, int64_t nb, bool write, cudaStream_t st) {
+  const int64_t tile = pick_tile(a.HWD, nb, VEC);
+  a.tile = tile;
+  dim3 grid((unsigned)((a.HWD + tile - 1) / tile), (unsigned)nb);
+  if (write)
+    chain_kernel<DT, VEC, true><<<grid, CHAIN_THREADS, 0, st>>>(a);
+  else
+    chain_kernel<DT, VEC, false><<<grid, CHAIN_THREADS, 0, st>>>(a);
+  return check_launch("ba_intensity_chain");
+}
+
+}  // namespace
+}  // namespace ba
+
+extern "C" size_t ba_intensity_workspace_bytes(const ba_chain_desc* desc) {
+  using namespace ba;
+  if (desc == nullptr || desc->n_ops < 1 || desc->n_ops > BA_MAX_OPS) return 0;
+  std::vector<Segment> segs;
+  int64_t ints = 0;
+  plan_segments(desc, segs, ints);
+  return (size_t)ints * sizeof(int32_t);
+}
+
+extern "C" ba_status ba_intensity_chain(const ba_chain_desc* desc, void* workspace,
+                                        size_t workspace_bytes, ba_stream_t stream) {
+  using namespace ba;
+  clear_error();
+  ba_status st = validate_chain(desc);
+  if (st != BA_OK) return st;
+  const ba_chain_desc& d = *desc;
+  std::vector<Segment> segs;
+  int64_t ws_ints = 0;
+  plan_segments(&d, segs, ws_ints);
+  BA_REQUIRE(workspace_bytes >= (size_t)ws_ints * sizeof(int32_t),
+             "ba_intensity_chain: workspace of %zu bytes, %lld needed", workspace_bytes,
+             (long long)(ws_ints * sizeof(int32_t)));
+  BA_REQUIRE(ws_ints == 0 || workspace != nullptr, "ba_intensity_chain: workspace is NULL");
+  BA_REQUIRE(ws_ints == 0 || (uintptr_t)workspace % 16 == 0,
+             "ba_intensity_chain: workspace not 16-byte aligned");
+  const int64_t HWD = d.H * d.W * d.D;
+  if (d.batch * d.channels * HWD == 0) return BA_OK;
+  cudaStream_t cs = (cudaStream_t)stream;
+  int32_t* keys = (int32_t*)workspace;
+  if (ws_ints > 0) {
+    init_keys_kernel<<<(unsigned)std::min<int64_t>((ws_ints / 2 + 255) / 256, 1024), 256, 0, cs>>>(
+        keys, ws_ints / 2);
+    st = check_launch("ba_intensity_chain");
+    if (st != BA_OK) return st;
+  }
+
+  const size_t esz = d.dtype == BA_BF16 ? 2 : 4;
+  const int vec = d.dtype == BA_BF16 ? 8 : 4;
+  const bool vec_ok = (HWD % vec) == 0 && ((uintptr_t)d.src % 16) == 0 &&
+                      ((uintptr_t)d.dst % 16) == 0 &&
+                      [&] {
+                        for (int i = 0; i < d.n_ops; ++i)
+                          if (d.ops[i].kind == BA_OP_NOISE &&
+                              !(d.ops[i].flags & BA_NOISE_PHILOX))
+                            return ((uintptr_t)d.ops[i].noise % 16) == 0;
+                        return true;
+                      }();
+
+  // Elements per slice: keep one slice of dst (re-read by later segments)
+  // within about half of L2.
+  const int64_t elem_bytes = d.channels * HWD * (int64_t)esz;
+  int64_t slice = d.batch;
+  if (segs.size() > 1 && elem_bytes > 0) {
+    slice = std::max<int64_t>(1, (l2_bytes() / 2) / elem_bytes);
+    slice = std::min<int64_t>(slice, d.batch);
+  }
+
+  ChainArgs a;
+  memset(&a, 0, sizeof(a));
+  a.C = d.channels;
+  a.H = d.H;
+  a.W = d.W;
+  a.D = d.D;
+  a.HWD = HWD;
+  for (int64_t b0 = 0; b0 < d.batch; b0 += slice) {
+    const int64_t nb = std::min(slice, d.batch - b0);
+    bool written = false;
+    for (size_t si = 0; si < segs.size(); ++si) {
+      const Segment& sg = segs[si];
+      const bool has_ops = sg.last > sg.first;
+      const bool is_last = si + 1 == segs.size();
+      // A segment without ops only reduces (a chain starting with a stats
+      // consumer); the last segment always writes dst.
+      const bool write = has_ops || (is_last && !written);
+      a.src = written ? d.dst : d.src;
+      a.dst = d.dst;
+      a.b0 = (int32_t)b0;
+      a.n_ops = sg.last - sg.first;
+      for (int i = sg.first; i < sg.last; ++i) {
+        const ba_op& op = d.ops[i];
+        OpArgs& o = a.ops[i - sg.first];
+        memset(&o, 0, sizeof(o));
+        o.kind = op.kind;
+        o.flags = op.flags;
+        o.mask = op.mask;
+        o.param = op.param;
+        o.param2 = op.param2;
+        o.noise = op.noise;
+        o.degree = op.degree;
+        o.seed_lo = (uint32_t)op.seed;
+        o.seed_hi = (uint32_t)(op.seed >> 32);
+        o.elem_offset = op.elem_offset;
+        o.minv = (float)op.c0;
+        o.span = (float)(op.c1 - op.c0);
+        o.factor1p = (float)(1.0 + op.c0);
+        if (needs_stats(op)) {
+          // Stats come from the previous segment.
+          const Segment& prev = segs[si - 1];
+          o.stats_in = keys + prev.stats_offset;
+          o.stats_per_channel =
+              (op.kind == BA_OP_RESCALE && (op.flags & BA_RESCALE_CHANNEL)) ? 1 : 0;
+        }
+      }
+      a.stats_out = nullptr;
+      a.stats_mode = 0;
+      if (sg.stats_for >= 0) {
+        const ba_op& nx = d.ops[sg.stats_for];
+        a.stats_out = keys + sg.stats_offset;
+        a.stats_mode = (nx.kind == BA_OP_RESCALE && (nx.flags & BA_RESCALE_CHANNEL)) ? 2 : 1;
+      }
+      if (!write && a.stats_mode == 0) continue;
+      if (d.dtype == BA_BF16)
+        st = vec_ok ? launch_segment<BA_BF16, 8>(a, nb, write, cs)
+                    : launch_segment<BA_BF16, 1>(a, nb, write, cs);
+      else
+        st = vec_ok ? launch_segment<BA_F32, 4>(a, nb, write, cs)
+                    : launch_segment<BA_F32, 1>(a, nb, write, cs);
+      if (st != BA_OK) return st;
+      if (write) written = true;
+    }
+  }
+  return BA_OK;
+}
+
+extern "C" ba_status ba_minmax(const void* x, int32_t dtype, int64_t n_groups, int64_t group_size,
+                               float* stats, ba_stream_t stream) {
+  using namespace ba;
+  clear_error();
+  BA_REQUIRE(dtype == BA_F32 || dtype == BA_BF16, "ba_minmax: bad dtype %d", dtype);
+  BA_REQUIRE(n_groups >= 0 && group_size >= 0, "ba_minmax: negative size");
+  BA_REQUIRE(n_groups <= 65535, "ba_minmax: n_groups %lld exceeds 65535", (long long)n_groups);
+  if (n_groups == 0) return BA_OK;
+  BA_REQUIRE(stats != nullptr, "ba_minmax: stats is NULL");
+  BA_REQUIRE((uintptr_t)stats % 8 == 0, "ba_minmax: stats not 8-byte aligned");
+  BA_REQUIRE(group_size == 0 || x != nullptr, "ba_minmax: x is NULL");
+  cudaStream_t cs = (cudaStream_t)stream;
+  int32_t* keys = (int32_t*)stats;
+  init_keys_kernel<<<(unsigned)std::min<int64_t>((n_groups + 255) / 256, 1024), 256, 0, cs>>>(
+      keys, n_groups);
+  ba_status st = check_launch("ba_minmax");
+  if (st != BA_OK) return st;
+  if (group_size > 0) {
+    const int vec = dtype == BA_BF16 ? 8 : 4;
+    const bool vec_ok = (group_size % vec) == 0 && ((uintptr_t)x % 16) == 0;
+    const int v = vec_ok ? vec : 1;
+    const int64_t tile = pick_tile(group_size, n_groups, v);
+    dim3 grid((unsigned)((group_size + tile - 1) / tile), (unsigned)n_groups);
+    if (dtype == BA_BF16) {
+      if (vec_ok)
+        minmax_kernel<BA_BF16, 8><<<grid, CHAIN_THREADS, 0, cs>>>(x, group_size, tile, keys);
+      else
+        minmax_kernel<BA_BF16, 1><<<grid, CHAIN_THREADS, 0, cs>>>(x, group_size, tile, keys);
+    } else {
+      if (vec_ok)
+        minmax_kernel<BA_F32, 4><<<grid, CHAIN_THREADS, 0, cs>>>(x, group_size, tile, keys);
+      else
+        minmax_kernel<BA_F32, 1><<<grid, CHAIN_THREADS, 0, cs>>>(x, group_size, tile, keys);
+    }
+    st = check_launch("ba_minmax");
+    if (st != BA_OK) return st;
+  }
+  decode_keys_kernel<<<(unsigned)std::min<int64_t>((n_groups + 255) / 256, 1024), 256, 0, cs>>>(
+      stats, n_groups);
+  return check_launch("ba_minmax");
+}

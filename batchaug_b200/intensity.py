@@ -1,0 +1,326 @@
+"""Intensity transforms: RandGaussianNoise, RandAdjustContrast,
+RandScaleIntensity, RandShiftIntensity, RandBiasField, ScaleIntensity,
+RandGaussianSmooth (+ dict wrappers).
+
+Constructors, params keys and results follow the reference PyTorch backend
+(batchaug/pytorch/intensity/*.py), op by op in the tensor dtype.  Each
+``apply`` is one fused ``ba_intensity_chain`` (or ``ba_smooth3d``) call; a
+``Compose`` fuses consecutive transforms of this module into a single chain
+per key (see :meth:`_FusibleIntensity.chain_op`).
+
+Gaussian noise is generated in-kernel from the params' ``noise_seed``
+(Philox4x32-10 keyed on the global element index and voxel position) and is
+never materialised; params holding an explicit ``"noise"`` tensor (the
+reference's params, or a test's injected noise) are applied as given.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from . import _rng, ops
+from .base import BatchDictTransform, BatchTransform, upload
+
+
+def _parse_range(param) -> tuple[float, float]:
+    """Scalar v -> (-v, v); (lo, hi) unchanged (scale_shift.py:8-16)."""
+    if isinstance(param, (int, float)):
+        v = float(param)
+        return (-v, v)
+    return (float(param[0]), float(param[1]))
+
+
+def _dev(params: dict, key: str, device) -> torch.Tensor:
+    t = params[key]
+    return t if t.device == device else t.to(device)
+
+
+def _mask_u8(params: dict, device) -> torch.Tensor:
+    m = params["mask"]
+    if m.device != device:
+        m = m.to(device)
+    return m.view(torch.uint8) if m.dtype == torch.bool else (m != 0).to(torch.uint8)
+
+
+class _FusibleIntensity(BatchTransform):
+    """An intensity transform that is one op of ba_intensity_chain."""
+
+    def chain_op(self, params: dict, tensor: torch.Tensor) -> ops.ChainOp:
+        raise NotImplementedError
+
+    def apply(self, tensor: torch.Tensor, params: dict) -> torch.Tensor:
+        return ops.intensity_chain(tensor, [self.chain_op(params, tensor)])
+
+
+class RandGaussianNoise(_FusibleIntensity):
+    """x + noise * mask with noise ~ N(mean, std) per element (noise.py:8-66)."""
+
+    _stream = _rng.S_NOISE
+
+    def __init__(self, prob: float = 0.1, mean=0.0, std=0.1):
+        super().__init__(prob=prob)
+        self.mean = mean
+        self.std = std
+
+    def _n_uniforms(self, shape):
+        return 3
+
+    @staticmethod
+    def _scalar(param, col: np.ndarray) -> np.ndarray:
+        if isinstance(param, (list, tuple)):
+            lo, hi = param
+            return (col * np.float32(hi - lo) + np.float32(lo)).astype(np.float32)
+        return np.full(col.shape, param, np.float32)
+
+    def _host_params(self, B, shape, u, seed):
+        return {"mask": u[:, 0] < self.prob, "std": self._scalar(self.std, u[:, 1]),
+                "mean": self._scalar(self.mean, u[:, 2]), "noise_seed": seed}
+
+    def _device_params(self, host, shape, device):
+        p = upload({"mask": host["mask"], "std": host["std"], "mean": host["mean"]}, device)
+        p["noise_seed"] = host["noise_seed"]
+        p["elem_offset"] = _rng.element_offset()
+        return p
+
+    def chain_op(self, params, tensor):
+        dev = tensor.device
+        if "noise" in params:  # injected noise tensor (already * std + mean)
+            noise = params["noise"].to(device=dev, dtype=torch.float32).contiguous()
+            if noise.shape != tensor.shape:
+                raise ValueError(f"noise shape {tuple(noise.shape)} != tensor shape "
+                                 f"{tuple(tensor.shape)}")
+            return ops.ChainOp(L.BA_OP_NOISE, mask=_mask_u8(params, dev), noise=noise)
+        return ops.ChainOp(L.BA_OP_NOISE, flags=L.BA_NOISE_PHILOX, mask=_mask_u8(params, dev),
+                           param=_dev(params, "std", dev), param2=_dev(params, "mean", dev),
+                           seed=params["noise_seed"], elem_offset=params.get("elem_offset", 0))
+
+
+class RandAdjustContrast(_FusibleIntensity):
+    """Gamma on per-element min/max, fp32 (contrast.py:88-131)."""
+
+    _stream = _rng.S_CONTRAST
+
+    def __init__(self, prob: float = 0.1, gamma=(0.5, 4.5)):
+        super().__init__(prob=prob)
+        self.gamma = gamma
+
+    def _n_uniforms(self, shape):
+        return 2
+
+    def _host_params(self, B, shape, u, seed):
+        lo, hi = self.gamma
+        return {"mask": u[:, 0] < self.prob,
+                "gamma": (u[:, 1] * np.float32(hi - lo) + np.float32(lo)).astype(np.float32)}
+
+    def _device_params(self, host, shape, device):
+        return upload({"mask": host["mask"], "gamma": host["gamma"]}, device)
+
+    def chain_op(self, params, tensor):
+        dev = tensor.device
+        return ops.ChainOp(L.BA_OP_CONTRAST, mask=_mask_u8(params, dev),
+                           param=_dev(params, "gamma", dev))
+
+
+class RandScaleIntensity(_FusibleIntensity):
+    """x * (1 + factor) in the tensor dtype (scale_shift.py:19-56)."""
+
+    _stream = _rng.S_SCALE
+
+    def __init__(self, prob: float = 0.1, factors=(0.0, 0.5)):
+        super().__init__(prob=prob)
+        self.factors = _parse_range(factors)
+
+    def _n_uniforms(self, shape):
+        return 2
+
+    def _host_params(self, B, shape, u, seed):
+        lo, hi = self.factors
+        return {"mask": u[:, 0] < self.prob,
+                "factor": (u[:, 1] * np.float32(hi - lo) + np.float32(lo)).astype(np.float32)}
+
+    def _device_params(self, host, shape, device):
+        return upload({"mask": host["mask"], "factor": host["factor"]}, device)
+
+    def chain_op(self, params, tensor):
+        dev = tensor.device
+        return ops.ChainOp(L.BA_OP_SCALE, mask=_mask_u8(params, dev),
+                           param=_dev(params, "factor", dev))
+
+
+class RandShiftIntensity(_FusibleIntensity):
+    """x + offset in the tensor dtype, optional clamp (scale_shift.py:72-113)."""
+
+    _stream = _rng.S_SHIFT
+
+    def __init__(self, prob: float = 0.1, offsets=(-0.1, 0.1), safe: bool = False):
+        super().__init__(prob=prob)
+        self.offsets = _parse_range(offsets)
+        self.safe = safe
+
+    def _n_uniforms(self, shape):
+        return 2
+
+    def _host_params(self, B, shape, u, seed):
+        lo, hi = self.offsets
+        return {"mask": u[:, 0] < self.prob,
+                "offset": (u[:, 1] * np.float32(hi - lo) + np.float32(lo)).astype(np.float32)}
+
+    def _device_params(self, host, shape, device):
+        return upload({"mask": host["mask"], "offset": host["offset"]}, device)
+
+    def chain_op(self, params, tensor):
+        dev = tensor.device
+        return ops.ChainOp(L.BA_OP_SHIFT, flags=L.BA_SHIFT_SAFE if self.safe else 0,
+                           mask=_mask_u8(params, dev), param=_dev(params, "offset", dev))
+
+
+class RandBiasField(_FusibleIntensity):
+    """x * exp(sum c * L_i L_j L_k), Legendre basis evaluated in-kernel
+    (bias_field.py:56-112)."""
+
+    _stream = _rng.S_BIAS
+
+    def __init__(self, prob: float = 0.1, degree: int = 3, coeff_range=(0.0, 0.1)):
+        super().__init__(prob=prob)
+        if degree < 1:
+            raise ValueError(f"degree should be no less than 1, got {degree}.")
+        self.degree = degree
+        self.coeff_range = coeff_range
+
+    @property
+    def n_coeff(self) -> int:
+        d = self.degree
+        return (d + 1) * (d + 2) * (d + 3) // 6
+
+    def _n_uniforms(self, shape):
+        return 1 + self.n_coeff
+
+    def _host_params(self, B, shape, u, seed):
+        lo, hi = self.coeff_range
+        return {"mask": u[:, 0] < self.prob,
+                "coeffs": (u[:, 1:] * np.float32(hi - lo) + np.float32(lo)).astype(np.float32)}
+
+    def _device_params(self, host, shape, device):
+        return upload({"mask": host["mask"], "coeffs": host["coeffs"]}, device)
+
+    def chain_op(self, params, tensor):
+        dev = tensor.device
+        coeffs = params["coeffs"].to(device=dev, dtype=torch.float32).contiguous()
+        return ops.ChainOp(L.BA_OP_BIAS_FIELD, mask=_mask_u8(params, dev), param=coeffs,
+                           degree=self.degree)
+
+
+class ScaleIntensity(_FusibleIntensity):
+    """Rescale to [minv, maxv] with per-(element, channel) or per-element
+    min/max, in the tensor dtype (contrast.py:8-68)."""
+
+    def __init__(self, minv=0.0, maxv=1.0, factor=None, channel_wise: bool = True):
+        super().__init__(prob=1.0)
+        self.minv = minv
+        self.maxv = maxv
+        self.factor = factor
+        self.channel_wise = channel_wise
+
+    def chain_op(self, params, tensor):
+        if self.factor is not None:
+            return ops.ChainOp(L.BA_OP_RESCALE, flags=L.BA_RESCALE_FACTOR, c0=self.factor)
+        flags = 0
+        if self.minv is not None:
+            flags |= L.BA_RESCALE_MINV
+        if self.maxv is not None:
+            flags |= L.BA_RESCALE_MAXV
+        if self.channel_wise:
+            flags |= L.BA_RESCALE_CHANNEL
+        return ops.ChainOp(L.BA_OP_RESCALE, flags=flags, c0=self.minv or 0.0,
+                           c1=self.maxv or 0.0)
+
+    def apply(self, tensor, params):
+        if self.factor is None and self.minv is None and self.maxv is None:
+            return tensor
+        return super().apply(tensor, params)
+
+
+class RandGaussianSmooth(BatchTransform):
+    """Separable Gaussian blur with per-element, per-axis sigma
+    (smooth.py:91-143)."""
+
+    _stream = _rng.S_SMOOTH
+
+    def __init__(self, prob: float = 0.1, sigma_x=(0.25, 1.5), sigma_y=(0.25, 1.5),
+                 sigma_z=(0.25, 1.5), padding_mode=None):
+        super().__init__(prob=prob)
+        self.sigma_x, self.sigma_y, self.sigma_z = sigma_x, sigma_y, sigma_z
+        self.padding_mode = padding_mode
+
+    def sample_host(self, batch_size, shape):
+        seed = _rng.draw_seed()
+        u_all, row = _rng.global_uniforms(seed, self._stream, batch_size, 4)
+        host = {"mask": u_all[row:row + batch_size, 0] < self.prob}
+        for i, (name, rng) in enumerate((("sigma_x", self.sigma_x), ("sigma_y", self.sigma_y),
+                                         ("sigma_z", self.sigma_z))):
+            lo, hi = rng
+            s_all = (u_all[:, 1 + i] * np.float32(hi - lo) + np.float32(lo)).astype(np.float32)
+            host[name] = s_all[row:row + batch_size]
+            # gaussian_1d_batch pads every kernel to the batch-max tail
+            host["K_" + name] = ops.gauss_taps_len(
+                float(np.maximum(s_all, np.float32(1e-6)).max()) if len(s_all) else 1e-6, 4.0)
+        return host
+
+    def sample_params(self, batch_size, shape, device):
+        host = self.sample_host(batch_size, shape)
+        p = upload({k: host[k] for k in ("mask", "sigma_x", "sigma_y", "sigma_z")}, device)
+        p["kernel_h"] = ops.gauss_taps(p["sigma_x"], host["K_sigma_x"])
+        p["kernel_w"] = ops.gauss_taps(p["sigma_y"], host["K_sigma_y"])
+        p["kernel_d"] = ops.gauss_taps(p["sigma_z"], host["K_sigma_z"])
+        p["_host"] = host
+        return p
+
+    def apply(self, tensor, params):
+        return ops.smooth3d(tensor, params["kernel_h"], params["kernel_w"], params["kernel_d"],
+                            mask=params["mask"], padding_mode=self.padding_mode)
+
+
+# ---------------------------------------------------------------------------
+# Dict wrappers (same keys/params sharing as the reference)
+# ---------------------------------------------------------------------------
+
+class RandGaussianNoised(BatchDictTransform):
+    def __init__(self, keys, prob: float = 0.1, mean=0.0, std=0.1):
+        super().__init__(keys=keys, transform=RandGaussianNoise(prob=prob, mean=mean, std=std))
+
+
+class RandAdjustContrastd(BatchDictTransform):
+    def __init__(self, keys, prob: float = 0.1, gamma=(0.5, 4.5)):
+        super().__init__(keys=keys, transform=RandAdjustContrast(prob=prob, gamma=gamma))
+
+
+class RandScaleIntensityd(BatchDictTransform):
+    def __init__(self, keys, prob: float = 0.1, factors=(0.0, 0.5)):
+        super().__init__(keys=keys, transform=RandScaleIntensity(prob=prob, factors=factors))
+
+
+class RandShiftIntensityd(BatchDictTransform):
+    def __init__(self, keys, prob: float = 0.1, offsets=(-0.1, 0.1), safe: bool = False):
+        super().__init__(keys=keys,
+                         transform=RandShiftIntensity(prob=prob, offsets=offsets, safe=safe))
+
+
+class RandBiasFieldd(BatchDictTransform):
+    def __init__(self, keys, prob: float = 0.1, degree: int = 3, coeff_range=(0.0, 0.1)):
+        super().__init__(keys=keys, transform=RandBiasField(prob=prob, degree=degree,
+                                                            coeff_range=coeff_range))
+
+
+class ScaleIntensityd(BatchDictTransform):
+    def __init__(self, keys, minv=0.0, maxv=1.0, factor=None, channel_wise: bool = True):
+        super().__init__(keys=keys, transform=ScaleIntensity(minv=minv, maxv=maxv, factor=factor,
+                                                             channel_wise=channel_wise))
+
+
+class RandGaussianSmoothd(BatchDictTransform):
+    def __init__(self, keys, prob: float = 0.1, sigma_x=(0.25, 1.5), sigma_y=(0.25, 1.5),
+                 sigma_z=(0.25, 1.5), padding_mode=None):
+        super().__init__(keys=keys, transform=RandGaussianSmooth(
+            prob=prob, sigma_x=sigma_x, sigma_y=sigma_y, sigma_z=sigma_z,
+            padding_mode=padding_mode))

@@ -1,0 +1,248 @@
+"""Functional entry points: torch tensors in, C-ABI calls out.
+
+Each function validates tensors (CUDA, contiguous, fp32/bf16), allocates the
+outputs and scratch with torch's caching allocator, and enqueues the kernels
+on torch's current stream.  These are what the transform classes call; they
+can also be used directly.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib as L
+
+
+def _contig(t: torch.Tensor, name: str) -> torch.Tensor:
+    L.require_cuda(t, name)
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def _dev_f32(x, device, name):
+    """Small parameter arrays (numpy or tensor) as contiguous fp32 on device."""
+    if isinstance(x, torch.Tensor):
+        return x.to(device=device, dtype=torch.float32).contiguous()
+    arr = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+    return torch.from_numpy(arr).to(device, non_blocking=False)
+
+
+def _dev_mask(mask, B, device):
+    if mask is None:
+        return None
+    if isinstance(mask, torch.Tensor):
+        m = mask.to(device=device).reshape(B)
+        return (m != 0).to(torch.uint8).contiguous()
+    arr = np.ascontiguousarray(np.asarray(mask).reshape(B).astype(np.uint8))
+    return torch.from_numpy(arr).to(device)
+
+
+# ---------------------------------------------------------------------------
+# Geometric
+# ---------------------------------------------------------------------------
+
+def resample3d(tensors, *, affine=None, theta=None, grid=None, modes="bilinear",
+               paddings="zeros", align_corners=False, mask=None, out=None):
+    """Resample one or more (B,C,H,W,D) tensors through one shared map.
+
+    Exactly one of ``affine`` (MONAI (B,4,4)), ``theta`` (affine_grid
+    (B,3|4,4)) or ``grid`` (grid_sample (B,H,W,D,3)) gives the map.  ``modes``
+    and ``paddings`` are a string or one entry per tensor.  Masked-out
+    elements are copied.  Returns a list of new tensors (or fills ``out``).
+    """
+    single = isinstance(tensors, torch.Tensor)
+    ts = [tensors] if single else list(tensors)
+    if not 1 <= len(ts) <= L.BA_MAX_KEYS:
+        raise ValueError(f"resample3d takes 1..{L.BA_MAX_KEYS} tensors")
+    ts = [_contig(t, "tensor") for t in ts]
+    for t in ts:
+        if t.dim() != 5:
+            raise ValueError(f"expected (B,C,H,W,D) tensors, got shape {tuple(t.shape)}")
+    B, _, H, W, D = ts[0].shape
+    device = ts[0].device
+    for t in ts[1:]:
+        if t.shape[0] != B or tuple(t.shape[2:]) != (H, W, D) or t.device != device:
+            raise ValueError("resample3d: tensors must share batch, spatial shape and device")
+    modes = [modes] * len(ts) if isinstance(modes, str) else list(modes)
+    paddings = [paddings] * len(ts) if isinstance(paddings, str) else list(paddings)
+    for m in modes:
+        if m not in L.MODES:
+            raise ValueError(f"unsupported interpolation mode {m!r} (bilinear or nearest)")
+    for p in paddings:
+        if p not in L.PADDINGS:
+            raise ValueError(f"unsupported padding_mode {p!r} (zeros, border or reflection)")
+    if sum(x is not None for x in (affine, theta, grid)) != 1:
+        raise ValueError("resample3d needs exactly one of affine, theta or grid")
+    if affine is not None:
+        xf = _dev_f32(affine, device, "affine").reshape(B, -1)
+        kind, stride = L.BA_XFORM_AFFINE, xf.shape[1]
+        if stride != 16:
+            raise ValueError("affine must be (B,4,4)")
+    elif theta is not None:
+        xf = _dev_f32(theta, device, "theta").reshape(B, -1)
+        kind, stride = L.BA_XFORM_THETA, xf.shape[1]
+        if stride not in (12, 16):
+            raise ValueError("theta must be (B,3,4) or (B,4,4)")
+    else:
+        xf = _dev_f32(grid, device, "grid")
+        if tuple(xf.shape) != (B, H, W, D, 3):
+            raise ValueError(f"grid must be {(B, H, W, D, 3)}, got {tuple(xf.shape)}")
+        kind, stride = L.BA_XFORM_GRID, 0
+    m = _dev_mask(mask, B, device)
+    outs = list(out) if out is not None else [torch.empty_like(t) for t in ts]
+    d = L.ResampleDesc()
+    d.batch, d.H, d.W, d.D = B, H, W, D
+    d.xform_kind = kind
+    d.align_corners = int(bool(align_corners))
+    d.n_keys = len(ts)
+    d.xform = xf.data_ptr()
+    d.xform_stride = stride
+    d.mask = L.ptr(m)
+    for i, (t, o) in enumerate(zip(ts, outs)):
+        k = d.keys[i]
+        k.src, k.dst = t.data_ptr(), o.data_ptr()
+        k.channels = t.shape[1]
+        k.dtype = L.dtype_code(t)
+        k.mode = L.MODES[modes[i]]
+        k.padding = L.PADDINGS[paddings[i]]
+    L.check(L.lib.ba_resample3d(ctypes.byref(d), L.stream_ptr(device)), "ba_resample3d")
+    return outs[0] if single else outs
+
+
+# ---------------------------------------------------------------------------
+# Intensity chain
+# ---------------------------------------------------------------------------
+
+class ChainOp:
+    """One op of a fused intensity chain (device tensors for its params)."""
+
+    __slots__ = ("kind", "flags", "mask", "param", "param2", "noise", "seed", "elem_offset",
+                 "degree", "c0", "c1")
+
+    def __init__(self, kind, flags=0, mask=None, param=None, param2=None, noise=None, seed=0,
+                 elem_offset=0, degree=0, c0=0.0, c1=0.0):
+        self.kind, self.flags, self.mask = kind, flags, mask
+        self.param, self.param2, self.noise = param, param2, noise
+        self.seed, self.elem_offset, self.degree = seed, elem_offset, degree
+        self.c0, self.c1 = c0, c1
+
+
+def intensity_chain(x: torch.Tensor, ops, out: torch.Tensor | None = None,
+                    inplace: bool = False) -> torch.Tensor:
+    """Apply a list of ChainOp to x in as few HBM passes as possible."""
+    x = _contig(x, "tensor")
+    if x.dim() != 5:
+        raise ValueError(f"expected a (B,C,H,W,D) tensor, got shape {tuple(x.shape)}")
+    if not 1 <= len(ops) <= L.BA_MAX_OPS:
+        raise ValueError(f"intensity_chain takes 1..{L.BA_MAX_OPS} ops")
+    B, C, H, W, D = x.shape
+    if out is None:
+        out = x if inplace else torch.empty_like(x)
+    d = L.ChainDesc()
+    d.src, d.dst = x.data_ptr(), out.data_ptr()
+    d.batch, d.channels, d.H, d.W, d.D = B, C, H, W, D
+    d.dtype = L.dtype_code(x)
+    d.n_ops = len(ops)
+    keep = []
+    for i, op in enumerate(ops):
+        o = d.ops[i]
+        o.kind, o.flags = op.kind, op.flags
+        for name in ("mask", "param", "param2", "noise"):
+            t = getattr(op, name)
+            if t is not None:
+                if t.device != x.device:
+                    raise ValueError(f"op {i} {name} is on {t.device}, tensor on {x.device}")
+                keep.append(t)
+            setattr(o, name, L.ptr(t))
+        o.seed = int(op.seed) & 0xFFFFFFFFFFFFFFFF
+        o.elem_offset = int(op.elem_offset)
+        o.degree = int(op.degree)
+        o.c0, o.c1 = float(op.c0), float(op.c1)
+    nbytes = L.lib.ba_intensity_workspace_bytes(ctypes.byref(d))
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device) if nbytes else None
+    L.check(L.lib.ba_intensity_chain(ctypes.byref(d), L.ptr(ws), nbytes, L.stream_ptr(x.device)),
+            "ba_intensity_chain")
+    return out
+
+
+def minmax(x: torch.Tensor, n_groups: int):
+    """Per-group (min, max) of x viewed as (n_groups, -1), fp32 tensors."""
+    x = _contig(x, "tensor")
+    if x.numel() % max(n_groups, 1):
+        raise ValueError("minmax: numel is not a multiple of n_groups")
+    stats = torch.empty(n_groups, 2, dtype=torch.float32, device=x.device)
+    L.check(L.lib.ba_minmax(x.data_ptr(), L.dtype_code(x), n_groups,
+                            x.numel() // max(n_groups, 1), stats.data_ptr(),
+                            L.stream_ptr(x.device)), "ba_minmax")
+    return stats[:, 0], stats[:, 1]
+
+
+# ---------------------------------------------------------------------------
+# Smoothing / elastic
+# ---------------------------------------------------------------------------
+
+def gauss_taps_len(max_sigma: float, truncated: float) -> int:
+    return int(L.lib.ba_gauss_taps_len(float(max_sigma), float(truncated)))
+
+
+def gauss_taps(sigmas: torch.Tensor, K: int) -> torch.Tensor:
+    """(B,K) taps of gaussian_1d_batch for sigmas already on device."""
+    s = sigmas.to(torch.float32).contiguous()
+    L.require_cuda(s, "sigmas")
+    taps = torch.empty(s.numel(), K, dtype=torch.float32, device=s.device)
+    L.check(L.lib.ba_gauss_taps(s.data_ptr(), s.numel(), K, taps.data_ptr(),
+                                L.stream_ptr(s.device)), "ba_gauss_taps")
+    return taps
+
+
+def smooth3d(x: torch.Tensor, taps_h, taps_w, taps_d, mask=None,
+             padding_mode=None) -> torch.Tensor:
+    """Separable Gaussian smoothing with per-element taps; padding_mode is
+    None/"constant" (zeros), "reflect" or "replicate" as in F.pad."""
+    if padding_mode not in L.SMOOTH_PADS:
+        raise ValueError(f"unsupported padding_mode {padding_mode!r}")
+    x = _contig(x, "tensor")
+    B, C, H, W, D = x.shape
+    th, tw, td = (_dev_f32(t, x.device, "taps") for t in (taps_h, taps_w, taps_d))
+    m = _dev_mask(mask, B, x.device)
+    out = torch.empty_like(x)
+    nbytes = L.lib.ba_smooth_workspace_bytes(B, C, H, W, D)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+    L.check(L.lib.ba_smooth3d(x.data_ptr(), out.data_ptr(), L.dtype_code(x), B, C, H, W, D,
+                              th.data_ptr(), th.shape[1], tw.data_ptr(), tw.shape[1],
+                              td.data_ptr(), td.shape[1], L.SMOOTH_PADS[padding_mode], L.ptr(m),
+                              ws.data_ptr(), nbytes,
+                              L.stream_ptr(x.device)), "ba_smooth3d")
+    return out
+
+
+def elastic_grid(shape, taps, magnitude, *, u=None, seed=0, elem_offset=0,
+                 device=None) -> torch.Tensor:
+    """grid_sample grid (B,H,W,D,3) of Rand3DElastic from taps (B,K) and
+    magnitude (B,); the uniform draw u (B,3,H,W,D) is generated in-kernel
+    from (seed, elem_offset) unless given."""
+    B, H, W, D = shape
+    device = device or (u.device if u is not None else taps.device)
+    tp = _dev_f32(taps, device, "taps")
+    mg = _dev_f32(magnitude, device, "magnitude").reshape(B)
+    uu = None if u is None else _contig(u.to(torch.float32), "u")
+    grid = torch.empty(B, H, W, D, 3, dtype=torch.float32, device=device)
+    nbytes = L.lib.ba_elastic_workspace_bytes(B, H, W, D)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+    L.check(L.lib.ba_elastic_grid(L.ptr(uu), int(seed) & 0xFFFFFFFFFFFFFFFF, int(elem_offset),
+                                  B, H, W, D, tp.data_ptr(), tp.shape[1], mg.data_ptr(),
+                                  grid.data_ptr(), ws.data_ptr(), nbytes,
+                                  L.stream_ptr(device)), "ba_elastic_grid")
+    return grid
+
+
+def host_uniform(seed: int, stream: int, elem_offset: int, n_elems: int,
+                 per_elem: int) -> np.ndarray:
+    """(n_elems, per_elem) uniforms in [0,1) keyed on global element index."""
+    out = np.empty((n_elems, per_elem), np.float32)
+    if n_elems and per_elem:
+        L.lib.ba_host_uniform(int(seed) & 0xFFFFFFFFFFFFFFFF, int(stream) & 0xFFFF,
+                              int(elem_offset), n_elems, per_elem, out.ctypes.data)
+    return out
+

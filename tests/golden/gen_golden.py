@@ -1,0 +1,211 @@
+"""Generate the golden fixtures of tests/golden/ from the reference itself.
+
+Runs halleewong/batchaug's PyTorch backend (``batchaug.pytorch``,
+``batchaug.compose``) on CPU with seeded inputs and stores inputs, the
+sampled params and the reference outputs as small .npz files (bf16 tensors
+as uint16 bit patterns).  The oracle is pinned against these
+(tests/test_oracle_golden.py) and the CUDA path is checked against both.
+
+    python tests/golden/gen_golden.py --reference /path/to/batchaug
+
+Needs the reference checkout on disk; the fixtures it writes are committed so
+nothing at test time reads the reference.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+
+OUT = os.path.dirname(os.path.abspath(__file__))
+
+
+def npy(t: torch.Tensor) -> np.ndarray:
+    t = t.detach().cpu()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(np.uint16).copy()
+    if t.dtype == torch.bool:
+        return t.numpy().astype(np.uint8)
+    return t.numpy().copy()
+
+
+def save(name: str, **arrays):
+    np.savez_compressed(os.path.join(OUT, name + ".npz"),
+                        **{k: (npy(v) if isinstance(v, torch.Tensor) else np.asarray(v))
+                           for k, v in arrays.items()})
+    print("wrote", name)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("BATCHAUG_REFERENCE", ""))
+    args = ap.parse_args()
+    if args.reference:
+        sys.path.insert(0, args.reference)
+    import torch.nn.functional as F
+
+    import batchaug.pytorch as P
+    from batchaug.pytorch.geometric.affine import monai_affine_to_theta
+    from batchaug.pytorch.intensity.smooth import gaussian_1d_batch
+    dev = torch.device("cpu")
+    torch.set_num_threads(1)
+
+    # --- resample: every mode/padding/align, fp32 and bf16, non-cubic -------
+    torch.manual_seed(101)
+    B, C, H, W, D = 2, 2, 9, 10, 12
+    x = torch.randn(B, C, H, W, D)
+    t = P.RandAffine(prob=1.0, rotate_range=0.785, shear_range=0.3, translate_range=3,
+                     scale_range=0.1)
+    p = t.sample_params(B, x.shape, dev)
+    out = {}
+    for dt in ("f32", "bf16"):
+        xt = x if dt == "f32" else x.bfloat16()
+        for mode in ("bilinear", "nearest"):
+            for pad in ("zeros", "border", "reflection"):
+                for align in (0, 1):
+                    grid = F.affine_grid(p["theta"][:, :3, :], list(x.shape), align_corners=bool(align))
+                    r = F.grid_sample(xt.float(), grid, mode=mode, padding_mode=pad,
+                                      align_corners=bool(align)).to(xt.dtype)
+                    out[f"{dt}_{mode}_{pad}_{align}"] = r
+    save("resample_modes", x=x, x_bf16=x.bfloat16(), affine=p["affine"], theta=p["theta"], **out)
+
+    # --- RandAffine.apply with a partial mask, border padding (config 2 style)
+    torch.manual_seed(102)
+    x = torch.rand(3, 1, 12, 12, 12)
+    t = P.RandAffine(prob=0.5, rotate_range=0.785, shear_range=0.3, translate_range=5,
+                     scale_range=0.1, padding_mode="border")
+    p = t.sample_params(3, x.shape, dev)
+    p["mask"] = torch.tensor([True, False, True])
+    save("affine_apply_border", x=x, mask=p["mask"], theta=p["theta"], affine=p["affine"],
+         out=t.apply(x, p))
+
+    # --- Compose._materialize of flip∘affine on vol (bilinear) + seg (nearest)
+    torch.manual_seed(103)
+    vol = torch.randn(2, 1, 16, 16, 16)
+    seg = torch.randint(0, 5, (2, 1, 16, 16, 16)).float()
+    flip = P.RandAxisFlip(prob=0.5)
+    aff = P.RandAffine(prob=1.0, rotate_range=0.785, shear_range=0.3, translate_range=5)
+    pf = flip.sample_params(2, vol.shape, dev)
+    pa = aff.sample_params(2, vol.shape, dev)
+    A = flip.to_affine(pf) @ aff.to_affine(pa)
+    m = pf["mask"] | pa["mask"]
+    theta = monai_affine_to_theta(A, vol.shape[2:], dev)
+    grid = F.affine_grid(theta[:, :3, :], list(vol.shape), align_corners=False)
+    vo = F.grid_sample(vol, grid, mode="bilinear", padding_mode="zeros", align_corners=False)
+    so = F.grid_sample(seg, grid, mode="nearest", padding_mode="zeros", align_corners=False)
+    vo = torch.where(m[:, None, None, None, None], vo, vol)
+    so = torch.where(m[:, None, None, None, None], so, seg)
+    save("compose_materialize", vol=vol, seg=seg, affine=A, mask=m, vol_out=vo, seg_out=so)
+
+    # --- exact voxel maps: eager flip and rot90 vs their affines -------------
+    torch.manual_seed(104)
+    v = torch.randn(4, 2, 8, 8, 6)
+    fl = P.RandAxisFlip(prob=1.0)
+    pfl = fl.sample_params(4, v.shape, dev)
+    r9 = P.RandRotate90(prob=1.0, max_k=3, spatial_axes=(0, 1))
+    pr = r9.sample_params(4, v.shape, dev)
+    save("flip_rot90", x=v, flip_axes=pfl["axes"], flip_affine=fl.to_affine(pfl),
+         flip_out=fl.apply(v, pfl), rot_k=pr["k"], rot_affine=r9.to_affine(pr),
+         rot_out=r9.apply(v, pr))
+
+    # --- elastic: grid from its uniform draw, and the resample with it -------
+    torch.manual_seed(105)
+    B, H, W, D = 2, 12, 14, 16
+    el = P.Rand3DElastic(prob=1.0, sigma_range=(5.0, 7.0), magnitude_range=(50.0, 150.0))
+    pe = el.sample_params(B, (B, 1, H, W, D), dev)
+    torch.manual_seed(105)
+    _mask = torch.rand(B)
+    u = torch.rand(B, 3, H, W, D)
+    sigma = torch.rand(B) * 2.0 + 5.0
+    magnitude = torch.rand(B) * 100.0 + 50.0
+    taps = gaussian_1d_batch(sigma, truncated=3.0)
+    vol = torch.rand(B, 2, H, W, D)
+    seg = torch.randint(0, 8, (B, 1, H, W, D)).float()
+    save("elastic", u=u, sigma=sigma, magnitude=magnitude, taps=taps, grid=pe["grid"],
+         vol=vol, seg=seg, vol_out=el.apply(vol, pe, mode="bilinear"),
+         seg_out=el.apply(seg, pe, mode="nearest"))
+
+    # --- intensity ops, fp32 and bf16 ----------------------------------------
+    for dt, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
+        torch.manual_seed(106)
+        B, C, H, W, D = 3, 2, 9, 10, 11
+        x = (0.5 + 0.2 * torch.randn(B, C, H, W, D)).clamp(0, 1).to(dt)
+        rec = {"x": x}
+        tn = P.RandGaussianNoise(prob=0.5, std=(0.1, 0.5))
+        pn = tn.sample_params(B, x.shape, dev)
+        rec.update(noise=pn["noise"], noise_mask=pn["mask"], noise_out=tn.apply(x, pn))
+        tc = P.RandAdjustContrast(prob=0.5, gamma=(0.5, 2.0))
+        pc = tc.sample_params(B, x.shape, dev)
+        rec.update(gamma=pc["gamma"], contrast_mask=pc["mask"], contrast_out=tc.apply(x, pc))
+        ts = P.RandScaleIntensity(prob=0.5, factors=0.2)
+        ps = ts.sample_params(B, x.shape, dev)
+        rec.update(factor=ps["factor"], scale_mask=ps["mask"], scale_out=ts.apply(x, ps))
+        th = P.RandShiftIntensity(prob=0.5, offsets=0.1, safe=True)
+        ph = th.sample_params(B, x.shape, dev)
+        rec.update(offset=ph["offset"], shift_mask=ph["mask"], shift_out=th.apply(x, ph))
+        tb = P.RandBiasField(prob=0.5, degree=3, coeff_range=(0.0, 0.1))
+        pb = tb.sample_params(B, x.shape, dev)
+        rec.update(coeffs=pb["coeffs"], bias_mask=pb["mask"], bias_out=tb.apply(x, pb))
+        xc = x.clone()
+        xc[1, 0] = 0.25  # a constant (element, channel) group
+        rec.update(xconst=xc, scaleint_cw_out=P.ScaleIntensity().apply(xc, {}),
+                   scaleint_el_out=P.ScaleIntensity(channel_wise=False).apply(xc, {}),
+                   scaleint_m13_out=P.ScaleIntensity(minv=-1.0, maxv=3.0).apply(x, {}),
+                   scaleint_factor_out=P.ScaleIntensity(factor=0.5).apply(x, {}))
+        tg = P.RandGaussianSmooth(prob=0.5, sigma_x=(0.5, 1.5), sigma_y=(0.5, 1.5),
+                                  sigma_z=(0.5, 1.5))
+        pg = tg.sample_params(B, x.shape, dev)
+        rec.update(kernel_h=pg["kernel_h"], kernel_w=pg["kernel_w"], kernel_d=pg["kernel_d"],
+                   sigma_x=pg["sigma_x"], smooth_mask=pg["mask"], smooth_out=tg.apply(x, pg))
+        for pm in ("reflect", "replicate"):
+            tgp = P.RandGaussianSmooth(prob=1.0, sigma_x=(0.5, 1.5), sigma_y=(0.5, 1.5),
+                                       sigma_z=(0.5, 1.5), padding_mode=pm)
+            rec[f"smooth_{pm}_out"] = tgp.apply(x, {**pg, "mask": torch.ones(B, dtype=torch.bool)})
+        save(f"intensity_{tag}", **rec)
+
+    # --- config 3 chain (noise -> contrast -> scale -> shift -> ScaleIntensity)
+    torch.manual_seed(107)
+    B, C, H, W, D = 4, 2, 10, 12, 8
+    x = (0.5 + 0.2 * torch.randn(B, C, H, W, D)).clamp(0, 1).bfloat16()
+    chain = [P.RandGaussianNoise(prob=1.0, std=(0.1, 0.5)),
+             P.RandAdjustContrast(prob=1.0, gamma=(0.5, 2.0)),
+             P.RandScaleIntensity(prob=1.0, factors=0.2),
+             P.RandShiftIntensity(prob=1.0, offsets=0.1),
+             P.ScaleIntensity(minv=0.0, maxv=1.0)]
+    ps = [c.sample_params(B, x.shape, dev) for c in chain]
+    y = x
+    for c, pp in zip(chain, ps):
+        y = c.apply(y, pp)
+    save("chain_cfg3", x=x, noise=ps[0]["noise"], gamma=ps[1]["gamma"], factor=ps[2]["factor"],
+         offset=ps[3]["offset"], out=y)
+
+    # --- config 1 pipeline with the reference's own params --------------------
+    torch.manual_seed(108)
+    vol = torch.randn(2, 1, 16, 16, 16)
+    seg = torch.randint(0, 5, (2, 1, 16, 16, 16)).float()
+    flip = P.RandAxisFlip(prob=0.5)
+    aff = P.RandAffine(prob=1.0, rotate_range=0.785, shear_range=0.3, translate_range=5)
+    pf = flip.sample_params(2, vol.shape, dev)
+    pa = aff.sample_params(2, vol.shape, dev)
+    A = flip.to_affine(pf) @ aff.to_affine(pa)
+    m = pf["mask"] | pa["mask"]
+    theta = monai_affine_to_theta(A, vol.shape[2:], dev)
+    grid = F.affine_grid(theta[:, :3, :], list(vol.shape), align_corners=False)
+    vo = torch.where(m[:, None, None, None, None],
+                     F.grid_sample(vol, grid, mode="bilinear", align_corners=False), vol)
+    so = torch.where(m[:, None, None, None, None],
+                     F.grid_sample(seg, grid, mode="nearest", align_corners=False), seg)
+    tn = P.RandGaussianNoise(prob=0.1, std=0.1)
+    pn = tn.sample_params(2, vol.shape, dev)
+    pn["mask"] = torch.tensor([True, False])
+    vo = tn.apply(vo, pn)
+    vo = P.ScaleIntensity().apply(vo, {})
+    save("pipeline_cfg1", vol=vol, seg=seg, affine=A, mask=m, noise=pn["noise"],
+         noise_mask=pn["mask"], vol_out=vo, seg_out=so)
+
+
+if __name__ == "__main__":
+    main()
