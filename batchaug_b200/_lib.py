@@ -1,6 +1,6 @@
 """ctypes binding of libbatchaug_b200.so (the C ABI in include/batchaug_b200.h).
 
-The shared library is built in-tree by ``python -m batchaug_b200.build``.
+The shared library is built in-tree by ``python batchaug_b200/build.py``.
 There is no fallback: if the library is missing or fails to load, importing
 ``batchaug_b200`` raises ImportError.  Status codes map to exceptions as the
 reference does for bad arguments (``ValueError``, batchaug/_backend.py:9-11,
@@ -83,6 +83,7 @@ SIGNATURES = {
     "ba_host_uniform": (None, [_U64, ctypes.c_uint32, _U64, _I64, _I64, _P]),
     "ba_last_error": (ctypes.c_char_p, []),
     "ba_version": (_I32, []),
+    "ba_kernel_launches": (ctypes.c_uint64, []),
 }
 
 
@@ -90,7 +91,7 @@ def _load():
     if not os.path.exists(LIB_PATH):
         raise ImportError(
             f"batchaug_b200: CUDA library {LIB_PATH} is missing; build it with "
-            "`python -m batchaug_b200.build` (there is no CPU fallback)")
+            "`python batchaug_b200/build.py` (there is no CPU fallback)")
     lib = ctypes.CDLL(LIB_PATH)
     for name, (res, args) in SIGNATURES.items():
         fn = getattr(lib, name)
@@ -117,6 +118,11 @@ def dtype_code(t: torch.Tensor) -> int:
     if t.dtype == torch.bfloat16:
         return BA_BF16
     raise ValueError(f"batchaug_b200 supports float32 and bfloat16 tensors, got {t.dtype}")
+
+
+def kernel_launches() -> int:
+    """Kernels the library has enqueued in this process so far."""
+    return int(lib.ba_kernel_launches())
 
 
 def stream_ptr(device: torch.device) -> int:

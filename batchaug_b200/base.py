@@ -15,27 +15,35 @@ import torch
 from . import _rng
 
 
-def upload(arrays: dict, device) -> dict:
-    """Copy a dict of small numpy arrays to ``device`` in one transfer per
-    dtype group (float32 arrays packed together; bool arrays together)."""
+def to_device(arr: np.ndarray, device) -> torch.Tensor:
+    """Asynchronous host-to-device copy of a small numpy array through pinned
+    memory (a pageable copy would synchronise the stream).  torch's caching
+    host allocator keeps the pinned block until the copy has completed."""
     device = torch.device(device)
+    t = torch.from_numpy(np.ascontiguousarray(arr))
+    if device.type != "cuda":
+        return t.to(device)
+    return t.pin_memory().to(device, non_blocking=True)
+
+
+def upload(arrays: dict, device) -> dict:
+    """Copy a dict of small numpy arrays to ``device``: float32 arrays packed
+    into one transfer, every other array (bool masks, int64 indices) in one
+    transfer of its own."""
     out = {}
     floats = {k: np.ascontiguousarray(v, dtype=np.float32) for k, v in arrays.items()
               if v.dtype != np.bool_ and v.dtype.kind == "f"}
     others = {k: v for k, v in arrays.items() if k not in floats}
     if floats:
         flat = np.concatenate([v.ravel() for v in floats.values()])
-        dev = torch.from_numpy(flat).to(device, non_blocking=False)
+        dev = to_device(flat, device)
         pos = 0
         for k, v in floats.items():
             n = v.size
             out[k] = dev[pos:pos + n].view(v.shape)
             pos += n
     for k, v in others.items():
-        if v.dtype == np.bool_:
-            out[k] = torch.from_numpy(np.ascontiguousarray(v)).to(device)
-        else:
-            out[k] = torch.from_numpy(np.ascontiguousarray(v)).to(device)
+        out[k] = to_device(v, device)
     return out
 
 

@@ -1,6 +1,6 @@
 """Build libbatchaug_b200.so in-tree for sm_100a.
 
-    python -m batchaug_b200.build [--force] [--jobs N]
+    python batchaug_b200/build.py [--force] [--jobs N]
 
 Each ``csrc/*.cu`` is compiled separately (in parallel) to an object under
 ``batchaug_b200/_build/`` and the objects are linked into

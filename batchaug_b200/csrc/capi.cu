@@ -1,6 +1,9 @@
-// Library-wide C ABI pieces: thread-local error reporting and the version.
+// Library-wide C ABI pieces: thread-local error reporting, the version, the
+// launch counter and the host-side Philox draw of per-element parameters.
 #include <stdarg.h>
 #include <stdio.h>
+
+#include <atomic>
 
 #include "ba_common.cuh"
 #include "philox.cuh"
@@ -8,6 +11,7 @@
 namespace ba {
 namespace {
 thread_local char g_last_error[512] = {0};
+std::atomic<uint64_t> g_launches{0};
 }
 
 void set_error(const char* fmt, ...) {
@@ -25,6 +29,7 @@ ba_status check_launch(const char* what) {
     set_error("%s: CUDA launch failed: %s", what, cudaGetErrorString(e));
     return BA_ECUDA;
   }
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   return BA_OK;
 }
 
@@ -50,3 +55,7 @@ extern "C" void ba_host_uniform(uint64_t seed, uint32_t stream, uint64_t elem_of
 }
 
 extern "C" int32_t ba_version(void) { return (1 << 16) | 0; }
+
+extern "C" uint64_t ba_kernel_launches(void) {
+  return ba::g_launches.load(std::memory_order_relaxed);
+}

@@ -207,6 +207,9 @@ class RandBiasField(_FusibleIntensity):
     def chain_op(self, params, tensor):
         dev = tensor.device
         coeffs = params["coeffs"].to(device=dev, dtype=torch.float32).contiguous()
+        if tuple(coeffs.shape) != (tensor.shape[0], self.n_coeff):
+            raise ValueError(f"coeffs must be {(tensor.shape[0], self.n_coeff)} for degree "
+                             f"{self.degree}, got {tuple(coeffs.shape)}")
         return ops.ChainOp(L.BA_OP_BIAS_FIELD, mask=_mask_u8(params, dev), param=coeffs,
                            degree=self.degree)
 

@@ -20,12 +20,17 @@ def _contig(t: torch.Tensor, name: str) -> torch.Tensor:
     return t if t.is_contiguous() else t.contiguous()
 
 
+def _to_device(arr: np.ndarray, device) -> torch.Tensor:
+    """Asynchronous small host-to-device copy through pinned memory."""
+    t = torch.from_numpy(np.ascontiguousarray(arr))
+    return t.pin_memory().to(device, non_blocking=True)
+
+
 def _dev_f32(x, device, name):
     """Small parameter arrays (numpy or tensor) as contiguous fp32 on device."""
     if isinstance(x, torch.Tensor):
         return x.to(device=device, dtype=torch.float32).contiguous()
-    arr = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
-    return torch.from_numpy(arr).to(device, non_blocking=False)
+    return _to_device(np.asarray(x, dtype=np.float32), device)
 
 
 def _dev_mask(mask, B, device):
@@ -33,9 +38,10 @@ def _dev_mask(mask, B, device):
         return None
     if isinstance(mask, torch.Tensor):
         m = mask.to(device=device).reshape(B)
+        if m.dtype in (torch.bool, torch.uint8):
+            return m.contiguous().view(torch.uint8)  # a view: no kernel
         return (m != 0).to(torch.uint8).contiguous()
-    arr = np.ascontiguousarray(np.asarray(mask).reshape(B).astype(np.uint8))
-    return torch.from_numpy(arr).to(device)
+    return _to_device(np.asarray(mask).reshape(B).astype(np.uint8), device)
 
 
 # ---------------------------------------------------------------------------

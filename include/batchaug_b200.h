@@ -258,6 +258,10 @@ BA_API const char* ba_last_error(void);
 /* ABI version: (major << 16) | minor. */
 BA_API int32_t ba_version(void);
 
+/* Number of CUDA kernels this library has enqueued in this process (a
+ * host-side counter, incremented after each successful launch). */
+BA_API uint64_t ba_kernel_launches(void);
+
 #ifdef __cplusplus
 }
 #endif

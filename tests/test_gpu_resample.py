@@ -1,0 +1,164 @@
+"""CUDA resample (ba_resample3d) against the oracle and the reference's golden
+outputs.  The kernel restates torch's CPU affine_grid/grid_sample operation
+by operation, so the bar here is bit-exactness for every mode, padding,
+align_corners and dtype (stricter than the 1e-5 / 2-ulp north-star bar)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from helpers import to_dev, to_np
+
+pytestmark = pytest.mark.gpu
+
+MODES = ("bilinear", "nearest")
+PADS = ("zeros", "border", "reflection")
+
+
+def _rand_affine(rng, B, scale=True):
+    """MONAI affines like RandAffine's (rotation, shear, translation, scale)."""
+    a = np.zeros((B, 4, 4), np.float32)
+    for b in range(B):
+        ang = rng.uniform(-0.785, 0.785, 3)
+        cx, cy, cz = np.cos(ang)
+        sx, sy, sz = np.sin(ang)
+        rx = np.array([[1, 0, 0], [0, cx, -sx], [0, sx, cx]])
+        ry = np.array([[cy, 0, sy], [0, 1, 0], [-sy, 0, cy]])
+        rz = np.array([[cz, -sz, 0], [sz, cz, 0], [0, 0, 1]])
+        sh = np.eye(3) + rng.uniform(-0.3, 0.3, (3, 3)) * (1 - np.eye(3))
+        sc = np.diag(1 + rng.uniform(-0.1, 0.1, 3)) if scale else np.eye(3)
+        a[b, :3, :3] = rx @ ry @ rz @ sh @ sc
+        a[b, :3, 3] = rng.uniform(-5, 5, 3)
+        a[b, 3, 3] = 1
+    return a
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("pad", PADS)
+@pytest.mark.parametrize("align", [0, 1])
+def test_golden_modes(ba, dt, mode, pad, align):
+    from batchaug_b200 import ops
+    g = load_golden("resample_modes")
+    x = to_dev(g["x"] if dt == "f32" else g["x_bf16"])
+    out = ops.resample3d(x, theta=to_dev(g["theta"]), modes=mode, paddings=pad,
+                         align_corners=bool(align))
+    assert np.array_equal(to_np(out), g[f"{dt}_{mode}_{pad}_{align}"])
+
+
+@pytest.mark.parametrize("shape", [(2, 1, 16, 16, 16), (3, 2, 9, 10, 12), (1, 3, 7, 5, 33),
+                                   (2, 1, 1, 8, 8), (2, 2, 12, 1, 1), (5, 1, 4, 4, 4)])
+@pytest.mark.parametrize("dt", [np.float32, "bf16"])
+def test_vs_oracle_random_shapes(ba, oracle_lib, shape, dt):
+    """Odd, non-cubic and 1-voxel extents; all modes and paddings, with a mask."""
+    from batchaug_b200 import ops
+    rng = np.random.default_rng(hash(shape) % 2**32)
+    x = rng.standard_normal(shape).astype(np.float32)
+    if dt == "bf16":
+        x = oracle_lib.to_bf16_bits(x)
+    A = _rand_affine(rng, shape[0])
+    mask = rng.random(shape[0]) < 0.7
+    mask[0] = True
+    xd = to_dev(x)
+    for mode in MODES:
+        for pad in PADS:
+            ref = oracle_lib.resample3d(x, affine=A, mode=mode, padding=pad, mask=mask)
+            out = ops.resample3d(xd, affine=A, modes=mode, paddings=pad, mask=mask)
+            assert np.array_equal(to_np(out), ref), (mode, pad)
+
+
+def test_multi_key_one_launch(ba, oracle_lib):
+    """vol bf16 bilinear + seg f32 nearest + a 3-channel key sharing one map."""
+    from batchaug_b200 import ops
+    rng = np.random.default_rng(7)
+    B, H, W, D = 3, 12, 10, 16
+    vol = oracle_lib.to_bf16_bits(rng.random((B, 2, H, W, D)).astype(np.float32))
+    seg = rng.integers(0, 8, (B, 1, H, W, D)).astype(np.float32)
+    img = rng.standard_normal((B, 3, H, W, D)).astype(np.float32)
+    A = _rand_affine(rng, B)
+    mask = np.array([True, False, True])
+    outs = ops.resample3d([to_dev(vol), to_dev(seg), to_dev(img)], affine=A, mask=mask,
+                          modes=["bilinear", "nearest", "bilinear"],
+                          paddings=["zeros", "zeros", "reflection"])
+    assert np.array_equal(to_np(outs[0]), oracle_lib.resample3d(vol, affine=A, mask=mask))
+    assert np.array_equal(to_np(outs[1]),
+                          oracle_lib.resample3d(seg, affine=A, mode="nearest", mask=mask))
+    assert np.array_equal(to_np(outs[2]),
+                          oracle_lib.resample3d(img, affine=A, padding="reflection", mask=mask))
+    # nearest keeps the label set; masked element copied bit for bit
+    assert set(np.unique(to_np(outs[1]))) <= set(range(8))
+    assert np.array_equal(to_np(outs[0])[1], vol[1])
+
+
+def test_grid_mode_align_corners(ba, oracle_lib):
+    from batchaug_b200 import ops
+    g = load_golden("elastic")
+    grid = to_dev(g["grid"])
+    vo = ops.resample3d(to_dev(g["vol"]), grid=grid, modes="bilinear", align_corners=True)
+    so = ops.resample3d(to_dev(g["seg"]), grid=grid, modes="nearest", align_corners=True)
+    assert np.array_equal(to_np(vo), g["vol_out"])
+    assert np.array_equal(to_np(so), g["seg_out"])
+
+
+def test_golden_compose_materialize(ba):
+    from batchaug_b200 import ops
+    g = load_golden("compose_materialize")
+    vo, so = ops.resample3d([to_dev(g["vol"]), to_dev(g["seg"])], affine=g["affine"],
+                            mask=g["mask"], modes=["bilinear", "nearest"])
+    assert np.array_equal(to_np(vo), g["vol_out"])
+    assert np.array_equal(to_np(so), g["seg_out"])
+
+
+def test_golden_affine_apply_border(ba):
+    g = load_golden("affine_apply_border")
+    t = ba.RandAffine(prob=1.0, padding_mode="border")
+    params = {"mask": to_dev(g["mask"]), "theta": to_dev(g["theta"]),
+              "affine": to_dev(g["affine"]), "spatial_shape": g["x"].shape[2:]}
+    out = t.apply(to_dev(g["x"]), params)
+    assert np.array_equal(to_np(out), g["out"])
+
+
+def test_golden_flip_rot90_exact(ba):
+    g = load_golden("flip_rot90")
+    x = to_dev(g["x"])
+    fl = ba.RandAxisFlip(prob=1.0)
+    pf = {"mask": torch.ones(4, dtype=torch.bool, device="cuda"),
+          "axes": to_dev(g["flip_axes"])}
+    assert np.array_equal(to_np(fl.apply(x, pf)), g["flip_out"])
+    r9 = ba.RandRotate90(prob=1.0, max_k=3)
+    pr = {"mask": torch.ones(4, dtype=torch.bool, device="cuda"), "k": to_dev(g["rot_k"])}
+    assert np.array_equal(to_np(r9.apply(x, pr)), g["rot_out"])
+
+
+def test_full_size_config2_properties(ba, oracle_lib):
+    """Config 2 at full size (B=8, 128^3, border): compare two elements with
+    the oracle exactly; identity affine is an exact copy; masked = copy."""
+    from batchaug_b200 import ops
+    torch.manual_seed(0)
+    x = torch.rand(8, 1, 128, 128, 128, device="cuda")
+    rng = np.random.default_rng(2)
+    A = _rand_affine(rng, 8)
+    out = ops.resample3d(x, affine=A, paddings="border")
+    xs = to_np(x[:2])
+    ref = oracle_lib.resample3d(xs, affine=A[:2], padding="border")
+    assert np.array_equal(to_np(out[:2]), ref)
+    eye = np.broadcast_to(np.eye(4, dtype=np.float32), (8, 4, 4)).copy()
+    ident = ops.resample3d(x, affine=eye, paddings="border")
+    assert torch.equal(ident, x)
+    m = np.zeros(8, bool)
+    copy = ops.resample3d(x, affine=A, mask=m)
+    assert torch.equal(copy, x)
+
+
+def test_errors_are_value_errors(ba):
+    from batchaug_b200 import ops
+    x = torch.zeros(2, 1, 4, 4, 4, device="cuda")
+    with pytest.raises(ValueError):
+        ops.resample3d(x, modes="bicubic", affine=np.eye(4, dtype=np.float32)[None].repeat(2, 0))
+    with pytest.raises(ValueError):
+        ops.resample3d(x.double(), affine=np.eye(4, dtype=np.float32)[None].repeat(2, 0))
+    with pytest.raises(ValueError):
+        # out-of-place only: dst must not alias src
+        ops.resample3d(x, affine=np.eye(4, dtype=np.float32)[None].repeat(2, 0), out=[x])
