@@ -3,25 +3,29 @@
 // Replaces batchaug/compose.py:71-110 (_materialize: monai_affine_to_theta,
 // F.affine_grid, F.grid_sample on an fp32 copy, .to(dtype), torch.where) and
 // the eager applies of RandAffine (affine.py:284-317), Rand3DElastic
-// (elastic.py:101-125) and RandRotate90's non-square fallback
-// (rotate90.py:100-112).
+// (elastic.py:101-125), RandZoom (zoom.py:90-121) and RandRotate90's
+// non-square fallback (rotate90.py:100-112).
 //
-// Design (B200): no grid tensor and no fp32 copy of the input ever reach
-// HBM.  Each thread owns VEC output voxels of one row along D (the
-// contiguous axis), derives their source coordinates in registers from the
-// element's theta (computed once per CTA in shared memory, straight from the
-// MONAI affine when given one), and for every key of the group and every
-// channel gathers the 8 trilinear taps (1 for nearest) through the read-only
-// cache and blends them.  A CTA covers a compact 32(D) x 4(W) x 4(H) output
-// brick so that its source footprint stays in L1; the input of an element
-// fits in the 126 MB L2, so HBM sees each input byte about once.  Masked-out
-// elements take a plain copy.
+// Design (B200).  No grid tensor and no fp32 copy of the input reach HBM.
+// A CTA covers a compact BD(D) x TY(W) x TZ(H) output brick of one element.
+// Its prologue puts in shared memory everything that does not vary per voxel:
+// the element's theta (derived from the MONAI affine when given one) and, for
+// the brick's D positions, affine_grid's base coordinate times theta's first
+// column — so the hot loop has no divisions.  Each thread then produces
+// output voxels in pairs, carrying both voxels of a pair through Blackwell's
+// packed fp32x2 arithmetic (add/mul/fma .f32x2, each lane rounded exactly like
+// a scalar op), and for every key and channel gathers the 8 trilinear taps
+// (1 for nearest) through the read-only cache: one base pointer and constant
+// tap deltas when the footprint is inside the volume, per-tap bounds checks
+// only near its faces.  Mode, padding and dtype are compile-time in the hot
+// path (a uniform switch per key).  Masked-out elements take a plain copy.
 //
 // Arithmetic reproduces torch's CPU affine_grid and grid_sample bit for bit:
 // the base grid is torch.linspace's two-sided fused formula scaled by
 // (N-1)/N, the bmm with theta is the fused chain MKL produces, and the
 // unnormalise / clip / reflect / trilinear steps round exactly where torch's
-// scalar code rounds (this file is compiled with -fmad=false).
+// scalar code rounds (this file is compiled with -fmad=false; fused or packed
+// operations appear only where written explicitly).
 #include <stdio.h>
 
 #include "ba_common.cuh"
@@ -29,9 +33,27 @@
 namespace ba {
 namespace {
 
-constexpr int TX = 8;  // threads along D (each VEC voxels)
-constexpr int TY = 4;  // threads along W
-constexpr int TZ = 4;  // threads along H
+#ifndef BA_RS_TX
+#define BA_RS_TX 8
+#endif
+#ifndef BA_RS_TY
+#define BA_RS_TY 4
+#endif
+#ifndef BA_RS_TZ
+#define BA_RS_TZ 4
+#endif
+#ifndef BA_RS_PAIRS
+#define BA_RS_PAIRS 2
+#endif
+#ifndef BA_RS_MINBLOCKS
+#define BA_RS_MINBLOCKS 6
+#endif
+
+constexpr int TX = BA_RS_TX;         // threads along D
+constexpr int TY = BA_RS_TY;         // threads along W
+constexpr int TZ = BA_RS_TZ;         // threads along H
+constexpr int PAIRS = BA_RS_PAIRS;   // voxel pairs per thread, along D
+constexpr int BD = TX * 2 * PAIRS;   // brick extent along D
 constexpr int NTHREADS = TX * TY * TZ;
 
 struct KeyArgs {
@@ -57,116 +79,64 @@ struct ResampleArgs {
   KeyArgs keys[BA_MAX_KEYS];
 };
 
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 neg2(float2 a) { return make_float2(-a.x, -a.y); }
+
 // affine_grid's linspace_from_neg_one.
 __device__ __forceinline__ float base_coord(int i, int n, int align_corners) {
   if (n <= 1) return 0.0f;
-  float step = 2.0f / (float)(n - 1);
+  const float step = 2.0f / (float)(n - 1);
   float r = linspace_at(-1.0f, 1.0f, step, i, n);
   if (!align_corners) r = (r * (float)(n - 1)) / (float)n;
   return r;
 }
 
-__device__ __forceinline__ float unnormalize(float coord, int size, int align_corners) {
-  if (align_corners) return ((coord + 1.0f) / 2.0f) * (float)(size - 1);
-  return ((coord + 1.0f) * (float)size - 1.0f) / 2.0f;
+// grid_sampler_unnormalize for a pair: align_corners ? ((c+1)/2)*(size-1)
+// : ((c+1)*size-1)/2, where /2 is the exact *0.5.
+template <bool ALIGN>
+__device__ __forceinline__ float2 unnormalize2(float2 c, float size) {
+  const float2 one = f2(1.0f), half = f2(0.5f);
+  if (ALIGN) return __fmul2_rn(__fmul2_rn(__fadd2_rn(c, one), half), f2(size - 1.0f));
+  return __fmul2_rn(__fadd2_rn(__fmul2_rn(__fadd2_rn(c, one), f2(size)), f2(-1.0f)), half);
 }
 
-// std::min(size-1, std::max(in, 0)) with std's argument order, so that a
-// NaN coordinate clips to size-1 exactly as torch's sampler does.
-__device__ __forceinline__ float clip_coord(float in, int size) {
-  float lo = (in < 0.0f) ? 0.0f : in;
-  float hi = (float)(size - 1);
+// std::min(size-1, std::max(in, 0)) with std's argument order: a NaN
+// coordinate clips to size-1 exactly as torch's sampler does.
+__device__ __forceinline__ float clip_coord(float in, float hi) {
+  const float lo = (in < 0.0f) ? 0.0f : in;
   return (lo < hi) ? lo : hi;
 }
 
 __device__ __forceinline__ float reflect_coord(float in, int twice_low, int twice_high) {
   if (twice_low == twice_high) return 0.0f;
-  float mn = (float)twice_low / 2.0f;
-  float span = (float)(twice_high - twice_low) / 2.0f;
+  const float mn = (float)twice_low * 0.5f;
+  const float span = (float)(twice_high - twice_low) * 0.5f;
   in = fabsf(in - mn);
-  float extra = fmodf(in, span);
-  int flips = (int)floorf(in / span);
+  const float extra = fmodf(in, span);
+  const int flips = (int)floorf(in / span);
   if ((flips & 1) == 0) return extra + mn;
   return span - extra + mn;
 }
 
-// Padding transform of an unnormalised coordinate, then the guard torch's
-// CUDA sampler applies before converting to an integer index (non-finite or
-// huge coordinates become -100, i.e. out of bounds).
-__device__ __forceinline__ float pad_coord(float coord, int size, int padding, int align_corners) {
-  if (padding == BA_PAD_BORDER) {
-    coord = clip_coord(coord, size);
-  } else if (padding == BA_PAD_REFLECTION) {
-    coord = align_corners ? reflect_coord(coord, 0, 2 * (size - 1))
-                          : reflect_coord(coord, -1, 2 * size - 1);
-    coord = clip_coord(coord, size);
+// Padding transform of one unnormalised coordinate, then the guard torch's
+// CUDA sampler applies before the integer conversion (non-finite or huge
+// coordinates become -100, i.e. out of bounds).
+template <int PAD, bool ALIGN>
+__device__ __forceinline__ float pad_coord(float c, int size) {
+  if (PAD == BA_PAD_BORDER) {
+    return clip_coord(c, (float)(size - 1));  // in [0, size-1] or NaN->size-1
+  } else if (PAD == BA_PAD_REFLECTION) {
+    c = ALIGN ? reflect_coord(c, 0, 2 * (size - 1)) : reflect_coord(c, -1, 2 * size - 1);
+    return clip_coord(c, (float)(size - 1));
   }
-  if (!(fabsf(coord) < 1.0e9f)) coord = -100.0f;
-  return coord;
-}
-
-// Precomputed sampling footprint of one output voxel for one key.
-struct Tap8 {
-  int32_t off[8];
-  float w[8];
-  uint32_t valid;  // bit k: tap k in bounds
-};
-
-__device__ __forceinline__ void trilinear_footprint(float ix, float iy, float iz, int H, int W,
-                                                    int D, Tap8& t) {
-  float x0f = floorf(ix), y0f = floorf(iy), z0f = floorf(iz);
-  int x0 = (int)x0f, y0 = (int)y0f, z0 = (int)z0f;
-  int x1 = x0 + 1, y1 = y0 + 1, z1 = z0 + 1;
-  float wx0 = (float)x1 - ix, wx1 = ix - (float)x0;
-  float wy0 = (float)y1 - iy, wy1 = iy - (float)y0;
-  float wz0 = (float)z1 - iz, wz1 = iz - (float)z0;
-  // torch's corner order tnw, tne, tsw, tse, bnw, bne, bsw, bse with each
-  // weight a left-to-right product (x * y) * z.
-  t.w[0] = wx0 * wy0 * wz0;
-  t.w[1] = wx1 * wy0 * wz0;
-  t.w[2] = wx0 * wy1 * wz0;
-  t.w[3] = wx1 * wy1 * wz0;
-  t.w[4] = wx0 * wy0 * wz1;
-  t.w[5] = wx1 * wy0 * wz1;
-  t.w[6] = wx0 * wy1 * wz1;
-  t.w[7] = wx1 * wy1 * wz1;
-  bool vx0 = (unsigned)x0 < (unsigned)D, vx1 = (unsigned)x1 < (unsigned)D;
-  bool vy0 = (unsigned)y0 < (unsigned)W, vy1 = (unsigned)y1 < (unsigned)W;
-  bool vz0 = (unsigned)z0 < (unsigned)H, vz1 = (unsigned)z1 < (unsigned)H;
-  // Offsets of out-of-bounds taps are never dereferenced; unsigned
-  // arithmetic keeps their computation well defined.
-  const uint32_t uW = (uint32_t)W, uD = (uint32_t)D;
-  uint32_t r00 = ((uint32_t)z0 * uW + (uint32_t)y0) * uD, r01 = ((uint32_t)z0 * uW + (uint32_t)y1) * uD;
-  uint32_t r10 = ((uint32_t)z1 * uW + (uint32_t)y0) * uD, r11 = ((uint32_t)z1 * uW + (uint32_t)y1) * uD;
-  t.off[0] = (int32_t)(r00 + (uint32_t)x0);
-  t.off[1] = (int32_t)(r00 + (uint32_t)x1);
-  t.off[2] = (int32_t)(r01 + (uint32_t)x0);
-  t.off[3] = (int32_t)(r01 + (uint32_t)x1);
-  t.off[4] = (int32_t)(r10 + (uint32_t)x0);
-  t.off[5] = (int32_t)(r10 + (uint32_t)x1);
-  t.off[6] = (int32_t)(r11 + (uint32_t)x0);
-  t.off[7] = (int32_t)(r11 + (uint32_t)x1);
-  t.valid = (uint32_t)(vz0 && vy0 && vx0) | ((uint32_t)(vz0 && vy0 && vx1) << 1) |
-            ((uint32_t)(vz0 && vy1 && vx0) << 2) | ((uint32_t)(vz0 && vy1 && vx1) << 3) |
-            ((uint32_t)(vz1 && vy0 && vx0) << 4) | ((uint32_t)(vz1 && vy0 && vx1) << 5) |
-            ((uint32_t)(vz1 && vy1 && vx0) << 6) | ((uint32_t)(vz1 && vy1 && vx1) << 7);
+  return (fabsf(c) < 1.0e9f) ? c : -100.0f;
 }
 
 template <int DT>
 __device__ __forceinline__ float ld(const void* base, int64_t i) {
   if (DT == BA_BF16) return bf16_bits_to_f32(__ldg((const uint16_t*)base + i));
   return __ldg((const float*)base + i);
-}
-
-template <int DT>
-__device__ __forceinline__ float gather8(const void* cbase, const Tap8& t) {
-  float out = 0.0f;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    float v = (t.valid >> k) & 1u ? ld<DT>(cbase, t.off[k]) : 0.0f;
-    out = out + v * t.w[k];
-  }
-  return out;
 }
 
 template <int DT>
@@ -177,67 +147,196 @@ __device__ __forceinline__ void st(void* base, int64_t i, float v) {
     ((float*)base)[i] = v;
 }
 
-// All channels of one key at one output voxel (flat spatial index s).
+// Integer footprint of one voxel: corner (x0,y0,z0), whether all 8 taps are
+// inside, and the per-tap validity bits (torch's corner order).
+struct Corner {
+  int32_t off;     // (z0*W + y0)*D + x0, meaningful when some tap is valid
+  uint32_t valid;  // bit k: tap k in bounds
+  bool interior;
+};
+
+__device__ __forceinline__ Corner corner_of(float x0f, float y0f, float z0f, int H, int W, int D) {
+  const int x0 = (int)x0f, y0 = (int)y0f, z0 = (int)z0f;
+  Corner c;
+  c.interior = (unsigned)x0 < (unsigned)(D - 1) && (unsigned)y0 < (unsigned)(W - 1) &&
+               (unsigned)z0 < (unsigned)(H - 1);
+  const bool vx0 = (unsigned)x0 < (unsigned)D, vx1 = (unsigned)(x0 + 1) < (unsigned)D;
+  const bool vy0 = (unsigned)y0 < (unsigned)W, vy1 = (unsigned)(y0 + 1) < (unsigned)W;
+  const bool vz0 = (unsigned)z0 < (unsigned)H, vz1 = (unsigned)(z0 + 1) < (unsigned)H;
+  const uint32_t mx = (uint32_t)vx0 | ((uint32_t)vx1 << 1);
+  const uint32_t r0 = (vz0 && vy0) ? mx : 0u, r1 = (vz0 && vy1) ? mx : 0u;
+  const uint32_t r2 = (vz1 && vy0) ? mx : 0u, r3 = (vz1 && vy1) ? mx : 0u;
+  c.valid = r0 | (r1 << 2) | (r2 << 4) | (r3 << 6);
+  // unsigned arithmetic: offsets of out-of-bounds corners are never used
+  c.off = (int32_t)(((uint32_t)z0 * (uint32_t)W + (uint32_t)y0) * (uint32_t)D + (uint32_t)x0);
+  return c;
+}
+
+// The 8 tap values of one voxel (0 for out-of-bounds taps), torch's order
+// tnw, tne, tsw, tse, bnw, bne, bsw, bse.
 template <int DT>
-__device__ __forceinline__ void sample_voxel(const KeyArgs& k, const ResampleArgs& a,
-                                             int64_t ebase, int64_t hwd, int64_t s, float ix,
-                                             float iy, float iz) {
-  const int H = a.H, W = a.W, D = a.D;
-  const float px = pad_coord(ix, D, k.padding, a.align_corners);
-  const float py = pad_coord(iy, W, k.padding, a.align_corners);
-  const float pz = pad_coord(iz, H, k.padding, a.align_corners);
-  if (k.mode == BA_NEAREST) {
-    const int xn = (int)rintf(px), yn = (int)rintf(py), zn = (int)rintf(pz);
-    const bool ok =
-        (unsigned)xn < (unsigned)D && (unsigned)yn < (unsigned)W && (unsigned)zn < (unsigned)H;
-    const int32_t off = ok ? (zn * W + yn) * D + xn : 0;
-    for (int c = 0; c < k.channels; ++c) {
-      const int64_t cb = ebase + (int64_t)c * hwd;
-      st<DT>(k.dst, cb + s, ok ? ld<DT>(k.src, cb + off) : 0.0f);
-    }
-    return;
-  }
-  Tap8 t;
-  trilinear_footprint(px, py, pz, H, W, D, t);
-  for (int c = 0; c < k.channels; ++c) {
-    const int64_t cb = ebase + (int64_t)c * hwd;
-    const void* cbase = (DT == BA_BF16) ? (const void*)((const uint16_t*)k.src + cb)
-                                        : (const void*)((const float*)k.src + cb);
-    st<DT>(k.dst, cb + s, gather8<DT>(cbase, t));
+__device__ __forceinline__ void taps8(const void* cbase, const Corner& c, int W, int D,
+                                      float* v) {
+  const int64_t dy = D, dz = (int64_t)W * D;
+  if (c.interior) {
+    const int64_t o = c.off;
+    v[0] = ld<DT>(cbase, o);
+    v[1] = ld<DT>(cbase, o + 1);
+    v[2] = ld<DT>(cbase, o + dy);
+    v[3] = ld<DT>(cbase, o + dy + 1);
+    v[4] = ld<DT>(cbase, o + dz);
+    v[5] = ld<DT>(cbase, o + dz + 1);
+    v[6] = ld<DT>(cbase, o + dz + dy);
+    v[7] = ld<DT>(cbase, o + dz + dy + 1);
+  } else {
+    const int64_t o = c.off;
+    const int64_t delta[8] = {0, 1, dy, dy + 1, dz, dz + 1, dz + dy, dz + dy + 1};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = ((c.valid >> k) & 1u) ? ld<DT>(cbase, o + delta[k]) : 0.0f;
   }
 }
 
-// A CTA covers a (TX*VEC)(D) x TY(W) x TZ(H) output brick.  Thread tx owns
-// the voxels d = brick_d0 + v*TX + tx, v < VEC, so that for each v the lanes
-// of a warp write TX consecutive voxels of TY rows (full 32-byte sectors for
-// fp32) while only one tap footprint is live per thread.
-template <int VEC>
-__global__ void __launch_bounds__(NTHREADS, 8)
+// All channels of one key at a pair of output voxels (flat spatial indices
+// sa, sb; sb is skipped when !has_b).  ix/iy/iz are the unnormalised source
+// coordinates of the two voxels.
+template <int MODE, int PAD, int DT, bool ALIGN>
+__device__ __forceinline__ void sample_pair(const KeyArgs& k, int64_t b, int H, int W, int D,
+                                            int64_t hwd, float2 ix, float2 iy, float2 iz,
+                                            int64_t sa, int64_t sb, bool has_b) {
+  const float2 px = f2(pad_coord<PAD, ALIGN>(ix.x, D), pad_coord<PAD, ALIGN>(ix.y, D));
+  const float2 py = f2(pad_coord<PAD, ALIGN>(iy.x, W), pad_coord<PAD, ALIGN>(iy.y, W));
+  const float2 pz = f2(pad_coord<PAD, ALIGN>(iz.x, H), pad_coord<PAD, ALIGN>(iz.y, H));
+  const size_t esz = DT == BA_BF16 ? 2 : 4;
+  const char* src_e = (const char*)k.src + (size_t)b * k.channels * hwd * esz;
+  char* dst_e = (char*)k.dst + (size_t)b * k.channels * hwd * esz;
+  if (MODE == BA_NEAREST) {
+    const int xa = (int)rintf(px.x), ya = (int)rintf(py.x), za = (int)rintf(pz.x);
+    const int xb = (int)rintf(px.y), yb = (int)rintf(py.y), zb = (int)rintf(pz.y);
+    const bool oka =
+        (unsigned)xa < (unsigned)D && (unsigned)ya < (unsigned)W && (unsigned)za < (unsigned)H;
+    const bool okb = has_b && (unsigned)xb < (unsigned)D && (unsigned)yb < (unsigned)W &&
+                     (unsigned)zb < (unsigned)H;
+    const int64_t oa = oka ? ((int64_t)za * W + ya) * D + xa : 0;
+    const int64_t ob = okb ? ((int64_t)zb * W + yb) * D + xb : 0;
+    for (int c = 0; c < k.channels; ++c) {
+      const void* cs = src_e + (size_t)c * hwd * esz;
+      void* cd = dst_e + (size_t)c * hwd * esz;
+      st<DT>(cd, sa, oka ? ld<DT>(cs, oa) : 0.0f);
+      if (has_b) st<DT>(cd, sb, okb ? ld<DT>(cs, ob) : 0.0f);
+    }
+    return;
+  }
+  // Trilinear: corner and the distances torch forms as (corner_int - coord)
+  // and (coord - corner_int), then the weights as (x * y) * z products.
+  const float2 x0 = f2(floorf(px.x), floorf(px.y)), y0 = f2(floorf(py.x), floorf(py.y));
+  const float2 z0 = f2(floorf(pz.x), floorf(pz.y));
+  const float2 one = f2(1.0f);
+  const float2 wx1 = __fadd2_rn(px, neg2(x0)), wx0 = __fadd2_rn(__fadd2_rn(x0, one), neg2(px));
+  const float2 wy1 = __fadd2_rn(py, neg2(y0)), wy0 = __fadd2_rn(__fadd2_rn(y0, one), neg2(py));
+  const float2 wz1 = __fadd2_rn(pz, neg2(z0)), wz0 = __fadd2_rn(__fadd2_rn(z0, one), neg2(pz));
+  const float2 xy00 = __fmul2_rn(wx0, wy0), xy10 = __fmul2_rn(wx1, wy0);
+  const float2 xy01 = __fmul2_rn(wx0, wy1), xy11 = __fmul2_rn(wx1, wy1);
+  float2 w[8];
+  w[0] = __fmul2_rn(xy00, wz0);
+  w[1] = __fmul2_rn(xy10, wz0);
+  w[2] = __fmul2_rn(xy01, wz0);
+  w[3] = __fmul2_rn(xy11, wz0);
+  w[4] = __fmul2_rn(xy00, wz1);
+  w[5] = __fmul2_rn(xy10, wz1);
+  w[6] = __fmul2_rn(xy01, wz1);
+  w[7] = __fmul2_rn(xy11, wz1);
+  const Corner ca = corner_of(x0.x, y0.x, z0.x, H, W, D);
+  Corner cb = corner_of(x0.y, y0.y, z0.y, H, W, D);
+  if (!has_b) {
+    cb.interior = false;
+    cb.valid = 0u;
+  }
+  for (int c = 0; c < k.channels; ++c) {
+    const void* cs = src_e + (size_t)c * hwd * esz;
+    void* cd = dst_e + (size_t)c * hwd * esz;
+    float va[8], vb[8];
+    taps8<DT>(cs, ca, W, D, va);
+    taps8<DT>(cs, cb, W, D, vb);
+    // out += v * w in torch's tap order, both voxels at once
+    float2 acc = f2(0.0f);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) acc = __fadd2_rn(acc, __fmul2_rn(f2(va[t], vb[t]), w[t]));
+    st<DT>(cd, sa, acc.x);
+    if (has_b) st<DT>(cd, sb, acc.y);
+  }
+}
+
+// A key's sampling spec as one compile-time code: (mode*3 + padding)*2 + dtype.
+__host__ __device__ constexpr int spec_code(int mode, int pad, int dt) { return (mode * 3 + pad) * 2 + dt; }
+__host__ __device__ constexpr int spec_mode(int s) { return s / 6; }
+__host__ __device__ constexpr int spec_pad(int s) { return (s / 2) % 3; }
+__host__ __device__ constexpr int spec_dt(int s) { return s % 2; }
+
+template <int S, bool ALIGN>
+__device__ __forceinline__ void sample_spec(const KeyArgs& k, int64_t b, int H, int W, int D,
+                                            int64_t hwd, float2 ix, float2 iy, float2 iz,
+                                            int64_t sa, int64_t sb, bool has_b) {
+  sample_pair<spec_mode(S), spec_pad(S), spec_dt(S), ALIGN>(k, b, H, W, D, hwd, ix, iy, iz, sa,
+                                                             sb, has_b);
+}
+
+// The kernel samples key 0 with spec S0 and, when S1 >= 0, key 1 with spec
+// S1 from the same coordinates; other key combinations are launched one key
+// at a time.
+template <int S0, int S1>
+__global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
     resample3d_kernel(const __grid_constant__ ResampleArgs a) {
+  const bool ALIGN = a.align_corners != 0;
   const int H = a.H, W = a.W, D = a.D;
-  const int tiles_d = (D + TX * VEC - 1) / (TX * VEC);
+  const int tiles_d = (D + BD - 1) / BD;
   const int tx = threadIdx.x % TX;
   const int ty = (threadIdx.x / TX) % TY;
   const int tz = threadIdx.x / (TX * TY);
-  const int d_brick = (blockIdx.x % tiles_d) * (TX * VEC);
-  const int w = (blockIdx.x / tiles_d) * TY + ty;
-  const int h = blockIdx.y * TZ + tz;
+  const int d_brick = (blockIdx.x % tiles_d) * BD;
+  const int w_brick = (blockIdx.x / tiles_d) * TY;
+  const int h_brick = blockIdx.y * TZ;
+  const int w = w_brick + ty;
+  const int h = h_brick + tz;
   const int64_t b = blockIdx.z;
   const int64_t hwd = (int64_t)H * W * D;
-
-  __shared__ float theta[12];
   const bool active = (a.mask == nullptr) || (a.mask[b] != 0);
-  if (active && a.xform_kind != BA_XFORM_GRID && threadIdx.x < 12) {
-    const int i = threadIdx.x / 4, j = threadIdx.x % 4;
-    const float* x = a.xform + b * a.xform_stride;
-    if (a.xform_kind == BA_XFORM_AFFINE) {
-      // monai_affine_to_theta: theta = P S_norm A S_inv P, P swapping 0 and 2.
-      const int pi = 2 - i, pj = (j == 3) ? 3 : 2 - j;
-      const float s_i = a.sn[pi];
-      const float s_j = (pj == 3) ? 1.0f : a.si[pj];
-      theta[threadIdx.x] = (s_i * x[pi * 4 + pj]) * s_j;
-    } else {
-      theta[threadIdx.x] = x[i * 4 + j];
+  const bool affine = a.xform_kind != BA_XFORM_GRID;
+
+  // Prologue: theta, then the brick's base coordinates and bx * theta[r][0].
+  __shared__ float s_theta[12];
+  __shared__ float s_by[TY], s_bz[TZ];
+  __shared__ float2 s_px[3][PAIRS][TX];
+  if (active && affine) {
+    const int t = threadIdx.x;
+    if (t < 12) {
+      const int i = t / 4, j = t % 4;
+      const float* x = a.xform + b * a.xform_stride;
+      if (a.xform_kind == BA_XFORM_AFFINE) {
+        // monai_affine_to_theta: theta = P S_norm A S_inv P, P swapping 0 and 2.
+        const int pi = 2 - i, pj = (j == 3) ? 3 : 2 - j;
+        const float s_j = (pj == 3) ? 1.0f : a.si[pj];
+        s_theta[t] = (a.sn[pi] * x[pi * 4 + pj]) * s_j;
+      } else {
+        s_theta[t] = x[i * 4 + j];
+      }
+    } else if (t < 12 + TY) {
+      s_by[t - 12] = base_coord(w_brick + t - 12, W, ALIGN);
+    } else if (t < 12 + TY + TZ) {
+      s_bz[t - 12 - TY] = base_coord(h_brick + t - 12 - TY, H, ALIGN);
+    }
+    __syncthreads();
+    if (t < BD) {
+      // voxel j = 2p + q of lane x sits at d = d_brick + j*TX + x
+      const int j = t / TX, x = t % TX;
+      const int d = d_brick + t;  // t = j*TX + x
+      const float bx = d < D ? base_coord(d, D, ALIGN) : 0.0f;
+      const int p = j / 2, q = j % 2;
+#pragma unroll
+      for (int r = 0; r < 3; ++r) {
+        const float v = bx * s_theta[r * 4];
+        float* slot = reinterpret_cast<float*>(&s_px[r][p][x]);
+        slot[q] = v;
+      }
     }
   }
   __syncthreads();
@@ -245,8 +344,8 @@ __global__ void __launch_bounds__(NTHREADS, 8)
   const int64_t row = ((int64_t)h * W + w) * D;
 
   if (!active) {
-    for (int v = 0; v < VEC; ++v) {
-      const int d = d_brick + v * TX + tx;
+    for (int j = 0; j < 2 * PAIRS; ++j) {
+      const int d = d_brick + j * TX + tx;
       if (d >= D) break;
       for (int ki = 0; ki < a.n_keys; ++ki) {
         const KeyArgs& k = a.keys[ki];
@@ -262,36 +361,54 @@ __global__ void __launch_bounds__(NTHREADS, 8)
     return;
   }
 
-  // affine_grid's y and z base coordinates are shared by the thread's voxels.
-  const float by = base_coord(w, W, a.align_corners);
-  const float bz = base_coord(h, H, a.align_corners);
-  for (int v = 0; v < VEC; ++v) {
-    const int d = d_brick + v * TX + tx;
-    if (d >= D) break;
-    float gx, gy, gz;
-    if (a.xform_kind == BA_XFORM_GRID) {
-      const float* g = a.xform + (b * hwd + row + d) * 3;
-      gx = __ldg(g);
-      gy = __ldg(g + 1);
-      gz = __ldg(g + 2);
-    } else {
-      // affine_grid's bmm as MKL accumulates it: x*t0, fused y and z terms,
-      // then the translation.
-      const float bx = base_coord(d, D, a.align_corners);
-      gx = __fmaf_rn(bz, theta[2], __fmaf_rn(by, theta[1], bx * theta[0])) + theta[3];
-      gy = __fmaf_rn(bz, theta[6], __fmaf_rn(by, theta[5], bx * theta[4])) + theta[7];
-      gz = __fmaf_rn(bz, theta[10], __fmaf_rn(by, theta[9], bx * theta[8])) + theta[11];
+  float2 t1[3], t2[3], t3[3];
+  float by = 0.0f, bz = 0.0f;
+  if (affine) {
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+      t1[r] = f2(s_theta[r * 4 + 1]);
+      t2[r] = f2(s_theta[r * 4 + 2]);
+      t3[r] = f2(s_theta[r * 4 + 3]);
     }
-    const float ix = unnormalize(gx, D, a.align_corners);
-    const float iy = unnormalize(gy, W, a.align_corners);
-    const float iz = unnormalize(gz, H, a.align_corners);
-    for (int ki = 0; ki < a.n_keys; ++ki) {
-      const KeyArgs& k = a.keys[ki];
-      const int64_t ebase = b * (int64_t)k.channels * hwd;
-      if (k.dtype == BA_BF16)
-        sample_voxel<BA_BF16>(k, a, ebase, hwd, row + d, ix, iy, iz);
-      else
-        sample_voxel<BA_F32>(k, a, ebase, hwd, row + d, ix, iy, iz);
+    by = s_by[ty];
+    bz = s_bz[tz];
+  }
+  const float2 by2 = f2(by), bz2 = f2(bz);
+  const float fD = (float)D, fW = (float)W, fH = (float)H;
+#pragma unroll
+  for (int p = 0; p < PAIRS; ++p) {
+    const int da = d_brick + (2 * p) * TX + tx, db = da + TX;
+    if (da >= D) break;
+    const bool has_b = db < D;
+    float2 g[3];
+    if (affine) {
+      // affine_grid's bmm as MKL accumulates it: x*t0, then the fused y and z
+      // terms, then the translation.
+#pragma unroll
+      for (int r = 0; r < 3; ++r)
+        g[r] = __fadd2_rn(__ffma2_rn(bz2, t2[r], __ffma2_rn(by2, t1[r], s_px[r][p][tx])), t3[r]);
+    } else {
+      const float* ga = a.xform + (b * hwd + row + da) * 3;
+      const float* gb = has_b ? ga + 3 * TX : ga;
+#pragma unroll
+      for (int r = 0; r < 3; ++r) g[r] = f2(__ldg(ga + r), __ldg(gb + r));
+    }
+    if (ALIGN) {
+      const float2 ix = unnormalize2<true>(g[0], fD);
+      const float2 iy = unnormalize2<true>(g[1], fW);
+      const float2 iz = unnormalize2<true>(g[2], fH);
+      sample_spec<S0, true>(a.keys[0], b, H, W, D, hwd, ix, iy, iz, row + da, row + db, has_b);
+      if (S1 >= 0)
+        sample_spec<(S1 < 0 ? 0 : S1), true>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da,
+                                             row + db, has_b);
+    } else {
+      const float2 ix = unnormalize2<false>(g[0], fD);
+      const float2 iy = unnormalize2<false>(g[1], fW);
+      const float2 iz = unnormalize2<false>(g[2], fH);
+      sample_spec<S0, false>(a.keys[0], b, H, W, D, hwd, ix, iy, iz, row + da, row + db, has_b);
+      if (S1 >= 0)
+        sample_spec<(S1 < 0 ? 0 : S1), false>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da,
+                                              row + db, has_b);
     }
   }
 }
@@ -376,12 +493,60 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
   }
   if (d.batch == 0) return BA_OK;
 
-  constexpr int VEC = 4;
-  const int tiles_d = (int)((d.D + TX * VEC - 1) / (TX * VEC));
+  const int tiles_d = (int)((d.D + BD - 1) / BD);
   const int64_t gx = (int64_t)tiles_d * ((d.W + TY - 1) / TY);
   const int64_t gy = (d.H + TZ - 1) / TZ;
   BA_REQUIRE(gx <= INT32_MAX && gy <= 65535, "ba_resample3d: spatial extent too large");
-  dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)d.batch);
-  resample3d_kernel<VEC><<<grid, NTHREADS, 0, (cudaStream_t)stream>>>(a);
-  return check_launch("ba_resample3d");
+  const dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)d.batch);
+  const cudaStream_t st = (cudaStream_t)stream;
+  auto code = [](const KeyArgs& k) { return spec_code(k.mode, k.padding, k.dtype); };
+  // vol (bilinear) + seg (nearest) with one padding: one fused launch
+  if (a.n_keys == 2) {
+    KeyArgs k0 = a.keys[0], k1 = a.keys[1];
+    if (k0.mode == BA_NEAREST && k1.mode == BA_BILINEAR) {
+      a.keys[0] = k1;
+      a.keys[1] = k0;
+      k0 = a.keys[0];
+      k1 = a.keys[1];
+    }
+    if (k0.mode == BA_BILINEAR && k1.mode == BA_NEAREST && k0.padding == k1.padding) {
+      bool launched = true;
+      switch (code(k0) * 16 + code(k1)) {
+#define BA_PAIR(P, T0, T1)                                                                 \
+  case spec_code(BA_BILINEAR, P, T0) * 16 + spec_code(BA_NEAREST, P, T1):                  \
+    resample3d_kernel<spec_code(BA_BILINEAR, P, T0), spec_code(BA_NEAREST, P, T1)>         \
+        <<<grid, NTHREADS, 0, st>>>(a);                                                    \
+    break;
+#define BA_PAIRS(P) BA_PAIR(P, 0, 0) BA_PAIR(P, 0, 1) BA_PAIR(P, 1, 0) BA_PAIR(P, 1, 1)
+        BA_PAIRS(BA_PAD_ZEROS)
+        BA_PAIRS(BA_PAD_BORDER)
+        BA_PAIRS(BA_PAD_REFLECTION)
+#undef BA_PAIRS
+#undef BA_PAIR
+        default:
+          launched = false;
+      }
+      if (launched) return check_launch("ba_resample3d");
+    }
+  }
+  // otherwise one launch per key, each with its own compile-time spec
+  ResampleArgs one = a;
+  one.n_keys = 1;
+  for (int i = 0; i < a.n_keys; ++i) {
+    one.keys[0] = a.keys[i];
+    switch (code(one.keys[0])) {
+#define BA_ONE(S)                                                      \
+  case S:                                                              \
+    resample3d_kernel<S, -1><<<grid, NTHREADS, 0, st>>>(one);          \
+    break;
+      BA_ONE(0) BA_ONE(1) BA_ONE(2) BA_ONE(3) BA_ONE(4) BA_ONE(5)
+      BA_ONE(6) BA_ONE(7) BA_ONE(8) BA_ONE(9) BA_ONE(10) BA_ONE(11)
+#undef BA_ONE
+      default:
+        break;
+    }
+    const ba_status s1 = check_launch("ba_resample3d");
+    if (s1 != BA_OK) return s1;
+  }
+  return BA_OK;
 }

@@ -134,7 +134,10 @@ def test_golden_flip_rot90_exact(ba):
 
 def test_full_size_config2_properties(ba, oracle_lib):
     """Config 2 at full size (B=8, 128^3, border): compare two elements with
-    the oracle exactly; identity affine is an exact copy; masked = copy."""
+    the oracle exactly; the identity affine reproduces the input to fp32
+    rounding (affine_grid's base grid is not exactly on voxel centres, so
+    torch's own result is not a bit copy either) and matches the oracle
+    exactly; masked-out elements are bit copies."""
     from batchaug_b200 import ops
     torch.manual_seed(0)
     x = torch.rand(8, 1, 128, 128, 128, device="cuda")
@@ -146,7 +149,9 @@ def test_full_size_config2_properties(ba, oracle_lib):
     assert np.array_equal(to_np(out[:2]), ref)
     eye = np.broadcast_to(np.eye(4, dtype=np.float32), (8, 4, 4)).copy()
     ident = ops.resample3d(x, affine=eye, paddings="border")
-    assert torch.equal(ident, x)
+    assert torch.allclose(ident, x, rtol=0, atol=1e-6)
+    assert np.array_equal(to_np(ident[:1]),
+                          oracle_lib.resample3d(xs[:1], affine=eye[:1], padding="border"))
     m = np.zeros(8, bool)
     copy = ops.resample3d(x, affine=A, mask=m)
     assert torch.equal(copy, x)

@@ -1,0 +1,160 @@
+"""Host logic of the drop-in API on CPU: parameter distributions and affine
+conventions, and Compose's lazy accumulation, key grouping, mask skipping
+and intensity-run fusion — with the two kernel entry points replaced by
+oracle-backed fakes that record their calls (the CUDA kernels themselves are
+covered by the -m gpu tests)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+
+def test_affine_params_distribution(ba):
+    torch.manual_seed(0)
+    t = ba.RandAffine(prob=0.3, rotate_range=0.785, shear_range=0.3, translate_range=5,
+                      scale_range=0.1)
+    h = t.sample_host(4000, (4000, 1, 8, 8, 8))
+    assert abs(h["mask"].mean() - 0.3) < 0.03
+    a = h["affine"]
+    assert np.allclose(a[:, 3], [0, 0, 0, 1])
+    assert np.abs(a[:, :3, 3]).max() <= 5 * 2.5  # rotated/sheared translations stay bounded
+    # masked elements map to the identity in to_affine
+    m = t.host_affine({"_host": h})
+    assert np.array_equal(m[~h["mask"]], np.broadcast_to(np.eye(4), m[~h["mask"]].shape))
+
+
+def test_theta_formula_matches_reference_chain(ba):
+    """monai_affine_to_theta restated: equals P @ S_norm @ A @ S_inv @ P."""
+    from batchaug_b200.geometric import monai_affine_to_theta
+    rng = np.random.default_rng(0)
+    A = rng.standard_normal((5, 4, 4)).astype(np.float32)
+    H, W, D = 12, 16, 20
+    P = np.eye(4, dtype=np.float32)[[2, 1, 0, 3]]
+    Sn = np.diag(np.array([2 / H, 2 / W, 2 / D, 1], np.float32))
+    Si = np.diag(np.array([H / 2, W / 2, D / 2, 1], np.float32))
+    ref = P @ Sn @ A @ Si @ P
+    assert np.allclose(monai_affine_to_theta(A, (H, W, D)), ref, rtol=1e-6, atol=1e-6)
+
+
+def test_flip_rot90_affines(ba):
+    h = {"mask": np.array([True, True, False]), "axes": np.array([0, 2, 1])}
+    a = ba.RandAxisFlip(prob=1.0).host_affine({"_host": h})
+    assert np.array_equal(np.diagonal(a, axis1=1, axis2=2),
+                          [[-1, 1, 1, 1], [1, 1, -1, 1], [1, 1, 1, 1]])
+    r = ba.RandRotate90(prob=1.0, max_k=3)
+    hk = {"mask": np.array([True, True, True]), "k": np.array([1, 2, 3])}
+    ar = r.host_affine({"_host": hk})
+    assert np.array_equal(ar[0, :2, :2], [[0, 1], [-1, 0]])
+    assert np.array_equal(ar[1, :2, :2], [[-1, 0], [0, -1]])
+    assert np.array_equal(ar[2, :2, :2], [[0, -1], [1, 0]])
+
+
+def test_ranges_and_k(ba):
+    torch.manual_seed(1)
+    h = ba.RandRotate90(prob=1.0, max_k=3).sample_host(3000, (3000, 1, 4, 4, 4))
+    assert set(np.unique(h["k"])) == {1, 2, 3}
+    f = ba.RandAxisFlip(prob=1.0).sample_host(3000, (3000, 1, 4, 4, 4))
+    assert set(np.unique(f["axes"])) == {0, 1, 2}
+    s = ba.RandScaleIntensity(prob=1.0, factors=0.2).sample_host(3000, (3000, 1, 4, 4, 4))
+    assert s["factor"].min() >= -0.2 and s["factor"].max() < 0.2
+    b = ba.RandBiasField(degree=3).sample_host(10, (10, 1, 4, 4, 4))
+    assert b["coeffs"].shape == (10, 20)
+
+
+class _Recorder:
+    """Oracle-backed stand-ins for ops.resample3d / ops.intensity_chain on CPU
+    tensors, recording each call."""
+
+    def __init__(self, oracle):
+        self.O = oracle
+        self.calls = []
+
+    def resample3d(self, tensors, *, affine=None, modes="bilinear", paddings="zeros",
+                   mask=None, **kw):
+        single = isinstance(tensors, torch.Tensor)
+        ts = [tensors] if single else list(tensors)
+        modes = [modes] * len(ts) if isinstance(modes, str) else modes
+        paddings = [paddings] * len(ts) if isinstance(paddings, str) else paddings
+        self.calls.append(("resample", len(ts), np.array(mask)))
+        outs = [torch.from_numpy(self.O.resample3d(t.numpy(), affine=affine, mode=m, padding=p,
+                                                   mask=mask)) for t, m, p in zip(ts, modes,
+                                                                                  paddings)]
+        return outs[0] if single else outs
+
+    def intensity_chain(self, x, ops_, **kw):
+        self.calls.append(("chain", len(ops_), [o.kind for o in ops_]))
+        return x + 0  # values are not checked here, only the plan
+
+
+@pytest.fixture
+def rec(ba, oracle_lib, monkeypatch):
+    from batchaug_b200 import compose, intensity
+    r = _Recorder(oracle_lib)
+    monkeypatch.setattr(compose.ops, "resample3d", r.resample3d)
+    monkeypatch.setattr(compose.ops, "intensity_chain", r.intensity_chain)
+
+    def fake_chain_op(self, params, tensor):
+        from batchaug_b200 import ops
+        return ops.ChainOp(type(self).__name__ and _KIND[type(self).__name__])
+    _KIND.update({"RandGaussianNoise": 1, "RandAdjustContrast": 2, "RandScaleIntensity": 3,
+                  "RandShiftIntensity": 4, "RandBiasField": 5, "ScaleIntensity": 6})
+    monkeypatch.setattr(intensity._FusibleIntensity, "chain_op", fake_chain_op)
+    monkeypatch.setattr(intensity.BatchTransform, "_device_params",
+                        lambda self, host, shape, device: {"mask": torch.from_numpy(host["mask"])})
+    return r
+
+
+_KIND: dict = {}
+
+
+def test_compose_plan_config4(ba, rec, oracle_lib):
+    """rot90, flip -> noise -> affine -> ScaleIntensity: two resamples of the
+    (vol, seg) pair, each ONE launch for both keys; intensity runs fused."""
+    torch.manual_seed(0)
+    vol = torch.randn(3, 2, 8, 8, 8)
+    seg = (torch.rand(3, 1, 8, 8, 8) > 0.5).float()
+    c = ba.Compose([ba.RandRotate90d(["vol", "seg"], prob=1.0, max_k=3),
+                    ba.RandAxisFlipd(["vol", "seg"], prob=1.0),
+                    ba.RandGaussianNoised(["vol"], std=0.5),
+                    ba.RandAffined(["vol", "seg"], prob=1.0, rotate_range=0.785),
+                    ba.ScaleIntensityd(["vol"]),
+                    ba.RandShiftIntensityd(["vol"], prob=1.0)],
+                   lazy=True, mode={"vol": "bilinear", "seg": "nearest"})
+    out = c({"vol": vol, "seg": seg})
+    kinds = [k[0] for k in rec.calls]
+    assert kinds == ["resample", "chain", "resample", "chain"]
+    assert rec.calls[0][1] == 2 and rec.calls[2][1] == 2
+    assert rec.calls[3][2] == [6, 4]  # ScaleIntensity then shift, one chain
+    # nearest keeps binary labels
+    assert set(np.unique(out["seg"].numpy())) <= {0.0, 1.0}
+
+
+def test_compose_accumulates_like_reference(ba, rec, oracle_lib):
+    """flip then rot90 on the pair: one resample through flip_A @ rot_A."""
+    torch.manual_seed(3)
+    vol = torch.randn(2, 1, 6, 6, 6)
+    t1 = ba.RandAxisFlipd(["vol", "seg"], prob=1.0)
+    t2 = ba.RandRotate90d(["vol", "seg"], prob=1.0)
+    torch.manual_seed(3)
+    out = ba.Compose([t1, t2], lazy=True, mode="nearest")({"vol": vol, "seg": vol.clone()})
+    torch.manual_seed(3)
+    h1 = t1.transform.sample_host(2, vol.shape)
+    h2 = t2.transform.sample_host(2, vol.shape)
+    A = t1.transform.host_affine({"_host": h1}) @ t2.transform.host_affine({"_host": h2})
+    ref = oracle_lib.resample3d(vol.numpy(), affine=A, mode="nearest")
+    assert np.array_equal(out["vol"].numpy(), ref)
+    assert len([c for c in rec.calls if c[0] == "resample"]) == 1
+
+
+def test_compose_skips_all_masked_and_splits_key_sets(ba, rec):
+    torch.manual_seed(0)
+    v = torch.randn(2, 1, 4, 4, 4)
+    c = ba.Compose([ba.RandAffined(["vol"], prob=0.0, rotate_range=0.5)], lazy=True)
+    out = c({"vol": v})
+    assert out["vol"] is v and rec.calls == []  # mask all false: no launch, same tensor
+    c2 = ba.Compose([ba.RandAxisFlipd(["vol", "seg"], prob=1.0),
+                     ba.RandRotate90d(["vol"], prob=1.0)], lazy=True, mode="nearest")
+    c2({"vol": v, "seg": v.clone()})
+    res = [k for k in rec.calls if k[0] == "resample"]
+    assert len(res) == 2 and sorted(r[1] for r in res) == [1, 1]  # different histories
