@@ -13,8 +13,10 @@
 // the brick's D positions, affine_grid's base coordinate times theta's first
 // column — so the hot loop has no divisions.  Each thread then produces
 // output voxels in pairs, carrying both voxels of a pair through Blackwell's
-// packed fp32x2 arithmetic (add/mul/fma .f32x2, each lane rounded exactly like
-// a scalar op), and for every key and channel gathers the 8 trilinear taps
+// packed fp32x2 arithmetic where that cannot change rounding (fma chains,
+// add-only and multiply-only steps; a packed multiply followed by a packed add
+// is contracted by the compiler, so those stay scalar), and for every key and
+// channel gathers the 8 trilinear taps
 // (1 for nearest) through the read-only cache: one base pointer and constant
 // tap deltas when the footprint is inside the volume, per-tap bounds checks
 // only near its faces.  Mode, padding and dtype are compile-time in the hot
@@ -92,13 +94,19 @@ __device__ __forceinline__ float base_coord(int i, int n, int align_corners) {
   return r;
 }
 
-// grid_sampler_unnormalize for a pair: align_corners ? ((c+1)/2)*(size-1)
-// : ((c+1)*size-1)/2, where /2 is the exact *0.5.
+// grid_sampler_unnormalize: align_corners ? ((c+1)/2)*(size-1)
+// : ((c+1)*size-1)/2, where /2 is the exact *0.5.  Scalar operations: the
+// compiler contracts a packed multiply followed by a packed add into one
+// fused op even under -fmad=false, which would change the rounding.
+template <bool ALIGN>
+__device__ __forceinline__ float unnormalize1(float c, float size) {
+  if (ALIGN) return ((c + 1.0f) * 0.5f) * (size - 1.0f);
+  return ((c + 1.0f) * size - 1.0f) * 0.5f;
+}
+
 template <bool ALIGN>
 __device__ __forceinline__ float2 unnormalize2(float2 c, float size) {
-  const float2 one = f2(1.0f), half = f2(0.5f);
-  if (ALIGN) return __fmul2_rn(__fmul2_rn(__fadd2_rn(c, one), half), f2(size - 1.0f));
-  return __fmul2_rn(__fadd2_rn(__fmul2_rn(__fadd2_rn(c, one), f2(size)), f2(-1.0f)), half);
+  return f2(unnormalize1<ALIGN>(c.x, size), unnormalize1<ALIGN>(c.y, size));
 }
 
 // std::min(size-1, std::max(in, 0)) with std's argument order: a NaN
@@ -257,12 +265,16 @@ __device__ __forceinline__ void sample_pair(const KeyArgs& k, int64_t b, int H, 
     float va[8], vb[8];
     taps8<DT>(cs, ca, W, D, va);
     taps8<DT>(cs, cb, W, D, vb);
-    // out += v * w in torch's tap order, both voxels at once
-    float2 acc = f2(0.0f);
+    // out += v * w in torch's tap order; scalar, separately rounded
+    // operations (a packed multiply-then-add would be contracted to a fma)
+    float acc_a = 0.0f, acc_b = 0.0f;
 #pragma unroll
-    for (int t = 0; t < 8; ++t) acc = __fadd2_rn(acc, __fmul2_rn(f2(va[t], vb[t]), w[t]));
-    st<DT>(cd, sa, acc.x);
-    if (has_b) st<DT>(cd, sb, acc.y);
+    for (int t = 0; t < 8; ++t) {
+      acc_a = __fadd_rn(acc_a, __fmul_rn(va[t], w[t].x));
+      acc_b = __fadd_rn(acc_b, __fmul_rn(vb[t], w[t].y));
+    }
+    st<DT>(cd, sa, acc_a);
+    if (has_b) st<DT>(cd, sb, acc_b);
   }
 }
 

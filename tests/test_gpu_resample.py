@@ -149,7 +149,8 @@ def test_full_size_config2_properties(ba, oracle_lib):
     assert np.array_equal(to_np(out[:2]), ref)
     eye = np.broadcast_to(np.eye(4, dtype=np.float32), (8, 4, 4)).copy()
     ident = ops.resample3d(x, affine=eye, paddings="border")
-    assert torch.allclose(ident, x, rtol=0, atol=1e-6)
+    # unnormalised coordinates carry ~size * ulp(1) of rounding: 128 * 6e-8
+    assert torch.allclose(ident, x, rtol=0, atol=2e-5)
     assert np.array_equal(to_np(ident[:1]),
                           oracle_lib.resample3d(xs[:1], affine=eye[:1], padding="border"))
     m = np.zeros(8, bool)
