@@ -171,6 +171,26 @@ BA_API ba_status ba_intensity_chain(const ba_chain_desc* desc, void* workspace, 
                              ba_stream_t stream);
 
 /*
+ * ba_intensity_chain for callers that cannot allocate device memory — no
+ * counterpart in the reference.  Some hosts of this library (plugin hosts,
+ * embedded pipelines) own all device memory through their own pool, or call
+ * the chain in a loop where cudaMalloc/cudaFree, which may synchronise the
+ * device, is not allowed; they cannot supply the chain's scratch.  This entry
+ * point takes it from a static device array of BA_NOALLOC_CHAIN_SCRATCH bytes
+ * instead (every GPU that loads the library holds that array until the
+ * process exits) and allocates nothing.  Chains needing more scratch than
+ * that (see ba_intensity_workspace_bytes) are rejected with BA_EINVAL.
+ * The first call on each device looks the array's device address up
+ * (cudaGetSymbolAddress) and caches it; make that first call before any
+ * stream capture.  All calls share the one array: calls that overlap on the
+ * GPU (for example on two streams at once) race on it and must not be
+ * issued.  Each call re-initialises the statistics it uses, so contents left
+ * by an earlier call are never read.
+ */
+#define BA_NOALLOC_CHAIN_SCRATCH 262144
+BA_API ba_status ba_intensity_chain_noalloc(const ba_chain_desc* desc, ba_stream_t stream);
+
+/*
  * Per-group min and max of a contiguous (n_groups, group_size) view, fp32
  * results in stats[2*g] (min) and stats[2*g+1] (max); a NaN in a group makes
  * both NaN.  Replaces batched_minmax, batchaug/triton/kernels/reduce.py:51-75
