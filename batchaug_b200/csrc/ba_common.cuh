@@ -32,23 +32,29 @@ ba_status check_launch(const char* what);
 
 // ---------------------------------------------------------------------------
 // Element access.  bf16 is stored as the upper half of an fp32 and rounded
-// to nearest even on store, which is what c10::BFloat16 does.
+// to nearest even on store, which is what c10::BFloat16 does.  (NaN payload
+// bits may differ from c10's canonical 0x7FC0; NaN stays NaN.)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) {
   return __uint_as_float(((uint32_t)h) << 16);
 }
 
+// Round-to-nearest-even through the hardware conversion (cvt.rn.bf16.f32),
+// the same result c10::BFloat16 gives for every non-NaN value.
 __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
-  if (f != f) return (uint16_t)0x7FC0;  // canonical NaN, as c10::BFloat16
-  uint32_t u = __float_as_uint(f);
-  u += 0x7FFFu + ((u >> 16) & 1u);
-  return (uint16_t)(u >> 16);
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+// Two values rounded and packed (lo = a, hi = b) in one conversion.
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 // Round an fp32 value to the nearest bf16 and back (one torch bf16 op's
 // rounding of its fp32 result).
 __device__ __forceinline__ float round_bf16(float f) {
-  return bf16_bits_to_f32(f32_to_bf16_bits(f));
+  return __bfloat162float(__float2bfloat16_rn(f));
 }
 
 template <int DT>
@@ -91,6 +97,22 @@ __device__ __forceinline__ int32_t fkey(float f) {
 __device__ __forceinline__ float fkey_inv(int32_t k) {
   return __int_as_float(k >= 0 ? k : (k ^ 0x7FFFFFFF));
 }
+// ---------------------------------------------------------------------------
+// Asynchronous 16-byte global->shared copies (cp.async, sm_80+).  A thread
+// waits for its own groups with cp.async.wait_group, a hardware wait.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
 constexpr int32_t KEY_MIN_NAN = (int32_t)0x80000000;  // below key(-inf)
 constexpr int32_t KEY_MAX_NAN = (int32_t)0x7FFFFFFF;  // above key(+inf)
 constexpr int32_t KEY_POS_INF = (int32_t)0x7F800000;

@@ -17,10 +17,10 @@
 // ops in registers (rounding to the tensor dtype after every op, as torch
 // does), writes the result and folds its min/max into per-group int32 keys
 // with one atomic per CTA and group.  The next segment re-reads that result.
-// The host walks the batch in slices whose working set fits in L2, running
-// every segment on a slice before moving on, so the re-reads hit L2 and HBM
-// sees the input once and the output once.  Gaussian noise is generated in
-// registers (Philox4x32-10 + Box-Muller) instead of being materialised.
+// Data streams through a per-thread cp.async ring in shared memory (deep
+// memory-level parallelism without register cost).  Gaussian noise is
+// generated in registers (Philox4x32-10 + Box-Muller) instead of being
+// materialised.
 #include <stdio.h>
 
 #include <algorithm>
@@ -33,6 +33,12 @@ namespace ba {
 namespace {
 
 constexpr int CHAIN_THREADS = 256;
+// Chunks in flight per thread in the cp.async ring (8 x 16 B x 256 threads =
+// 32 KB of shared memory per CTA) and the resident CTAs per SM it is sized
+// for: ~128 KB in flight per SM, enough to stream HBM at full rate.
+constexpr int CHAIN_PIPE = 8;
+constexpr int CHAIN_MINBLOCKS = 4;
+constexpr int CHAIN_MIN_CHUNKS = 16;
 
 struct OpArgs {
   int32_t kind;
@@ -137,29 +143,83 @@ __device__ __forceinline__ void bias_run(const OpArgs& op, int64_t b, int64_t s0
 }
 
 // ---------------------------------------------------------------------------
-// Apply ops to n consecutive values of one channel (positions s0..s0+n-1).
+// Per-(element, channel) constants of each op, resolved once per channel into
+// shared memory so the per-vector loop reads no parameters from global memory.
 // ---------------------------------------------------------------------------
+struct OpConst {
+  float k0, k1, k2, k3;
+  int on;
+};
+
+template <int DT>
+__device__ __forceinline__ void resolve_op(const ChainArgs& a, int oi, int64_t b, int64_t c,
+                                           OpConst& o) {
+  const OpArgs& op = a.ops[oi];
+  o.on = (op.mask == nullptr || op.mask[b] != 0) ? 1 : 0;
+  o.k0 = o.k1 = o.k2 = o.k3 = 0.0f;
+  switch (op.kind) {
+    case BA_OP_NOISE:
+      if (op.flags & BA_NOISE_PHILOX) {
+        o.k0 = op.param[b];   // std
+        o.k1 = op.param2[b];  // mean
+      }
+      break;
+    case BA_OP_CONTRAST: {
+      const float mn = decode_min_key(op.stats_in[2 * b]);
+      const float mx = decode_max_key(op.stats_in[2 * b + 1]);
+      const float rng = mx - mn;
+      o.k0 = mn;
+      o.k1 = rng;
+      o.k2 = rng + 1e-7f;
+      o.k3 = op.param[b];  // gamma
+      break;
+    }
+    case BA_OP_SCALE:
+      o.k0 = round_dt<DT>(1.0f + round_dt<DT>(op.param[b]));
+      break;
+    case BA_OP_SHIFT:
+      o.k0 = round_dt<DT>(op.param[b]);
+      break;
+    case BA_OP_RESCALE:
+      if (!(op.flags & BA_RESCALE_FACTOR) && (op.flags & (BA_RESCALE_MINV | BA_RESCALE_MAXV))) {
+        const int64_t g = op.stats_per_channel ? b * a.C + c : b;
+        const float mn = decode_min_key(op.stats_in[2 * g]);
+        const float mx = decode_max_key(op.stats_in[2 * g + 1]);
+        float den = round_dt<DT>(mx - mn);
+        const bool is_const = den == 0.0f;
+        o.k0 = mn;
+        o.k1 = is_const ? 1.0f : den;
+        o.k2 = is_const ? 1.0f : 0.0f;
+      }
+      break;
+    default:
+      break;
+  }
+}
+
+// Apply the segment's ops to n consecutive values of one channel (positions
+// s0..s0+n-1), every op rounding its result to the tensor dtype.
 template <int DT, int VEC>
-__device__ __forceinline__ void apply_ops(const ChainArgs& a, int64_t b, int64_t c, int64_t s0,
-                                          int n, float* v) {
+__device__ __forceinline__ void apply_ops(const ChainArgs& a, const OpConst* oc, int64_t b,
+                                          int64_t c, int64_t s0, int n, float* v) {
   for (int oi = 0; oi < a.n_ops; ++oi) {
     const OpArgs& op = a.ops[oi];
-    const bool on = op.mask == nullptr || op.mask[b] != 0;
+    const OpConst k = oc[oi];
+    const bool on = k.on != 0;
     switch (op.kind) {
       case BA_OP_NOISE: {
         // x + dt(noise) * dt(mask): computed for masked elements too (adds 0).
         const float m = on ? 1.0f : 0.0f;
         float nz[VEC];
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) nz[i] = 0.0f;
         if (op.flags & BA_NOISE_PHILOX) {
           // Noise of flat position p = c*HWD + s of element b is normal
           // (p & 3) of Philox block (seed; p >> 2, element, NOISE stream),
           // times std plus mean in fp32 as torch.randn(...) * std + mean.
-          const float sd = __ldg(op.param + b), mu = __ldg(op.param2 + b);
-          const uint64_t eb = op.elem_offset + (uint64_t)b;
-          const int64_t first = c * a.HWD + s0;
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) nz[i] = 0.0f;
           if (on) {
+            const uint64_t eb = op.elem_offset + (uint64_t)b;
+            const int64_t first = c * a.HWD + s0;
             if (VEC >= 4) {
               // vector path: first is a multiple of 4 (HWD % VEC == 0)
 #pragma unroll
@@ -171,7 +231,7 @@ __device__ __forceinline__ void apply_ops(const ChainArgs& a, int64_t b, int64_t
                 normal4(philox4x32_10(ctr, op.seed_lo, op.seed_hi), z4);
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
-                  if (base + i < VEC) nz[base + i] = z4[i] * sd + mu;
+                  if (base + i < VEC) nz[base + i] = z4[i] * k.k0 + k.k1;
               }
             } else {
               const uint64_t q = (uint64_t)first >> 2;
@@ -181,7 +241,7 @@ __device__ __forceinline__ void apply_ops(const ChainArgs& a, int64_t b, int64_t
               normal4(philox4x32_10(ctr, op.seed_lo, op.seed_hi), z4);
               const int l = (int)(first & 3);
               const float z = l == 0 ? z4[0] : (l == 1 ? z4[1] : (l == 2 ? z4[2] : z4[3]));
-              nz[0] = z * sd + mu;
+              nz[0] = z * k.k0 + k.k1;
             }
           }
         } else {
@@ -198,33 +258,26 @@ __device__ __forceinline__ void apply_ops(const ChainArgs& a, int64_t b, int64_t
       }
       case BA_OP_CONTRAST: {
         if (!on) break;
-        const float mn = decode_min_key(op.stats_in[2 * b]);
-        const float mx = decode_max_key(op.stats_in[2 * b + 1]);
-        const float g = __ldg(op.param + b);
-        const float rng = mx - mn;
-        const float den = rng + 1e-7f;
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
-          float nrm = (v[i] - mn) / den;
+          float nrm = (v[i] - k.k0) / k.k2;
           nrm = (nrm < 0.0f) ? 0.0f : nrm;
-          v[i] = round_dt<DT>(powf(nrm, g) * rng + mn);
+          v[i] = round_dt<DT>(powf(nrm, k.k3) * k.k1 + k.k0);
         }
         break;
       }
       case BA_OP_SCALE: {
         if (!on) break;
-        const float s = round_dt<DT>(1.0f + round_dt<DT>(__ldg(op.param + b)));
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) v[i] = round_dt<DT>(v[i] * s);
+        for (int i = 0; i < VEC; ++i) v[i] = round_dt<DT>(v[i] * k.k0);
         break;
       }
       case BA_OP_SHIFT: {
         if (!on) break;
-        const float o = round_dt<DT>(__ldg(op.param + b));
         const bool safe = op.flags & BA_SHIFT_SAFE;
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
-          float r = round_dt<DT>(v[i] + o);
+          float r = round_dt<DT>(v[i] + k.k0);
           if (safe) r = (r < 0.0f) ? 0.0f : ((r > 1.0f) ? 1.0f : r);
           v[i] = r;
         }
@@ -255,15 +308,10 @@ __device__ __forceinline__ void apply_ops(const ChainArgs& a, int64_t b, int64_t
         }
         const bool has_min = op.flags & BA_RESCALE_MINV, has_max = op.flags & BA_RESCALE_MAXV;
         if (!has_min && !has_max) break;
-        const int64_t g = op.stats_per_channel ? b * a.C + c : b;
-        const float mn = decode_min_key(op.stats_in[2 * g]);
-        const float mx = decode_max_key(op.stats_in[2 * g + 1]);
-        float den = round_dt<DT>(mx - mn);
-        const bool is_const = den == 0.0f;
-        if (is_const) den = 1.0f;
+        const bool is_const = k.k2 != 0.0f;
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
-          const float nrm = round_dt<DT>(round_dt<DT>(v[i] - mn) / den);
+          const float nrm = round_dt<DT>(round_dt<DT>(v[i] - k.k0) / k.k1);
           float r = nrm;
           if (has_min && has_max) r = round_dt<DT>(round_dt<DT>(nrm * op.span) + op.minv);
           if (has_min && is_const) r = round_dt<DT>(v[i] * op.minv);
@@ -273,58 +321,6 @@ __device__ __forceinline__ void apply_ops(const ChainArgs& a, int64_t b, int64_t
       }
       default:
         break;
-    }
-  }
-}
-
-template <int DT, int VEC>
-__device__ __forceinline__ void load_run(const void* p, int64_t idx, int n, float* v) {
-  if (DT == BA_F32) {
-    const float* q = (const float*)p + idx;
-    if (VEC == 4 && n == 4) {
-      const float4 t = *(const float4*)q;
-      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-    } else {
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) v[i] = (i < n) ? q[i] : 0.0f;
-    }
-  } else {
-    const uint16_t* q = (const uint16_t*)p + idx;
-    if (VEC == 8 && n == 8) {
-      const uint4 t = *(const uint4*)q;
-      const uint32_t w[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        v[2 * i] = __uint_as_float(w[i] << 16);
-        v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) v[i] = (i < n) ? bf16_bits_to_f32(q[i]) : 0.0f;
-    }
-  }
-}
-
-template <int DT, int VEC>
-__device__ __forceinline__ void store_run(void* p, int64_t idx, int n, const float* v) {
-  if (DT == BA_F32) {
-    float* q = (float*)p + idx;
-    if (VEC == 4 && n == 4) {
-      *(float4*)q = make_float4(v[0], v[1], v[2], v[3]);
-    } else {
-      for (int i = 0; i < n; ++i) q[i] = v[i];
-    }
-  } else {
-    uint16_t* q = (uint16_t*)p + idx;
-    if (VEC == 8 && n == 8) {
-      uint4 t;
-      t.x = (uint32_t)f32_to_bf16_bits(v[0]) | ((uint32_t)f32_to_bf16_bits(v[1]) << 16);
-      t.y = (uint32_t)f32_to_bf16_bits(v[2]) | ((uint32_t)f32_to_bf16_bits(v[3]) << 16);
-      t.z = (uint32_t)f32_to_bf16_bits(v[4]) | ((uint32_t)f32_to_bf16_bits(v[5]) << 16);
-      t.w = (uint32_t)f32_to_bf16_bits(v[6]) | ((uint32_t)f32_to_bf16_bits(v[7]) << 16);
-      *(uint4*)q = t;
-    } else {
-      for (int i = 0; i < n; ++i) q[i] = f32_to_bf16_bits(v[i]);
     }
   }
 }
@@ -370,47 +366,119 @@ __device__ __forceinline__ void fold_minmax(const float* v, int n, float& mn, fl
   }
 }
 
-// One segment of the chain over elements [b0, b0 + gridDim.y), spatial
-// positions [blockIdx.x * tile, +tile) of every channel.
+// 16 bytes <-> VEC floats of the dtype.
+template <int DT, int VEC>
+__device__ __forceinline__ void unpack16(const uint4& t, float* v) {
+  const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+  if (DT == BA_BF16) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(w[i]);
+  }
+}
+
+template <int DT, int VEC>
+__device__ __forceinline__ uint4 pack16(const float* v) {
+  uint4 t;
+  if (DT == BA_BF16) {
+    t.x = pack_bf16x2(v[0], v[1]);
+    t.y = pack_bf16x2(v[2], v[3]);
+    t.z = pack_bf16x2(v[4], v[5]);
+    t.w = pack_bf16x2(v[6], v[7]);
+  } else {
+    t = make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]),
+                   __float_as_uint(v[3]));
+  }
+  return t;
+}
+
+// Vector path over positions [s_begin, s_end) of one channel: 16-byte chunks
+// handed to threads round-robin, each thread streaming its own chunks through
+// a private ring of PIPE slots in shared memory with cp.async, so PIPE chunks
+// per thread are in flight without holding registers.  A thread only reads
+// the slots it filled itself, so cp.async.wait_group alone orders the data.
 template <int DT, int VEC, bool WRITE>
-__global__ void __launch_bounds__(CHAIN_THREADS)
+__device__ __forceinline__ void run_range_vec(const ChainArgs& a, const OpConst* oc, int64_t b,
+                                              int64_t c, int64_t s_begin, int64_t s_end,
+                                              bool stats, float& mn, float& mx, bool& nan,
+                                              uint4* ring) {
+  const int tid = threadIdx.x;
+  const int64_t n_chunks = (s_end - s_begin) / VEC;
+  const int64_t base = (b * a.C + c) * a.HWD + s_begin;
+  const uint4* src = reinterpret_cast<const uint4*>(
+      (const char*)a.src + base * (DT == BA_BF16 ? 2 : 4));
+  uint4* dst = reinterpret_cast<uint4*>((char*)a.dst + base * (DT == BA_BF16 ? 2 : 4));
+#pragma unroll
+  for (int k = 0; k < CHAIN_PIPE - 1; ++k) {
+    const int64_t j = tid + (int64_t)k * CHAIN_THREADS;
+    if (j < n_chunks) cp_async16(&ring[k * CHAIN_THREADS + tid], src + j);
+    cp_async_commit();
+  }
+  int slot = 0;
+  for (int64_t j = tid; j < n_chunks; j += CHAIN_THREADS) {
+    const int64_t jp = j + (int64_t)(CHAIN_PIPE - 1) * CHAIN_THREADS;
+    const int pslot = slot == 0 ? CHAIN_PIPE - 1 : slot - 1;
+    if (jp < n_chunks) cp_async16(&ring[pslot * CHAIN_THREADS + tid], src + jp);
+    cp_async_commit();
+    cp_async_wait<CHAIN_PIPE - 1>();
+    float v[VEC];
+    unpack16<DT, VEC>(ring[slot * CHAIN_THREADS + tid], v);
+    apply_ops<DT, VEC>(a, oc, b, c, s_begin + j * VEC, VEC, v);
+    if (WRITE) dst[j] = pack16<DT, VEC>(v);
+    if (stats) fold_minmax<VEC>(v, VEC, mn, mx, nan);
+    slot = slot + 1 == CHAIN_PIPE ? 0 : slot + 1;
+  }
+  cp_async_wait<0>();
+}
+
+// Scalar path (spatial size not a multiple of the vector width, or
+// unaligned pointers): one element at a time.
+template <int DT, bool WRITE>
+__device__ __forceinline__ void run_range_scalar(const ChainArgs& a, const OpConst* oc,
+                                                 int64_t b, int64_t c, int64_t s_begin,
+                                                 int64_t s_end, bool stats, float& mn, float& mx,
+                                                 bool& nan) {
+  const int64_t base = (b * a.C + c) * a.HWD;
+  for (int64_t s = s_begin + threadIdx.x; s < s_end; s += CHAIN_THREADS) {
+    float v[1];
+    v[0] = load_f(a.src, DT, base + s);
+    apply_ops<DT, 1>(a, oc, b, c, s, 1, v);
+    if (WRITE) store_f(a.dst, DT, base + s, v[0]);
+    if (stats) fold_minmax<1>(v, 1, mn, mx, nan);
+  }
+}
+
+// One segment of the chain.  CTA (x, y) handles spatial positions
+// [x * tile, +tile) of channel y % C of element b0 + y / C, so the cp.async
+// ring runs uninterrupted over the whole range and the op constants are
+// resolved once per CTA.
+template <int DT, int VEC, bool WRITE>
+__global__ void __launch_bounds__(CHAIN_THREADS, CHAIN_MINBLOCKS)
     chain_kernel(const __grid_constant__ ChainArgs a) {
-  const int64_t b = a.b0 + blockIdx.y;
+  __shared__ OpConst s_oc[BA_MAX_OPS];
+  __shared__ uint4 s_ring[VEC > 1 ? CHAIN_PIPE * CHAIN_THREADS : 1];
+  const int64_t b = a.b0 + blockIdx.y / a.C;
+  const int64_t c = blockIdx.y % a.C;
   const int64_t s_begin = (int64_t)blockIdx.x * a.tile;
   const int64_t s_end = min(s_begin + a.tile, a.HWD);
-  if (a.stats_mode == 2) {
-    // statistics per (element, channel): channel-outer, one commit each
-    for (int64_t c = 0; c < a.C; ++c) {
-      float mn = INFINITY, mx = -INFINITY;
-      bool nan = false;
-      for (int64_t s = s_begin + (int64_t)threadIdx.x * VEC; s < s_end;
-           s += CHAIN_THREADS * VEC) {
-        const int n = (int)min((int64_t)VEC, s_end - s);
-        const int64_t idx = (b * a.C + c) * a.HWD + s;
-        float v[VEC];
-        load_run<DT, VEC>(a.src, idx, n, v);
-        apply_ops<DT, VEC>(a, b, c, s, n, v);
-        if (WRITE) store_run<DT, VEC>(a.dst, idx, n, v);
-        fold_minmax<VEC>(v, n, mn, mx, nan);
-      }
-      block_minmax_commit(mn, mx, nan, a.stats_out + 2 * (b * a.C + c));
-    }
-    return;
-  }
+  if (threadIdx.x < a.n_ops) resolve_op<DT>(a, threadIdx.x, b, c, s_oc[threadIdx.x]);
+  __syncthreads();
   float mn = INFINITY, mx = -INFINITY;
   bool nan = false;
-  for (int64_t s = s_begin + (int64_t)threadIdx.x * VEC; s < s_end; s += CHAIN_THREADS * VEC) {
-    const int n = (int)min((int64_t)VEC, s_end - s);
-    for (int64_t c = 0; c < a.C; ++c) {
-      const int64_t idx = (b * a.C + c) * a.HWD + s;
-      float v[VEC];
-      load_run<DT, VEC>(a.src, idx, n, v);
-      apply_ops<DT, VEC>(a, b, c, s, n, v);
-      if (WRITE) store_run<DT, VEC>(a.dst, idx, n, v);
-      if (a.stats_mode == 1) fold_minmax<VEC>(v, n, mn, mx, nan);
-    }
-  }
-  if (a.stats_mode == 1) block_minmax_commit(mn, mx, nan, a.stats_out + 2 * b);
+  if (VEC > 1)
+    run_range_vec<DT, VEC, WRITE>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx, nan,
+                                  s_ring);
+  else
+    run_range_scalar<DT, WRITE>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx, nan);
+  if (a.stats_mode == 2)
+    block_minmax_commit(mn, mx, nan, a.stats_out + 2 * (b * a.C + c));
+  else if (a.stats_mode == 1)
+    block_minmax_commit(mn, mx, nan, a.stats_out + 2 * b);
 }
 
 __global__ void init_keys_kernel(int32_t* keys, int64_t n_groups) {
@@ -432,26 +500,46 @@ __global__ void decode_keys_kernel(float* stats, int64_t n_groups) {
   }
 }
 
-// Plain per-group min/max over a (n_groups, group_size) view.
+// Plain per-group min/max over a (n_groups, group_size) view, streamed
+// through the same per-thread cp.async ring as the chain.
 template <int DT, int VEC>
-__global__ void __launch_bounds__(CHAIN_THREADS)
+__global__ void __launch_bounds__(CHAIN_THREADS, CHAIN_MINBLOCKS)
     minmax_kernel(const void* x, int64_t group_size, int64_t tile, int32_t* keys) {
+  __shared__ uint4 s_ring[VEC > 1 ? CHAIN_PIPE * CHAIN_THREADS : 1];
   const int64_t g = blockIdx.y;
   const int64_t s_begin = (int64_t)blockIdx.x * tile;
   const int64_t s_end = min(s_begin + tile, group_size);
   float mn = INFINITY, mx = -INFINITY;
   bool nan = false;
-  for (int64_t s = s_begin + (int64_t)threadIdx.x * VEC; s < s_end; s += CHAIN_THREADS * VEC) {
-    const int n = (int)min((int64_t)VEC, s_end - s);
-    float v[VEC];
-    load_run<DT, VEC>(x, g * group_size + s, n, v);
+  if (VEC > 1) {
+    const int tid = threadIdx.x;
+    const int64_t n_chunks = (s_end - s_begin) / VEC;
+    const uint4* src = reinterpret_cast<const uint4*>(
+        (const char*)x + (g * group_size + s_begin) * (DT == BA_BF16 ? 2 : 4));
 #pragma unroll
-    for (int i = 0; i < VEC; ++i)
-      if (i < n) {
-        nan |= (v[i] != v[i]);
-        mn = v[i] < mn ? v[i] : mn;
-        mx = v[i] > mx ? v[i] : mx;
-      }
+    for (int k = 0; k < CHAIN_PIPE - 1; ++k) {
+      const int64_t j = tid + (int64_t)k * CHAIN_THREADS;
+      if (j < n_chunks) cp_async16(&s_ring[k * CHAIN_THREADS + tid], src + j);
+      cp_async_commit();
+    }
+    int slot = 0;
+    for (int64_t j = tid; j < n_chunks; j += CHAIN_THREADS) {
+      const int64_t jp = j + (int64_t)(CHAIN_PIPE - 1) * CHAIN_THREADS;
+      const int pslot = slot == 0 ? CHAIN_PIPE - 1 : slot - 1;
+      if (jp < n_chunks) cp_async16(&s_ring[pslot * CHAIN_THREADS + tid], src + jp);
+      cp_async_commit();
+      cp_async_wait<CHAIN_PIPE - 1>();
+      float v[VEC];
+      unpack16<DT, VEC>(s_ring[slot * CHAIN_THREADS + tid], v);
+      fold_minmax<VEC>(v, VEC, mn, mx, nan);
+      slot = slot + 1 == CHAIN_PIPE ? 0 : slot + 1;
+    }
+    cp_async_wait<0>();
+  } else {
+    for (int64_t s = s_begin + threadIdx.x; s < s_end; s += CHAIN_THREADS) {
+      float v[1] = {load_f(x, DT, g * group_size + s)};
+      fold_minmax<1>(v, 1, mn, mx, nan);
+    }
   }
   block_minmax_commit(mn, mx, nan, keys + 2 * g);
 }
@@ -469,26 +557,16 @@ int sm_count() {
   return cached;
 }
 
-int64_t l2_bytes() {
-  static int64_t cached = 0;
-  if (cached == 0) {
-    int dev = 0, n = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess &&
-        cudaDeviceGetAttribute(&n, cudaDevAttrL2CacheSize, dev) == cudaSuccess && n > 0)
-      cached = n;
-    else
-      cached = 126ll << 20;
-  }
-  return cached;
-}
-
-// Spatial positions per CTA: aim for ~4 CTAs per SM over the launch.
+// Spatial positions per CTA: enough CTAs for about two waves, but at least
+// CHAIN_MIN_CHUNKS 16-byte chunks per thread so the cp.async ring is full
+// for most of a CTA's life.
 int64_t pick_tile(int64_t positions, int64_t n_blocks_y, int vec) {
-  const int64_t target_blocks = (int64_t)sm_count() * 4;
-  int64_t per_y = std::max<int64_t>(1, target_blocks / std::max<int64_t>(1, n_blocks_y));
-  int64_t tile = (positions + per_y - 1) / per_y;
+  const int64_t target_blocks = (int64_t)sm_count() * CHAIN_MINBLOCKS * 2;
+  const int64_t per_y = std::max<int64_t>(1, target_blocks / std::max<int64_t>(1, n_blocks_y));
   const int64_t quantum = (int64_t)CHAIN_THREADS * vec;
-  tile = std::max<int64_t>(quantum, (tile + quantum - 1) / quantum * quantum);
+  int64_t tile = (positions + per_y - 1) / per_y;
+  tile = std::max<int64_t>(tile, quantum * (vec > 1 ? CHAIN_MIN_CHUNKS : 1));
+  tile = (tile + quantum - 1) / quantum * quantum;
   return tile;
 }
 
@@ -514,7 +592,8 @@ ba_status validate_chain(const ba_chain_desc* d) {
   BA_REQUIRE(d != nullptr, "ba_intensity_chain: desc is NULL");
   BA_REQUIRE(d->batch >= 0 && d->channels >= 0 && d->H > 0 && d->W > 0 && d->D > 0,
              "ba_intensity_chain: bad shape");
-  BA_REQUIRE(d->batch <= 65535, "ba_intensity_chain: batch exceeds 65535");
+  BA_REQUIRE(d->batch * d->channels <= 65535,
+             "ba_intensity_chain: batch * channels exceeds 65535");
   BA_REQUIRE(d->dtype == BA_F32 || d->dtype == BA_BF16, "ba_intensity_chain: bad dtype %d",
              d->dtype);
   BA_REQUIRE(d->n_ops >= 1 && d->n_ops <= BA_MAX_OPS, "ba_intensity_chain: n_ops=%d not in 1..%d",
@@ -585,9 +664,9 @@ void plan_segments(const ba_chain_desc* d, std::vector<Segment>& segs, int64_t& 
 
 template <int DT, int VEC>
 ba_status launch_segment(ChainArgs& a, int64_t nb, bool write, cudaStream_t st) {
-  const int64_t tile = pick_tile(a.HWD, nb, VEC);
+  const int64_t tile = pick_tile(a.HWD, nb * a.C, VEC);
   a.tile = tile;
-  dim3 grid((unsigned)((a.HWD + tile - 1) / tile), (unsigned)nb);
+  dim3 grid((unsigned)((a.HWD + tile - 1) / tile), (unsigned)(nb * a.C));
   if (write)
     chain_kernel<DT, VEC, true><<<grid, CHAIN_THREADS, 0, st>>>(a);
   else
@@ -646,14 +725,7 @@ extern "C" ba_status ba_intensity_chain(const ba_chain_desc* desc, void* workspa
                         return true;
                       }();
 
-  // Elements per slice: keep one slice of dst (re-read by later segments)
-  // within about half of L2.
-  const int64_t elem_bytes = d.channels * HWD * (int64_t)esz;
-  int64_t slice = d.batch;
-  if (segs.size() > 1 && elem_bytes > 0) {
-    slice = std::max<int64_t>(1, (l2_bytes() / 2) / elem_bytes);
-    slice = std::min<int64_t>(slice, d.batch);
-  }
+  const int64_t slice = d.batch;  // measured: slicing the batch for L2 reuse did not pay
 
   ChainArgs a;
   memset(&a, 0, sizeof(a));

@@ -61,13 +61,16 @@ __host__ __device__ __forceinline__ float u01(uint32_t r) {
 }
 
 #ifdef __CUDACC__
-// Four standard normals from one Philox block (two Box-Muller pairs).
+// Four standard normals from one Philox block (two Box-Muller pairs).  The
+// angle is drawn in [-pi, pi), where the hardware sine/cosine are accurate to
+// about 2^-21; only the distribution matters for augmentation noise.
 __device__ __forceinline__ void normal4(U4 r, float* z) {
   const float r0 = sqrtf(-2.0f * __logf(u01_open0(r.x)));
   const float r1 = sqrtf(-2.0f * __logf(u01_open0(r.z)));
+  constexpr float TWO_PI = 6.283185307179586f, PI = 3.141592653589793f;
   float s0, c0, s1, c1;
-  sincospif(2.0f * u01(r.y), &s0, &c0);
-  sincospif(2.0f * u01(r.w), &s1, &c1);
+  __sincosf(u01(r.y) * TWO_PI - PI, &s0, &c0);
+  __sincosf(u01(r.w) * TWO_PI - PI, &s1, &c1);
   z[0] = r0 * c0;
   z[1] = r0 * s0;
   z[2] = r1 * c1;

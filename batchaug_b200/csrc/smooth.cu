@@ -177,6 +177,288 @@ __global__ void __launch_bounds__(SM_THREADS)
   }
 }
 
+// ===========================================================================
+// Tiled separable smoothing (used when the taps fit TILE_KMAX).
+//
+// Pass A convolves each H-plane along D then W inside a shared-memory tile
+// (halo loaded with the padding rule), writing an fp32 intermediate; pass B
+// convolves along H over column strips of that intermediate and writes the
+// result (the output dtype, or one component of the elastic grid).  Taps sit
+// in registers zero-padded to a compile-time KMAX, and each thread produces R
+// outputs per window it reads, so the loops are FMA-bound rather than bound
+// by shared-memory loads.  Rows read with stride R per thread use the padded
+// index q + q/8, which keeps those reads free of bank conflicts.  The three
+// 1-D operators (each "pad, then correlate" along one axis) commute, so
+// running D, W, H instead of the reference's H, W, D changes only rounding.
+// ===========================================================================
+constexpr int TS_THREADS = 256;
+constexpr int TS_TD = 64;   // tile extent along D (pass A and B)
+constexpr int TS_TW = 32;   // tile extent along W (pass A)
+constexpr int TS_TH = 64;   // tile extent along H (pass B)
+constexpr int TS_RD = 8;    // pass A D-outputs per thread unit
+constexpr int TS_RW = 8;    // pass A W-outputs per thread (TS_TW / TS_RW = 4 groups)
+constexpr int TS_RH = 16;   // pass B H-outputs per thread (TS_TH / TS_RH = 4 groups)
+constexpr int TILE_KMAX = 63;
+
+__host__ __device__ __forceinline__ int pidx(int q) { return q + (q >> 3); }
+
+struct TiledArgs {
+  const void* in;  // pass A: input volume (in_dtype), pass B: fp32 intermediate
+  int32_t in_dtype;
+  float* mid;      // fp32 intermediate (B*P, H, W, D)
+  void* out;       // pass B output
+  int32_t out_dtype;
+  const float* taps_h;
+  const float* taps_w;
+  const float* taps_d;
+  int32_t Kh, Kw, Kd;
+  int32_t padding;
+  int64_t P, H, W, D, HWD;
+  const uint8_t* mask;    // masked-out elements copy `copy_src` in pass B
+  const void* copy_src;
+  // elastic grid output (pass B): grid != nullptr
+  float* grid;
+  const float* magnitude;
+};
+
+template <int KMAX>
+__device__ __forceinline__ void load_taps(const float* taps, int64_t b, int K, float* w) {
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) w[k] = k < K ? __ldg(taps + b * K + k) : 0.0f;
+}
+
+// Pass A: grid (tiles_w * tiles_d, H, B*P).
+template <int KMAX>
+__global__ void __launch_bounds__(TS_THREADS) smooth_plane_kernel(const __grid_constant__ TiledArgs a) {
+  extern __shared__ float sm[];
+  const int64_t bp = blockIdx.z;
+  const int64_t b = bp / a.P;
+  if (a.mask != nullptr && a.mask[b] == 0) return;  // pass B copies the input
+  const int H = (int)a.H, W = (int)a.W, D = (int)a.D;
+  const int h = blockIdx.y;
+  const int tiles_d = (D + TS_TD - 1) / TS_TD;
+  const int td0 = (blockIdx.x % tiles_d) * TS_TD;
+  const int tw0 = (blockIdx.x / tiles_d) * TS_TW;
+  const int pd = a.Kd / 2, pw = a.Kw / 2;
+  // tile with halo: KMAX-wide windows read up to KMAX-1 past each output
+  const int rowsA = TS_TW + KMAX - 1, colsA = TS_TD + KMAX - 1;
+  const int PA = pidx(colsA - 1) + 1;
+  float* A = sm;                      // rowsA x PA (padded index)
+  float* Bm = sm + rowsA * PA;        // rowsA x TS_TD
+  const int64_t plane = (bp * a.H + h) * a.HWD / a.H;  // start of plane h of bp
+  for (int idx = threadIdx.x; idx < rowsA * colsA; idx += TS_THREADS) {
+    const int r = idx / colsA, q = idx % colsA;
+    // rows/cols beyond the real halo meet zero taps; keep them finite
+    float v = 0.0f;
+    if (r < TS_TW + 2 * pw && q < TS_TD + 2 * pd) {
+      const int64_t wi = pad_index(tw0 - pw + r, W, a.padding);
+      const int64_t di = pad_index(td0 - pd + q, D, a.padding);
+      if (wi >= 0 && di >= 0) v = load_in(a.in, a.in_dtype, plane + wi * D + di);
+    }
+    A[r * PA + pidx(q)] = v;
+  }
+  float wd[KMAX];
+  load_taps<KMAX>(a.taps_d, b, a.Kd, wd);
+  __syncthreads();
+  // D pass: units of TS_RD consecutive outputs of one row
+  constexpr int GROUPS_D = TS_TD / TS_RD;
+  for (int u = threadIdx.x; u < rowsA * GROUPS_D; u += TS_THREADS) {
+    const int r = u / GROUPS_D, q0 = (u % GROUPS_D) * TS_RD;
+    float acc[TS_RD];
+#pragma unroll
+    for (int i = 0; i < TS_RD; ++i) acc[i] = 0.0f;
+    const float* row = A + r * PA;
+#pragma unroll
+    for (int j = 0; j < TS_RD + KMAX - 1; ++j) {
+      const float x = row[pidx(q0 + j)];
+#pragma unroll
+      for (int i = 0; i < TS_RD; ++i) {
+        const int k = j - i;
+        if (k >= 0 && k < KMAX) acc[i] = acc[i] + wd[k] * x;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < TS_RD; ++i) Bm[r * TS_TD + q0 + i] = acc[i];
+  }
+  float ww[KMAX];
+  load_taps<KMAX>(a.taps_w, b, a.Kw, ww);
+  __syncthreads();
+  // W pass: thread (q, wg) produces rows wg*TS_RW .. +TS_RW-1 of column q
+  const int q = threadIdx.x % TS_TD, wg = threadIdx.x / TS_TD;
+  float acc[TS_RW];
+#pragma unroll
+  for (int i = 0; i < TS_RW; ++i) acc[i] = 0.0f;
+#pragma unroll
+  for (int j = 0; j < TS_RW + KMAX - 1; ++j) {
+    const float x = Bm[(wg * TS_RW + j) * TS_TD + q];
+#pragma unroll
+    for (int i = 0; i < TS_RW; ++i) {
+      const int k = j - i;
+      if (k >= 0 && k < KMAX) acc[i] = acc[i] + ww[k] * x;
+    }
+  }
+  const int d = td0 + q;
+  if (d < D) {
+#pragma unroll
+    for (int i = 0; i < TS_RW; ++i) {
+      const int w = tw0 + wg * TS_RW + i;
+      if (w < W) a.mid[plane + (int64_t)w * D + d] = acc[i];
+    }
+  }
+}
+
+// Pass B: grid (tiles_h * tiles_d, W, B*P).
+template <int KMAX>
+__global__ void __launch_bounds__(TS_THREADS) smooth_column_kernel(const __grid_constant__ TiledArgs a) {
+  extern __shared__ float sm[];
+  const int64_t bp = blockIdx.z;
+  const int64_t b = bp / a.P;
+  const int H = (int)a.H, W = (int)a.W, D = (int)a.D;
+  const int w = blockIdx.y;
+  const int tiles_d = (D + TS_TD - 1) / TS_TD;
+  const int td0 = (blockIdx.x % tiles_d) * TS_TD;
+  const int th0 = (blockIdx.x / tiles_d) * TS_TH;
+  const int q = threadIdx.x % TS_TD, hg = threadIdx.x / TS_TD;
+  const int d = td0 + q;
+  const int64_t col = bp * a.HWD + (int64_t)w * D + d;  // + h * W * D
+  const int64_t plane_stride = (int64_t)W * D;
+  if (a.mask != nullptr && a.mask[b] == 0) {
+    if (a.copy_src != nullptr && d < D) {
+      for (int i = 0; i < TS_RH; ++i) {
+        const int h = th0 + hg * TS_RH + i;
+        if (h >= H) break;
+        const int64_t o = col + h * plane_stride;
+        if (a.out_dtype == BA_BF16)
+          ((uint16_t*)a.out)[o] = ((const uint16_t*)a.copy_src)[o];
+        else
+          ((float*)a.out)[o] = ((const float*)a.copy_src)[o];
+      }
+    }
+    return;
+  }
+  const int ph = a.Kh / 2;
+  const int rowsS = TS_TH + KMAX - 1;
+  float* S = sm;  // rowsS x TS_TD
+  for (int idx = threadIdx.x; idx < rowsS * TS_TD; idx += TS_THREADS) {
+    const int r = idx / TS_TD, qq = idx % TS_TD;
+    float v = 0.0f;
+    if (r < TS_TH + 2 * ph && td0 + qq < D) {
+      const int64_t hi = pad_index(th0 - ph + r, H, a.padding);
+      if (hi >= 0) v = a.mid[bp * a.HWD + hi * plane_stride + (int64_t)w * D + td0 + qq];
+    }
+    S[r * TS_TD + qq] = v;
+  }
+  float wh[KMAX];
+  load_taps<KMAX>(a.taps_h, b, a.Kh, wh);
+  __syncthreads();
+  float acc[TS_RH];
+#pragma unroll
+  for (int i = 0; i < TS_RH; ++i) acc[i] = 0.0f;
+#pragma unroll
+  for (int j = 0; j < TS_RH + KMAX - 1; ++j) {
+    const float x = S[(hg * TS_RH + j) * TS_TD + q];
+#pragma unroll
+    for (int i = 0; i < TS_RH; ++i) {
+      const int k = j - i;
+      if (k >= 0 && k < KMAX) acc[i] = acc[i] + wh[k] * x;
+    }
+  }
+  if (d >= D) return;
+  if (a.grid != nullptr) {
+    // elastic: component P-index of bp is the displacement axis
+    const int comp = (int)(bp % a.P);
+    const float mag = a.magnitude[b];
+    const int64_t sz = comp == 0 ? a.H : (comp == 1 ? a.W : a.D);
+    const float n = (float)sz;
+    const float half_lo = (n - 1.0f) / 2.0f;
+    const float step = (half_lo - (-half_lo)) / (n - 1.0f);
+    const float half = half_lo < 1e-6f ? 1e-6f : half_lo;
+#pragma unroll
+    for (int i = 0; i < TS_RH; ++i) {
+      const int h = th0 + hg * TS_RH + i;
+      if (h < H) {
+        const int64_t idx = comp == 0 ? h : (comp == 1 ? w : d);
+        const float c0 = linspace_at(-half_lo, half_lo, step, idx, sz);
+        const int64_t s = (int64_t)h * plane_stride + (int64_t)w * D + d;
+        a.grid[(b * a.HWD + s) * 3 + (2 - comp)] = (c0 + acc[i] * mag) / half;
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < TS_RH; ++i) {
+    const int h = th0 + hg * TS_RH + i;
+    if (h < H) {
+      const int64_t o = col + h * plane_stride;
+      if (a.out_dtype == BA_BF16)
+        ((uint16_t*)a.out)[o] = f32_to_bf16_bits(acc[i]);
+      else
+        ((float*)a.out)[o] = acc[i];
+    }
+  }
+}
+
+int tiled_kmax(int K) {
+  for (int k : {7, 15, 23, 31, 47, 63})
+    if (K <= k) return k;
+  return 0;
+}
+
+size_t plane_smem(int kmax) {
+  const int rowsA = TS_TW + kmax - 1, colsA = TS_TD + kmax - 1;
+  const int PA = pidx(colsA - 1) + 1;
+  return (size_t)(rowsA * PA + rowsA * TS_TD) * sizeof(float);
+}
+
+size_t column_smem(int kmax) { return (size_t)((TS_TH + kmax - 1) * TS_TD) * sizeof(float); }
+
+template <int KMAX>
+ba_status launch_tiled_kmax(const TiledArgs& a, int64_t planes, cudaStream_t st) {
+  const size_t sa = plane_smem(KMAX), sb = column_smem(KMAX);
+  // opt in to more than 48 KB of dynamic shared memory (B200: 227 KB per CTA)
+  cudaFuncSetAttribute(smooth_plane_kernel<KMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)sa);
+  cudaFuncSetAttribute(smooth_column_kernel<KMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)sb);
+  const int tiles_d = (int)((a.D + TS_TD - 1) / TS_TD);
+  dim3 ga((unsigned)(tiles_d * ((a.W + TS_TW - 1) / TS_TW)), (unsigned)a.H, (unsigned)planes);
+  smooth_plane_kernel<KMAX><<<ga, TS_THREADS, sa, st>>>(a);
+  ba_status s = check_launch("smooth pass A");
+  if (s != BA_OK) return s;
+  dim3 gb((unsigned)(tiles_d * ((a.H + TS_TH - 1) / TS_TH)), (unsigned)a.W, (unsigned)planes);
+  smooth_column_kernel<KMAX><<<gb, TS_THREADS, sb, st>>>(a);
+  return check_launch("smooth pass B");
+}
+
+ba_status launch_tiled(const TiledArgs& a, int64_t planes, cudaStream_t st) {
+  const int K = std::max(a.Kh, std::max(a.Kw, a.Kd));
+  switch (tiled_kmax(K)) {
+    case 7: return launch_tiled_kmax<7>(a, planes, st);
+    case 15: return launch_tiled_kmax<15>(a, planes, st);
+    case 23: return launch_tiled_kmax<23>(a, planes, st);
+    case 31: return launch_tiled_kmax<31>(a, planes, st);
+    case 47: return launch_tiled_kmax<47>(a, planes, st);
+    default: return launch_tiled_kmax<63>(a, planes, st);
+  }
+}
+
+// Uniform draw of the elastic field mapped to [-1,1), four values per thread
+// from one Philox block (requires HWD % 4 == 0).
+__global__ void elastic_draw4_kernel(uint32_t seed_lo, uint32_t seed_hi, uint64_t elem_offset,
+                                     int64_t HWD, int64_t total4, float4* out) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= total4) return;
+  const int64_t per4 = 3 * HWD / 4;
+  const int64_t b = i / per4;
+  const uint64_t q = (uint64_t)(i - b * per4);  // (comp*HWD + s) >> 2
+  const uint64_t eb = elem_offset + (uint64_t)b;
+  const U4 ctr = {(uint32_t)q, (uint32_t)eb, (uint32_t)(eb >> 32),
+                  STREAM_ELASTIC | (uint32_t)(q >> 32)};
+  const U4 r = philox4x32_10(ctr, seed_lo, seed_hi);
+  out[i] = make_float4(u01(r.x) * 2.0f - 1.0f, u01(r.y) * 2.0f - 1.0f, u01(r.z) * 2.0f - 1.0f,
+                       u01(r.w) * 2.0f - 1.0f);
+}
+
 ba_status launch_axis(int axis, const AxisArgs& a, int64_t planes, cudaStream_t st) {
   dim3 grid((unsigned)((a.HWD + SM_THREADS - 1) / SM_THREADS), (unsigned)planes);
   if (axis == 0)
@@ -257,6 +539,30 @@ extern "C" ba_status ba_smooth3d(const void* src, void* dst, int32_t dtype, int6
   float* t1 = t0 + n;
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t planes = batch * channels;
+  if (tiled_kmax((int)std::max(Kh, std::max(Kw, Kd))) != 0 && H <= 65535 && W <= 65535) {
+    TiledArgs t;
+    memset(&t, 0, sizeof(t));
+    t.in = src;
+    t.in_dtype = dtype;
+    t.mid = t0;
+    t.out = dst;
+    t.out_dtype = dtype;
+    t.taps_h = taps_h;
+    t.taps_w = taps_w;
+    t.taps_d = taps_d;
+    t.Kh = (int32_t)Kh;
+    t.Kw = (int32_t)Kw;
+    t.Kd = (int32_t)Kd;
+    t.padding = padding;
+    t.P = channels;
+    t.H = H;
+    t.W = W;
+    t.D = D;
+    t.HWD = HWD;
+    t.mask = mask;
+    t.copy_src = src;
+    return launch_tiled(t, planes, st);
+  }
   AxisArgs a;
   memset(&a, 0, sizeof(a));
   a.P = channels;
@@ -319,10 +625,35 @@ extern "C" ba_status ba_elastic_grid(const float* u, uint64_t seed, uint64_t ele
   float* t0 = (float*)workspace;
   float* t1 = t0 + batch * 3 * HWD;
   const int64_t total = batch * 3 * HWD;
-  elastic_draw_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
-      u, (uint32_t)seed, (uint32_t)(seed >> 32), elem_offset, HWD, total, t0);
-  ba_status s = check_launch("ba_elastic_grid");
+  ba_status s;
+  if (u == nullptr && (HWD % 4) == 0) {
+    const int64_t total4 = total / 4;
+    elastic_draw4_kernel<<<(unsigned)((total4 + 255) / 256), 256, 0, st>>>(
+        (uint32_t)seed, (uint32_t)(seed >> 32), elem_offset, HWD, total4, (float4*)t0);
+  } else {
+    elastic_draw_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+        u, (uint32_t)seed, (uint32_t)(seed >> 32), elem_offset, HWD, total, t0);
+  }
+  s = check_launch("ba_elastic_grid");
   if (s != BA_OK) return s;
+  if (tiled_kmax((int)K) != 0 && H <= 65535 && W <= 65535) {
+    TiledArgs t;
+    memset(&t, 0, sizeof(t));
+    t.in = t0;
+    t.in_dtype = BA_F32;
+    t.mid = t1;
+    t.taps_h = t.taps_w = t.taps_d = taps;
+    t.Kh = t.Kw = t.Kd = (int32_t)K;
+    t.padding = BA_SMOOTH_ZEROS;
+    t.P = 3;
+    t.H = H;
+    t.W = W;
+    t.D = D;
+    t.HWD = HWD;
+    t.grid = grid;
+    t.magnitude = magnitude;
+    return launch_tiled(t, batch * 3, st);
+  }
   AxisArgs a;
   memset(&a, 0, sizeof(a));
   a.P = 3;
