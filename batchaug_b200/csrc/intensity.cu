@@ -147,22 +147,70 @@ __device__ __forceinline__ void bias_run(const OpArgs& op, int64_t b, int64_t s0
 // shared memory so the per-vector loop reads no parameters from global memory.
 // ---------------------------------------------------------------------------
 struct OpConst {
-  float k0, k1, k2, k3;
+  float k0, k1, k2, k3, k4;
   int on;
+  // bf16 kernels: operands as bf16x2 splats, and whether the op can run on
+  // packed bf16 arithmetic (every scalar it uses is a bf16 value)
+  uint32_t h0, h1, h2;
+  int packed;
 };
+
+__device__ __forceinline__ bool is_bf16_value(float f) { return round_bf16(f) == f; }
+__device__ __forceinline__ uint32_t splat_bf16(float f) { return pack_bf16x2(f, f); }
+
+// RN(1/b) when a/b can take the reciprocal path of div_rn, else 0.
+__device__ __forceinline__ float recip_for_div(float b) {
+  const float m = fabsf(b);
+  return (m >= 0x1p-120f && m <= 0x1p120f) ? __frcp_rn(b) : 0.0f;
+}
+
+// a / b rounded to nearest, from y = RN(1/b) (recip_for_div): q = RN(a*y),
+// the remainder r = a - b*q is exact in one fma, and RN(q + r*y) is the
+// correctly rounded quotient (P. Markstein, "IA-64 and Elementary Functions",
+// 2000, the correction step for a correctly rounded reciprocal) whenever a, b
+// and the quotient are normal.  Zero, tiny, huge and non-finite quotients take
+// the plain division.
+__device__ __forceinline__ float div_rn(float a, float b, float y) {
+  if (y != 0.0f) {
+    const float q = __fmul_rn(a, y);
+    const float aq = fabsf(q);
+    if (a == 0.0f) return q;
+    if (aq >= 0x1p-100f && aq <= 0x1p100f) return __fmaf_rn(__fmaf_rn(-q, b, a), y, q);
+  }
+  return __fdiv_rn(a, b);
+}
+
+// a / b rounded to fp32 and then to bf16, for bf16 values a and b: the
+// bf16 rounding of RN(a * RN(1/b)) already equals it.  Reason: a/b of two
+// 8-bit significands is never a bf16 midpoint and, when not exact, is at
+// least ~2^-17 (relative) away from one, while a * RN(1/b) is within 2^-23 of
+// a/b; fp32-then-bf16 rounding of a quotient equals its bf16 rounding because
+// fp32 carries more than 2*8+2 bits (Figueroa, "When is double rounding
+// innocuous?", 1995).  Checked exhaustively over all significand pairs.
+__device__ __forceinline__ float div_for_bf16(float a, float b, float y) {
+  if (y != 0.0f) {
+    const float q = __fmul_rn(a, y);
+    const float aq = fabsf(q);
+    if (a == 0.0f || (aq >= 0x1p-100f && aq <= 0x1p100f)) return q;
+  }
+  return __fdiv_rn(a, b);
+}
 
 template <int DT>
 __device__ __forceinline__ void resolve_op(const ChainArgs& a, int oi, int64_t b, int64_t c,
                                            OpConst& o) {
   const OpArgs& op = a.ops[oi];
   o.on = (op.mask == nullptr || op.mask[b] != 0) ? 1 : 0;
-  o.k0 = o.k1 = o.k2 = o.k3 = 0.0f;
+  o.k0 = o.k1 = o.k2 = o.k3 = o.k4 = 0.0f;
+  o.h0 = o.h1 = o.h2 = 0u;
+  o.packed = 0;
   switch (op.kind) {
     case BA_OP_NOISE:
       if (op.flags & BA_NOISE_PHILOX) {
         o.k0 = op.param[b];   // std
         o.k1 = op.param2[b];  // mean
       }
+      o.h0 = splat_bf16(o.on ? 1.0f : 0.0f);
       break;
     case BA_OP_CONTRAST: {
       const float mn = decode_min_key(op.stats_in[2 * b]);
@@ -172,13 +220,16 @@ __device__ __forceinline__ void resolve_op(const ChainArgs& a, int oi, int64_t b
       o.k1 = rng;
       o.k2 = rng + 1e-7f;
       o.k3 = op.param[b];  // gamma
+      o.k4 = recip_for_div(o.k2);
       break;
     }
     case BA_OP_SCALE:
       o.k0 = round_dt<DT>(1.0f + round_dt<DT>(op.param[b]));
+      o.h0 = splat_bf16(o.k0);
       break;
     case BA_OP_SHIFT:
       o.k0 = round_dt<DT>(op.param[b]);
+      o.h0 = splat_bf16(o.k0);
       break;
     case BA_OP_RESCALE:
       if (!(op.flags & BA_RESCALE_FACTOR) && (op.flags & (BA_RESCALE_MINV | BA_RESCALE_MAXV))) {
@@ -190,6 +241,14 @@ __device__ __forceinline__ void resolve_op(const ChainArgs& a, int oi, int64_t b
         o.k0 = mn;
         o.k1 = is_const ? 1.0f : den;
         o.k2 = is_const ? 1.0f : 0.0f;
+        o.k3 = recip_for_div(o.k1);
+        o.h0 = splat_bf16(mn);
+        o.h1 = splat_bf16(op.span);
+        o.h2 = splat_bf16(op.minv);
+        o.packed = !is_const && is_bf16_value(op.span) && is_bf16_value(op.minv);
+      } else if (op.flags & BA_RESCALE_FACTOR) {
+        o.h0 = splat_bf16(op.factor1p);
+        o.packed = is_bf16_value(op.factor1p);
       }
       break;
     default:
@@ -197,18 +256,23 @@ __device__ __forceinline__ void resolve_op(const ChainArgs& a, int oi, int64_t b
   }
 }
 
-// Apply the segment's ops to n consecutive values of one channel (positions
-// s0..s0+n-1), every op rounding its result to the tensor dtype.
+// Apply op oi to n consecutive values of one channel (positions
+// s0..s0+n-1), rounding its result to the tensor dtype as torch does.
 template <int DT, int VEC>
-__device__ __forceinline__ void apply_ops(const ChainArgs& a, const OpConst* oc, int64_t b,
+__device__ __forceinline__ void apply_one(const ChainArgs& a, int oi, const OpConst& k, int64_t b,
                                           int64_t c, int64_t s0, int n, float* v) {
-  for (int oi = 0; oi < a.n_ops; ++oi) {
+  {
     const OpArgs& op = a.ops[oi];
-    const OpConst k = oc[oi];
     const bool on = k.on != 0;
     switch (op.kind) {
       case BA_OP_NOISE: {
-        // x + dt(noise) * dt(mask): computed for masked elements too (adds 0).
+        // x + dt(noise) * dt(mask).  A masked-out element with generated noise
+        // adds a zero; injected noise keeps the product (its sign of zero).
+        if (!on && (op.flags & BA_NOISE_PHILOX)) {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) v[i] = v[i] + 0.0f;
+          break;
+        }
         const float m = on ? 1.0f : 0.0f;
         float nz[VEC];
 #pragma unroll
@@ -260,7 +324,7 @@ __device__ __forceinline__ void apply_ops(const ChainArgs& a, const OpConst* oc,
         if (!on) break;
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
-          float nrm = (v[i] - k.k0) / k.k2;
+          float nrm = div_rn(v[i] - k.k0, k.k2, k.k4);
           nrm = (nrm < 0.0f) ? 0.0f : nrm;
           v[i] = round_dt<DT>(powf(nrm, k.k3) * k.k1 + k.k0);
         }
@@ -311,7 +375,7 @@ __device__ __forceinline__ void apply_ops(const ChainArgs& a, const OpConst* oc,
         const bool is_const = k.k2 != 0.0f;
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
-          const float nrm = round_dt<DT>(round_dt<DT>(v[i] - k.k0) / k.k1);
+          const float nrm = round_dt<DT>(div_rn(round_dt<DT>(v[i] - k.k0), k.k1, k.k3));
           float r = nrm;
           if (has_min && has_max) r = round_dt<DT>(round_dt<DT>(nrm * op.span) + op.minv);
           if (has_min && is_const) r = round_dt<DT>(v[i] * op.minv);
@@ -325,9 +389,153 @@ __device__ __forceinline__ void apply_ops(const ChainArgs& a, const OpConst* oc,
   }
 }
 
-// Block-wide min/max of (mn, mx, nan) followed by one atomic pair.
-__device__ __forceinline__ void block_minmax_commit(float mn, float mx, bool nan, int32_t* keys) {
+// The segment's ops, in order, on n consecutive values of one channel.
+template <int DT, int VEC>
+__device__ __forceinline__ void apply_ops(const ChainArgs& a, const OpConst* oc, int64_t b,
+                                          int64_t c, int64_t s0, int n, float* v) {
+  for (int oi = 0; oi < a.n_ops; ++oi) apply_one<DT, VEC>(a, oi, oc[oi], b, c, s0, n, v);
+}
+
+// ---------------------------------------------------------------------------
+// bf16 tensors: 8 values (one 16-byte chunk) as four bf16x2 words.  For two
+// bf16 operands, torch's "compute in fp32, round to bf16" equals one
+// correctly rounded bf16 operation (fp32 has more than 2*8+2 significand
+// bits, so the double rounding is innocuous for +, -, *, /), which is what
+// the packed bf16x2 instructions compute.  Ops whose scalars are all bf16
+// values run packed; the others (contrast, bias field, fp32 scalars, clamped
+// shift) take the fp32 path of apply_one on the unpacked values.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t w) {
+  return *reinterpret_cast<const __nv_bfloat162*>(&w);
+}
+__device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 h) {
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ void unpack_words(const uint32_t* w, float* v) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[2 * j] = __uint_as_float(w[j] << 16);
+    v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+  }
+}
+// values already rounded to bf16: the packing is a byte permutation
+__device__ __forceinline__ void pack_words(const float* v, uint32_t* w) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    w[j] = __byte_perm(__float_as_uint(v[2 * j]), __float_as_uint(v[2 * j + 1]), 0x7632);
+}
+
+__device__ __forceinline__ void apply_ops_bf16x8(const ChainArgs& a, const OpConst* oc,
+                                                 int64_t b, int64_t c, int64_t s0, uint32_t* w) {
+  for (int oi = 0; oi < a.n_ops; ++oi) {
+    const OpArgs& op = a.ops[oi];
+    const OpConst& k = oc[oi];
+    const bool on = k.on != 0;
+    bool done = true;
+    switch (op.kind) {
+      case BA_OP_NOISE:
+        if (op.flags & BA_NOISE_PHILOX) {
+          if (!on) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) w[j] = as_u32(__hadd2_rn(as_bf2(w[j]), as_bf2(0u)));
+            break;
+          }
+          const uint64_t eb = op.elem_offset + (uint64_t)b;
+          const int64_t first = c * a.HWD + s0;  // a multiple of 8
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const uint64_t q = (uint64_t)(first + 4 * half) >> 2;
+            const U4 ctr = {(uint32_t)q, (uint32_t)eb, (uint32_t)(eb >> 32),
+                            STREAM_NOISE | (uint32_t)(q >> 32)};
+            float z[4];
+            normal4(philox4x32_10(ctr, op.seed_lo, op.seed_hi), z);
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              // torch.randn(...) * std + mean in fp32, then .to(bf16)
+              const float n0 = __fadd_rn(__fmul_rn(z[2 * t], k.k0), k.k1);
+              const float n1 = __fadd_rn(__fmul_rn(z[2 * t + 1], k.k0), k.k1);
+              const int j = 2 * half + t;
+              w[j] = as_u32(__hadd2_rn(as_bf2(w[j]), __floats2bfloat162_rn(n0, n1)));
+            }
+          }
+        } else {
+          const float* np = op.noise + (b * a.C + c) * a.HWD + s0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const __nv_bfloat162 n2 = __floats2bfloat162_rn(__ldg(np + 2 * j), __ldg(np + 2 * j + 1));
+            w[j] = as_u32(__hadd2_rn(as_bf2(w[j]), __hmul2_rn(n2, as_bf2(k.h0))));
+          }
+        }
+        break;
+      case BA_OP_SCALE:
+        if (!on) break;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = as_u32(__hmul2_rn(as_bf2(w[j]), as_bf2(k.h0)));
+        break;
+      case BA_OP_SHIFT:
+        if (!on) break;
+        if (op.flags & BA_SHIFT_SAFE) {
+          done = false;
+          break;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = as_u32(__hadd2_rn(as_bf2(w[j]), as_bf2(k.h0)));
+        break;
+      case BA_OP_RESCALE:
+        if (op.flags & BA_RESCALE_FACTOR) {
+          if (!k.packed) {
+            done = false;
+            break;
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) w[j] = as_u32(__hmul2_rn(as_bf2(w[j]), as_bf2(k.h0)));
+          break;
+        }
+        if (!(op.flags & (BA_RESCALE_MINV | BA_RESCALE_MAXV))) break;
+        if (!k.packed) {
+          done = false;
+          break;
+        }
+        {
+          const bool both = (op.flags & BA_RESCALE_MINV) && (op.flags & BA_RESCALE_MAXV);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            // (x - mn) / den in bf16, then * (maxv - minv) + minv in bf16
+            const uint32_t num = as_u32(__hsub2_rn(as_bf2(w[j]), as_bf2(k.h0)));
+            const float q0 = div_for_bf16(__uint_as_float(num << 16), k.k1, k.k3);
+            const float q1 = div_for_bf16(__uint_as_float(num & 0xFFFF0000u), k.k1, k.k3);
+            __nv_bfloat162 r = __floats2bfloat162_rn(q0, q1);
+            if (both) r = __hadd2_rn(__hmul2_rn(r, as_bf2(k.h1)), as_bf2(k.h2));
+            w[j] = as_u32(r);
+          }
+        }
+        break;
+      default:
+        done = false;  // contrast, bias field: fp32 arithmetic, one rounding
+        break;
+    }
+    if (!done) {
+      float v[8];
+      unpack_words(w, v);
+      apply_one<BA_BF16, 8>(a, oi, k, b, c, s0, 8, v);
+      pack_words(v, w);
+    }
+  }
+}
+
+__device__ __forceinline__ void fold_minmax_bf16x8(const uint32_t* w, __nv_bfloat162& mn,
+                                                   __nv_bfloat162& mx) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    mn = __hmin2_nan(mn, as_bf2(w[j]));
+    mx = __hmax2_nan(mx, as_bf2(w[j]));
+  }
+}
+
+// Block-wide min/max of (mn, mx) followed by one atomic pair.
+__device__ __forceinline__ void block_minmax_commit(float mn, float mx, int32_t* keys) {
   __shared__ int32_t s_min[CHAIN_THREADS / 32], s_max[CHAIN_THREADS / 32];
+  const bool nan = (mn != mn) || (mx != mx);
   int32_t kmin = nan ? KEY_MIN_NAN : fkey(mn);
   int32_t kmax = nan ? KEY_MAX_NAN : fkey(mx);
 #pragma unroll
@@ -352,16 +560,26 @@ __device__ __forceinline__ void block_minmax_commit(float mn, float mx, bool nan
   }
 }
 
+// NaN-propagating min/max (PTX min.NaN / max.NaN, sm_80+): a NaN anywhere
+// makes the running value NaN, as torch.min / torch.max propagate it.
+__device__ __forceinline__ float min_nan(float a, float b) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
 template <int VEC>
-__device__ __forceinline__ void fold_minmax(const float* v, int n, float& mn, float& mx,
-                                            bool& nan) {
+__device__ __forceinline__ void fold_minmax(const float* v, int n, float& mn, float& mx) {
 #pragma unroll
   for (int i = 0; i < VEC; ++i) {
     if (i < n) {
-      // a NaN compares false both ways and only raises the flag
-      nan |= (v[i] != v[i]);
-      mn = v[i] < mn ? v[i] : mn;
-      mx = v[i] > mx ? v[i] : mx;
+      mn = min_nan(mn, v[i]);
+      mx = max_nan(mx, v[i]);
     }
   }
 }
@@ -405,11 +623,12 @@ __device__ __forceinline__ uint4 pack16(const float* v) {
 template <int DT, int VEC, bool WRITE>
 __device__ __forceinline__ void run_range_vec(const ChainArgs& a, const OpConst* oc, int64_t b,
                                               int64_t c, int64_t s_begin, int64_t s_end,
-                                              bool stats, float& mn, float& mx, bool& nan,
-                                              uint4* ring) {
+                                              bool stats, float& mn, float& mx, uint4* ring) {
   const int tid = threadIdx.x;
   const int64_t n_chunks = (s_end - s_begin) / VEC;
   const int64_t base = (b * a.C + c) * a.HWD + s_begin;
+  __nv_bfloat162 mn2 = __floats2bfloat162_rn(INFINITY, INFINITY);
+  __nv_bfloat162 mx2 = __floats2bfloat162_rn(-INFINITY, -INFINITY);
   const uint4* src = reinterpret_cast<const uint4*>(
       (const char*)a.src + base * (DT == BA_BF16 ? 2 : 4));
   uint4* dst = reinterpret_cast<uint4*>((char*)a.dst + base * (DT == BA_BF16 ? 2 : 4));
@@ -426,14 +645,26 @@ __device__ __forceinline__ void run_range_vec(const ChainArgs& a, const OpConst*
     if (jp < n_chunks) cp_async16(&ring[pslot * CHAIN_THREADS + tid], src + jp);
     cp_async_commit();
     cp_async_wait<CHAIN_PIPE - 1>();
-    float v[VEC];
-    unpack16<DT, VEC>(ring[slot * CHAIN_THREADS + tid], v);
-    apply_ops<DT, VEC>(a, oc, b, c, s_begin + j * VEC, VEC, v);
-    if (WRITE) dst[j] = pack16<DT, VEC>(v);
-    if (stats) fold_minmax<VEC>(v, VEC, mn, mx, nan);
+    if constexpr (DT == BA_BF16) {
+      const uint4 t = ring[slot * CHAIN_THREADS + tid];
+      uint32_t w[4] = {t.x, t.y, t.z, t.w};
+      apply_ops_bf16x8(a, oc, b, c, s_begin + j * VEC, w);
+      if (WRITE) dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
+      if (stats) fold_minmax_bf16x8(w, mn2, mx2);
+    } else {
+      float v[VEC];
+      unpack16<DT, VEC>(ring[slot * CHAIN_THREADS + tid], v);
+      apply_ops<DT, VEC>(a, oc, b, c, s_begin + j * VEC, VEC, v);
+      if (WRITE) dst[j] = pack16<DT, VEC>(v);
+      if (stats) fold_minmax<VEC>(v, VEC, mn, mx);
+    }
     slot = slot + 1 == CHAIN_PIPE ? 0 : slot + 1;
   }
   cp_async_wait<0>();
+  if constexpr (DT == BA_BF16) {
+    mn = min_nan(mn, min_nan(__low2float(mn2), __high2float(mn2)));
+    mx = max_nan(mx, max_nan(__low2float(mx2), __high2float(mx2)));
+  }
 }
 
 // Scalar path (spatial size not a multiple of the vector width, or
@@ -441,15 +672,14 @@ __device__ __forceinline__ void run_range_vec(const ChainArgs& a, const OpConst*
 template <int DT, bool WRITE>
 __device__ __forceinline__ void run_range_scalar(const ChainArgs& a, const OpConst* oc,
                                                  int64_t b, int64_t c, int64_t s_begin,
-                                                 int64_t s_end, bool stats, float& mn, float& mx,
-                                                 bool& nan) {
+                                                 int64_t s_end, bool stats, float& mn, float& mx) {
   const int64_t base = (b * a.C + c) * a.HWD;
   for (int64_t s = s_begin + threadIdx.x; s < s_end; s += CHAIN_THREADS) {
     float v[1];
     v[0] = load_f(a.src, DT, base + s);
     apply_ops<DT, 1>(a, oc, b, c, s, 1, v);
     if (WRITE) store_f(a.dst, DT, base + s, v[0]);
-    if (stats) fold_minmax<1>(v, 1, mn, mx, nan);
+    if (stats) fold_minmax<1>(v, 1, mn, mx);
   }
 }
 
@@ -469,16 +699,14 @@ __global__ void __launch_bounds__(CHAIN_THREADS, CHAIN_MINBLOCKS)
   if (threadIdx.x < a.n_ops) resolve_op<DT>(a, threadIdx.x, b, c, s_oc[threadIdx.x]);
   __syncthreads();
   float mn = INFINITY, mx = -INFINITY;
-  bool nan = false;
   if (VEC > 1)
-    run_range_vec<DT, VEC, WRITE>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx, nan,
-                                  s_ring);
+    run_range_vec<DT, VEC, WRITE>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx, s_ring);
   else
-    run_range_scalar<DT, WRITE>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx, nan);
+    run_range_scalar<DT, WRITE>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx);
   if (a.stats_mode == 2)
-    block_minmax_commit(mn, mx, nan, a.stats_out + 2 * (b * a.C + c));
+    block_minmax_commit(mn, mx, a.stats_out + 2 * (b * a.C + c));
   else if (a.stats_mode == 1)
-    block_minmax_commit(mn, mx, nan, a.stats_out + 2 * b);
+    block_minmax_commit(mn, mx, a.stats_out + 2 * b);
 }
 
 __global__ void init_keys_kernel(int32_t* keys, int64_t n_groups) {
@@ -510,12 +738,13 @@ __global__ void __launch_bounds__(CHAIN_THREADS, CHAIN_MINBLOCKS)
   const int64_t s_begin = (int64_t)blockIdx.x * tile;
   const int64_t s_end = min(s_begin + tile, group_size);
   float mn = INFINITY, mx = -INFINITY;
-  bool nan = false;
   if (VEC > 1) {
     const int tid = threadIdx.x;
     const int64_t n_chunks = (s_end - s_begin) / VEC;
     const uint4* src = reinterpret_cast<const uint4*>(
         (const char*)x + (g * group_size + s_begin) * (DT == BA_BF16 ? 2 : 4));
+    __nv_bfloat162 mn2 = __floats2bfloat162_rn(INFINITY, INFINITY);
+    __nv_bfloat162 mx2 = __floats2bfloat162_rn(-INFINITY, -INFINITY);
 #pragma unroll
     for (int k = 0; k < CHAIN_PIPE - 1; ++k) {
       const int64_t j = tid + (int64_t)k * CHAIN_THREADS;
@@ -529,19 +758,29 @@ __global__ void __launch_bounds__(CHAIN_THREADS, CHAIN_MINBLOCKS)
       if (jp < n_chunks) cp_async16(&s_ring[pslot * CHAIN_THREADS + tid], src + jp);
       cp_async_commit();
       cp_async_wait<CHAIN_PIPE - 1>();
-      float v[VEC];
-      unpack16<DT, VEC>(s_ring[slot * CHAIN_THREADS + tid], v);
-      fold_minmax<VEC>(v, VEC, mn, mx, nan);
+      if constexpr (DT == BA_BF16) {
+        const uint4 t = s_ring[slot * CHAIN_THREADS + tid];
+        const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+        fold_minmax_bf16x8(w, mn2, mx2);
+      } else {
+        float v[VEC];
+        unpack16<DT, VEC>(s_ring[slot * CHAIN_THREADS + tid], v);
+        fold_minmax<VEC>(v, VEC, mn, mx);
+      }
       slot = slot + 1 == CHAIN_PIPE ? 0 : slot + 1;
     }
     cp_async_wait<0>();
+    if constexpr (DT == BA_BF16) {
+      mn = min_nan(mn, min_nan(__low2float(mn2), __high2float(mn2)));
+      mx = max_nan(mx, max_nan(__low2float(mx2), __high2float(mx2)));
+    }
   } else {
     for (int64_t s = s_begin + threadIdx.x; s < s_end; s += CHAIN_THREADS) {
       float v[1] = {load_f(x, DT, g * group_size + s)};
-      fold_minmax<1>(v, 1, mn, mx, nan);
+      fold_minmax<1>(v, 1, mn, mx);
     }
   }
-  block_minmax_commit(mn, mx, nan, keys + 2 * g);
+  block_minmax_commit(mn, mx, keys + 2 * g);
 }
 
 int sm_count() {

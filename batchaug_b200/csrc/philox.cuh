@@ -61,16 +61,31 @@ __host__ __device__ __forceinline__ float u01(uint32_t r) {
 }
 
 #ifdef __CUDACC__
+// Uniform in (0, 1] from the top 23 bits, built in the float's bit pattern
+// (2 - [1, 2)), so the integer-to-float conversion unit is not needed.
+__device__ __forceinline__ float u01_open0_bits(uint32_t r) {
+  return 2.0f - __uint_as_float(0x3F800000u | (r >> 9));
+}
+// Uniform in [-pi, pi) from the top 23 bits: pi * ([1, 2) * 2 - 3).
+__device__ __forceinline__ float angle_bits(uint32_t r) {
+  constexpr float PI = 3.141592653589793f;
+  return (__uint_as_float(0x3F800000u | (r >> 9)) * 2.0f - 3.0f) * PI;
+}
+__device__ __forceinline__ float sqrt_approx(float x) {
+  float r;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // Four standard normals from one Philox block (two Box-Muller pairs).  The
 // angle is drawn in [-pi, pi), where the hardware sine/cosine are accurate to
 // about 2^-21; only the distribution matters for augmentation noise.
 __device__ __forceinline__ void normal4(U4 r, float* z) {
-  const float r0 = sqrtf(-2.0f * __logf(u01_open0(r.x)));
-  const float r1 = sqrtf(-2.0f * __logf(u01_open0(r.z)));
-  constexpr float TWO_PI = 6.283185307179586f, PI = 3.141592653589793f;
+  const float r0 = sqrt_approx(-2.0f * __logf(u01_open0_bits(r.x)));
+  const float r1 = sqrt_approx(-2.0f * __logf(u01_open0_bits(r.z)));
   float s0, c0, s1, c1;
-  __sincosf(u01(r.y) * TWO_PI - PI, &s0, &c0);
-  __sincosf(u01(r.w) * TWO_PI - PI, &s1, &c1);
+  __sincosf(angle_bits(r.y), &s0, &c0);
+  __sincosf(angle_bits(r.w), &s1, &c1);
   z[0] = r0 * c0;
   z[1] = r0 * s0;
   z[2] = r1 * c1;

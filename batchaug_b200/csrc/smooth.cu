@@ -192,14 +192,22 @@ __global__ void __launch_bounds__(SM_THREADS)
 // running D, W, H instead of the reference's H, W, D changes only rounding.
 // ===========================================================================
 constexpr int TS_THREADS = 256;
-constexpr int TS_TD = 64;   // tile extent along D (pass A and B)
-constexpr int TS_TW = 32;   // tile extent along W (pass A)
-constexpr int TS_TH = 64;   // tile extent along H (pass B)
+constexpr int TS_TD = 64;   // pass A tile extent along D
 constexpr int TS_RD = 8;    // pass A D-outputs per thread unit
-constexpr int TS_RW = 8;    // pass A W-outputs per thread (TS_TW / TS_RW = 4 groups)
-constexpr int TS_RH = 16;   // pass B H-outputs per thread (TS_TH / TS_RH = 4 groups)
+constexpr int TS_RW = 8;    // pass A W-outputs per thread unit
+constexpr int TB_TD = 32;   // pass B tile extent along D
+constexpr int TS_TH = 64;   // pass B tile extent along H
+constexpr int TS_RH = 8;    // pass B H-outputs per thread (TS_TH / TS_RH = 8 groups)
 constexpr int TILE_KMAX = 63;
+constexpr int MAX_COLS = TS_TD + TILE_KMAX - 1;
+constexpr int MAX_ROWS = 64 + TILE_KMAX - 1;
 
+// Tile extent along W of pass A: wider tiles for wide kernels keep the
+// D-pass halo rows (KMAX-1 of them) a small fraction of the work.
+__host__ __device__ constexpr int plane_tw(int kmax) { return kmax > 23 ? 64 : 32; }
+
+// Shared-memory row index with one pad word every 8: a thread reading R=8
+// consecutive entries starting at 8*t hits distinct banks across a warp.
 __host__ __device__ __forceinline__ int pidx(int q) { return q + (q >> 3); }
 
 struct TiledArgs {
@@ -221,107 +229,113 @@ struct TiledArgs {
   const float* magnitude;
 };
 
-template <int KMAX>
-__device__ __forceinline__ void load_taps(const float* taps, int64_t b, int K, float* w) {
+// R outputs out[i] = sum_k w[k] * x[i + k] for k < KMAX from a register
+// window x of R + KMAX - 1 values; taps come from shared memory (one
+// broadcast read per tap, reused by all R outputs).
+template <int R, int KMAX>
+__device__ __forceinline__ void conv_window(const float* xw, const float* s_w, float* acc) {
 #pragma unroll
-  for (int k = 0; k < KMAX; ++k) w[k] = k < K ? __ldg(taps + b * K + k) : 0.0f;
+  for (int i = 0; i < R; ++i) acc[i] = 0.0f;
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) {
+    const float w = s_w[k];
+#pragma unroll
+    for (int i = 0; i < R; ++i) acc[i] = __fmaf_rn(w, xw[i + k], acc[i]);
+  }
+}
+
+template <int KMAX>
+__device__ __forceinline__ void load_taps_smem(const float* taps, int64_t b, int K, float* s_w) {
+  for (int k = threadIdx.x; k < KMAX; k += blockDim.x) s_w[k] = k < K ? taps[b * K + k] : 0.0f;
 }
 
 // Pass A: grid (tiles_w * tiles_d, H, B*P).
 template <int KMAX>
 __global__ void __launch_bounds__(TS_THREADS) smooth_plane_kernel(const __grid_constant__ TiledArgs a) {
+  constexpr int TW = plane_tw(KMAX);
   extern __shared__ float sm[];
+  __shared__ float s_wd[KMAX], s_ww[KMAX];
+  __shared__ int s_di[MAX_COLS];
   const int64_t bp = blockIdx.z;
   const int64_t b = bp / a.P;
   if (a.mask != nullptr && a.mask[b] == 0) return;  // pass B copies the input
-  const int H = (int)a.H, W = (int)a.W, D = (int)a.D;
+  const int W = (int)a.W, D = (int)a.D;
   const int h = blockIdx.y;
   const int tiles_d = (D + TS_TD - 1) / TS_TD;
   const int td0 = (blockIdx.x % tiles_d) * TS_TD;
-  const int tw0 = (blockIdx.x / tiles_d) * TS_TW;
+  const int tw0 = (blockIdx.x / tiles_d) * TW;
   const int pd = a.Kd / 2, pw = a.Kw / 2;
   // tile with halo: KMAX-wide windows read up to KMAX-1 past each output
-  const int rowsA = TS_TW + KMAX - 1, colsA = TS_TD + KMAX - 1;
-  const int PA = pidx(colsA - 1) + 1;
-  float* A = sm;                      // rowsA x PA (padded index)
-  float* Bm = sm + rowsA * PA;        // rowsA x TS_TD
-  const int64_t plane = (bp * a.H + h) * a.HWD / a.H;  // start of plane h of bp
-  for (int idx = threadIdx.x; idx < rowsA * colsA; idx += TS_THREADS) {
-    const int r = idx / colsA, q = idx % colsA;
-    // rows/cols beyond the real halo meet zero taps; keep them finite
-    float v = 0.0f;
-    if (r < TS_TW + 2 * pw && q < TS_TD + 2 * pd) {
-      const int64_t wi = pad_index(tw0 - pw + r, W, a.padding);
-      const int64_t di = pad_index(td0 - pd + q, D, a.padding);
-      if (wi >= 0 && di >= 0) v = load_in(a.in, a.in_dtype, plane + wi * D + di);
+  constexpr int rowsA = TW + KMAX - 1, colsA = TS_TD + KMAX - 1;
+  constexpr int PA = (colsA - 1) + ((colsA - 1) >> 3) + 1;
+  float* A = sm;                   // rowsA x PA (padded index)
+  float* Bm = sm + rowsA * PA;     // rowsA x TS_TD
+  const int64_t plane = (bp * a.H + h) * (int64_t)W * D;
+  for (int q = threadIdx.x; q < colsA; q += TS_THREADS)
+    s_di[q] = q < TS_TD + 2 * pd ? (int)pad_index(td0 - pd + q, D, a.padding) : -1;
+  load_taps_smem<KMAX>(a.taps_d, b, a.Kd, s_wd);
+  load_taps_smem<KMAX>(a.taps_w, b, a.Kw, s_ww);
+  __syncthreads();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  for (int r = warp; r < rowsA; r += TS_THREADS / 32) {
+    // rows and columns beyond the real halo meet zero taps; keep them finite
+    const int64_t wi = r < TW + 2 * pw ? pad_index(tw0 - pw + r, W, a.padding) : -1;
+    const int64_t row = plane + wi * D;
+    for (int q = lane; q < colsA; q += 32) {
+      const int di = s_di[q];
+      A[r * PA + pidx(q)] = (wi >= 0 && di >= 0) ? load_in(a.in, a.in_dtype, row + di) : 0.0f;
     }
-    A[r * PA + pidx(q)] = v;
   }
-  float wd[KMAX];
-  load_taps<KMAX>(a.taps_d, b, a.Kd, wd);
   __syncthreads();
   // D pass: units of TS_RD consecutive outputs of one row
   constexpr int GROUPS_D = TS_TD / TS_RD;
   for (int u = threadIdx.x; u < rowsA * GROUPS_D; u += TS_THREADS) {
     const int r = u / GROUPS_D, q0 = (u % GROUPS_D) * TS_RD;
-    float acc[TS_RD];
+    float xw[TS_RD + KMAX - 1], acc[TS_RD];
+    const float* rowp = A + r * PA;
 #pragma unroll
-    for (int i = 0; i < TS_RD; ++i) acc[i] = 0.0f;
-    const float* row = A + r * PA;
-#pragma unroll
-    for (int j = 0; j < TS_RD + KMAX - 1; ++j) {
-      const float x = row[pidx(q0 + j)];
-#pragma unroll
-      for (int i = 0; i < TS_RD; ++i) {
-        const int k = j - i;
-        if (k >= 0 && k < KMAX) acc[i] = acc[i] + wd[k] * x;
-      }
-    }
+    for (int j = 0; j < TS_RD + KMAX - 1; ++j) xw[j] = rowp[pidx(q0 + j)];
+    conv_window<TS_RD, KMAX>(xw, s_wd, acc);
 #pragma unroll
     for (int i = 0; i < TS_RD; ++i) Bm[r * TS_TD + q0 + i] = acc[i];
   }
-  float ww[KMAX];
-  load_taps<KMAX>(a.taps_w, b, a.Kw, ww);
   __syncthreads();
-  // W pass: thread (q, wg) produces rows wg*TS_RW .. +TS_RW-1 of column q
-  const int q = threadIdx.x % TS_TD, wg = threadIdx.x / TS_TD;
-  float acc[TS_RW];
-#pragma unroll
-  for (int i = 0; i < TS_RW; ++i) acc[i] = 0.0f;
-#pragma unroll
-  for (int j = 0; j < TS_RW + KMAX - 1; ++j) {
-    const float x = Bm[(wg * TS_RW + j) * TS_TD + q];
-#pragma unroll
-    for (int i = 0; i < TS_RW; ++i) {
-      const int k = j - i;
-      if (k >= 0 && k < KMAX) acc[i] = acc[i] + ww[k] * x;
-    }
-  }
+  // W pass: thread (q, group) produces rows group*TS_RW .. +TS_RW-1 of column q
+  const int q = threadIdx.x % TS_TD;
   const int d = td0 + q;
-  if (d < D) {
+  for (int wg = threadIdx.x / TS_TD; wg < TW / TS_RW; wg += TS_THREADS / TS_TD) {
+    float xw[TS_RW + KMAX - 1], acc[TS_RW];
 #pragma unroll
-    for (int i = 0; i < TS_RW; ++i) {
-      const int w = tw0 + wg * TS_RW + i;
-      if (w < W) a.mid[plane + (int64_t)w * D + d] = acc[i];
+    for (int j = 0; j < TS_RW + KMAX - 1; ++j) xw[j] = Bm[(wg * TS_RW + j) * TS_TD + q];
+    conv_window<TS_RW, KMAX>(xw, s_ww, acc);
+    if (d < D) {
+#pragma unroll
+      for (int i = 0; i < TS_RW; ++i) {
+        const int w = tw0 + wg * TS_RW + i;
+        if (w < W) a.mid[plane + (int64_t)w * D + d] = acc[i];
+      }
     }
   }
 }
 
-// Pass B: grid (tiles_h * tiles_d, W, B*P).
+// Pass B: grid (tiles_h * tiles_d, W, B*P); thread (q, group) of a
+// TS_TH x TB_TD strip produces TS_RH consecutive h of column q.
 template <int KMAX>
 __global__ void __launch_bounds__(TS_THREADS) smooth_column_kernel(const __grid_constant__ TiledArgs a) {
   extern __shared__ float sm[];
+  __shared__ float s_wh[KMAX];
+  __shared__ int s_hi[MAX_ROWS];
   const int64_t bp = blockIdx.z;
   const int64_t b = bp / a.P;
   const int H = (int)a.H, W = (int)a.W, D = (int)a.D;
   const int w = blockIdx.y;
-  const int tiles_d = (D + TS_TD - 1) / TS_TD;
-  const int td0 = (blockIdx.x % tiles_d) * TS_TD;
+  const int tiles_d = (D + TB_TD - 1) / TB_TD;
+  const int td0 = (blockIdx.x % tiles_d) * TB_TD;
   const int th0 = (blockIdx.x / tiles_d) * TS_TH;
-  const int q = threadIdx.x % TS_TD, hg = threadIdx.x / TS_TD;
+  const int q = threadIdx.x % TB_TD, hg = threadIdx.x / TB_TD;
   const int d = td0 + q;
-  const int64_t col = bp * a.HWD + (int64_t)w * D + d;  // + h * W * D
   const int64_t plane_stride = (int64_t)W * D;
+  const int64_t col = bp * a.HWD + (int64_t)w * D + d;  // + h * plane_stride
   if (a.mask != nullptr && a.mask[b] == 0) {
     if (a.copy_src != nullptr && d < D) {
       for (int i = 0; i < TS_RH; ++i) {
@@ -337,35 +351,25 @@ __global__ void __launch_bounds__(TS_THREADS) smooth_column_kernel(const __grid_
     return;
   }
   const int ph = a.Kh / 2;
-  const int rowsS = TS_TH + KMAX - 1;
-  float* S = sm;  // rowsS x TS_TD
-  for (int idx = threadIdx.x; idx < rowsS * TS_TD; idx += TS_THREADS) {
-    const int r = idx / TS_TD, qq = idx % TS_TD;
-    float v = 0.0f;
-    if (r < TS_TH + 2 * ph && td0 + qq < D) {
-      const int64_t hi = pad_index(th0 - ph + r, H, a.padding);
-      if (hi >= 0) v = a.mid[bp * a.HWD + hi * plane_stride + (int64_t)w * D + td0 + qq];
-    }
-    S[r * TS_TD + qq] = v;
-  }
-  float wh[KMAX];
-  load_taps<KMAX>(a.taps_h, b, a.Kh, wh);
+  constexpr int rowsS = TS_TH + KMAX - 1;
+  float* S = sm;  // rowsS x TB_TD
+  for (int r = threadIdx.x; r < rowsS; r += TS_THREADS)
+    s_hi[r] = r < TS_TH + 2 * ph ? (int)pad_index(th0 - ph + r, H, a.padding) : -1;
+  load_taps_smem<KMAX>(a.taps_h, b, a.Kh, s_wh);
   __syncthreads();
-  float acc[TS_RH];
-#pragma unroll
-  for (int i = 0; i < TS_RH; ++i) acc[i] = 0.0f;
-#pragma unroll
-  for (int j = 0; j < TS_RH + KMAX - 1; ++j) {
-    const float x = S[(hg * TS_RH + j) * TS_TD + q];
-#pragma unroll
-    for (int i = 0; i < TS_RH; ++i) {
-      const int k = j - i;
-      if (k >= 0 && k < KMAX) acc[i] = acc[i] + wh[k] * x;
-    }
+  for (int r = hg; r < rowsS; r += TS_THREADS / TB_TD) {
+    const int hi = s_hi[r];
+    S[r * TB_TD + q] = (hi >= 0 && d < D) ? a.mid[bp * a.HWD + hi * plane_stride + (int64_t)w * D + d]
+                                          : 0.0f;
   }
+  __syncthreads();
+  float xw[TS_RH + KMAX - 1], acc[TS_RH];
+#pragma unroll
+  for (int j = 0; j < TS_RH + KMAX - 1; ++j) xw[j] = S[(hg * TS_RH + j) * TB_TD + q];
+  conv_window<TS_RH, KMAX>(xw, s_wh, acc);
   if (d >= D) return;
   if (a.grid != nullptr) {
-    // elastic: component P-index of bp is the displacement axis
+    // elastic: the component (P index of bp) is the displacement axis
     const int comp = (int)(bp % a.P);
     const float mag = a.magnitude[b];
     const int64_t sz = comp == 0 ? a.H : (comp == 1 ? a.W : a.D);
@@ -405,12 +409,12 @@ int tiled_kmax(int K) {
 }
 
 size_t plane_smem(int kmax) {
-  const int rowsA = TS_TW + kmax - 1, colsA = TS_TD + kmax - 1;
+  const int rowsA = plane_tw(kmax) + kmax - 1, colsA = TS_TD + kmax - 1;
   const int PA = pidx(colsA - 1) + 1;
   return (size_t)(rowsA * PA + rowsA * TS_TD) * sizeof(float);
 }
 
-size_t column_smem(int kmax) { return (size_t)((TS_TH + kmax - 1) * TS_TD) * sizeof(float); }
+size_t column_smem(int kmax) { return (size_t)((TS_TH + kmax - 1) * TB_TD) * sizeof(float); }
 
 template <int KMAX>
 ba_status launch_tiled_kmax(const TiledArgs& a, int64_t planes, cudaStream_t st) {
@@ -420,12 +424,14 @@ ba_status launch_tiled_kmax(const TiledArgs& a, int64_t planes, cudaStream_t st)
                        (int)sa);
   cudaFuncSetAttribute(smooth_column_kernel<KMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)sb);
+  constexpr int TW = plane_tw(KMAX);
   const int tiles_d = (int)((a.D + TS_TD - 1) / TS_TD);
-  dim3 ga((unsigned)(tiles_d * ((a.W + TS_TW - 1) / TS_TW)), (unsigned)a.H, (unsigned)planes);
+  dim3 ga((unsigned)(tiles_d * ((a.W + TW - 1) / TW)), (unsigned)a.H, (unsigned)planes);
   smooth_plane_kernel<KMAX><<<ga, TS_THREADS, sa, st>>>(a);
   ba_status s = check_launch("smooth pass A");
   if (s != BA_OK) return s;
-  dim3 gb((unsigned)(tiles_d * ((a.H + TS_TH - 1) / TS_TH)), (unsigned)a.W, (unsigned)planes);
+  const int tiles_db = (int)((a.D + TB_TD - 1) / TB_TD);
+  dim3 gb((unsigned)(tiles_db * ((a.H + TS_TH - 1) / TS_TH)), (unsigned)a.W, (unsigned)planes);
   smooth_column_kernel<KMAX><<<gb, TS_THREADS, sb, st>>>(a);
   return check_launch("smooth pass B");
 }
