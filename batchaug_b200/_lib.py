@@ -83,6 +83,8 @@ SIGNATURES = {
     "ba_elastic_grid": (_I32, [_P, _U64, _U64, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P,
                                ctypes.c_size_t, _P]),
     "ba_host_uniform": (None, [_U64, ctypes.c_uint32, _U64, _I64, _I64, _P]),
+    "ba_host_rand_affine": (None, [_P, _I64, _I64, ctypes.c_float, _P, _P, _P, ctypes.c_uint32,
+                                   ctypes.c_uint32, _I64, _I64, _I64, _P, _P, _P]),
     "ba_last_error": (ctypes.c_char_p, []),
     "ba_version": (_I32, []),
     "ba_kernel_launches": (ctypes.c_uint64, []),

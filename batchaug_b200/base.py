@@ -26,24 +26,32 @@ def to_device(arr: np.ndarray, device) -> torch.Tensor:
     return t.pin_memory().to(device, non_blocking=True)
 
 
+_TORCH_DTYPES = {np.dtype(np.bool_): torch.bool, np.dtype(np.uint8): torch.uint8,
+                 np.dtype(np.float32): torch.float32, np.dtype(np.int64): torch.int64,
+                 np.dtype(np.int32): torch.int32}
+
+
 def upload(arrays: dict, device) -> dict:
-    """Copy a dict of small numpy arrays to ``device``: float32 arrays packed
-    into one transfer, every other array (bool masks, int64 indices) in one
-    transfer of its own."""
+    """Copy a dict of small numpy arrays to ``device`` in one transfer: the
+    arrays are packed into one byte buffer (floats as float32, each piece
+    8-byte aligned) and the returned tensors are typed views of its copy."""
+    pieces, off = [], 0
+    for k, v in arrays.items():
+        v = np.ascontiguousarray(v)
+        if v.dtype.kind == "f":
+            v = v.astype(np.float32, copy=False)
+        if v.dtype not in _TORCH_DTYPES:
+            raise ValueError(f"upload: unsupported dtype {v.dtype} for {k!r}")
+        off = (off + 7) & ~7
+        pieces.append((k, v, off))
+        off += v.nbytes
+    buf = np.zeros(max(off, 1), np.uint8)
+    for _, v, o in pieces:
+        buf[o:o + v.nbytes] = v.reshape(-1).view(np.uint8)
+    dev = to_device(buf, device)
     out = {}
-    floats = {k: np.ascontiguousarray(v, dtype=np.float32) for k, v in arrays.items()
-              if v.dtype != np.bool_ and v.dtype.kind == "f"}
-    others = {k: v for k, v in arrays.items() if k not in floats}
-    if floats:
-        flat = np.concatenate([v.ravel() for v in floats.values()])
-        dev = to_device(flat, device)
-        pos = 0
-        for k, v in floats.items():
-            n = v.size
-            out[k] = dev[pos:pos + n].view(v.shape)
-            pos += n
-    for k, v in others.items():
-        out[k] = to_device(v, device)
+    for k, v, o in pieces:
+        out[k] = dev[o:o + v.nbytes].view(_TORCH_DTYPES[v.dtype]).view(v.shape)
     return out
 
 

@@ -38,6 +38,10 @@ constexpr int CHAIN_THREADS = 256;
 // for: ~128 KB in flight per SM, enough to stream HBM at full rate.
 constexpr int CHAIN_PIPE = 8;
 constexpr int CHAIN_MINBLOCKS = 4;
+// bf16 segments hold more live values per thread (packed words plus the
+// unpacked fallback): one CTA fewer per SM keeps them out of local memory.
+template <int DT>
+constexpr int chain_minblocks() { return DT == BA_BF16 ? 3 : CHAIN_MINBLOCKS; }
 constexpr int CHAIN_MIN_CHUNKS = 16;
 
 struct OpArgs {
@@ -147,7 +151,7 @@ __device__ __forceinline__ void bias_run(const OpArgs& op, int64_t b, int64_t s0
 // shared memory so the per-vector loop reads no parameters from global memory.
 // ---------------------------------------------------------------------------
 struct OpConst {
-  float k0, k1, k2, k3, k4;
+  float k0, k1, k2, k3, k4, k5;
   int on;
   // bf16 kernels: operands as bf16x2 splats, and whether the op can run on
   // packed bf16 arithmetic (every scalar it uses is a bf16 value)
@@ -201,7 +205,7 @@ __device__ __forceinline__ void resolve_op(const ChainArgs& a, int oi, int64_t b
                                            OpConst& o) {
   const OpArgs& op = a.ops[oi];
   o.on = (op.mask == nullptr || op.mask[b] != 0) ? 1 : 0;
-  o.k0 = o.k1 = o.k2 = o.k3 = o.k4 = 0.0f;
+  o.k0 = o.k1 = o.k2 = o.k3 = o.k4 = o.k5 = 0.0f;
   o.h0 = o.h1 = o.h2 = 0u;
   o.packed = 0;
   switch (op.kind) {
@@ -221,6 +225,7 @@ __device__ __forceinline__ void resolve_op(const ChainArgs& a, int oi, int64_t b
       o.k2 = rng + 1e-7f;
       o.k3 = op.param[b];  // gamma
       o.k4 = recip_for_div(o.k2);
+      o.k5 = powf(0.0f, o.k3);  // 0^gamma, taken apart from the fast power below
       break;
     }
     case BA_OP_SCALE:
@@ -326,7 +331,10 @@ __device__ __forceinline__ void apply_one(const ChainArgs& a, int oi, const OpCo
         for (int i = 0; i < VEC; ++i) {
           float nrm = div_rn(v[i] - k.k0, k.k2, k.k4);
           nrm = (nrm < 0.0f) ? 0.0f : nrm;
-          v[i] = round_dt<DT>(powf(nrm, k.k3) * k.k1 + k.k0);
+          // nrm in [0, 1]: the hardware exp2(gamma * log2(nrm)) power is
+          // within a few fp32 ulp there (far inside the op's tolerance)
+          const float pw = nrm == 0.0f ? k.k5 : __powf(nrm, k.k3);
+          v[i] = round_dt<DT>(pw * k.k1 + k.k0);
         }
         break;
       }
@@ -688,7 +696,7 @@ __device__ __forceinline__ void run_range_scalar(const ChainArgs& a, const OpCon
 // ring runs uninterrupted over the whole range and the op constants are
 // resolved once per CTA.
 template <int DT, int VEC, bool WRITE>
-__global__ void __launch_bounds__(CHAIN_THREADS, CHAIN_MINBLOCKS)
+__global__ void __launch_bounds__(CHAIN_THREADS, chain_minblocks<DT>())
     chain_kernel(const __grid_constant__ ChainArgs a) {
   __shared__ OpConst s_oc[BA_MAX_OPS];
   __shared__ uint4 s_ring[VEC > 1 ? CHAIN_PIPE * CHAIN_THREADS : 1];

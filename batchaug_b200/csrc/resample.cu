@@ -39,24 +39,29 @@ namespace {
 #define BA_RS_TX 8
 #endif
 #ifndef BA_RS_TY
-#define BA_RS_TY 4
+#define BA_RS_TY 2
 #endif
 #ifndef BA_RS_TZ
-#define BA_RS_TZ 4
+#define BA_RS_TZ 8
 #endif
 #ifndef BA_RS_PAIRS
 #define BA_RS_PAIRS 2
 #endif
+#ifndef BA_RS_NB
+#define BA_RS_NB 4
+#endif
 #ifndef BA_RS_MINBLOCKS
-#define BA_RS_MINBLOCKS 6
+#define BA_RS_MINBLOCKS 5
 #endif
 
 constexpr int TX = BA_RS_TX;         // threads along D
 constexpr int TY = BA_RS_TY;         // threads along W
 constexpr int TZ = BA_RS_TZ;         // threads along H
-constexpr int PAIRS = BA_RS_PAIRS;   // voxel pairs per thread, along D
+constexpr int PAIRS = BA_RS_PAIRS;   // voxel pairs per thread and brick, along D
+constexpr int NB = BA_RS_NB;         // bricks per CTA, stacked along H
 constexpr int BD = TX * 2 * PAIRS;   // brick extent along D
 constexpr int NTHREADS = TX * TY * TZ;
+static_assert(NTHREADS % 32 == 0, "whole warps");
 
 struct KeyArgs {
   const void* src;
@@ -81,9 +86,19 @@ struct ResampleArgs {
   KeyArgs keys[BA_MAX_KEYS];
 };
 
+// ---------------------------------------------------------------------------
+// Packed fp32x2 arithmetic (sm_100), two voxels per instruction.  A packed
+// multiply whose result feeds a packed add can come out fused into one fma
+// even under -fmad=false, so packed multiplies are used only where no add
+// follows (the weight products); multiply-then-add steps (unnormalise, the
+// tap accumulation) are scalar __fmul_rn / __fadd_rn, which are never fused.
+// ---------------------------------------------------------------------------
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
-__device__ __forceinline__ float2 neg2(float2 a) { return make_float2(-a.x, -a.y); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) { return __fadd2_rn(a, f2(-b.x, -b.y)); }
+__device__ __forceinline__ float2 add2_down(float2 a, float2 b) { return __fadd2_rd(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 
 // affine_grid's linspace_from_neg_one.
 __device__ __forceinline__ float base_coord(int i, int n, int align_corners) {
@@ -94,26 +109,21 @@ __device__ __forceinline__ float base_coord(int i, int n, int align_corners) {
   return r;
 }
 
-// grid_sampler_unnormalize: align_corners ? ((c+1)/2)*(size-1)
-// : ((c+1)*size-1)/2, where /2 is the exact *0.5.  Scalar operations: the
-// compiler contracts a packed multiply followed by a packed add into one
-// fused op even under -fmad=false, which would change the rounding.
-template <bool ALIGN>
-__device__ __forceinline__ float unnormalize1(float c, float size) {
-  if (ALIGN) return ((c + 1.0f) * 0.5f) * (size - 1.0f);
-  return ((c + 1.0f) * size - 1.0f) * 0.5f;
-}
-
+// grid_sampler_unnormalize for two voxels: align_corners ? ((c+1)/2)*(size-1)
+// : ((c+1)*size-1)/2, where /2 is the exact *0.5.
 template <bool ALIGN>
 __device__ __forceinline__ float2 unnormalize2(float2 c, float size) {
-  return f2(unnormalize1<ALIGN>(c.x, size), unnormalize1<ALIGN>(c.y, size));
+  if (ALIGN) return mul2(mul2(add2(c, f2(1.0f)), f2(0.5f)), f2(size - 1.0f));
+  return f2(__fmul_rn(__fsub_rn(__fmul_rn(__fadd_rn(c.x, 1.0f), size), 1.0f), 0.5f),
+            __fmul_rn(__fsub_rn(__fmul_rn(__fadd_rn(c.y, 1.0f), size), 1.0f), 0.5f));
 }
 
-// std::min(size-1, std::max(in, 0)) with std's argument order: a NaN
-// coordinate clips to size-1 exactly as torch's sampler does.
+// std::min(size-1, std::max(in, 0)) with std's argument order: max keeps a
+// NaN (max.NaN), then min turns it into size-1, as torch's clip does.
 __device__ __forceinline__ float clip_coord(float in, float hi) {
-  const float lo = (in < 0.0f) ? 0.0f : in;
-  return (lo < hi) ? lo : hi;
+  float lo;
+  asm("max.NaN.f32 %0, %1, 0f00000000;" : "=f"(lo) : "f"(in));
+  return fminf(lo, hi);
 }
 
 __device__ __forceinline__ float reflect_coord(float in, int twice_low, int twice_high) {
@@ -127,9 +137,12 @@ __device__ __forceinline__ float reflect_coord(float in, int twice_low, int twic
   return span - extra + mn;
 }
 
-// Padding transform of one unnormalised coordinate, then the guard torch's
-// CUDA sampler applies before the integer conversion (non-finite or huge
-// coordinates become -100, i.e. out of bounds).
+// Magnitude below which floor() is taken by rounding-mode addition: any
+// coordinate at or beyond it is outside every supported volume, so the zeros
+// padding maps it to -100 (out of bounds) like torch's sampler maps
+// non-finite coordinates.
+constexpr float COORD_LIMIT = 4194304.0f;  // 2^22
+
 template <int PAD, bool ALIGN>
 __device__ __forceinline__ float pad_coord(float c, int size) {
   if (PAD == BA_PAD_BORDER) {
@@ -138,7 +151,28 @@ __device__ __forceinline__ float pad_coord(float c, int size) {
     c = ALIGN ? reflect_coord(c, 0, 2 * (size - 1)) : reflect_coord(c, -1, 2 * size - 1);
     return clip_coord(c, (float)(size - 1));
   }
-  return (fabsf(c) < 1.0e9f) ? c : -100.0f;
+  return (fabsf(c) < COORD_LIMIT) ? c : -100.0f;
+}
+
+template <int PAD, bool ALIGN>
+__device__ __forceinline__ float2 pad2(float2 c, int size) {
+  return f2(pad_coord<PAD, ALIGN>(c.x, size), pad_coord<PAD, ALIGN>(c.y, size));
+}
+
+// floor of two coordinates with |c| < 2^22: c + 1.5*2^23 rounded toward -inf
+// is floor(c) + 1.5*2^23, an integer whose float bits hold floor(c).
+struct Floor2 {
+  float2 f;   // floor as floats
+  int lo, hi; // floor as ints
+};
+__device__ __forceinline__ Floor2 floor2(float2 c) {
+  constexpr float M = 12582912.0f;  // 1.5 * 2^23
+  const float2 t = add2_down(c, f2(M));
+  Floor2 r;
+  r.f = sub2(t, f2(M));
+  r.lo = __float_as_int(t.x) - 0x4B400000;
+  r.hi = __float_as_int(t.y) - 0x4B400000;
+  return r;
 }
 
 template <int DT>
@@ -155,39 +189,14 @@ __device__ __forceinline__ void st(void* base, int64_t i, float v) {
     ((float*)base)[i] = v;
 }
 
-// Integer footprint of one voxel: corner (x0,y0,z0), whether all 8 taps are
-// inside, and the per-tap validity bits (torch's corner order).
-struct Corner {
-  int32_t off;     // (z0*W + y0)*D + x0, meaningful when some tap is valid
-  uint32_t valid;  // bit k: tap k in bounds
-  bool interior;
-};
-
-__device__ __forceinline__ Corner corner_of(float x0f, float y0f, float z0f, int H, int W, int D) {
-  const int x0 = (int)x0f, y0 = (int)y0f, z0 = (int)z0f;
-  Corner c;
-  c.interior = (unsigned)x0 < (unsigned)(D - 1) && (unsigned)y0 < (unsigned)(W - 1) &&
-               (unsigned)z0 < (unsigned)(H - 1);
-  const bool vx0 = (unsigned)x0 < (unsigned)D, vx1 = (unsigned)(x0 + 1) < (unsigned)D;
-  const bool vy0 = (unsigned)y0 < (unsigned)W, vy1 = (unsigned)(y0 + 1) < (unsigned)W;
-  const bool vz0 = (unsigned)z0 < (unsigned)H, vz1 = (unsigned)(z0 + 1) < (unsigned)H;
-  const uint32_t mx = (uint32_t)vx0 | ((uint32_t)vx1 << 1);
-  const uint32_t r0 = (vz0 && vy0) ? mx : 0u, r1 = (vz0 && vy1) ? mx : 0u;
-  const uint32_t r2 = (vz1 && vy0) ? mx : 0u, r3 = (vz1 && vy1) ? mx : 0u;
-  c.valid = r0 | (r1 << 2) | (r2 << 4) | (r3 << 6);
-  // unsigned arithmetic: offsets of out-of-bounds corners are never used
-  c.off = (int32_t)(((uint32_t)z0 * (uint32_t)W + (uint32_t)y0) * (uint32_t)D + (uint32_t)x0);
-  return c;
-}
-
-// The 8 tap values of one voxel (0 for out-of-bounds taps), torch's order
-// tnw, tne, tsw, tse, bnw, bne, bsw, bse.
+// The 8 tap values of one voxel with corner (x0, y0, z0), 0 for taps outside
+// the volume, in torch's order tnw, tne, tsw, tse, bnw, bne, bsw, bse.
 template <int DT>
-__device__ __forceinline__ void taps8(const void* cbase, const Corner& c, int W, int D,
-                                      float* v) {
-  const int64_t dy = D, dz = (int64_t)W * D;
-  if (c.interior) {
-    const int64_t o = c.off;
+__device__ __forceinline__ void taps8(const void* cbase, int x0, int y0, int z0, int H, int W,
+                                      int D, bool interior, float* v) {
+  const int dy = D, dz = W * D;
+  if (interior) {
+    const int o = (z0 * W + y0) * D + x0;
     v[0] = ld<DT>(cbase, o);
     v[1] = ld<DT>(cbase, o + 1);
     v[2] = ld<DT>(cbase, o + dy);
@@ -196,12 +205,21 @@ __device__ __forceinline__ void taps8(const void* cbase, const Corner& c, int W,
     v[5] = ld<DT>(cbase, o + dz + 1);
     v[6] = ld<DT>(cbase, o + dz + dy);
     v[7] = ld<DT>(cbase, o + dz + dy + 1);
-  } else {
-    const int64_t o = c.off;
-    const int64_t delta[8] = {0, 1, dy, dy + 1, dz, dz + 1, dz + dy, dz + dy + 1};
-#pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = ((c.valid >> k) & 1u) ? ld<DT>(cbase, o + delta[k]) : 0.0f;
+    return;
   }
+  const bool vx0 = (unsigned)x0 < (unsigned)D, vx1 = (unsigned)(x0 + 1) < (unsigned)D;
+  const bool vy0 = (unsigned)y0 < (unsigned)W, vy1 = (unsigned)(y0 + 1) < (unsigned)W;
+  const bool vz0 = (unsigned)z0 < (unsigned)H, vz1 = (unsigned)(z0 + 1) < (unsigned)H;
+  // unsigned arithmetic: offsets of out-of-bounds taps are never used
+  const uint32_t o = ((uint32_t)z0 * (uint32_t)W + (uint32_t)y0) * (uint32_t)D + (uint32_t)x0;
+  v[0] = (vz0 && vy0 && vx0) ? ld<DT>(cbase, o) : 0.0f;
+  v[1] = (vz0 && vy0 && vx1) ? ld<DT>(cbase, o + 1u) : 0.0f;
+  v[2] = (vz0 && vy1 && vx0) ? ld<DT>(cbase, o + dy) : 0.0f;
+  v[3] = (vz0 && vy1 && vx1) ? ld<DT>(cbase, o + dy + 1u) : 0.0f;
+  v[4] = (vz1 && vy0 && vx0) ? ld<DT>(cbase, o + dz) : 0.0f;
+  v[5] = (vz1 && vy0 && vx1) ? ld<DT>(cbase, o + dz + 1u) : 0.0f;
+  v[6] = (vz1 && vy1 && vx0) ? ld<DT>(cbase, o + dz + dy) : 0.0f;
+  v[7] = (vz1 && vy1 && vx1) ? ld<DT>(cbase, o + dz + dy + 1u) : 0.0f;
 }
 
 // All channels of one key at a pair of output voxels (flat spatial indices
@@ -209,72 +227,73 @@ __device__ __forceinline__ void taps8(const void* cbase, const Corner& c, int W,
 // coordinates of the two voxels.
 template <int MODE, int PAD, int DT, bool ALIGN>
 __device__ __forceinline__ void sample_pair(const KeyArgs& k, int64_t b, int H, int W, int D,
-                                            int64_t hwd, float2 ix, float2 iy, float2 iz,
-                                            int64_t sa, int64_t sb, bool has_b) {
-  const float2 px = f2(pad_coord<PAD, ALIGN>(ix.x, D), pad_coord<PAD, ALIGN>(ix.y, D));
-  const float2 py = f2(pad_coord<PAD, ALIGN>(iy.x, W), pad_coord<PAD, ALIGN>(iy.y, W));
-  const float2 pz = f2(pad_coord<PAD, ALIGN>(iz.x, H), pad_coord<PAD, ALIGN>(iz.y, H));
+                                            int hwd, float2 ix, float2 iy, float2 iz, int sa,
+                                            int sb, bool has_b) {
+  const float2 px = pad2<PAD, ALIGN>(ix, D);
+  const float2 py = pad2<PAD, ALIGN>(iy, W);
+  const float2 pz = pad2<PAD, ALIGN>(iz, H);
   const size_t esz = DT == BA_BF16 ? 2 : 4;
   const char* src_e = (const char*)k.src + (size_t)b * k.channels * hwd * esz;
   char* dst_e = (char*)k.dst + (size_t)b * k.channels * hwd * esz;
   if (MODE == BA_NEAREST) {
-    const int xa = (int)rintf(px.x), ya = (int)rintf(py.x), za = (int)rintf(pz.x);
-    const int xb = (int)rintf(px.y), yb = (int)rintf(py.y), zb = (int)rintf(pz.y);
+    // nearbyint (round half to even) in one conversion
+    const int xa = __float2int_rn(px.x), ya = __float2int_rn(py.x), za = __float2int_rn(pz.x);
+    const int xb = __float2int_rn(px.y), yb = __float2int_rn(py.y), zb = __float2int_rn(pz.y);
     const bool oka =
         (unsigned)xa < (unsigned)D && (unsigned)ya < (unsigned)W && (unsigned)za < (unsigned)H;
     const bool okb = has_b && (unsigned)xb < (unsigned)D && (unsigned)yb < (unsigned)W &&
                      (unsigned)zb < (unsigned)H;
-    const int64_t oa = oka ? ((int64_t)za * W + ya) * D + xa : 0;
-    const int64_t ob = okb ? ((int64_t)zb * W + yb) * D + xb : 0;
+    const int oa = oka ? (za * W + ya) * D + xa : 0;
+    const int ob = okb ? (zb * W + yb) * D + xb : 0;
     for (int c = 0; c < k.channels; ++c) {
       const void* cs = src_e + (size_t)c * hwd * esz;
       void* cd = dst_e + (size_t)c * hwd * esz;
-      st<DT>(cd, sa, oka ? ld<DT>(cs, oa) : 0.0f);
-      if (has_b) st<DT>(cd, sb, okb ? ld<DT>(cs, ob) : 0.0f);
+      const float va = oka ? ld<DT>(cs, oa) : 0.0f;
+      const float vb = okb ? ld<DT>(cs, ob) : 0.0f;
+      st<DT>(cd, sa, va);
+      if (has_b) st<DT>(cd, sb, vb);
     }
     return;
   }
-  // Trilinear: corner and the distances torch forms as (corner_int - coord)
-  // and (coord - corner_int), then the weights as (x * y) * z products.
-  const float2 x0 = f2(floorf(px.x), floorf(px.y)), y0 = f2(floorf(py.x), floorf(py.y));
-  const float2 z0 = f2(floorf(pz.x), floorf(pz.y));
+  // Trilinear: corner and the distances torch forms as (corner + 1 - coord)
+  // and (coord - corner), then the weights as (x * y) * z products.
+  const Floor2 fx = floor2(px), fy = floor2(py), fz = floor2(pz);
   const float2 one = f2(1.0f);
-  const float2 wx1 = __fadd2_rn(px, neg2(x0)), wx0 = __fadd2_rn(__fadd2_rn(x0, one), neg2(px));
-  const float2 wy1 = __fadd2_rn(py, neg2(y0)), wy0 = __fadd2_rn(__fadd2_rn(y0, one), neg2(py));
-  const float2 wz1 = __fadd2_rn(pz, neg2(z0)), wz0 = __fadd2_rn(__fadd2_rn(z0, one), neg2(pz));
-  const float2 xy00 = __fmul2_rn(wx0, wy0), xy10 = __fmul2_rn(wx1, wy0);
-  const float2 xy01 = __fmul2_rn(wx0, wy1), xy11 = __fmul2_rn(wx1, wy1);
+  const float2 wx1 = sub2(px, fx.f), wx0 = sub2(add2(fx.f, one), px);
+  const float2 wy1 = sub2(py, fy.f), wy0 = sub2(add2(fy.f, one), py);
+  const float2 wz1 = sub2(pz, fz.f), wz0 = sub2(add2(fz.f, one), pz);
+  const float2 xy00 = mul2(wx0, wy0), xy10 = mul2(wx1, wy0);
+  const float2 xy01 = mul2(wx0, wy1), xy11 = mul2(wx1, wy1);
   float2 w[8];
-  w[0] = __fmul2_rn(xy00, wz0);
-  w[1] = __fmul2_rn(xy10, wz0);
-  w[2] = __fmul2_rn(xy01, wz0);
-  w[3] = __fmul2_rn(xy11, wz0);
-  w[4] = __fmul2_rn(xy00, wz1);
-  w[5] = __fmul2_rn(xy10, wz1);
-  w[6] = __fmul2_rn(xy01, wz1);
-  w[7] = __fmul2_rn(xy11, wz1);
-  const Corner ca = corner_of(x0.x, y0.x, z0.x, H, W, D);
-  Corner cb = corner_of(x0.y, y0.y, z0.y, H, W, D);
-  if (!has_b) {
-    cb.interior = false;
-    cb.valid = 0u;
-  }
+  w[0] = mul2(xy00, wz0);
+  w[1] = mul2(xy10, wz0);
+  w[2] = mul2(xy01, wz0);
+  w[3] = mul2(xy11, wz0);
+  w[4] = mul2(xy00, wz1);
+  w[5] = mul2(xy10, wz1);
+  w[6] = mul2(xy01, wz1);
+  w[7] = mul2(xy11, wz1);
+  const bool ia = (unsigned)fx.lo < (unsigned)(D - 1) && (unsigned)fy.lo < (unsigned)(W - 1) &&
+                  (unsigned)fz.lo < (unsigned)(H - 1);
+  const bool ib = (unsigned)fx.hi < (unsigned)(D - 1) && (unsigned)fy.hi < (unsigned)(W - 1) &&
+                  (unsigned)fz.hi < (unsigned)(H - 1);
+  // voxel b of a pair past the volume's end reuses voxel a's corner
+  const int xb = has_b ? fx.hi : fx.lo, yb = has_b ? fy.hi : fy.lo, zb = has_b ? fz.hi : fz.lo;
   for (int c = 0; c < k.channels; ++c) {
     const void* cs = src_e + (size_t)c * hwd * esz;
     void* cd = dst_e + (size_t)c * hwd * esz;
     float va[8], vb[8];
-    taps8<DT>(cs, ca, W, D, va);
-    taps8<DT>(cs, cb, W, D, vb);
-    // out += v * w in torch's tap order; scalar, separately rounded
-    // operations (a packed multiply-then-add would be contracted to a fma)
-    float acc_a = 0.0f, acc_b = 0.0f;
+    taps8<DT>(cs, fx.lo, fy.lo, fz.lo, H, W, D, ia, va);
+    taps8<DT>(cs, xb, yb, zb, H, W, D, has_b ? ib : ia, vb);
+    // out += v * w in torch's tap order
+    float2 acc = f2(0.0f);
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-      acc_a = __fadd_rn(acc_a, __fmul_rn(va[t], w[t].x));
-      acc_b = __fadd_rn(acc_b, __fmul_rn(vb[t], w[t].y));
+      acc.x = __fadd_rn(acc.x, __fmul_rn(va[t], w[t].x));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(vb[t], w[t].y));
     }
-    st<DT>(cd, sa, acc_a);
-    if (has_b) st<DT>(cd, sb, acc_b);
+    st<DT>(cd, sa, acc.x);
+    if (has_b) st<DT>(cd, sb, acc.y);
   }
 }
 
@@ -286,15 +305,19 @@ __host__ __device__ constexpr int spec_dt(int s) { return s % 2; }
 
 template <int S, bool ALIGN>
 __device__ __forceinline__ void sample_spec(const KeyArgs& k, int64_t b, int H, int W, int D,
-                                            int64_t hwd, float2 ix, float2 iy, float2 iz,
-                                            int64_t sa, int64_t sb, bool has_b) {
+                                            int hwd, float2 ix, float2 iy, float2 iz, int sa,
+                                            int sb, bool has_b) {
   sample_pair<spec_mode(S), spec_pad(S), spec_dt(S), ALIGN>(k, b, H, W, D, hwd, ix, iy, iz, sa,
                                                              sb, has_b);
 }
 
 // The kernel samples key 0 with spec S0 and, when S1 >= 0, key 1 with spec
 // S1 from the same coordinates; other key combinations are launched one key
-// at a time.
+// at a time.  CTA (x, y, z) covers NB bricks of BD(D) x TY(W) x TZ(H) output
+// voxels of element z, stacked along H; the prologue (theta, base
+// coordinates) is shared by the bricks.  A warp's 32 threads cover a
+// TX x TY x (32 / (TX*TY)) block of voxels, which keeps the source rows one
+// gather request touches few for rotated maps.
 template <int S0, int S1>
 __global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
     resample3d_kernel(const __grid_constant__ ResampleArgs a) {
@@ -306,17 +329,17 @@ __global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
   const int tz = threadIdx.x / (TX * TY);
   const int d_brick = (blockIdx.x % tiles_d) * BD;
   const int w_brick = (blockIdx.x / tiles_d) * TY;
-  const int h_brick = blockIdx.y * TZ;
+  const int h_first = blockIdx.y * (TZ * NB);
   const int w = w_brick + ty;
-  const int h = h_brick + tz;
   const int64_t b = blockIdx.z;
-  const int64_t hwd = (int64_t)H * W * D;
+  const int hwd = H * W * D;
   const bool active = (a.mask == nullptr) || (a.mask[b] != 0);
   const bool affine = a.xform_kind != BA_XFORM_GRID;
 
-  // Prologue: theta, then the brick's base coordinates and bx * theta[r][0].
+  // Prologue: theta, then the base coordinates of the CTA's rows and
+  // bx * theta[r][0] for the brick's D positions.
   __shared__ float s_theta[12];
-  __shared__ float s_by[TY], s_bz[TZ];
+  __shared__ float s_by[TY], s_bz[TZ * NB];
   __shared__ float2 s_px[3][PAIRS][TX];
   if (active && affine) {
     const int t = threadIdx.x;
@@ -331,10 +354,12 @@ __global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
       } else {
         s_theta[t] = x[i * 4 + j];
       }
-    } else if (t < 12 + TY) {
-      s_by[t - 12] = base_coord(w_brick + t - 12, W, ALIGN);
-    } else if (t < 12 + TY + TZ) {
-      s_bz[t - 12 - TY] = base_coord(h_brick + t - 12 - TY, H, ALIGN);
+    }
+    for (int q = t; q < TY + TZ * NB; q += NTHREADS) {
+      if (q < TY)
+        s_by[q] = base_coord(w_brick + q, W, ALIGN);
+      else
+        s_bz[q - TY] = base_coord(h_first + q - TY, H, ALIGN);
     }
     __syncthreads();
     if (t < BD) {
@@ -352,21 +377,25 @@ __global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
     }
   }
   __syncthreads();
-  if (h >= H || w >= W) return;
-  const int64_t row = ((int64_t)h * W + w) * D;
+  if (w >= W) return;
 
   if (!active) {
-    for (int j = 0; j < 2 * PAIRS; ++j) {
-      const int d = d_brick + j * TX + tx;
-      if (d >= D) break;
-      for (int ki = 0; ki < a.n_keys; ++ki) {
-        const KeyArgs& k = a.keys[ki];
-        for (int c = 0; c < k.channels; ++c) {
-          const int64_t i = (b * k.channels + c) * hwd + row + d;
-          if (k.dtype == BA_BF16)
-            ((uint16_t*)k.dst)[i] = __ldg((const uint16_t*)k.src + i);
-          else
-            ((float*)k.dst)[i] = __ldg((const float*)k.src + i);
+    for (int nb = 0; nb < NB; ++nb) {
+      const int h = h_first + nb * TZ + tz;
+      if (h >= H) break;
+      const int row = (h * W + w) * D;
+      for (int j = 0; j < 2 * PAIRS; ++j) {
+        const int d = d_brick + j * TX + tx;
+        if (d >= D) break;
+        for (int ki = 0; ki < a.n_keys; ++ki) {
+          const KeyArgs& k = a.keys[ki];
+          for (int c = 0; c < k.channels; ++c) {
+            const int64_t i = (b * k.channels + c) * (int64_t)hwd + row + d;
+            if (k.dtype == BA_BF16)
+              ((uint16_t*)k.dst)[i] = __ldg((const uint16_t*)k.src + i);
+            else
+              ((float*)k.dst)[i] = __ldg((const float*)k.src + i);
+          }
         }
       }
     }
@@ -374,7 +403,7 @@ __global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
   }
 
   float2 t1[3], t2[3], t3[3];
-  float by = 0.0f, bz = 0.0f;
+  float by = 0.0f;
   if (affine) {
 #pragma unroll
     for (int r = 0; r < 3; ++r) {
@@ -383,44 +412,49 @@ __global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
       t3[r] = f2(s_theta[r * 4 + 3]);
     }
     by = s_by[ty];
-    bz = s_bz[tz];
   }
-  const float2 by2 = f2(by), bz2 = f2(bz);
+  const float2 by2 = f2(by);
   const float fD = (float)D, fW = (float)W, fH = (float)H;
+  for (int nb = 0; nb < NB; ++nb) {
+    const int h = h_first + nb * TZ + tz;
+    if (h >= H) break;
+    const int row = (h * W + w) * D;
+    const float2 bz2 = f2(affine ? s_bz[nb * TZ + tz] : 0.0f);
 #pragma unroll
-  for (int p = 0; p < PAIRS; ++p) {
-    const int da = d_brick + (2 * p) * TX + tx, db = da + TX;
-    if (da >= D) break;
-    const bool has_b = db < D;
-    float2 g[3];
-    if (affine) {
-      // affine_grid's bmm as MKL accumulates it: x*t0, then the fused y and z
-      // terms, then the translation.
+    for (int p = 0; p < PAIRS; ++p) {
+      const int da = d_brick + (2 * p) * TX + tx, db = da + TX;
+      if (da >= D) break;
+      const bool has_b = db < D;
+      float2 g[3];
+      if (affine) {
+        // affine_grid's bmm as MKL accumulates it: x*t0, then the fused y
+        // and z terms, then the translation.
 #pragma unroll
-      for (int r = 0; r < 3; ++r)
-        g[r] = __fadd2_rn(__ffma2_rn(bz2, t2[r], __ffma2_rn(by2, t1[r], s_px[r][p][tx])), t3[r]);
-    } else {
-      const float* ga = a.xform + (b * hwd + row + da) * 3;
-      const float* gb = has_b ? ga + 3 * TX : ga;
+        for (int r = 0; r < 3; ++r)
+          g[r] = add2(__ffma2_rn(bz2, t2[r], __ffma2_rn(by2, t1[r], s_px[r][p][tx])), t3[r]);
+      } else {
+        const float* ga = a.xform + (b * hwd + row + da) * 3;
+        const float* gb = has_b ? ga + 3 * TX : ga;
 #pragma unroll
-      for (int r = 0; r < 3; ++r) g[r] = f2(__ldg(ga + r), __ldg(gb + r));
-    }
-    if (ALIGN) {
-      const float2 ix = unnormalize2<true>(g[0], fD);
-      const float2 iy = unnormalize2<true>(g[1], fW);
-      const float2 iz = unnormalize2<true>(g[2], fH);
-      sample_spec<S0, true>(a.keys[0], b, H, W, D, hwd, ix, iy, iz, row + da, row + db, has_b);
-      if (S1 >= 0)
-        sample_spec<(S1 < 0 ? 0 : S1), true>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da,
-                                             row + db, has_b);
-    } else {
-      const float2 ix = unnormalize2<false>(g[0], fD);
-      const float2 iy = unnormalize2<false>(g[1], fW);
-      const float2 iz = unnormalize2<false>(g[2], fH);
-      sample_spec<S0, false>(a.keys[0], b, H, W, D, hwd, ix, iy, iz, row + da, row + db, has_b);
-      if (S1 >= 0)
-        sample_spec<(S1 < 0 ? 0 : S1), false>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da,
-                                              row + db, has_b);
+        for (int r = 0; r < 3; ++r) g[r] = f2(__ldg(ga + r), __ldg(gb + r));
+      }
+      if (ALIGN) {
+        const float2 ix = unnormalize2<true>(g[0], fD);
+        const float2 iy = unnormalize2<true>(g[1], fW);
+        const float2 iz = unnormalize2<true>(g[2], fH);
+        sample_spec<S0, true>(a.keys[0], b, H, W, D, hwd, ix, iy, iz, row + da, row + db, has_b);
+        if (S1 >= 0)
+          sample_spec<(S1 < 0 ? 0 : S1), true>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da,
+                                               row + db, has_b);
+      } else {
+        const float2 ix = unnormalize2<false>(g[0], fD);
+        const float2 iy = unnormalize2<false>(g[1], fW);
+        const float2 iz = unnormalize2<false>(g[2], fH);
+        sample_spec<S0, false>(a.keys[0], b, H, W, D, hwd, ix, iy, iz, row + da, row + db, has_b);
+        if (S1 >= 0)
+          sample_spec<(S1 < 0 ? 0 : S1), false>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da,
+                                                row + db, has_b);
+      }
     }
   }
 }
@@ -507,7 +541,7 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
 
   const int tiles_d = (int)((d.D + BD - 1) / BD);
   const int64_t gx = (int64_t)tiles_d * ((d.W + TY - 1) / TY);
-  const int64_t gy = (d.H + TZ - 1) / TZ;
+  const int64_t gy = (d.H + TZ * NB - 1) / (TZ * NB);
   BA_REQUIRE(gx <= INT32_MAX && gy <= 65535, "ba_resample3d: spatial extent too large");
   const dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)d.batch);
   const cudaStream_t st = (cudaStream_t)stream;

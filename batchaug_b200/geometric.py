@@ -80,8 +80,10 @@ class _AffineFamily(BatchTransform):
     padding_mode = "zeros"
 
     def _device_params(self, host, shape, device):
-        p = upload({"mask": host["mask"], "affine": host["affine"],
-                    "theta": monai_affine_to_theta(host["affine"], shape[2:])}, device)
+        theta = host.get("theta")
+        if theta is None:
+            theta = monai_affine_to_theta(host["affine"], shape[2:])
+        p = upload({"mask": host["mask"], "affine": host["affine"], "theta": theta}, device)
         p["spatial_shape"] = tuple(shape[2:])
         return p
 
@@ -121,32 +123,50 @@ class RandAffine(_AffineFamily):
     def _n_uniforms(self, shape):
         return 16  # mask, 3 angles, 6 shears, 3 shifts, 3 scales
 
+    def _range_table(self):
+        """(a, b, c, present, groups) of ba_host_rand_affine for this
+        transform's ranges, following _sample_range (affine.py:119-151):
+        None -> the fixed value c; scalar s -> U(-s, s) + c; (lo, hi) ->
+        U(lo, hi) + c."""
+        key = (self.rotate_range, self.shear_range, self.translate_range, self.scale_range)
+        if getattr(self, "_table_key", None) == key:
+            return self._table
+        a = np.zeros(15, np.float32)
+        b = np.zeros(15, np.float32)
+        c = np.zeros(15, np.float32)
+        present = groups = 0
+        for g, (spec, first, n, add) in enumerate([(self.rotate_range, 0, 3, 0.0),
+                                                    (self.shear_range, 3, 6, 0.0),
+                                                    (self.translate_range, 9, 3, 0.0),
+                                                    (self.scale_range, 12, 3, 1.0)]):
+            if spec is None:
+                continue
+            groups |= 1 << g
+            entries = [spec] * n if isinstance(spec, (int, float)) else list(spec)
+            for i, e in enumerate(entries):
+                k = first + i
+                c[k] = add
+                if e is None:
+                    continue
+                present |= 1 << k
+                if isinstance(e, (int, float)):
+                    a[k], b[k] = np.float32(2 * e), -np.float32(e)
+                else:
+                    lo, hi = e
+                    a[k], b[k] = np.float32(hi - lo), np.float32(lo)
+        self._table_key, self._table = key, (a, b, c, present, groups)
+        return self._table
+
     def _host_params(self, B, shape, u, seed):
-        ndim = len(shape) - 2
-        affine = _eye_batch(B)
-        if self.rotate_range is not None:
-            affine = affine @ _rotation(_range_cols(self.rotate_range, u[:, 1:4], ndim))
-        if self.shear_range is not None:
-            n_shear = ndim * (ndim - 1)
-            spec = self.shear_range
-            if isinstance(spec, (int, float)):
-                spec = [spec] * n_shear
-            sh = _range_cols(spec, u[:, 4:10], n_shear)
-            m = _eye_batch(B)
-            m[:, 0, 1], m[:, 0, 2], m[:, 1, 0] = sh[:, 0], sh[:, 1], sh[:, 2]
-            m[:, 1, 2], m[:, 2, 0], m[:, 2, 1] = sh[:, 3], sh[:, 4], sh[:, 5]
-            affine = affine @ m
-        if self.translate_range is not None:
-            t = _range_cols(self.translate_range, u[:, 10:13], ndim)
-            m = _eye_batch(B)
-            m[:, 0, 3], m[:, 1, 3], m[:, 2, 3] = t[:, 0], t[:, 1], t[:, 2]
-            affine = affine @ m
-        if self.scale_range is not None:
-            sc = _range_cols(self.scale_range, u[:, 13:16], ndim, add_scalar=1.0)
-            m = _eye_batch(B)
-            m[:, 0, 0], m[:, 1, 1], m[:, 2, 2] = sc[:, 0], sc[:, 1], sc[:, 2]
-            affine = affine @ m
-        return {"mask": u[:, 0] < self.prob, "affine": affine.astype(np.float32)}
+        a, b, c, present, groups = self._range_table()
+        H, W, D = shape[2:]
+        u = np.ascontiguousarray(u, dtype=np.float32)
+        mask = np.empty(B, np.uint8)
+        affine = np.empty((B, 4, 4), np.float32)
+        theta = np.empty((B, 4, 4), np.float32)
+        ops.host_rand_affine(u, self.prob, a, b, c, present, groups, (H, W, D), mask, affine,
+                             theta)
+        return {"mask": mask.view(np.bool_), "affine": affine, "theta": theta}
 
 
 class RandZoom(_AffineFamily):

@@ -243,6 +243,16 @@ def elastic_grid(shape, taps, magnitude, *, u=None, seed=0, elem_offset=0,
     return grid
 
 
+def host_rand_affine(u, prob, a, b, c, present, groups, spatial_shape, mask, affine, theta):
+    """ba_host_rand_affine into the given numpy outputs (mask u8 (B,),
+    affine and theta (B,4,4) float32)."""
+    H, W, D = spatial_shape
+    B = u.shape[0]
+    L.lib.ba_host_rand_affine(u.ctypes.data, B, u.shape[1], float(prob), a.ctypes.data,
+                              b.ctypes.data, c.ctypes.data, int(present), int(groups), H, W, D,
+                              mask.ctypes.data, affine.ctypes.data, theta.ctypes.data)
+
+
 def host_uniform(seed: int, stream: int, elem_offset: int, n_elems: int,
                  per_elem: int) -> np.ndarray:
     """(n_elems, per_elem) uniforms in [0,1) keyed on global element index."""

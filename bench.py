@@ -390,6 +390,123 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def _secondary(name, torch, ba, device, rank):
+    """Other configurations of the reference's benchmark set, for profiling
+    and per-config numbers: returns (text, step(i), voxels, bytes) where bytes
+    are the algorithmic bytes of a step (every key read once, written once)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(7 + rank)
+    if name == "config3":
+        xs = [(0.5 + 0.2 * torch.randn(16, 4, 128, 128, 128, device=device, generator=g))
+              .clamp(0, 1).bfloat16() for _ in range(2)]
+        c = ba.Compose([ba.RandGaussianNoised(["v"], prob=1.0, std=(0.1, 0.5)),
+                        ba.RandAdjustContrastd(["v"], prob=1.0, gamma=(0.5, 2.0)),
+                        ba.RandScaleIntensityd(["v"], prob=1.0, factors=0.2),
+                        ba.RandShiftIntensityd(["v"], prob=1.0, offsets=0.1),
+                        ba.ScaleIntensityd(["v"], minv=0.0, maxv=1.0)], lazy=True)
+        n = xs[0].numel()
+        return ("config 3 (prob=1 variant): noise -> contrast -> scale -> shift -> "
+                "ScaleIntensity, B=16 C=4 128^3 bf16", lambda i: c({"v": xs[i % 2]}), n, n * 4)
+    if name == "config4":
+        vols = [torch.randn(5, 4, 128, 128, 128, device=device, generator=g) for _ in range(2)]
+        segs = [(torch.rand(5, 1, 128, 128, 128, device=device, generator=g) > 0.5).float()
+                for _ in range(2)]
+        c = ba.Compose([ba.RandRotate90d(["vol", "seg"], prob=0.5, max_k=3),
+                        ba.RandAxisFlipd(["vol", "seg"], prob=0.5),
+                        ba.RandGaussianNoised(["vol"], std=0.5),
+                        ba.RandAffined(["vol", "seg"], prob=0.5, rotate_range=0.785,
+                                       shear_range=0.3, translate_range=5),
+                        ba.ScaleIntensityd(["vol"])], lazy=True,
+                       mode={"vol": "bilinear", "seg": "nearest"})
+        n = vols[0].numel() + segs[0].numel()
+        return ("config 4: rot90, flip, noise, affine, ScaleIntensity on vol (5x4x128^3 f32) "
+                "+ seg (5x1x128^3 f32)", lambda i: c({"vol": vols[i % 2], "seg": segs[i % 2]}),
+                n, n * 8)
+    if name == "config5":
+        vol = torch.rand(8, 2, 160, 160, 160, device=device, generator=g).bfloat16()
+        seg = torch.randint(0, 8, (8, 2, 160, 160, 160), device=device, generator=g).float()
+        c = ba.Compose([ba.Rand3DElasticd(["vol", "seg"], prob=1.0, sigma_range=(5, 7),
+                                          magnitude_range=(50, 150),
+                                          mode={"vol": "bilinear", "seg": "nearest"}),
+                        ba.RandAffined(["vol", "seg"], prob=0.1, rotate_range=0.5),
+                        ba.RandBiasFieldd(["vol"], prob=0.1),
+                        ba.RandGaussianSmoothd(["vol"], prob=0.1, sigma_x=(0.5, 1.5),
+                                               sigma_y=(0.5, 1.5), sigma_z=(0.5, 1.5)),
+                        ba.ScaleIntensityd(["vol"])], lazy=True,
+                       mode={"vol": "bilinear", "seg": "nearest"})
+        n = vol.numel() + seg.numel()
+        return ("config 5 per-GPU shard: elastic + affine(0.1) -> bias(0.1) -> smooth(0.1) -> "
+                "ScaleIntensity, vol 8x2x160^3 bf16 + seg 8x2x160^3 f32",
+                lambda i: c({"vol": vol, "seg": seg}), n, vol.numel() * 4 + seg.numel() * 8)
+    if name == "config5-smooth":
+        vol = torch.rand(8, 2, 160, 160, 160, device=device, generator=g).bfloat16()
+        sm = ba.RandGaussianSmooth(prob=1.0, sigma_x=(0.5, 1.5), sigma_y=(0.5, 1.5),
+                                   sigma_z=(0.5, 1.5))
+        p = sm.sample_params(8, vol.shape, device)
+        n = vol.numel()
+        return ("RandGaussianSmooth(prob=1, sigma 0.5..1.5) on config 5's vol shard "
+                "(8x2x160^3 bf16)", lambda i: sm.apply(vol, p), n, n * 4)
+    raise SystemExit(f"unknown workload {name}")
+
+
+def run_secondary(args):
+    import torch
+    import torch.distributed as dist
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+    import batchaug_b200 as ba
+    from batchaug_b200 import _lib as L
+
+    torch.manual_seed(1234)
+    text, step, voxels, alg_bytes = _secondary(args.workload, torch, ba, device, rank)
+    stream = torch.cuda.current_stream(device)
+    for i in range(args.warmup):
+        step(i)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = L.kernel_launches()
+    clocks.start()
+    start.record(stream)
+    for i in range(args.steps):
+        step(i)
+    end.record(stream)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.stop()
+    ms = torch.tensor([start.elapsed_time(end)], device=device, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    total_ms = float(ms.item())
+    if rank == 0:
+        peak, peak_kind = _peaks()
+        achieved = alg_bytes / (total_ms / args.steps * 1e-3) / 1e9
+        print(json.dumps({
+            "metric": METRIC, "value": ws * voxels * args.steps / (total_ms * 1e-3), "unit": UNIT,
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "mixed", "data": "synthetic",
+            "config": {"workload": text, "l2": "inputs larger than L2 or rotating"},
+            "roofline": {"bound": "hbm", "scope": "whole step (all kernels and host work)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                         "algorithmic_bytes_per_step": alg_bytes},
+            "gpu_launches": int(L.kernel_launches() - launches0),
+            "clocks": clocks.summary()}), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -399,11 +516,17 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="config2",
+                    choices=["config2", "config3", "config4", "config5", "config5-smooth"],
+                    help="config2 is the headline; the others time one whole step of that "
+                         "configuration (for profiling and per-config numbers)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "config2":
+        run_secondary(args)
     else:
         run_b200(args)
 

@@ -268,6 +268,26 @@ BA_API ba_status ba_elastic_grid(const float* u, uint64_t seed, uint64_t elem_of
 BA_API void ba_host_uniform(uint64_t seed, uint32_t stream, uint64_t elem_offset, int64_t n_elems,
                      int64_t per_elem, float* out);
 
+/*
+ * RandAffine's per-element parameters, on the host: replaces the tensor
+ * arithmetic of RandAffine.sample_params / to_affine and the builders of
+ * batchaug/pytorch/geometric/affine.py:9-151 and :229-282, plus
+ * monai_affine_to_theta (affine.py:154-195) for the sampled matrices.
+ * u is (batch, u_stride) uniforms: column 0 the mask draw, columns 1..15 the
+ * 3 angles, 6 shears, 3 shifts and 3 scales.  Component k is
+ * (u[1+k] * range_a[k] + range_b[k]) + range_c[k] when bit k of `present` is
+ * set (a sampled range) and range_c[k] otherwise (a fixed value).  Bits of
+ * `groups` select the factors of I @ R @ Sh @ T @ Sc that exist (1 rotate,
+ * 2 shear, 4 translate, 8 scale).  Writes mask (u < prob) as 0/1 bytes, the
+ * (batch, 4, 4) MONAI affines and the (batch, 4, 4) thetas (affine_grid takes
+ * the first three rows) for a volume of H x W x D; any output pointer may be
+ * NULL.
+ */
+BA_API void ba_host_rand_affine(const float* u, int64_t batch, int64_t u_stride, float prob,
+                                const float* range_a, const float* range_b, const float* range_c,
+                                uint32_t present, uint32_t groups, int64_t H, int64_t W, int64_t D,
+                                uint8_t* mask, float* affine, float* theta);
+
 /* ---------------------------------------------------------------------- */
 /* Library                                                                 */
 /* ---------------------------------------------------------------------- */

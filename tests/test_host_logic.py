@@ -158,3 +158,67 @@ def test_compose_skips_all_masked_and_splits_key_sets(ba, rec):
     c2({"vol": v, "seg": v.clone()})
     res = [k for k in rec.calls if k[0] == "resample"]
     assert len(res) == 2 and sorted(r[1] for r in res) == [1, 1]  # different histories
+
+
+def _numpy_rand_affine(u, rot, shear, trans, scale):
+    """RandAffine's affine chain I @ R @ Sh @ T @ Sc restated in numpy
+    (affine.py:9-151), used to check the native host builder."""
+    B = u.shape[0]
+    eye = lambda: np.broadcast_to(np.eye(4, dtype=np.float32), (B, 4, 4)).copy()
+
+    def cols(spec, uu, n, add=0.0):
+        spec = [spec] * n if isinstance(spec, (int, float)) else list(spec)
+        out = np.zeros((B, n), np.float32)
+        for i, s in enumerate(spec):
+            if s is None:
+                out[:, i] = add
+            elif isinstance(s, (int, float)):
+                out[:, i] = uu[:, i] * np.float32(2 * s) - np.float32(s) + np.float32(add)
+            else:
+                out[:, i] = uu[:, i] * np.float32(s[1] - s[0]) + np.float32(s[0]) + np.float32(add)
+        return out
+
+    A = eye()
+    if rot is not None:
+        a = cols(rot, u[:, 1:4], 3)
+        c, s = np.cos(a).astype(np.float32), np.sin(a).astype(np.float32)
+        rx, ry, rz = eye(), eye(), eye()
+        rx[:, 1, 1], rx[:, 1, 2], rx[:, 2, 1], rx[:, 2, 2] = c[:, 0], -s[:, 0], s[:, 0], c[:, 0]
+        ry[:, 0, 0], ry[:, 0, 2], ry[:, 2, 0], ry[:, 2, 2] = c[:, 1], s[:, 1], -s[:, 1], c[:, 1]
+        rz[:, 0, 0], rz[:, 0, 1], rz[:, 1, 0], rz[:, 1, 1] = c[:, 2], -s[:, 2], s[:, 2], c[:, 2]
+        A = A @ (rx @ ry @ rz)
+    if shear is not None:
+        sh = cols(shear, u[:, 4:10], 6)
+        m = eye()
+        m[:, 0, 1], m[:, 0, 2], m[:, 1, 0] = sh[:, 0], sh[:, 1], sh[:, 2]
+        m[:, 1, 2], m[:, 2, 0], m[:, 2, 1] = sh[:, 3], sh[:, 4], sh[:, 5]
+        A = A @ m
+    if trans is not None:
+        t = cols(trans, u[:, 10:13], 3)
+        m = eye()
+        m[:, 0, 3], m[:, 1, 3], m[:, 2, 3] = t[:, 0], t[:, 1], t[:, 2]
+        A = A @ m
+    if scale is not None:
+        sc = cols(scale, u[:, 13:16], 3, 1.0)
+        m = eye()
+        m[:, 0, 0], m[:, 1, 1], m[:, 2, 2] = sc[:, 0], sc[:, 1], sc[:, 2]
+        A = A @ m
+    return A.astype(np.float32)
+
+
+@pytest.mark.parametrize("ranges", [
+    (0.785, 0.3, 5, 0.1),
+    ((0.1, 0.5), None, (None, 2, (1, 3)), None),
+    (None, (0.1, None, 0.2, None, 0.3, None), None, (0.9, 1.1)),
+])
+def test_native_affine_builder_matches_numpy_chain(ba, ranges):
+    from batchaug_b200.geometric import monai_affine_to_theta
+    rot, shear, trans, scale = ranges
+    t = ba.RandAffine(prob=0.6, rotate_range=rot, shear_range=shear, translate_range=trans,
+                      scale_range=scale)
+    u = np.random.default_rng(3).random((64, 16), dtype=np.float32)
+    h = t._host_params(64, (64, 1, 12, 16, 20), u, 0)
+    ref = _numpy_rand_affine(u, rot, shear, trans, scale)
+    np.testing.assert_allclose(h["affine"], ref, rtol=0, atol=2e-6)
+    assert np.array_equal(h["mask"], u[:, 0] < 0.6)
+    np.testing.assert_array_equal(h["theta"], monai_affine_to_theta(h["affine"], (12, 16, 20)))
