@@ -64,12 +64,15 @@ def _peaks():
 
 
 def _traffic_per_launch():
-    """DRAM bytes per launch of the resample kernel from the committed ncu
-    summary (profiles/resample3d_cfg2.json), or None."""
-    p = os.path.join(ROOT, "profiles", "resample3d_cfg2.json")
+    """DRAM bytes (read + write) per launch of the resample kernel from the
+    committed ncu summary (profiles/resample3d_config2.md), or None."""
+    import re
+    p = os.path.join(ROOT, "profiles", "resample3d_config2.md")
     if os.path.exists(p):
         with open(p) as f:
-            return json.load(f).get("dram_bytes_per_launch")
+            m = re.search(r"^dram_bytes_per_launch:\s*(\d+)", f.read(), re.M)
+        if m:
+            return int(m.group(1))
     return None
 
 
