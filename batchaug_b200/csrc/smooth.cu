@@ -184,9 +184,9 @@ __global__ void __launch_bounds__(SM_THREADS)
 // (halo loaded with the padding rule), writing an fp32 intermediate; pass B
 // convolves along H over column strips of that intermediate and writes the
 // result (the output dtype, or one component of the elastic grid).  Taps sit
-// in registers zero-padded to a compile-time KMAX, and each thread produces R
-// outputs per window it reads, so the loops are FMA-bound rather than bound
-// by shared-memory loads.  Rows read with stride R per thread use the padded
+// in shared memory zero-padded to a compile-time KMAX (one broadcast read per
+// tap, reused for R outputs) and the input window rolls through registers,
+// one shared-memory read per tap step.  Rows read with stride R per thread use the padded
 // index q + q/8, which keeps those reads free of bank conflicts.  The three
 // 1-D operators (each "pad, then correlate" along one axis) commute, so
 // running D, W, H instead of the reference's H, W, D changes only rounding.
@@ -232,12 +232,19 @@ struct TiledArgs {
 // R outputs out[i] = sum_k w[k] * x[i + k] for k < KMAX from a register
 // window x of R + KMAX - 1 values; taps come from shared memory (one
 // broadcast read per tap, reused by all R outputs).
-template <int R, int KMAX>
-__device__ __forceinline__ void conv_window(const float* xw, const float* s_w, float* acc) {
+// R outputs acc[i] = sum_k w[k] * x[i + k], k < KMAX.  The window rolls:
+// tap k loads x[k + R - 1] only, so R values of x are live at a time, not
+// R + KMAX - 1 (which would not fit the registers for wide kernels).
+template <int R, int KMAX, typename Load>
+__device__ __forceinline__ void conv_rolling(Load x, const float* s_w, float* acc) {
+  float xw[R + KMAX - 1];
 #pragma unroll
   for (int i = 0; i < R; ++i) acc[i] = 0.0f;
 #pragma unroll
+  for (int j = 0; j < R - 1; ++j) xw[j] = x(j);
+#pragma unroll
   for (int k = 0; k < KMAX; ++k) {
+    xw[k + R - 1] = x(k + R - 1);
     const float w = s_w[k];
 #pragma unroll
     for (int i = 0; i < R; ++i) acc[i] = __fmaf_rn(w, xw[i + k], acc[i]);
@@ -291,11 +298,9 @@ __global__ void __launch_bounds__(TS_THREADS) smooth_plane_kernel(const __grid_c
   constexpr int GROUPS_D = TS_TD / TS_RD;
   for (int u = threadIdx.x; u < rowsA * GROUPS_D; u += TS_THREADS) {
     const int r = u / GROUPS_D, q0 = (u % GROUPS_D) * TS_RD;
-    float xw[TS_RD + KMAX - 1], acc[TS_RD];
+    float acc[TS_RD];
     const float* rowp = A + r * PA;
-#pragma unroll
-    for (int j = 0; j < TS_RD + KMAX - 1; ++j) xw[j] = rowp[pidx(q0 + j)];
-    conv_window<TS_RD, KMAX>(xw, s_wd, acc);
+    conv_rolling<TS_RD, KMAX>([&](int j) { return rowp[pidx(q0 + j)]; }, s_wd, acc);
 #pragma unroll
     for (int i = 0; i < TS_RD; ++i) Bm[r * TS_TD + q0 + i] = acc[i];
   }
@@ -304,10 +309,9 @@ __global__ void __launch_bounds__(TS_THREADS) smooth_plane_kernel(const __grid_c
   const int q = threadIdx.x % TS_TD;
   const int d = td0 + q;
   for (int wg = threadIdx.x / TS_TD; wg < TW / TS_RW; wg += TS_THREADS / TS_TD) {
-    float xw[TS_RW + KMAX - 1], acc[TS_RW];
-#pragma unroll
-    for (int j = 0; j < TS_RW + KMAX - 1; ++j) xw[j] = Bm[(wg * TS_RW + j) * TS_TD + q];
-    conv_window<TS_RW, KMAX>(xw, s_ww, acc);
+    float acc[TS_RW];
+    conv_rolling<TS_RW, KMAX>([&](int j) { return Bm[(wg * TS_RW + j) * TS_TD + q]; }, s_ww,
+                              acc);
     if (d < D) {
 #pragma unroll
       for (int i = 0; i < TS_RW; ++i) {
@@ -363,10 +367,8 @@ __global__ void __launch_bounds__(TS_THREADS) smooth_column_kernel(const __grid_
                                           : 0.0f;
   }
   __syncthreads();
-  float xw[TS_RH + KMAX - 1], acc[TS_RH];
-#pragma unroll
-  for (int j = 0; j < TS_RH + KMAX - 1; ++j) xw[j] = S[(hg * TS_RH + j) * TB_TD + q];
-  conv_window<TS_RH, KMAX>(xw, s_wh, acc);
+  float acc[TS_RH];
+  conv_rolling<TS_RH, KMAX>([&](int j) { return S[(hg * TS_RH + j) * TB_TD + q]; }, s_wh, acc);
   if (d >= D) return;
   if (a.grid != nullptr) {
     // elastic: the component (P index of bp) is the displacement axis

@@ -253,10 +253,12 @@ def run_b200(args):
                 s_in.wait_event(used[i - 2])
             x_devs[buf].copy_(hosts[buf], non_blocking=True)
             in_done[i].record(s_in)
-        stream.wait_event(in_done[i])
+        # the parameters (their small upload included) before the wait on the
+        # volume's upload, so they do not queue behind the next volume's copy
         params = t.sample_params(B, x_devs[buf].shape, device)
         param_bytes = sum(v.numel() * v.element_size() for k, v in params.items()
                           if isinstance(v, torch.Tensor))
+        stream.wait_event(in_done[i])
         out = t.apply(x_devs[buf], params)
         used[i].record(stream)
         with torch.cuda.stream(s_out):
