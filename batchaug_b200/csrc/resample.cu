@@ -459,6 +459,309 @@ __global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
   }
 }
 
+// ===========================================================================
+// Staged resample: the source footprint of each output tile in shared memory.
+//
+// For affine maps (bilinear key, zeros or border padding) a CTA covers a
+// 16(D) x 8(W) x 8(H) output tile.  Its prologue maps the tile's 8 corners
+// to source voxels and takes their bounding box (the corner coordinates bound
+// all others up to rounding, far below the 0.01-voxel slack used), and, when
+// the box fits ST_MAX_FLOATS floats, copies it into shared memory with 16-byte
+// cp.async copies (zero-filled outside the volume, which is exactly the value
+// an out-of-bounds tap contributes).  The 8 taps of each voxel are then read
+// from shared memory; a voxel whose footprint leaves the box (or a CTA whose
+// box does not fit) gathers from global memory as resample3d_kernel does.
+// Arithmetic is the same operation for operation, so results are identical.
+// A second, nearest-mode key (the label map of a dict transform) is sampled
+// from global memory with the same coordinates.
+// ===========================================================================
+#ifndef BA_ST_TW
+#define BA_ST_TW 8
+#endif
+#ifndef BA_ST_TH
+#define BA_ST_TH 8
+#endif
+#ifndef BA_ST_MAX_FLOATS
+#define BA_ST_MAX_FLOATS 8192
+#endif
+#ifndef BA_ST_MINBLOCKS
+#define BA_ST_MINBLOCKS 5
+#endif
+constexpr int ST_TD = 16, ST_TW = BA_ST_TW, ST_TH = BA_ST_TH;
+constexpr int ST_THREADS = 128;
+constexpr int ST_MAX_FLOATS = BA_ST_MAX_FLOATS;  // 32 KB of staged source
+constexpr int ST_PW = ST_TW / 2, ST_PH = ST_TH / 8;
+static_assert(ST_TW % 2 == 0 && ST_TH % 8 == 0, "tile covered by the thread layout");
+
+template <int DT>
+__device__ __forceinline__ float4 ld4(const void* base, int64_t i) {
+  if (DT == BA_BF16) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>((const uint16_t*)base + i));
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+  }
+  return __ldg(reinterpret_cast<const float4*>((const float*)base + i));
+}
+
+template <int S0, int S1>
+__global__ void __launch_bounds__(ST_THREADS, BA_ST_MINBLOCKS)
+    resample3d_staged_kernel(const __grid_constant__ ResampleArgs a) {
+  extern __shared__ float4 s_dyn4[];
+  float* s_src = reinterpret_cast<float*>(s_dyn4);
+  __shared__ float s_theta[12];
+  __shared__ float s_by[ST_TW], s_bz[ST_TH];
+  __shared__ float2 s_px[3][8];
+  __shared__ int s_lo[3], s_hi[3];
+  __shared__ int s_box[6];
+  constexpr int MODE = spec_mode(S0), PAD = spec_pad(S0), DT = spec_dt(S0);
+  const bool ALIGN = a.align_corners != 0;
+  const int H = a.H, W = a.W, D = a.D;
+  const int tiles_d = (D + ST_TD - 1) / ST_TD;
+  const int d0 = (blockIdx.x % tiles_d) * ST_TD;
+  const int w0 = (blockIdx.x / tiles_d) * ST_TW;
+  const int h0 = blockIdx.y * ST_TH;
+  const int64_t b = blockIdx.z;
+  const int hwd = H * W * D;
+  const int t = threadIdx.x;
+  const int tx = t & 7, ty = (t >> 3) & 1, tz = (t >> 4) & 1, wp = t >> 5;
+  const KeyArgs& k = a.keys[0];
+  const size_t esz = DT == BA_BF16 ? 2 : 4;
+  const bool active = (a.mask == nullptr) || (a.mask[b] != 0);
+  if (!active) {
+    for (int pp = 0; pp < ST_PW * ST_PH; ++pp) {
+      const int pw = pp % ST_PW, ph = pp / ST_PW;
+      const int w = w0 + ty + 2 * pw, h = h0 + tz + 2 * wp + 8 * ph;
+      if (w >= W || h >= H) continue;
+      for (int j = 0; j < 2; ++j) {
+        const int d = d0 + tx + 8 * j;
+        if (d >= D) continue;
+        for (int ki = 0; ki < a.n_keys; ++ki) {
+          const KeyArgs& kc = a.keys[ki];
+          for (int c = 0; c < kc.channels; ++c) {
+            const int64_t i = (b * kc.channels + c) * (int64_t)hwd + ((int64_t)h * W + w) * D + d;
+            if (kc.dtype == BA_BF16)
+              ((uint16_t*)kc.dst)[i] = __ldg((const uint16_t*)kc.src + i);
+            else
+              ((float*)kc.dst)[i] = __ldg((const float*)kc.src + i);
+          }
+        }
+      }
+    }
+    return;
+  }
+  if (t < 12) {
+    const int i = t / 4, j = t % 4;
+    const float* x = a.xform + b * a.xform_stride;
+    if (a.xform_kind == BA_XFORM_AFFINE) {
+      const int pi = 2 - i, pj = (j == 3) ? 3 : 2 - j;
+      const float s_j = (pj == 3) ? 1.0f : a.si[pj];
+      s_theta[t] = (a.sn[pi] * x[pi * 4 + pj]) * s_j;
+    } else {
+      s_theta[t] = x[i * 4 + j];
+    }
+  } else if (t >= 32 && t < 32 + ST_TW) {
+    s_by[t - 32] = base_coord(w0 + t - 32, W, ALIGN);
+  } else if (t >= 64 && t < 64 + ST_TH) {
+    s_bz[t - 64] = base_coord(h0 + t - 64, H, ALIGN);
+  } else if (t >= 96 && t < 99) {
+    s_lo[t - 96] = 0x7fffffff;
+    s_hi[t - 96] = -0x7fffffff;
+  }
+  __syncthreads();
+  if (t < 16) {
+    const int d = d0 + t;
+    const float bx = d < D ? base_coord(d, D, ALIGN) : 0.0f;
+    const int j = t & 7, q = t >> 3;
+#pragma unroll
+    for (int r = 0; r < 3; ++r) reinterpret_cast<float*>(&s_px[r][j])[q] = bx * s_theta[r * 4];
+  } else if (t >= 32 && t < 40) {
+    // bounding box of the tile's corners in source voxels
+    const int c = t - 32;
+    const int dc = (c & 1) ? min(d0 + ST_TD - 1, D - 1) : d0;
+    const int wc = (c & 2) ? min(w0 + ST_TW - 1, W - 1) : w0;
+    const int hc = (c & 4) ? min(h0 + ST_TH - 1, H - 1) : h0;
+    const float bx = base_coord(dc, D, ALIGN), by = base_coord(wc, W, ALIGN),
+                bz = base_coord(hc, H, ALIGN);
+    const float sz[3] = {(float)D, (float)W, (float)H};
+    const int isz[3] = {D, W, H};
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+      const float g = __fadd_rn(
+          __fmaf_rn(bz, s_theta[r * 4 + 2], __fmaf_rn(by, s_theta[r * 4 + 1], bx * s_theta[r * 4])),
+          s_theta[r * 4 + 3]);
+      const float u = ALIGN ? __fmul_rn(__fmul_rn(__fadd_rn(g, 1.0f), 0.5f), sz[r] - 1.0f)
+                            : __fmul_rn(__fsub_rn(__fmul_rn(__fadd_rn(g, 1.0f), sz[r]), 1.0f), 0.5f);
+      // every voxel's coordinate is within rounding (< 1e-3 voxel) of the
+      // affine image of its index, whose extremes are at the corners
+      const float p = fminf(fmaxf(pad_coord<PAD, false>(u, isz[r]), -1.0e6f), 1.0e6f);
+      atomicMin(&s_lo[r], (int)floorf(p - 0.01f));
+      atomicMax(&s_hi[r], (int)floorf(p + 0.01f));
+    }
+  }
+  __syncthreads();
+  if (t == 0) {
+    const int isz[3] = {D, W, H};
+    int lo[3], hi[3];
+    for (int r = 0; r < 3; ++r) {
+      lo[r] = max(s_lo[r], -1);
+      hi[r] = min(s_hi[r] + 1, isz[r]);  // + 1: the upper taps
+    }
+    const int lx4 = (lo[0] >= 0) ? (lo[0] & ~3) : -4;
+    const int ex = ((hi[0] - lx4 + 1) + 3) & ~3;
+    const int ey = hi[1] - lo[1] + 1, ez = hi[2] - lo[2] + 1;
+    const bool ok = PAD != BA_PAD_REFLECTION && ex >= 4 && ey >= 2 && ez >= 2 &&
+                    ex / 4 <= ST_THREADS && (int64_t)ex * ey * ez <= ST_MAX_FLOATS;
+    s_box[0] = lx4;
+    s_box[1] = lo[1];
+    s_box[2] = lo[2];
+    s_box[3] = ok ? ex / 4 : 0;
+    s_box[4] = ey;
+    s_box[5] = ez;
+  }
+  __syncthreads();
+  const int lx4 = s_box[0], ly = s_box[1], lz = s_box[2], nx4 = s_box[3], ey = s_box[4],
+            ez = s_box[5];
+  const int ex = nx4 * 4;
+  const bool staged = nx4 > 0;
+  float2 t1[3], t2[3], t3[3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    t1[r] = f2(s_theta[r * 4 + 1]);
+    t2[r] = f2(s_theta[r * 4 + 2]);
+    t3[r] = f2(s_theta[r * 4 + 3]);
+  }
+  const float fD = (float)D, fW = (float)W, fH = (float)H;
+
+  for (int c = 0; c < k.channels; ++c) {
+    const char* src_c = (const char*)k.src + ((size_t)b * k.channels + c) * hwd * esz;
+    char* dst_c = (char*)k.dst + ((size_t)b * k.channels + c) * hwd * esz;
+    if (staged) {
+      // cp.async 16-byte chunks; chunks outside the volume are zero-filled
+      // (source size 0)
+      const int rows = ey * ez;
+      const int rpp = ST_THREADS / nx4;  // rows per pass (nx4 <= ST_THREADS)
+      const int lc = t % nx4;
+      int row = t / nx4;
+      int y = row % ey, z = row / ey;
+      if (row < rpp) {
+        for (; row < rows; row += rpp) {
+          const int gy = ly + y, gz = lz + z, gx = lx4 + 4 * lc;
+          const bool in = (unsigned)gy < (unsigned)W && (unsigned)gz < (unsigned)H && gx >= 0 && gx < D;
+          const int64_t gi = in ? ((int64_t)gz * W + gy) * D + gx : 0;
+          const unsigned sdst = (unsigned)__cvta_generic_to_shared(&s_dyn4[row * nx4 + lc]);
+          if (DT == BA_F32) {
+            const void* gsrc = (const float*)src_c + gi;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sdst), "l"(gsrc),
+                         "r"(in ? 16 : 0) : "memory");
+          } else {
+            s_dyn4[row * nx4 + lc] = in ? ld4<DT>(src_c, gi) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+          y += rpp;
+          while (y >= ey) {
+            y -= ey;
+            ++z;
+          }
+        }
+      }
+      asm volatile("cp.async.commit_group;\n" ::: "memory");
+      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+      __syncthreads();
+    }
+    for (int pp = 0; pp < ST_PW * ST_PH; ++pp) {
+      const int pw = pp % ST_PW, ph = pp / ST_PW;
+      const int h = h0 + tz + 2 * wp + 8 * ph;
+      const float2 bz2 = f2(s_bz[tz + 2 * wp + 8 * ph]);
+      const int w = w0 + ty + 2 * pw;
+      if (w >= W || h >= H) continue;
+      const int da = d0 + tx, db = da + 8;
+      if (da >= D) continue;
+      const bool has_b = db < D;
+      const float2 by2 = f2(s_by[ty + 2 * pw]);
+      float2 g[3];
+#pragma unroll
+      for (int r = 0; r < 3; ++r)
+        g[r] = add2(__ffma2_rn(bz2, t2[r], __ffma2_rn(by2, t1[r], s_px[r][tx])), t3[r]);
+      float2 ix, iy, iz;
+      if (ALIGN) {
+        ix = unnormalize2<true>(g[0], fD);
+        iy = unnormalize2<true>(g[1], fW);
+        iz = unnormalize2<true>(g[2], fH);
+      } else {
+        ix = unnormalize2<false>(g[0], fD);
+        iy = unnormalize2<false>(g[1], fW);
+        iz = unnormalize2<false>(g[2], fH);
+      }
+      const float2 px = ALIGN ? pad2<PAD, true>(ix, D) : pad2<PAD, false>(ix, D);
+      const float2 py = ALIGN ? pad2<PAD, true>(iy, W) : pad2<PAD, false>(iy, W);
+      const float2 pz = ALIGN ? pad2<PAD, true>(iz, H) : pad2<PAD, false>(iz, H);
+      const int row = (h * W + w) * D;
+      const Floor2 fx = floor2(px), fy = floor2(py), fz = floor2(pz);
+      const float2 one = f2(1.0f);
+      const float2 wx1 = sub2(px, fx.f), wx0 = sub2(add2(fx.f, one), px);
+      const float2 wy1 = sub2(py, fy.f), wy0 = sub2(add2(fy.f, one), py);
+      const float2 wz1 = sub2(pz, fz.f), wz0 = sub2(add2(fz.f, one), pz);
+      const float2 xy00 = mul2(wx0, wy0), xy10 = mul2(wx1, wy0);
+      const float2 xy01 = mul2(wx0, wy1), xy11 = mul2(wx1, wy1);
+      float2 wt[8];
+      wt[0] = mul2(xy00, wz0);
+      wt[1] = mul2(xy10, wz0);
+      wt[2] = mul2(xy01, wz0);
+      wt[3] = mul2(xy11, wz0);
+      wt[4] = mul2(xy00, wz1);
+      wt[5] = mul2(xy10, wz1);
+      wt[6] = mul2(xy01, wz1);
+      wt[7] = mul2(xy11, wz1);
+      float va[8], vb[8];
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        const int x0 = s ? (has_b ? fx.hi : fx.lo) : fx.lo;
+        const int y0 = s ? (has_b ? fy.hi : fy.lo) : fy.lo;
+        const int z0 = s ? (has_b ? fz.hi : fz.lo) : fz.lo;
+        float* v = s ? vb : va;
+        // all 8 taps inside the box: 0 <= x0 - lx4 and x0 + 1 - lx4 < ex, etc.
+        const int ux = x0 - lx4, uy = y0 - ly, uz = z0 - lz;
+        const bool inbox = staged && ux >= 0 && ux < ex - 1 && uy >= 0 && uy < ey - 1 &&
+                           uz >= 0 && uz < ez - 1;
+        if (inbox) {
+          const int si = ((z0 - lz) * ey + (y0 - ly)) * ex + (x0 - lx4);
+          const int pl = ey * ex;
+          v[0] = s_src[si];
+          v[1] = s_src[si + 1];
+          v[2] = s_src[si + ex];
+          v[3] = s_src[si + ex + 1];
+          v[4] = s_src[si + pl];
+          v[5] = s_src[si + pl + 1];
+          v[6] = s_src[si + pl + ex];
+          v[7] = s_src[si + pl + ex + 1];
+        } else {
+          const bool in_vol = (unsigned)x0 < (unsigned)(D - 1) && (unsigned)y0 < (unsigned)(W - 1) &&
+                              (unsigned)z0 < (unsigned)(H - 1);
+          taps8<DT>(src_c, x0, y0, z0, H, W, D, in_vol, v);
+        }
+      }
+      if (S1 >= 0 && c == 0) {
+        if (ALIGN)
+          sample_spec<(S1 < 0 ? 0 : S1), true>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da,
+                                               row + db, has_b);
+        else
+          sample_spec<(S1 < 0 ? 0 : S1), false>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da,
+                                                row + db, has_b);
+      }
+      float2 acc = f2(0.0f);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        acc.x = __fadd_rn(acc.x, __fmul_rn(va[q], wt[q].x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(vb[q], wt[q].y));
+      }
+      st<DT>(dst_c, row + da, acc.x);
+      if (has_b) st<DT>(dst_c, row + db, acc.y);
+    }
+    if (staged) __syncthreads();
+  }
+  (void)MODE;
+}
+
+
 bool overlaps(const void* a, size_t na, const void* b, size_t nb) {
   const char* pa = (const char*)a;
   const char* pb = (const char*)b;
@@ -546,6 +849,37 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
   const dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)d.batch);
   const cudaStream_t st = (cudaStream_t)stream;
   auto code = [](const KeyArgs& k) { return spec_code(k.mode, k.padding, k.dtype); };
+  // The staged kernel serves a bilinear key (zeros or border padding) of an
+  // affine map whose rows start on 16-byte (fp32) or 8-byte (bf16) boundaries.
+  auto stageable = [&](const KeyArgs& k) {
+    const uintptr_t align = k.dtype == BA_BF16 ? 8 : 16;
+    return k.mode == BA_BILINEAR && k.padding != BA_PAD_REFLECTION &&
+           a.xform_kind != BA_XFORM_GRID && (d.D % 4) == 0 && ((uintptr_t)k.src % align) == 0;
+  };
+  const int st_tiles = (int)(((d.D + ST_TD - 1) / ST_TD) * ((d.W + ST_TW - 1) / ST_TW));
+  const dim3 st_grid((unsigned)st_tiles, (unsigned)((d.H + ST_TH - 1) / ST_TH), (unsigned)d.batch);
+  const int st_smem = ST_MAX_FLOATS * (int)sizeof(float);
+  // returns false when (s0, s1) has no staged instantiation
+  auto launch_staged = [&](const ResampleArgs& args, int s0, int s1) -> bool {
+    switch (s0 * 16 + (s1 + 1)) {
+#define BA_ST(S0, S1)                                                            \
+  case S0 * 16 + (S1 + 1):                                                       \
+    resample3d_staged_kernel<S0, S1><<<st_grid, ST_THREADS, st_smem, st>>>(args); \
+    return true;
+#define BA_ST_KEY(P, T0)                                                               \
+  BA_ST(spec_code(BA_BILINEAR, P, T0), -1)                                             \
+  BA_ST(spec_code(BA_BILINEAR, P, T0), spec_code(BA_NEAREST, P, BA_F32))               \
+  BA_ST(spec_code(BA_BILINEAR, P, T0), spec_code(BA_NEAREST, P, BA_BF16))
+      BA_ST_KEY(BA_PAD_ZEROS, BA_F32)
+      BA_ST_KEY(BA_PAD_ZEROS, BA_BF16)
+      BA_ST_KEY(BA_PAD_BORDER, BA_F32)
+      BA_ST_KEY(BA_PAD_BORDER, BA_BF16)
+#undef BA_ST_KEY
+#undef BA_ST
+      default:
+        return false;
+    }
+  };
   // vol (bilinear) + seg (nearest) with one padding: one fused launch
   if (a.n_keys == 2) {
     KeyArgs k0 = a.keys[0], k1 = a.keys[1];
@@ -555,6 +889,9 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
       k0 = a.keys[0];
       k1 = a.keys[1];
     }
+    if (k0.mode == BA_BILINEAR && k1.mode == BA_NEAREST && k0.padding == k1.padding &&
+        stageable(k0) && launch_staged(a, code(k0), code(k1)))
+      return check_launch("ba_resample3d");
     if (k0.mode == BA_BILINEAR && k1.mode == BA_NEAREST && k0.padding == k1.padding) {
       bool launched = true;
       switch (code(k0) * 16 + code(k1)) {
@@ -580,6 +917,11 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
   one.n_keys = 1;
   for (int i = 0; i < a.n_keys; ++i) {
     one.keys[0] = a.keys[i];
+    if (stageable(one.keys[0]) && launch_staged(one, code(one.keys[0]), -1)) {
+      const ba_status s1 = check_launch("ba_resample3d");
+      if (s1 != BA_OK) return s1;
+      continue;
+    }
     switch (code(one.keys[0])) {
 #define BA_ONE(S)                                                      \
   case S:                                                              \

@@ -168,3 +168,31 @@ def test_errors_are_value_errors(ba):
     with pytest.raises(ValueError):
         # out-of-place only: dst must not alias src
         ops.resample3d(x, affine=np.eye(4, dtype=np.float32)[None].repeat(2, 0), out=[x])
+
+
+@pytest.mark.parametrize("dt", [np.float32, "bf16"])
+@pytest.mark.parametrize("pad", ["zeros", "border"])
+@pytest.mark.parametrize("align", [False, True])
+def test_staged_tiles_vs_oracle(ba, oracle_lib, dt, pad, align):
+    """Volumes spanning several partial 16x16x8 tiles with D % 4 == 0 (the
+    shared-memory staged path), one element zoomed out so far that its tiles'
+    source boxes do not fit and fall back to global gathers, and a masked-out
+    element; a nearest label key rides along in the same launch."""
+    from batchaug_b200 import ops
+    rng = np.random.default_rng(11)
+    shape = (4, 2, 21, 35, 44)
+    x = rng.standard_normal(shape).astype(np.float32)
+    if dt == "bf16":
+        x = oracle_lib.to_bf16_bits(x)
+    seg = rng.integers(0, 5, (4, 1) + shape[2:]).astype(np.float32)
+    A = _rand_affine(rng, 4)
+    A[1, :3, :3] *= 3.5  # zoom out: large source footprints
+    mask = np.array([True, True, False, True])
+    outs = ops.resample3d([to_dev(x), to_dev(seg)], affine=A, modes=["bilinear", "nearest"],
+                          paddings=pad, align_corners=align, mask=mask)
+    ref = oracle_lib.resample3d(x, affine=A, mode="bilinear", padding=pad, mask=mask,
+                                align_corners=align)
+    ref_seg = oracle_lib.resample3d(seg, affine=A, mode="nearest", padding=pad, mask=mask,
+                                    align_corners=align)
+    assert np.array_equal(to_np(outs[0]), ref)
+    assert np.array_equal(to_np(outs[1]), ref_seg)
