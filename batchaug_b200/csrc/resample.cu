@@ -89,9 +89,10 @@ struct ResampleArgs {
 // ---------------------------------------------------------------------------
 // Packed fp32x2 arithmetic (sm_100), two voxels per instruction.  A packed
 // multiply whose result feeds a packed add can come out fused into one fma
-// even under -fmad=false, so packed multiplies are used only where no add
-// follows (the weight products); multiply-then-add steps (unnormalise, the
-// tap accumulation) are scalar __fmul_rn / __fadd_rn, which are never fused.
+// even under -fmad=false, so no packed multiply feeds a packed add where the
+// fusion could change a result: the tap products are packed but summed with
+// scalar __fadd_rn, and unnormalise is packed only for power-of-two sizes
+// (where the product is exact); elsewhere it is scalar __fmul_rn / __fadd_rn.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
@@ -111,6 +112,12 @@ __device__ __forceinline__ float base_coord(int i, int n, int align_corners) {
 
 // grid_sampler_unnormalize for two voxels: align_corners ? ((c+1)/2)*(size-1)
 // : ((c+1)*size-1)/2, where /2 is the exact *0.5.
+// For a power-of-two size (c+1)*size is exact, so a fused multiply-subtract
+// gives the same result: the packed form is safe.
+__device__ __forceinline__ float2 unnormalize2_pow2(float2 c, float size) {
+  return mul2(sub2(mul2(add2(c, f2(1.0f)), f2(size)), f2(1.0f)), f2(0.5f));
+}
+
 template <bool ALIGN>
 __device__ __forceinline__ float2 unnormalize2(float2 c, float size) {
   if (ALIGN) return mul2(mul2(add2(c, f2(1.0f)), f2(0.5f)), f2(size - 1.0f));
@@ -285,12 +292,14 @@ __device__ __forceinline__ void sample_pair(const KeyArgs& k, int64_t b, int H, 
     float va[8], vb[8];
     taps8<DT>(cs, fx.lo, fy.lo, fz.lo, H, W, D, ia, va);
     taps8<DT>(cs, xb, yb, zb, H, W, D, has_b ? ib : ia, vb);
-    // out += v * w in torch's tap order
+    // out += v * w in torch's tap order: products packed, sums scalar (a
+    // packed product feeding a scalar add is never fused)
     float2 acc = f2(0.0f);
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-      acc.x = __fadd_rn(acc.x, __fmul_rn(va[t], w[t].x));
-      acc.y = __fadd_rn(acc.y, __fmul_rn(vb[t], w[t].y));
+      const float2 pr = mul2(f2(va[t], vb[t]), w[t]);
+      acc.x = __fadd_rn(acc.x, pr.x);
+      acc.y = __fadd_rn(acc.y, pr.y);
     }
     st<DT>(cd, sa, acc.x);
     if (has_b) st<DT>(cd, sb, acc.y);
@@ -415,6 +424,7 @@ __global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
   }
   const float2 by2 = f2(by);
   const float fD = (float)D, fW = (float)W, fH = (float)H;
+  const bool pD = (D & (D - 1)) == 0, pW = (W & (W - 1)) == 0, pH = (H & (H - 1)) == 0;
   for (int nb = 0; nb < NB; ++nb) {
     const int h = h_first + nb * TZ + tz;
     if (h >= H) break;
@@ -447,9 +457,9 @@ __global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
           sample_spec<(S1 < 0 ? 0 : S1), true>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da,
                                                row + db, has_b);
       } else {
-        const float2 ix = unnormalize2<false>(g[0], fD);
-        const float2 iy = unnormalize2<false>(g[1], fW);
-        const float2 iz = unnormalize2<false>(g[2], fH);
+        const float2 ix = pD ? unnormalize2_pow2(g[0], fD) : unnormalize2<false>(g[0], fD);
+        const float2 iy = pW ? unnormalize2_pow2(g[1], fW) : unnormalize2<false>(g[1], fW);
+        const float2 iz = pH ? unnormalize2_pow2(g[2], fH) : unnormalize2<false>(g[2], fH);
         sample_spec<S0, false>(a.keys[0], b, H, W, D, hwd, ix, iy, iz, row + da, row + db, has_b);
         if (S1 >= 0)
           sample_spec<(S1 < 0 ? 0 : S1), false>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da,
@@ -463,7 +473,7 @@ __global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
 // Staged resample: the source footprint of each output tile in shared memory.
 //
 // For affine maps (bilinear key, zeros or border padding) a CTA covers a
-// 16(D) x 8(W) x 8(H) output tile.  Its prologue maps the tile's 8 corners
+// 16(D) x 16(W) x 8(H) output tile.  Its prologue maps the tile's 8 corners
 // to source voxels and takes their bounding box (the corner coordinates bound
 // all others up to rounding, far below the 0.01-voxel slack used), and, when
 // the box fits ST_MAX_FLOATS floats, copies it into shared memory with 16-byte
@@ -476,20 +486,20 @@ __global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
 // from global memory with the same coordinates.
 // ===========================================================================
 #ifndef BA_ST_TW
-#define BA_ST_TW 8
+#define BA_ST_TW 16
 #endif
 #ifndef BA_ST_TH
 #define BA_ST_TH 8
 #endif
 #ifndef BA_ST_MAX_FLOATS
-#define BA_ST_MAX_FLOATS 8192
+#define BA_ST_MAX_FLOATS 12288
 #endif
 #ifndef BA_ST_MINBLOCKS
-#define BA_ST_MINBLOCKS 5
+#define BA_ST_MINBLOCKS 4
 #endif
 constexpr int ST_TD = 16, ST_TW = BA_ST_TW, ST_TH = BA_ST_TH;
 constexpr int ST_THREADS = 128;
-constexpr int ST_MAX_FLOATS = BA_ST_MAX_FLOATS;  // 32 KB of staged source
+constexpr int ST_MAX_FLOATS = BA_ST_MAX_FLOATS;  // 48 KB of staged source
 constexpr int ST_PW = ST_TW / 2, ST_PH = ST_TH / 8;
 static_assert(ST_TW % 2 == 0 && ST_TH % 8 == 0, "tile covered by the thread layout");
 
@@ -631,7 +641,7 @@ __global__ void __launch_bounds__(ST_THREADS, BA_ST_MINBLOCKS)
     t3[r] = f2(s_theta[r * 4 + 3]);
   }
   const float fD = (float)D, fW = (float)W, fH = (float)H;
-
+  const bool pD = (D & (D - 1)) == 0, pW = (W & (W - 1)) == 0, pH = (H & (H - 1)) == 0;
   for (int c = 0; c < k.channels; ++c) {
     const char* src_c = (const char*)k.src + ((size_t)b * k.channels + c) * hwd * esz;
     char* dst_c = (char*)k.dst + ((size_t)b * k.channels + c) * hwd * esz;
@@ -687,9 +697,9 @@ __global__ void __launch_bounds__(ST_THREADS, BA_ST_MINBLOCKS)
         iy = unnormalize2<true>(g[1], fW);
         iz = unnormalize2<true>(g[2], fH);
       } else {
-        ix = unnormalize2<false>(g[0], fD);
-        iy = unnormalize2<false>(g[1], fW);
-        iz = unnormalize2<false>(g[2], fH);
+        ix = pD ? unnormalize2_pow2(g[0], fD) : unnormalize2<false>(g[0], fD);
+        iy = pW ? unnormalize2_pow2(g[1], fW) : unnormalize2<false>(g[1], fW);
+        iz = pH ? unnormalize2_pow2(g[2], fH) : unnormalize2<false>(g[2], fH);
       }
       const float2 px = ALIGN ? pad2<PAD, true>(ix, D) : pad2<PAD, false>(ix, D);
       const float2 py = ALIGN ? pad2<PAD, true>(iy, W) : pad2<PAD, false>(iy, W);
@@ -750,8 +760,10 @@ __global__ void __launch_bounds__(ST_THREADS, BA_ST_MINBLOCKS)
       float2 acc = f2(0.0f);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        acc.x = __fadd_rn(acc.x, __fmul_rn(va[q], wt[q].x));
-        acc.y = __fadd_rn(acc.y, __fmul_rn(vb[q], wt[q].y));
+        // products packed, sums scalar (never fused), in torch's tap order
+        const float2 pr = mul2(f2(va[q], vb[q]), wt[q]);
+        acc.x = __fadd_rn(acc.x, pr.x);
+        acc.y = __fadd_rn(acc.y, pr.y);
       }
       st<DT>(dst_c, row + da, acc.x);
       if (has_b) st<DT>(dst_c, row + db, acc.y);
@@ -761,6 +773,18 @@ __global__ void __launch_bounds__(ST_THREADS, BA_ST_MINBLOCKS)
   (void)MODE;
 }
 
+
+// Opt the staged kernel in to its dynamic shared memory once per process
+// (needed above 48 KB; idempotent, so concurrent first calls are harmless).
+template <int S0, int S1>
+void allow_staged_smem(int bytes) {
+  static bool done = false;
+  if (!done) {
+    cudaFuncSetAttribute(resample3d_staged_kernel<S0, S1>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    done = true;
+  }
+}
 
 bool overlaps(const void* a, size_t na, const void* b, size_t nb) {
   const char* pa = (const char*)a;
@@ -864,6 +888,7 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
     switch (s0 * 16 + (s1 + 1)) {
 #define BA_ST(S0, S1)                                                            \
   case S0 * 16 + (S1 + 1):                                                       \
+    allow_staged_smem<S0, S1>(st_smem);                                          \
     resample3d_staged_kernel<S0, S1><<<st_grid, ST_THREADS, st_smem, st>>>(args); \
     return true;
 #define BA_ST_KEY(P, T0)                                                               \

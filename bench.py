@@ -308,7 +308,7 @@ def run_b200(args):
                     "d2h_bytes_per_step": VOXELS * 4, "steps": e2e_steps,
                     "copies": "pinned host buffers, upload/download on their own streams, "
                               "double-buffered"},
-            "roofline": {"bound": "hbm", "kernel": "resample3d_kernel",
+            "roofline": {"bound": "hbm", "kernel": "resample3d_staged_kernel",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
                          "traffic": traffic, "algorithmic_bytes_per_launch": alg_bytes,
