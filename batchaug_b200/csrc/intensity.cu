@@ -224,7 +224,7 @@ __device__ __forceinline__ void resolve_op(const ChainArgs& a, int oi, int64_t b
       o.k1 = rng;
       o.k2 = rng + 1e-7f;
       o.k3 = op.param[b];  // gamma
-      o.k4 = recip_for_div(o.k2);
+      o.k4 = 1.0f / o.k2;
       o.k5 = powf(0.0f, o.k3);  // 0^gamma, taken apart from the fast power below
       break;
     }
@@ -329,7 +329,9 @@ __device__ __forceinline__ void apply_one(const ChainArgs& a, int oi, const OpCo
         if (!on) break;
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
-          float nrm = div_rn(v[i] - k.k0, k.k2, k.k4);
+          // the power below is approximate (a few fp32 ulp), so the
+          // normalisation takes the reciprocal instead of a rounded division
+          float nrm = (v[i] - k.k0) * k.k4;
           nrm = (nrm < 0.0f) ? 0.0f : nrm;
           // nrm in [0, 1]: the hardware exp2(gamma * log2(nrm)) power is
           // within a few fp32 ulp there (far inside the op's tolerance)
@@ -960,7 +962,6 @@ extern "C" ba_status ba_intensity_chain(const ba_chain_desc* desc, void* workspa
     if (st != BA_OK) return st;
   }
 
-  const size_t esz = d.dtype == BA_BF16 ? 2 : 4;
   const int vec = d.dtype == BA_BF16 ? 8 : 4;
   const bool vec_ok = (HWD % vec) == 0 && ((uintptr_t)d.src % 16) == 0 &&
                       ((uintptr_t)d.dst % 16) == 0 &&

@@ -451,6 +451,13 @@ def _secondary(name, torch, ba, device, rank):
         n = vol.numel()
         return ("RandGaussianSmooth(prob=1, sigma 0.5..1.5) on config 5's vol shard "
                 "(8x2x160^3 bf16)", lambda i: sm.apply(vol, p), n, n * 4)
+    if name == "config5-elastic":
+        el = ba.Rand3DElastic(prob=1.0, sigma_range=(5, 7), magnitude_range=(50, 150))
+        shape = (8, 2, 160, 160, 160)
+        n = 8 * 160 ** 3
+        return ("Rand3DElastic.sample_params (sigma 5..7, magnitude 50..150) for config 5's "
+                "per-GPU shard: Philox field, separable Gaussian (K=43), grid 8x160^3x3 fp32",
+                lambda i: el.sample_params(8, shape, device), n, n * 12)
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -522,7 +529,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="config2",
-                    choices=["config2", "config3", "config4", "config5", "config5-smooth"],
+                    choices=["config2", "config3", "config4", "config5", "config5-smooth",
+                             "config5-elastic"],
                     help="config2 is the headline; the others time one whole step of that "
                          "configuration (for profiling and per-config numbers)")
     args = ap.parse_args()
