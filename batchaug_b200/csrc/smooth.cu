@@ -200,7 +200,8 @@ constexpr int TS_TH = 64;   // pass B tile extent along H
 constexpr int TS_RH = 8;    // pass B H-outputs per thread (TS_TH / TS_RH = 8 groups)
 constexpr int TILE_KMAX = 63;
 constexpr int MAX_COLS = TS_TD + TILE_KMAX - 1;
-constexpr int MAX_ROWS = 64 + TILE_KMAX - 1;
+constexpr int MAX_ROWS = TS_TH + TILE_KMAX - 1;  // pass B rows with halo
+static_assert(TS_TH == (TS_THREADS / TB_TD) * TS_RH, "pass B: one run of TS_RH rows per thread group");
 
 // Tile extent along W of pass A: wider tiles for wide kernels keep the
 // D-pass halo rows (KMAX-1 of them) a small fraction of the work.
