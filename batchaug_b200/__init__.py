@@ -43,10 +43,16 @@ from .intensity import (
     RandGaussianNoised,
     RandGaussianSmooth,
     RandGaussianSmoothd,
+    RandRicianNoise,
+    RandRicianNoised,
     RandScaleIntensity,
     RandScaleIntensityd,
+    RandScaleIntensityFixedMean,
+    RandScaleIntensityFixedMeand,
     RandShiftIntensity,
     RandShiftIntensityd,
+    RandStdShiftIntensity,
+    RandStdShiftIntensityd,
     ScaleIntensity,
     ScaleIntensityd,
 )
@@ -76,6 +82,8 @@ __all__ = [
     "RandRotate90d", "RandZoom", "RandZoomd",
     "RandAdjustContrast", "RandAdjustContrastd", "RandBiasField", "RandBiasFieldd",
     "RandGaussianNoise", "RandGaussianNoised", "RandGaussianSmooth", "RandGaussianSmoothd",
-    "RandScaleIntensity", "RandScaleIntensityd", "RandShiftIntensity", "RandShiftIntensityd",
+    "RandRicianNoise", "RandRicianNoised", "RandScaleIntensity", "RandScaleIntensityd",
+    "RandScaleIntensityFixedMean", "RandScaleIntensityFixedMeand", "RandShiftIntensity",
+    "RandShiftIntensityd", "RandStdShiftIntensity", "RandStdShiftIntensityd",
     "ScaleIntensity", "ScaleIntensityd",
 ]

@@ -26,7 +26,10 @@ BA_MAX_OPS = 8
 BA_NOALLOC_CHAIN_SCRATCH = 262144  # bytes of the static scratch of ba_intensity_chain_noalloc
 
 BA_OP_NOISE, BA_OP_CONTRAST, BA_OP_SCALE, BA_OP_SHIFT, BA_OP_BIAS_FIELD, BA_OP_RESCALE = 1, 2, 3, 4, 5, 6
+BA_OP_RICIAN, BA_OP_STD_SHIFT, BA_OP_FIXED_MEAN = 7, 8, 9
 BA_NOISE_PHILOX = 0x1
+BA_RICIAN_PHILOX, BA_RICIAN_RELATIVE = 0x1, 0x2
+BA_STD_NONZERO, BA_STAT_CHANNEL = 0x2, 0x4
 BA_SHIFT_SAFE = 0x1
 BA_RESCALE_MINV, BA_RESCALE_MAXV, BA_RESCALE_CHANNEL, BA_RESCALE_FACTOR = 0x1, 0x2, 0x4, 0x8
 

@@ -38,6 +38,9 @@ S_SHIFT = 9
 S_BIAS = 10
 S_SMOOTH = 11
 S_ZOOM = 12
+S_RICIAN = 13
+S_STD_SHIFT = 14
+S_FIXED_MEAN = 15
 
 
 def set_shard(element_offset: int = 0, global_batch: int | None = None) -> None:

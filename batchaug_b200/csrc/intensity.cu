@@ -51,12 +51,16 @@ struct OpArgs {
   const float* param;
   const float* param2;
   const float* noise;
-  const int32_t* stats_in;  // keys (groups, 2) the op reads (CONTRAST, RESCALE)
+  const int32_t* stats_in;     // keys (groups, 2) the op reads (CONTRAST, RESCALE)
+  const double* moments_in;    // (groups, 3): sum, sum of squares, nonzero count
+                               // (STD_SHIFT, FIXED_MEAN, relative RICIAN)
+  int64_t moments_n;           // values per moments group
   int32_t stats_per_channel;
   int32_t degree;
   uint32_t seed_lo, seed_hi;
   uint64_t elem_offset;
   float minv, span, factor1p;  // RESCALE constants as the reference rounds them
+  float mean;                  // RICIAN noise mean
 };
 
 struct ChainArgs {
@@ -66,8 +70,10 @@ struct ChainArgs {
   int32_t b0;       // first element of this launch
   int32_t n_ops;
   int32_t stats_mode;  // 0: none, 1: per element, 2: per (element, channel)
+  int32_t stats_moments;  // 0: min/max keys, 1: moments
   int64_t tile;        // spatial positions per CTA (multiple of VEC)
   int32_t* stats_out;  // keys (groups, 2)
+  double* moments_out;  // moments (groups, 3)
   OpArgs ops[BA_MAX_OPS];
 };
 
@@ -200,6 +206,19 @@ __device__ __forceinline__ float div_for_bf16(float a, float b, float y) {
   return __fdiv_rn(a, b);
 }
 
+// torch.std (unbiased) of a group from its moments (sum, sum of squares,
+// nonzero count) in double; with nonzero, of the nonzero values when there
+// are at least two of them (scale_shift.py:174-189).  Fewer than two values:
+// NaN, as torch gives.
+__device__ __forceinline__ float moment_std(const double* m, int64_t g, int64_t n, bool nonzero) {
+  const double s = m[3 * g], ss = m[3 * g + 1], nnz = m[3 * g + 2];
+  const double cnt = (nonzero && nnz > 1.0) ? nnz : (double)n;
+  if (cnt < 2.0) return __int_as_float(0x7FC00000);
+  double v = (ss - s * (s / cnt)) / (cnt - 1.0);
+  v = v < 0.0 ? 0.0 : v;
+  return (float)sqrt(v);
+}
+
 template <int DT>
 __device__ __forceinline__ void resolve_op(const ChainArgs& a, int oi, int64_t b, int64_t c,
                                            OpConst& o) {
@@ -256,6 +275,24 @@ __device__ __forceinline__ void resolve_op(const ChainArgs& a, int oi, int64_t b
         o.packed = is_bf16_value(op.factor1p);
       }
       break;
+    case BA_OP_RICIAN: {
+      float sd = op.param[b];
+      if (op.flags & BA_RICIAN_RELATIVE) sd = sd * moment_std(op.moments_in, b, op.moments_n, false);
+      o.k0 = sd;
+      o.k1 = op.mean;
+      break;
+    }
+    case BA_OP_STD_SHIFT: {
+      const int64_t g = op.stats_per_channel ? b * a.C + c : b;
+      o.k0 = op.param[b] * moment_std(op.moments_in, g, op.moments_n, op.flags & BA_STD_NONZERO);
+      break;
+    }
+    case BA_OP_FIXED_MEAN: {
+      const int64_t g = op.stats_per_channel ? b * a.C + c : b;
+      o.k0 = (float)(op.moments_in[3 * g] / (double)op.moments_n);
+      o.k1 = 1.0f + op.param[b];
+      break;
+    }
     default:
       break;
   }
@@ -372,6 +409,70 @@ __device__ __forceinline__ void apply_one(const ChainArgs& a, int oi, const OpCo
         }
 #pragma unroll
         for (int i = 0; i < VEC; ++i) v[i] = round_dt<DT>(t[i]);
+        break;
+      }
+      case BA_OP_RICIAN: {
+        // sqrt((x + n1)^2 + n2^2), n = mean + std * u in fp32 (noise.py:146-164)
+        if (!on) break;
+        float u1[VEC], u2[VEC];
+        if (op.flags & BA_RICIAN_PHILOX) {
+          // u of flat position p = c*HWD + s of element b is normal (p & 3)
+          // of Philox block (seed; p >> 2, element, RICIAN1 / RICIAN2 stream)
+          const uint64_t eb = op.elem_offset + (uint64_t)b;
+          const int64_t first = c * a.HWD + s0;
+#pragma unroll
+          for (int base = 0; base < (VEC >= 4 ? VEC : 4); base += 4) {
+            const uint64_t q = (uint64_t)(first + (VEC >= 4 ? base : 0)) >> 2;
+            const U4 c1 = {(uint32_t)q, (uint32_t)eb, (uint32_t)(eb >> 32),
+                           STREAM_RICIAN1 | (uint32_t)(q >> 32)};
+            const U4 c2 = {(uint32_t)q, (uint32_t)eb, (uint32_t)(eb >> 32),
+                           STREAM_RICIAN2 | (uint32_t)(q >> 32)};
+            float z1[4], z2[4];
+            normal4(philox4x32_10(c1, op.seed_lo, op.seed_hi), z1);
+            normal4(philox4x32_10(c2, op.seed_lo, op.seed_hi), z2);
+            if (VEC >= 4) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                if (base + i < VEC) {
+                  u1[base + i] = z1[i];
+                  u2[base + i] = z2[i];
+                }
+            } else {
+              const int l = (int)(first & 3);
+              u1[0] = l == 0 ? z1[0] : (l == 1 ? z1[1] : (l == 2 ? z1[2] : z1[3]));
+              u2[0] = l == 0 ? z2[0] : (l == 1 ? z2[1] : (l == 2 ? z2[2] : z2[3]));
+            }
+          }
+        } else {
+          const int64_t off = (b * a.C + c) * a.HWD + s0;
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) {
+            u1[i] = (i < n) ? __ldg(op.noise + off + i) : 0.0f;
+            u2[i] = (i < n) ? __ldg(op.param2 + off + i) : 0.0f;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          const float n1 = __fadd_rn(__fmul_rn(k.k0, u1[i]), k.k1);
+          const float n2 = __fadd_rn(__fmul_rn(k.k0, u2[i]), k.k1);
+          const float x1 = __fadd_rn(v[i], n1);
+          v[i] = round_dt<DT>(__fsqrt_rn(__fadd_rn(__fmul_rn(x1, x1), __fmul_rn(n2, n2))));
+        }
+        break;
+      }
+      case BA_OP_STD_SHIFT: {
+        // x + factor * std, fp32, one cast (scale_shift.py:168-198)
+        if (!on) break;
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) v[i] = round_dt<DT>(__fadd_rn(v[i], k.k0));
+        break;
+      }
+      case BA_OP_FIXED_MEAN: {
+        // mean + (x - mean) * (1 + factor), fp32, one cast (scale_shift.py:252-274)
+        if (!on) break;
+#pragma unroll
+        for (int i = 0; i < VEC; ++i)
+          v[i] = round_dt<DT>(__fadd_rn(k.k0, __fmul_rn(__fsub_rn(v[i], k.k0), k.k1)));
         break;
       }
       case BA_OP_RESCALE: {
@@ -594,6 +695,58 @@ __device__ __forceinline__ void fold_minmax(const float* v, int n, float& mn, fl
   }
 }
 
+// Per-thread moments of a segment's results (STD_SHIFT, FIXED_MEAN and
+// relative RICIAN read the mean / std of their input): each chunk is summed
+// in fp32, the chunk sums are accumulated in double.
+struct Moments {
+  double s, ss, nz;
+};
+
+template <int VEC>
+__device__ __forceinline__ void fold_moments(const float* v, int n, Moments& mo) {
+  float cs = 0.0f, css = 0.0f, cnz = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    if (i < n) {
+      cs = __fadd_rn(cs, v[i]);
+      css = __fmaf_rn(v[i], v[i], css);
+      cnz = __fadd_rn(cnz, v[i] != 0.0f ? 1.0f : 0.0f);
+    }
+  }
+  mo.s += (double)cs;
+  mo.ss += (double)css;
+  mo.nz += (double)cnz;
+}
+
+// Block-wide sum of the moments followed by one atomic per quantity.
+__device__ __forceinline__ void block_moments_commit(Moments mo, double* out) {
+  __shared__ double s_m[3][CHAIN_THREADS / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mo.s += __shfl_xor_sync(0xFFFFFFFFu, mo.s, o);
+    mo.ss += __shfl_xor_sync(0xFFFFFFFFu, mo.ss, o);
+    mo.nz += __shfl_xor_sync(0xFFFFFFFFu, mo.nz, o);
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  __syncthreads();
+  if (lane == 0) {
+    s_m[0][warp] = mo.s;
+    s_m[1][warp] = mo.ss;
+    s_m[2][warp] = mo.nz;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < CHAIN_THREADS / 32; ++i) {
+      mo.s += s_m[0][i];
+      mo.ss += s_m[1][i];
+      mo.nz += s_m[2][i];
+    }
+    atomicAdd(out, mo.s);
+    atomicAdd(out + 1, mo.ss);
+    atomicAdd(out + 2, mo.nz);
+  }
+}
+
 // 16 bytes <-> VEC floats of the dtype.
 template <int DT, int VEC>
 __device__ __forceinline__ void unpack16(const uint4& t, float* v) {
@@ -633,7 +786,8 @@ __device__ __forceinline__ uint4 pack16(const float* v) {
 template <int DT, int VEC, bool WRITE>
 __device__ __forceinline__ void run_range_vec(const ChainArgs& a, const OpConst* oc, int64_t b,
                                               int64_t c, int64_t s_begin, int64_t s_end,
-                                              bool stats, float& mn, float& mx, uint4* ring) {
+                                              bool stats, float& mn, float& mx, Moments& mo,
+                                              uint4* ring) {
   const int tid = threadIdx.x;
   const int64_t n_chunks = (s_end - s_begin) / VEC;
   const int64_t base = (b * a.C + c) * a.HWD + s_begin;
@@ -660,13 +814,26 @@ __device__ __forceinline__ void run_range_vec(const ChainArgs& a, const OpConst*
       uint32_t w[4] = {t.x, t.y, t.z, t.w};
       apply_ops_bf16x8(a, oc, b, c, s_begin + j * VEC, w);
       if (WRITE) dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
-      if (stats) fold_minmax_bf16x8(w, mn2, mx2);
+      if (stats) {
+        if (a.stats_moments) {
+          float v[8];
+          unpack_words(w, v);
+          fold_moments<8>(v, 8, mo);
+        } else {
+          fold_minmax_bf16x8(w, mn2, mx2);
+        }
+      }
     } else {
       float v[VEC];
       unpack16<DT, VEC>(ring[slot * CHAIN_THREADS + tid], v);
       apply_ops<DT, VEC>(a, oc, b, c, s_begin + j * VEC, VEC, v);
       if (WRITE) dst[j] = pack16<DT, VEC>(v);
-      if (stats) fold_minmax<VEC>(v, VEC, mn, mx);
+      if (stats) {
+        if (a.stats_moments)
+          fold_moments<VEC>(v, VEC, mo);
+        else
+          fold_minmax<VEC>(v, VEC, mn, mx);
+      }
     }
     slot = slot + 1 == CHAIN_PIPE ? 0 : slot + 1;
   }
@@ -682,14 +849,20 @@ __device__ __forceinline__ void run_range_vec(const ChainArgs& a, const OpConst*
 template <int DT, bool WRITE>
 __device__ __forceinline__ void run_range_scalar(const ChainArgs& a, const OpConst* oc,
                                                  int64_t b, int64_t c, int64_t s_begin,
-                                                 int64_t s_end, bool stats, float& mn, float& mx) {
+                                                 int64_t s_end, bool stats, float& mn, float& mx,
+                                                 Moments& mo) {
   const int64_t base = (b * a.C + c) * a.HWD;
   for (int64_t s = s_begin + threadIdx.x; s < s_end; s += CHAIN_THREADS) {
     float v[1];
     v[0] = load_f(a.src, DT, base + s);
     apply_ops<DT, 1>(a, oc, b, c, s, 1, v);
     if (WRITE) store_f(a.dst, DT, base + s, v[0]);
-    if (stats) fold_minmax<1>(v, 1, mn, mx);
+    if (stats) {
+      if (a.stats_moments)
+        fold_moments<1>(v, 1, mo);
+      else
+        fold_minmax<1>(v, 1, mn, mx);
+    }
   }
 }
 
@@ -709,14 +882,19 @@ __global__ void __launch_bounds__(CHAIN_THREADS, chain_minblocks<DT>())
   if (threadIdx.x < a.n_ops) resolve_op<DT>(a, threadIdx.x, b, c, s_oc[threadIdx.x]);
   __syncthreads();
   float mn = INFINITY, mx = -INFINITY;
+  Moments mo = {0.0, 0.0, 0.0};
   if (VEC > 1)
-    run_range_vec<DT, VEC, WRITE>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx, s_ring);
+    run_range_vec<DT, VEC, WRITE>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx, mo,
+                                  s_ring);
   else
-    run_range_scalar<DT, WRITE>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx);
-  if (a.stats_mode == 2)
-    block_minmax_commit(mn, mx, a.stats_out + 2 * (b * a.C + c));
-  else if (a.stats_mode == 1)
-    block_minmax_commit(mn, mx, a.stats_out + 2 * b);
+    run_range_scalar<DT, WRITE>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx, mo);
+  if (a.stats_mode != 0) {
+    const int64_t g = a.stats_mode == 2 ? b * a.C + c : b;
+    if (a.stats_moments)
+      block_moments_commit(mo, a.moments_out + 3 * g);
+    else
+      block_minmax_commit(mn, mx, a.stats_out + 2 * g);
+  }
 }
 
 __global__ void init_keys_kernel(int32_t* keys, int64_t n_groups) {
@@ -819,22 +997,38 @@ int64_t pick_tile(int64_t positions, int64_t n_blocks_y, int vec) {
   return tile;
 }
 
+// Ops that read statistics of their own input: min/max (CONTRAST, min/max
+// RESCALE) or moments (STD_SHIFT, FIXED_MEAN, relative RICIAN).
+bool needs_moments(const ba_op& op) {
+  return op.kind == BA_OP_STD_SHIFT || op.kind == BA_OP_FIXED_MEAN ||
+         (op.kind == BA_OP_RICIAN && (op.flags & BA_RICIAN_RELATIVE));
+}
+
 bool needs_stats(const ba_op& op) {
-  if (op.kind == BA_OP_CONTRAST) return true;
+  if (op.kind == BA_OP_CONTRAST || needs_moments(op)) return true;
   if (op.kind == BA_OP_RESCALE)
     return !(op.flags & BA_RESCALE_FACTOR) && (op.flags & (BA_RESCALE_MINV | BA_RESCALE_MAXV));
   return false;
 }
 
-int64_t stats_groups(const ba_op& op, int64_t B, int64_t C) {
-  if (op.kind == BA_OP_RESCALE && (op.flags & BA_RESCALE_CHANNEL)) return B * C;
-  return B;
+bool stats_per_channel(const ba_op& op) {
+  if (op.kind == BA_OP_RESCALE) return op.flags & BA_RESCALE_CHANNEL;
+  if (op.kind == BA_OP_STD_SHIFT || op.kind == BA_OP_FIXED_MEAN) return op.flags & BA_STAT_CHANNEL;
+  return false;
 }
+
+int64_t stats_groups(const ba_op& op, int64_t B, int64_t C) {
+  return stats_per_channel(op) ? B * C : B;
+}
+
+// int32 words of workspace per statistics group: two order-preserving keys
+// (min/max) or three doubles (moments).
+int64_t stats_words(const ba_op& op) { return needs_moments(op) ? 6 : 2; }
 
 struct Segment {
   int first, last;      // ops [first, last)
   int stats_for;        // op index whose stats this segment produces, -1 none
-  int64_t stats_offset;  // int32 offset of those keys in the workspace
+  int64_t stats_offset;  // int32 offset of those stats in the workspace (8-byte aligned)
 };
 
 ba_status validate_chain(const ba_chain_desc* d) {
@@ -849,7 +1043,7 @@ ba_status validate_chain(const ba_chain_desc* d) {
              d->n_ops, BA_MAX_OPS);
   for (int i = 0; i < d->n_ops; ++i) {
     const ba_op& op = d->ops[i];
-    BA_REQUIRE(op.kind >= BA_OP_NOISE && op.kind <= BA_OP_RESCALE,
+    BA_REQUIRE(op.kind >= BA_OP_NOISE && op.kind <= BA_OP_FIXED_MEAN,
                "ba_intensity_chain: op %d unknown kind %d", i, op.kind);
     switch (op.kind) {
       case BA_OP_NOISE:
@@ -864,6 +1058,16 @@ ba_status validate_chain(const ba_chain_desc* d) {
       case BA_OP_SCALE:
       case BA_OP_SHIFT:
         BA_REQUIRE(op.param, "ba_intensity_chain: op %d needs its per-element parameter", i);
+        break;
+      case BA_OP_RICIAN:
+        BA_REQUIRE(op.param, "ba_intensity_chain: op %d RICIAN needs noise_std", i);
+        if (!(op.flags & BA_RICIAN_PHILOX))
+          BA_REQUIRE(op.noise && op.param2,
+                     "ba_intensity_chain: op %d RICIAN needs injected u1 and u2", i);
+        break;
+      case BA_OP_STD_SHIFT:
+      case BA_OP_FIXED_MEAN:
+        BA_REQUIRE(op.param, "ba_intensity_chain: op %d needs its per-element factor", i);
         break;
       case BA_OP_BIAS_FIELD:
         BA_REQUIRE(op.param, "ba_intensity_chain: op %d BIAS_FIELD needs coefficients", i);
@@ -903,8 +1107,9 @@ void plan_segments(const ba_chain_desc* d, std::vector<Segment>& segs, int64_t& 
     s.stats_for = (i < d->n_ops) ? i : -1;
     s.stats_offset = 0;
     if (s.stats_for >= 0) {
+      ws_ints = (ws_ints + 1) & ~(int64_t)1;  // doubles stay 8-byte aligned
       s.stats_offset = ws_ints;
-      ws_ints += 2 * stats_groups(d->ops[i], d->batch, d->channels);
+      ws_ints += stats_words(d->ops[i]) * stats_groups(d->ops[i], d->batch, d->channels);
     }
     segs.push_back(s);
     first = i;
@@ -955,21 +1160,37 @@ extern "C" ba_status ba_intensity_chain(const ba_chain_desc* desc, void* workspa
   if (d.batch * d.channels * HWD == 0) return BA_OK;
   cudaStream_t cs = (cudaStream_t)stream;
   int32_t* keys = (int32_t*)workspace;
-  if (ws_ints > 0) {
-    init_keys_kernel<<<(unsigned)std::min<int64_t>((ws_ints / 2 + 255) / 256, 1024), 256, 0, cs>>>(
-        keys, ws_ints / 2);
-    st = check_launch("ba_intensity_chain");
-    if (st != BA_OK) return st;
+  for (const Segment& sg : segs) {
+    if (sg.stats_for < 0) continue;
+    const ba_op& op = d.ops[sg.stats_for];
+    const int64_t groups = stats_groups(op, d.batch, d.channels);
+    if (needs_moments(op)) {
+      if (cudaMemsetAsync(keys + sg.stats_offset, 0, (size_t)groups * 3 * sizeof(double), cs) !=
+          cudaSuccess) {
+        set_error("ba_intensity_chain: clearing the statistics failed");
+        return BA_ECUDA;
+      }
+    } else {
+      init_keys_kernel<<<(unsigned)std::min<int64_t>((groups + 255) / 256, 1024), 256, 0, cs>>>(
+          keys + sg.stats_offset, groups);
+      st = check_launch("ba_intensity_chain");
+      if (st != BA_OK) return st;
+    }
   }
 
   const int vec = d.dtype == BA_BF16 ? 8 : 4;
   const bool vec_ok = (HWD % vec) == 0 && ((uintptr_t)d.src % 16) == 0 &&
                       ((uintptr_t)d.dst % 16) == 0 &&
                       [&] {
-                        for (int i = 0; i < d.n_ops; ++i)
-                          if (d.ops[i].kind == BA_OP_NOISE &&
-                              !(d.ops[i].flags & BA_NOISE_PHILOX))
-                            return ((uintptr_t)d.ops[i].noise % 16) == 0;
+                        for (int i = 0; i < d.n_ops; ++i) {
+                          const ba_op& op = d.ops[i];
+                          if (op.kind == BA_OP_NOISE && !(op.flags & BA_NOISE_PHILOX) &&
+                              ((uintptr_t)op.noise % 16) != 0)
+                            return false;
+                          if (op.kind == BA_OP_RICIAN && !(op.flags & BA_RICIAN_PHILOX) &&
+                              (((uintptr_t)op.noise % 16) != 0 || ((uintptr_t)op.param2 % 16) != 0))
+                            return false;
+                        }
                         return true;
                       }();
 
@@ -1013,20 +1234,31 @@ extern "C" ba_status ba_intensity_chain(const ba_chain_desc* desc, void* workspa
         o.minv = (float)op.c0;
         o.span = (float)(op.c1 - op.c0);
         o.factor1p = (float)(1.0 + op.c0);
+        o.mean = (float)op.c0;
         if (needs_stats(op)) {
           // Stats come from the previous segment.
           const Segment& prev = segs[si - 1];
-          o.stats_in = keys + prev.stats_offset;
-          o.stats_per_channel =
-              (op.kind == BA_OP_RESCALE && (op.flags & BA_RESCALE_CHANNEL)) ? 1 : 0;
+          o.stats_per_channel = stats_per_channel(op) ? 1 : 0;
+          if (needs_moments(op)) {
+            o.moments_in = (const double*)(keys + prev.stats_offset);
+            o.moments_n = o.stats_per_channel ? HWD : d.channels * HWD;
+          } else {
+            o.stats_in = keys + prev.stats_offset;
+          }
         }
       }
       a.stats_out = nullptr;
+      a.moments_out = nullptr;
       a.stats_mode = 0;
+      a.stats_moments = 0;
       if (sg.stats_for >= 0) {
         const ba_op& nx = d.ops[sg.stats_for];
-        a.stats_out = keys + sg.stats_offset;
-        a.stats_mode = (nx.kind == BA_OP_RESCALE && (nx.flags & BA_RESCALE_CHANNEL)) ? 2 : 1;
+        a.stats_mode = stats_per_channel(nx) ? 2 : 1;
+        a.stats_moments = needs_moments(nx) ? 1 : 0;
+        if (a.stats_moments)
+          a.moments_out = (double*)(keys + sg.stats_offset);
+        else
+          a.stats_out = keys + sg.stats_offset;
       }
       if (!write && a.stats_mode == 0) continue;
       if (d.dtype == BA_BF16)

@@ -97,5 +97,7 @@ __device__ __forceinline__ void normal4(U4 r, float* z) {
 constexpr uint32_t STREAM_NOISE = 0x4E4F0000u;    // Gaussian noise volume
 constexpr uint32_t STREAM_ELASTIC = 0x454C0000u;  // elastic uniform field
 constexpr uint32_t STREAM_PARAMS = 0x50410000u;   // per-element scalar params
+constexpr uint32_t STREAM_RICIAN1 = 0x52310000u;  // Rician noise, first component
+constexpr uint32_t STREAM_RICIAN2 = 0x52320000u;  // Rician noise, second component
 
 }  // namespace ba

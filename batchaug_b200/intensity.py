@@ -1,6 +1,7 @@
-"""Intensity transforms: RandGaussianNoise, RandAdjustContrast,
-RandScaleIntensity, RandShiftIntensity, RandBiasField, ScaleIntensity,
-RandGaussianSmooth (+ dict wrappers).
+"""Intensity transforms: RandGaussianNoise, RandRicianNoise,
+RandAdjustContrast, RandScaleIntensity, RandShiftIntensity,
+RandStdShiftIntensity, RandScaleIntensityFixedMean, RandBiasField,
+ScaleIntensity, RandGaussianSmooth (+ dict wrappers).
 
 Constructors, params keys and results follow the reference PyTorch backend
 (batchaug/pytorch/intensity/*.py), op by op in the tensor dtype.  Each
@@ -8,10 +9,13 @@ Constructors, params keys and results follow the reference PyTorch backend
 ``Compose`` fuses consecutive transforms of this module into a single chain
 per key (see :meth:`_FusibleIntensity.chain_op`).
 
-Gaussian noise is generated in-kernel from the params' ``noise_seed``
-(Philox4x32-10 keyed on the global element index and voxel position) and is
-never materialised; params holding an explicit ``"noise"`` tensor (the
-reference's params, or a test's injected noise) are applied as given.
+Gaussian (and Rician) noise is generated in-kernel from the params'
+``noise_seed`` (Philox4x32-10 keyed on the global element index and voxel
+position) and is never materialised; params holding explicit ``"noise"`` (or
+``"u1"``/``"u2"``) tensors (the reference's params, or a test's injected
+noise) are applied as given.  The statistics that RandStdShiftIntensity,
+RandScaleIntensityFixedMean and relative RandRicianNoise read (mean, std of
+their input) are reduced in the pass that produces that input.
 """
 from __future__ import annotations
 
@@ -214,6 +218,119 @@ class RandBiasField(_FusibleIntensity):
                            degree=self.degree)
 
 
+class RandRicianNoise(_FusibleIntensity):
+    """sqrt((x + n1)^2 + n2^2) with n = mean + std * u, u ~ N(0, 1) per
+    voxel, in fp32 (noise.py:86-164).  ``relative`` multiplies the element's
+    std by the (unbiased) std of its input over all channels.
+
+    The unit draws u1, u2 come from Philox in-kernel (keyed on the params'
+    ``noise_seed``, the global element index and the voxel); params holding
+    explicit ``"u1"`` and ``"u2"`` tensors (the reference's params) are
+    applied as given."""
+
+    _stream = _rng.S_RICIAN
+
+    def __init__(self, prob: float = 0.1, mean: float = 0.0, std: float = 0.1,
+                 relative: bool = False, sample_std: bool = True):
+        super().__init__(prob=prob)
+        self.mean = mean
+        self.std = std
+        self.relative = relative
+        self.sample_std = sample_std
+
+    def _n_uniforms(self, shape):
+        return 2
+
+    def _host_params(self, B, shape, u, seed):
+        if self.sample_std:
+            noise_std = (u[:, 1] * np.float32(self.std)).astype(np.float32)
+        else:
+            noise_std = np.full((B,), self.std, np.float32)
+        return {"mask": u[:, 0] < self.prob, "noise_std": noise_std, "noise_seed": seed}
+
+    def _device_params(self, host, shape, device):
+        p = upload({"mask": host["mask"], "noise_std": host["noise_std"]}, device)
+        p["noise_seed"] = host["noise_seed"]
+        p["elem_offset"] = _rng.element_offset()
+        return p
+
+    def chain_op(self, params, tensor):
+        dev = tensor.device
+        flags = L.BA_RICIAN_RELATIVE if self.relative else 0
+        std = _dev(params, "noise_std", dev).to(torch.float32).contiguous()
+        if "u1" in params or "u2" in params:
+            u = []
+            for name in ("u1", "u2"):
+                t = params[name].to(device=dev, dtype=torch.float32).contiguous()
+                if t.shape != tensor.shape:
+                    raise ValueError(f"{name} shape {tuple(t.shape)} != tensor shape "
+                                     f"{tuple(tensor.shape)}")
+                u.append(t)
+            return ops.ChainOp(L.BA_OP_RICIAN, flags=flags, mask=_mask_u8(params, dev), param=std,
+                               noise=u[0], param2=u[1], c0=float(self.mean))
+        return ops.ChainOp(L.BA_OP_RICIAN, flags=flags | L.BA_RICIAN_PHILOX,
+                           mask=_mask_u8(params, dev), param=std, c0=float(self.mean),
+                           seed=params["noise_seed"], elem_offset=params.get("elem_offset", 0))
+
+
+class _FactorIntensity(_FusibleIntensity):
+    """A transform with one factor ~ U(lo, hi) per element."""
+
+    def _n_uniforms(self, shape):
+        return 2
+
+    def _host_params(self, B, shape, u, seed):
+        lo, hi = self.factors
+        return {"mask": u[:, 0] < self.prob,
+                "factor": (u[:, 1] * np.float32(hi - lo) + np.float32(lo)).astype(np.float32)}
+
+    def _device_params(self, host, shape, device):
+        return upload({"mask": host["mask"], "factor": host["factor"]}, device)
+
+
+class RandStdShiftIntensity(_FactorIntensity):
+    """x + factor * std, fp32 then one cast (scale_shift.py:120-198).  The
+    std is unbiased, over the element (or each channel with
+    ``channel_wise``); ``nonzero`` takes it over the nonzero voxels when
+    there are at least two of them."""
+
+    _stream = _rng.S_STD_SHIFT
+
+    def __init__(self, prob: float = 0.1, factors=(-3.0, 3.0), nonzero: bool = False,
+                 channel_wise: bool = False):
+        super().__init__(prob=prob)
+        self.factors = _parse_range(factors)
+        self.nonzero = nonzero
+        self.channel_wise = channel_wise
+
+    def chain_op(self, params, tensor):
+        dev = tensor.device
+        flags = (L.BA_STD_NONZERO if self.nonzero else 0) | \
+            (L.BA_STAT_CHANNEL if self.channel_wise else 0)
+        return ops.ChainOp(L.BA_OP_STD_SHIFT, flags=flags, mask=_mask_u8(params, dev),
+                           param=_dev(params, "factor", dev).to(torch.float32).contiguous())
+
+
+class RandScaleIntensityFixedMean(_FactorIntensity):
+    """mean + (x - mean) * (1 + factor), fp32 then one cast, the mean over
+    the element (or each channel with ``channel_wise``)
+    (scale_shift.py:219-274)."""
+
+    _stream = _rng.S_FIXED_MEAN
+
+    def __init__(self, prob: float = 0.1, factors=(-0.5, 0.5), channel_wise: bool = False):
+        super().__init__(prob=prob)
+        self.factors = _parse_range(factors)
+        self.channel_wise = channel_wise
+
+    def chain_op(self, params, tensor):
+        dev = tensor.device
+        return ops.ChainOp(L.BA_OP_FIXED_MEAN,
+                           flags=L.BA_STAT_CHANNEL if self.channel_wise else 0,
+                           mask=_mask_u8(params, dev),
+                           param=_dev(params, "factor", dev).to(torch.float32).contiguous())
+
+
 class ScaleIntensity(_FusibleIntensity):
     """Rescale to [minv, maxv] with per-(element, channel) or per-element
     min/max, in the tensor dtype (contrast.py:8-68)."""
@@ -313,6 +430,28 @@ class RandBiasFieldd(BatchDictTransform):
     def __init__(self, keys, prob: float = 0.1, degree: int = 3, coeff_range=(0.0, 0.1)):
         super().__init__(keys=keys, transform=RandBiasField(prob=prob, degree=degree,
                                                             coeff_range=coeff_range))
+
+
+class RandRicianNoised(BatchDictTransform):
+    """Every key gets the same unit draws and mask (noise.py:167-185)."""
+
+    def __init__(self, keys, prob: float = 0.1, mean: float = 0.0, std: float = 0.1,
+                 relative: bool = False, sample_std: bool = True):
+        super().__init__(keys=keys, transform=RandRicianNoise(
+            prob=prob, mean=mean, std=std, relative=relative, sample_std=sample_std))
+
+
+class RandStdShiftIntensityd(BatchDictTransform):
+    def __init__(self, keys, prob: float = 0.1, factors=(-3.0, 3.0), nonzero: bool = False,
+                 channel_wise: bool = False):
+        super().__init__(keys=keys, transform=RandStdShiftIntensity(
+            prob=prob, factors=factors, nonzero=nonzero, channel_wise=channel_wise))
+
+
+class RandScaleIntensityFixedMeand(BatchDictTransform):
+    def __init__(self, keys, prob: float = 0.1, factors=(-0.5, 0.5), channel_wise: bool = False):
+        super().__init__(keys=keys, transform=RandScaleIntensityFixedMean(
+            prob=prob, factors=factors, channel_wise=channel_wise))
 
 
 class ScaleIntensityd(BatchDictTransform):

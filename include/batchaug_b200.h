@@ -111,7 +111,10 @@ typedef enum ba_op_kind {
   BA_OP_SCALE = 3,      /* x * dt(1 + dt(factor))          scale_shift.py:51-56 */
   BA_OP_SHIFT = 4,      /* x + dt(offset) [clamp 0..1]     scale_shift.py:106-113 */
   BA_OP_BIAS_FIELD = 5, /* x * exp(sum c L L L)            bias_field.py:99-112 */
-  BA_OP_RESCALE = 6     /* ScaleIntensity min/max rescale  contrast.py:35-68 */
+  BA_OP_RESCALE = 6,    /* ScaleIntensity min/max rescale  contrast.py:35-68 */
+  BA_OP_RICIAN = 7,     /* sqrt((x+n1)^2 + n2^2)           noise.py:146-164 */
+  BA_OP_STD_SHIFT = 8,  /* x + factor * std(x)             scale_shift.py:168-198 */
+  BA_OP_FIXED_MEAN = 9  /* mean + (x - mean) * (1+factor)  scale_shift.py:252-274 */
 } ba_op_kind;
 
 /* ba_op.flags */
@@ -121,6 +124,10 @@ typedef enum ba_op_kind {
 #define BA_RESCALE_MAXV 0x2    /* RESCALE: maxv given */
 #define BA_RESCALE_CHANNEL 0x4 /* RESCALE: min/max per (element, channel) */
 #define BA_RESCALE_FACTOR 0x8  /* RESCALE: x * (1 + c0) instead of min/max */
+#define BA_RICIAN_PHILOX 0x1   /* RICIAN: generate u1, u2 ~ N(0,1) in-kernel */
+#define BA_RICIAN_RELATIVE 0x2 /* RICIAN: std * std(x) over the element */
+#define BA_STD_NONZERO 0x2     /* STD_SHIFT: std of the nonzero values (if > 1 of them) */
+#define BA_STAT_CHANNEL 0x4    /* STD_SHIFT, FIXED_MEAN: statistics per (element, channel) */
 
 #define BA_MAX_OPS 8
 
@@ -129,15 +136,19 @@ typedef struct ba_op {
   int32_t flags; /* BA_* flags above */
   const uint8_t* mask; /* (B,) 0/1 or NULL = every element (RESCALE ignores it) */
   const float* param;  /* NOISE: std (B,); CONTRAST: gamma (B,); SCALE: factor (B,);
-                          SHIFT: offset (B,); BIAS_FIELD: coeffs (B, n_coeff) */
-  const float* param2; /* NOISE: mean (B,) */
+                          SHIFT: offset (B,); BIAS_FIELD: coeffs (B, n_coeff);
+                          RICIAN: noise_std (B,); STD_SHIFT, FIXED_MEAN: factor (B,) */
+  const float* param2; /* NOISE: mean (B,); RICIAN without BA_RICIAN_PHILOX:
+                          injected u2, fp32 (B,C,H,W,D) */
   const float* noise;  /* NOISE without BA_NOISE_PHILOX: injected noise, fp32
-                          (B,C,H,W,D), already scaled by std and shifted by mean */
-  uint64_t seed;        /* NOISE with BA_NOISE_PHILOX: Philox key */
-  uint64_t elem_offset; /* NOISE with BA_NOISE_PHILOX: global index of element 0 */
+                          (B,C,H,W,D), already scaled by std and shifted by mean;
+                          RICIAN without BA_RICIAN_PHILOX: injected u1 */
+  uint64_t seed;        /* NOISE / RICIAN with the Philox flag: Philox key */
+  uint64_t elem_offset; /* ... and the global index of element 0 */
   int32_t degree;       /* BIAS_FIELD: Legendre degree 1..6 */
   int32_t reserved;
-  double c0, c1; /* RESCALE: minv, maxv (or factor in c0 with BA_RESCALE_FACTOR) */
+  double c0, c1; /* RESCALE: minv, maxv (or factor in c0 with BA_RESCALE_FACTOR);
+                    RICIAN: the noise mean in c0 */
 } ba_op;
 
 typedef struct ba_chain_desc {
@@ -150,22 +161,25 @@ typedef struct ba_chain_desc {
   ba_op ops[BA_MAX_OPS];
 } ba_chain_desc;
 
-/* Scratch bytes ba_intensity_chain needs for desc (min/max statistics of
- * the intermediate results that CONTRAST and RESCALE read). */
+/* Scratch bytes ba_intensity_chain needs for desc: the statistics of the
+ * intermediate results that CONTRAST and RESCALE (min/max) and STD_SHIFT,
+ * FIXED_MEAN and relative RICIAN (mean, std) read. */
 BA_API size_t ba_intensity_workspace_bytes(const ba_chain_desc* desc);
 
 /*
  * Applies a chain of intensity transforms in as few HBM passes as the
- * statistics allow.  CONTRAST and RESCALE need min/max of their own input, so
- * the chain is cut before each of them: every segment but the last writes
- * its result to dst and reduces its min/max on the fly; the batch is walked
- * in slices sized for L2 so the re-read of dst by the next segment hits L2.
+ * statistics allow.  CONTRAST and RESCALE need min/max, STD_SHIFT,
+ * FIXED_MEAN and relative RICIAN need the mean or std of their own input, so
+ * the chain is cut before each of them: every segment but the last writes its
+ * result to dst and reduces those statistics on the fly.
  * Replaces the eager apply of RandGaussianNoise, RandAdjustContrast,
- * RandScaleIntensity, RandShiftIntensity, RandBiasField and ScaleIntensity
+ * RandScaleIntensity, RandShiftIntensity, RandBiasField, ScaleIntensity,
+ * RandRicianNoise, RandStdShiftIntensity and RandScaleIntensityFixedMean
  * (files above) and the Triton kernels batchaug/triton/kernels/
- * elementwise.py:9-110, scale_shift.py:69-135, bias_field.py:9-124.
+ * elementwise.py:9-110, scale_shift.py:13-241, bias_field.py:9-124,
+ * rician_noise.py:21-63.
  * workspace: device scratch of ba_intensity_workspace_bytes(desc) bytes,
- * 256-byte aligned (may be NULL when that is 0).
+ * 16-byte aligned (may be NULL when that is 0).
  */
 BA_API ba_status ba_intensity_chain(const ba_chain_desc* desc, void* workspace, size_t workspace_bytes,
                              ba_stream_t stream);

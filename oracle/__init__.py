@@ -87,6 +87,9 @@ def _declare(L):
     L.ora_separable_gauss.argtypes = [P, P, I, P, I64, P, I64, P, I64, I64, I64, I64, I64, I64, I,
                                       I]
     L.ora_elastic_grid.argtypes = [P, P, I64, P, I64, I64, I64, I64, P, I]
+    L.ora_std_shift.argtypes = [P, P, I, P, P, I64, I64, I64, I, I, I]
+    L.ora_fixed_mean.argtypes = [P, P, I, P, P, I64, I64, I64, I, I]
+    L.ora_rician.argtypes = [P, P, I, P, P, P, D, I, P, I64, I64, I]
 
 
 # ---------------------------------------------------------------------------
@@ -296,4 +299,44 @@ def elastic_grid(u, taps, magnitude, nthreads=0):
     out = np.empty((B, H, W, D, 3), np.float32)
     lib().ora_elastic_grid(u.ctypes.data, taps.ctypes.data, taps.shape[1], mag.ctypes.data, B,
                            H, W, D, out.ctypes.data, int(nthreads))
+    return out
+
+
+def std_shift(x, factor, mask=None, nonzero=False, channel_wise=False, nthreads=0):
+    """RandStdShiftIntensity.apply (scale_shift.py:130-198)."""
+    x = _c(x)
+    B, C = x.shape[:2]
+    f = _c(np.asarray(factor, np.float32).reshape(B))
+    out = np.empty_like(x)
+    m = _mask(mask, B)
+    lib().ora_std_shift(x.ctypes.data, out.ctypes.data, _dt(x), f.ctypes.data, _p(m), B, C,
+                        x.size // (B * C) if B * C else 0, int(bool(nonzero)),
+                        int(bool(channel_wise)), int(nthreads))
+    return out
+
+
+def fixed_mean(x, factor, mask=None, channel_wise=False, nthreads=0):
+    """RandScaleIntensityFixedMean.apply (scale_shift.py:201-274)."""
+    x = _c(x)
+    B, C = x.shape[:2]
+    f = _c(np.asarray(factor, np.float32).reshape(B))
+    out = np.empty_like(x)
+    m = _mask(mask, B)
+    lib().ora_fixed_mean(x.ctypes.data, out.ctypes.data, _dt(x), f.ctypes.data, _p(m), B, C,
+                         x.size // (B * C) if B * C else 0, int(bool(channel_wise)),
+                         int(nthreads))
+    return out
+
+
+def rician(x, u1, u2, noise_std, mean=0.0, relative=False, mask=None, nthreads=0):
+    """RandRicianNoise.apply (noise.py:146-164) with injected unit normals."""
+    x = _c(x)
+    B = x.shape[0]
+    a1, a2 = _c(u1, np.float32), _c(u2, np.float32)
+    sd = _c(np.asarray(noise_std, np.float32).reshape(B))
+    out = np.empty_like(x)
+    m = _mask(mask, B)
+    lib().ora_rician(x.ctypes.data, out.ctypes.data, _dt(x), a1.ctypes.data, a2.ctypes.data,
+                     sd.ctypes.data, float(mean), int(bool(relative)), _p(m), B,
+                     x.size // B if B else 0, int(nthreads))
     return out

@@ -417,3 +417,124 @@ void ora_elastic_grid(const float* u, const float* taps, int64_t K, const float*
   free(a);
   free(t);
 }
+
+/* Per-group moments in double: sum, sum of squares and the count of nonzero
+ * values (torch reduces float tensors with double accumulators on CPU). */
+static void group_moments(const void* x, int dtype, int64_t n_groups, int64_t gsize, double* sum,
+                          double* sumsq, int64_t* nnz, int nthreads) {
+  set_threads(nthreads);
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static)
+#endif
+  for (int64_t g = 0; g < n_groups; ++g) {
+    double s = 0.0, ss = 0.0;
+    int64_t nz = 0;
+    for (int64_t i = 0; i < gsize; ++i) {
+      const double v = (double)ld(x, dtype, g * gsize + i);
+      s += v;
+      ss += v * v;
+      nz += v != 0.0;
+    }
+    sum[g] = s;
+    sumsq[g] = ss;
+    nnz[g] = nz;
+  }
+}
+
+/* torch.std (unbiased) of n values from their sum and sum of squares. */
+static float std_of(double s, double ss, int64_t n) {
+  if (n < 2) return NAN;
+  const double m = s / (double)n;
+  double v = (ss - s * m) / (double)(n - 1);
+  if (v < 0.0) v = 0.0;
+  return (float)sqrt(v);
+}
+
+/* scale_shift.py:130-198: out = x + factor * std(x), std per element or per
+ * channel (channel_wise); nonzero: std of the nonzero values when there are
+ * at least two of them, else of all values.  fp32 arithmetic, one cast. */
+void ora_std_shift(const void* x, void* out, int dtype, const float* factor, const uint8_t* mask,
+                   int64_t B, int64_t C, int64_t n_spatial, int nonzero, int channel_wise,
+                   int nthreads) {
+  const int64_t n_groups = channel_wise ? B * C : B;
+  const int64_t gsize = channel_wise ? n_spatial : C * n_spatial;
+  const int64_t ng = n_groups > 0 ? n_groups : 1;
+  double* s = (double*)malloc(sizeof(double) * ng);
+  double* ss = (double*)malloc(sizeof(double) * ng);
+  int64_t* nz = (int64_t*)malloc(sizeof(int64_t) * ng);
+  group_moments(x, dtype, n_groups, gsize, s, ss, nz, nthreads);
+  for (int64_t g = 0; g < n_groups; ++g) {
+    const int64_t b = channel_wise ? g / C : g;
+    float sd = (nonzero && nz[g] > 1) ? std_of(s[g], ss[g], nz[g]) : std_of(s[g], ss[g], gsize);
+    const float shift = factor[b] * sd;
+    for (int64_t i = 0; i < gsize; ++i) {
+      const int64_t k = g * gsize + i;
+      const float v = ld(x, dtype, k);
+      st(out, dtype, k, (mask && !mask[b]) ? v : v + shift);
+    }
+  }
+  free(s);
+  free(ss);
+  free(nz);
+}
+
+/* scale_shift.py:201-274: out = mean + (x - mean) * (1 + factor), mean per
+ * element or per channel, fp32 arithmetic, one cast. */
+void ora_fixed_mean(const void* x, void* out, int dtype, const float* factor, const uint8_t* mask,
+                    int64_t B, int64_t C, int64_t n_spatial, int channel_wise, int nthreads) {
+  const int64_t n_groups = channel_wise ? B * C : B;
+  const int64_t gsize = channel_wise ? n_spatial : C * n_spatial;
+  const int64_t ng = n_groups > 0 ? n_groups : 1;
+  double* s = (double*)malloc(sizeof(double) * ng);
+  double* ss = (double*)malloc(sizeof(double) * ng);
+  int64_t* nz = (int64_t*)malloc(sizeof(int64_t) * ng);
+  group_moments(x, dtype, n_groups, gsize, s, ss, nz, nthreads);
+  for (int64_t g = 0; g < n_groups; ++g) {
+    const int64_t b = channel_wise ? g / C : g;
+    const float mean = (float)(s[g] / (double)gsize);
+    const float f1 = 1.0f + factor[b];
+    for (int64_t i = 0; i < gsize; ++i) {
+      const int64_t k = g * gsize + i;
+      const float v = ld(x, dtype, k);
+      st(out, dtype, k, (mask && !mask[b]) ? v : mean + (v - mean) * f1);
+    }
+  }
+  free(s);
+  free(ss);
+  free(nz);
+}
+
+/* noise.py:86-164: out = sqrt((x + n1)^2 + n2^2), n = mean + std * u with
+ * u1, u2 ~ N(0,1) (injected), std per element (times std(x) over the element
+ * when relative); fp32 arithmetic, one cast. */
+void ora_rician(const void* x, void* out, int dtype, const float* u1, const float* u2,
+                const float* noise_std, double mean, int relative, const uint8_t* mask, int64_t B,
+                int64_t n_per_b, int nthreads) {
+  const int64_t nb = B > 0 ? B : 1;
+  double* s = (double*)malloc(sizeof(double) * nb);
+  double* ss = (double*)malloc(sizeof(double) * nb);
+  int64_t* nz = (int64_t*)malloc(sizeof(int64_t) * nb);
+  if (relative) group_moments(x, dtype, B, n_per_b, s, ss, nz, nthreads);
+  const float fm = (float)mean;
+  set_threads(nthreads);
+#ifdef _OPENMP
+#pragma omp parallel for collapse(2) schedule(static)
+#endif
+  for (int64_t b = 0; b < B; ++b)
+    for (int64_t i = 0; i < n_per_b; ++i) {
+      const int64_t k = b * n_per_b + i;
+      const float v = ld(x, dtype, k);
+      if (mask && !mask[b]) {
+        st(out, dtype, k, v);
+        continue;
+      }
+      const float sd = relative ? noise_std[b] * std_of(s[b], ss[b], n_per_b) : noise_std[b];
+      const float n1 = fm + sd * u1[k];
+      const float n2 = fm + sd * u2[k];
+      const float a = v + n1;
+      st(out, dtype, k, sqrtf(a * a + n2 * n2));
+    }
+  free(s);
+  free(ss);
+  free(nz);
+}

@@ -42,12 +42,17 @@ def save(name: str, **arrays):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("BATCHAUG_REFERENCE", ""))
+    ap.add_argument("--only", choices=["stats"], default=None,
+                    help="write only this group of fixtures")
     args = ap.parse_args()
     if args.reference:
         sys.path.insert(0, args.reference)
     import torch.nn.functional as F
 
     import batchaug.pytorch as P
+    if args.only == "stats":
+        gen_stats_ops(P)
+        return
     from batchaug.pytorch.geometric.affine import monai_affine_to_theta
     from batchaug.pytorch.intensity.smooth import gaussian_1d_batch
     dev = torch.device("cpu")
@@ -205,6 +210,44 @@ def main():
     vo = P.ScaleIntensity().apply(vo, {})
     save("pipeline_cfg1", vol=vol, seg=seg, affine=A, mask=m, noise=pn["noise"],
          noise_mask=pn["mask"], vol_out=vo, seg_out=so)
+    gen_stats_ops(P)
+
+
+def gen_stats_ops(P):
+    """RandRicianNoise, RandStdShiftIntensity and RandScaleIntensityFixedMean:
+    the intensity ops that reduce their own input to a mean or std."""
+    dev = torch.device("cpu")
+    torch.set_num_threads(1)
+    for dt, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
+        torch.manual_seed(108)
+        B, C, H, W, D = 3, 2, 9, 10, 12
+        x = (0.5 + 0.2 * torch.randn(B, C, H, W, D)).clamp(0, 1)
+        x[2, 1, :4] = 0.0  # zeros for the nonzero std
+        x = x.to(dt)
+        rec = {"x": x}
+        for rel in (False, True):
+            tr = P.RandRicianNoise(prob=0.7, std=0.2, relative=rel)
+            pr = tr.sample_params(B, x.shape, dev)
+            pr["mask"][0] = True
+            k = "rician_rel" if rel else "rician"
+            rec.update({f"{k}_mask": pr["mask"], f"{k}_std": pr["noise_std"],
+                        f"{k}_u1": pr["u1"], f"{k}_u2": pr["u2"], f"{k}_out": tr.apply(x, pr)})
+        for cw in (False, True):
+            for nz in (False, True):
+                ts = P.RandStdShiftIntensity(prob=0.7, factors=(-2.0, 2.0), nonzero=nz,
+                                             channel_wise=cw)
+                ps = ts.sample_params(B, x.shape, dev)
+                ps["mask"][0] = True
+                k = f"stdshift_cw{int(cw)}_nz{int(nz)}"
+                rec.update({f"{k}_mask": ps["mask"], f"{k}_factor": ps["factor"],
+                            f"{k}_out": ts.apply(x, ps)})
+            tf = P.RandScaleIntensityFixedMean(prob=0.7, factors=0.5, channel_wise=cw)
+            pf = tf.sample_params(B, x.shape, dev)
+            pf["mask"][0] = True
+            k = f"fixedmean_cw{int(cw)}"
+            rec.update({f"{k}_mask": pf["mask"], f"{k}_factor": pf["factor"],
+                        f"{k}_out": tf.apply(x, pf)})
+        save(f"intensity_stats_{tag}", **rec)
 
 
 if __name__ == "__main__":

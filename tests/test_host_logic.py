@@ -222,3 +222,50 @@ def test_native_affine_builder_matches_numpy_chain(ba, ranges):
     np.testing.assert_allclose(h["affine"], ref, rtol=0, atol=2e-6)
     assert np.array_equal(h["mask"], u[:, 0] < 0.6)
     np.testing.assert_array_equal(h["theta"], monai_affine_to_theta(h["affine"], (12, 16, 20)))
+
+
+def test_stats_transforms_host_params_and_ops(ba):
+    """RandRicianNoise / RandStdShiftIntensity / RandScaleIntensityFixedMean:
+    parameter ranges (noise.py:125-141, scale_shift.py:158-166, 245-250) and
+    the chain op each one asks for (built on CPU tensors, not launched)."""
+    from batchaug_b200 import _lib as L
+    torch.manual_seed(5)
+    shape = (4000, 1, 4, 4, 4)
+    r = ba.RandRicianNoise(prob=0.25, std=0.3).sample_host(4000, shape)
+    assert abs(r["mask"].mean() - 0.25) < 0.03
+    assert r["noise_std"].dtype == np.float32
+    assert r["noise_std"].min() >= 0 and r["noise_std"].max() < 0.3
+    assert abs(r["noise_std"].mean() - 0.15) < 0.01
+    fixed = ba.RandRicianNoise(std=0.3, sample_std=False).sample_host(8, (8, 1, 4, 4, 4))
+    assert np.array_equal(fixed["noise_std"], np.full(8, 0.3, np.float32))
+    s = ba.RandStdShiftIntensity(prob=1.0, factors=2.5).sample_host(4000, shape)
+    assert s["factor"].min() >= -2.5 and s["factor"].max() < 2.5
+    assert ba.RandStdShiftIntensity().factors == (-3.0, 3.0)
+    f = ba.RandScaleIntensityFixedMean(prob=1.0).sample_host(4000, shape)
+    assert f["factor"].min() >= -0.5 and f["factor"].max() < 0.5
+    # draws differ from transform to transform for one seed (own streams)
+    torch.manual_seed(9)
+    a = ba.RandStdShiftIntensity(prob=1.0, factors=(0, 1)).sample_host(16, (16, 1, 2, 2, 2))
+    torch.manual_seed(9)
+    b = ba.RandScaleIntensityFixedMean(prob=1.0, factors=(0, 1)).sample_host(16, (16, 1, 2, 2, 2))
+    assert not np.array_equal(a["factor"], b["factor"])
+
+    x = torch.zeros(2, 1, 4, 4, 4)
+    mask = torch.tensor([True, False])
+    p = {"mask": mask, "noise_std": torch.tensor([0.1, 0.2]), "noise_seed": 7, "elem_offset": 3}
+    op = ba.RandRicianNoise(mean=0.25, relative=True).chain_op(p, x)
+    assert op.kind == L.BA_OP_RICIAN and op.seed == 7 and op.elem_offset == 3
+    assert op.flags == L.BA_RICIAN_PHILOX | L.BA_RICIAN_RELATIVE and op.c0 == 0.25
+    u = torch.ones_like(x)
+    op = ba.RandRicianNoise().chain_op({"mask": mask, "noise_std": p["noise_std"], "u1": u,
+                                        "u2": 2 * u}, x)
+    assert op.flags == 0 and op.noise is not None and float(op.param2.max()) == 2.0
+    with pytest.raises(ValueError):
+        ba.RandRicianNoise().chain_op({"mask": mask, "noise_std": p["noise_std"],
+                                       "u1": u[:, :, :2], "u2": u}, x)
+    pf = {"mask": mask, "factor": torch.tensor([0.5, -0.5])}
+    op = ba.RandStdShiftIntensity(nonzero=True, channel_wise=True).chain_op(pf, x)
+    assert op.kind == L.BA_OP_STD_SHIFT and op.flags == L.BA_STD_NONZERO | L.BA_STAT_CHANNEL
+    op = ba.RandScaleIntensityFixedMean(channel_wise=True).chain_op(pf, x)
+    assert op.kind == L.BA_OP_FIXED_MEAN and op.flags == L.BA_STAT_CHANNEL
+    assert ba.RandRicianNoised(["a"]).transform.std == 0.1

@@ -139,3 +139,35 @@ def test_pipeline_cfg1(oracle_lib):
     vo = O.scale_intensity(vo, 0.0, 1.0)
     assert np.array_equal(so, g["seg_out"])
     assert np.array_equal(vo, g["vol_out"])
+
+
+def _close(out, ref, f32_atol=2e-6, bf16_ulp=1):
+    """fp32 within a few ulp of values ~1; bf16 within one ulp (the reductions
+    and libm differ from torch's only in the last bits)."""
+    if ref.dtype == np.uint16:
+        from helpers import bf16_ulp_diff
+        assert bf16_ulp_diff(out, ref) <= bf16_ulp
+    else:
+        np.testing.assert_allclose(out, ref, rtol=0, atol=f32_atol)
+
+
+@pytest.mark.parametrize("tag", ["f32", "bf16"])
+def test_stats_ops(oracle_lib, tag):
+    """Rician noise (absolute and relative std), std shift (per element / per
+    channel, all values / nonzero values) and fixed-mean scaling against the
+    reference's outputs."""
+    g = load_golden(f"intensity_stats_{tag}")
+    x = g["x"]
+    for k, rel in (("rician", False), ("rician_rel", True)):
+        out = oracle_lib.rician(x, g[f"{k}_u1"], g[f"{k}_u2"], g[f"{k}_std"], relative=rel,
+                                mask=g[f"{k}_mask"])
+        _close(out, g[f"{k}_out"])
+    for cw in (0, 1):
+        for nz in (0, 1):
+            k = f"stdshift_cw{cw}_nz{nz}"
+            out = oracle_lib.std_shift(x, g[f"{k}_factor"], mask=g[f"{k}_mask"], nonzero=nz,
+                                       channel_wise=cw)
+            _close(out, g[f"{k}_out"])
+        k = f"fixedmean_cw{cw}"
+        out = oracle_lib.fixed_mean(x, g[f"{k}_factor"], mask=g[f"{k}_mask"], channel_wise=cw)
+        _close(out, g[f"{k}_out"])
