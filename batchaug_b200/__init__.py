@@ -41,6 +41,8 @@ from .intensity import (
     RandBiasFieldd,
     RandGaussianNoise,
     RandGaussianNoised,
+    RandGaussianSharpen,
+    RandGaussianSharpend,
     RandGaussianSmooth,
     RandGaussianSmoothd,
     RandRicianNoise,
@@ -81,7 +83,8 @@ __all__ = [
     "RandAxisFlipd", "RandFlip", "RandFlipd", "RandRotate", "RandRotated", "RandRotate90",
     "RandRotate90d", "RandZoom", "RandZoomd",
     "RandAdjustContrast", "RandAdjustContrastd", "RandBiasField", "RandBiasFieldd",
-    "RandGaussianNoise", "RandGaussianNoised", "RandGaussianSmooth", "RandGaussianSmoothd",
+    "RandGaussianNoise", "RandGaussianNoised", "RandGaussianSharpen", "RandGaussianSharpend",
+    "RandGaussianSmooth", "RandGaussianSmoothd",
     "RandRicianNoise", "RandRicianNoised", "RandScaleIntensity", "RandScaleIntensityd",
     "RandScaleIntensityFixedMean", "RandScaleIntensityFixedMeand", "RandShiftIntensity",
     "RandShiftIntensityd", "RandStdShiftIntensity", "RandStdShiftIntensityd",

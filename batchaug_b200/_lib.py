@@ -70,6 +70,13 @@ class ChainDesc(ctypes.Structure):
                 ("ops", Op * BA_MAX_OPS)]
 
 
+class SharpenDesc(ctypes.Structure):
+    _fields_ = [("src", _P), ("dst", _P), ("dtype", _I32), ("padding", _I32), ("batch", _I64),
+                ("channels", _I64), ("H", _I64), ("W", _I64), ("D", _I64),
+                ("taps1", _P * 3), ("K1", _I64 * 3), ("taps2", _P * 3), ("K2", _I64 * 3),
+                ("alpha", _P), ("mask", _P)]
+
+
 # Every symbol include/batchaug_b200.h declares, with its ctypes signature.
 SIGNATURES = {
     "ba_resample3d": (_I32, [ctypes.POINTER(ResampleDesc), _P]),
@@ -82,6 +89,8 @@ SIGNATURES = {
     "ba_smooth_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, _I64]),
     "ba_smooth3d": (_I32, [_P, _P, _I32, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _P,
                            _I64, _I32, _P, _P, ctypes.c_size_t, _P]),
+    "ba_sharpen_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SharpenDesc)]),
+    "ba_sharpen3d": (_I32, [ctypes.POINTER(SharpenDesc), _P, ctypes.c_size_t, _P]),
     "ba_elastic_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _I64]),
     "ba_elastic_grid": (_I32, [_P, _U64, _U64, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P,
                                ctypes.c_size_t, _P]),

@@ -41,6 +41,7 @@ S_ZOOM = 12
 S_RICIAN = 13
 S_STD_SHIFT = 14
 S_FIXED_MEAN = 15
+S_SHARPEN = 16
 
 
 def set_shard(element_offset: int = 0, global_batch: int | None = None) -> None:

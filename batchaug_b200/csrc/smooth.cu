@@ -5,6 +5,7 @@
 //   separable_gaussian_conv3d   batchaug/pytorch/intensity/smooth.py:37-88
 //   RandGaussianSmooth.apply    batchaug/pytorch/intensity/smooth.py:110-117
 //   Rand3DElastic.sample_params batchaug/pytorch/geometric/elastic.py:37-99
+//   RandGaussianSharpen.apply   batchaug/pytorch/intensity/sharpen.py:117-136
 //
 // Design: three axis passes (H, then W, then D, as the reference's three
 // grouped conv3d calls) with per-element taps held in shared memory; the
@@ -13,7 +14,9 @@
 // forms the grid_sample grid in place: centred MONAI grid + magnitude *
 // displacement, divided by (N-1)/2, components reordered to x=D, y=W, z=H).
 // The uniform draw of the elastic field is generated in-kernel by Philox
-// unless the caller injects it.
+// unless the caller injects it.  Unsharp masking runs two smooths; the last
+// pass of the second one combines its result with the first blur as it
+// writes, so the double blur is never stored.
 #include <stdio.h>
 
 #include <algorithm>
@@ -29,6 +32,18 @@ constexpr int MAX_TAPS = 255;
 
 __device__ __forceinline__ float load_in(const void* p, int dtype, int64_t i) {
   return dtype == BA_BF16 ? bf16_bits_to_f32(((const uint16_t*)p)[i]) : ((const float*)p)[i];
+}
+
+// blurred + alpha * (blurred - double_blurred), one op at a time in the
+// dtype with alpha cast to it first (sharpen.py:131); `db` is the second
+// blur's fp32 sum before its cast.
+__device__ __forceinline__ float sharpen_combine(float blurred, float db, float alpha, int dtype) {
+  if (dtype == BA_BF16) {
+    const float d = round_bf16(__fsub_rn(blurred, round_bf16(db)));
+    const float t = round_bf16(__fmul_rn(round_bf16(alpha), d));
+    return round_bf16(__fadd_rn(blurred, t));
+  }
+  return __fadd_rn(blurred, __fmul_rn(alpha, __fsub_rn(blurred, db)));
 }
 
 __global__ void gauss_taps_kernel(const float* sigmas, int64_t B, int64_t K, float* taps) {
@@ -65,6 +80,9 @@ struct AxisArgs {
   int32_t padding;  // ba_smooth_pad
   const uint8_t* mask;
   const void* copy_src;
+  // unsharp masking (last pass of the second blur): out = combine(sharp_blur, acc)
+  const void* sharp_blur;
+  const float* alpha;
 };
 
 // Source index of padded position q (may be outside [0, n)) along an axis of
@@ -111,6 +129,8 @@ __global__ void __launch_bounds__(SM_THREADS) axis_pass_kernel(const __grid_cons
     if (q < 0) continue;
     acc = acc + load_in(a.in, a.in_dtype, base + q * stride) * w[k];
   }
+  if (a.sharp_blur != nullptr)
+    acc = sharpen_combine(load_in(a.sharp_blur, a.out_dtype, idx), acc, a.alpha[b], a.out_dtype);
   if (a.out_dtype == BA_BF16)
     ((uint16_t*)a.out)[idx] = f32_to_bf16_bits(acc);
   else
@@ -228,6 +248,9 @@ struct TiledArgs {
   // elastic grid output (pass B): grid != nullptr
   float* grid;
   const float* magnitude;
+  // unsharp masking (pass B of the second blur): out = combine(sharp_blur, acc)
+  const void* sharp_blur;
+  const float* alpha;
 };
 
 // R outputs out[i] = sum_k w[k] * x[i + k] for k < KMAX from a register
@@ -392,6 +415,17 @@ __global__ void __launch_bounds__(TS_THREADS) smooth_column_kernel(const __grid_
     }
     return;
   }
+  if (a.sharp_blur != nullptr) {
+    const float al = a.alpha[b];
+#pragma unroll
+    for (int i = 0; i < TS_RH; ++i) {
+      const int h = th0 + hg * TS_RH + i;
+      if (h < H) {
+        const int64_t o = col + h * plane_stride;
+        acc[i] = sharpen_combine(load_in(a.sharp_blur, a.out_dtype, o), acc[i], al, a.out_dtype);
+      }
+    }
+  }
 #pragma unroll
   for (int i = 0; i < TS_RH; ++i) {
     const int h = th0 + hg * TS_RH + i;
@@ -512,6 +546,116 @@ extern "C" size_t ba_smooth_workspace_bytes(int64_t batch, int64_t channels, int
   return (size_t)(2 * batch * channels * H * W * D) * sizeof(float);
 }
 
+namespace ba {
+namespace {
+
+// One separable smooth of (planes = B*P, H, W, D) from `src` (in_dtype) to
+// `dst` (out_dtype), scratch t0/t1 (fp32, planes*HWD each; the tiled path
+// uses t0 only).  Masked-out elements copy copy_src (or are skipped when it
+// is NULL); with sharp_blur set, the last pass writes the unsharp-mask
+// combination instead of the blur.
+struct SmoothJob {
+  const void* src;
+  int32_t in_dtype;
+  void* dst;
+  int32_t out_dtype;
+  int64_t P, planes, H, W, D;
+  const float* taps[3];  // H, W, D
+  int64_t K[3];
+  int32_t padding;
+  const uint8_t* mask;
+  const void* copy_src;
+  const void* sharp_blur;
+  const float* alpha;
+  float* t0;
+  float* t1;
+};
+
+ba_status run_smooth(const SmoothJob& j, cudaStream_t st) {
+  const int64_t HWD = j.H * j.W * j.D;
+  const int64_t kmax = std::max(j.K[0], std::max(j.K[1], j.K[2]));
+  if (tiled_kmax((int)kmax) != 0 && j.H <= 65535 && j.W <= 65535) {
+    TiledArgs t;
+    memset(&t, 0, sizeof(t));
+    t.in = j.src;
+    t.in_dtype = j.in_dtype;
+    t.mid = j.t0;
+    t.out = j.dst;
+    t.out_dtype = j.out_dtype;
+    t.taps_h = j.taps[0];
+    t.taps_w = j.taps[1];
+    t.taps_d = j.taps[2];
+    t.Kh = (int32_t)j.K[0];
+    t.Kw = (int32_t)j.K[1];
+    t.Kd = (int32_t)j.K[2];
+    t.padding = j.padding;
+    t.P = j.P;
+    t.H = j.H;
+    t.W = j.W;
+    t.D = j.D;
+    t.HWD = HWD;
+    t.mask = j.mask;
+    t.copy_src = j.copy_src;
+    t.sharp_blur = j.sharp_blur;
+    t.alpha = j.alpha;
+    return launch_tiled(t, j.planes, st);
+  }
+  AxisArgs a;
+  memset(&a, 0, sizeof(a));
+  a.P = j.P;
+  a.H = j.H;
+  a.W = j.W;
+  a.D = j.D;
+  a.HWD = HWD;
+  a.padding = j.padding;
+  // H pass: src -> t0
+  a.in = j.src;
+  a.in_dtype = j.in_dtype;
+  a.out = j.t0;
+  a.out_dtype = BA_F32;
+  a.taps = j.taps[0];
+  a.K = (int32_t)j.K[0];
+  ba_status s = launch_axis(0, a, j.planes, st);
+  if (s != BA_OK) return s;
+  // W pass: t0 -> t1
+  a.in = j.t0;
+  a.in_dtype = BA_F32;
+  a.out = j.t1;
+  a.taps = j.taps[1];
+  a.K = (int32_t)j.K[1];
+  s = launch_axis(1, a, j.planes, st);
+  if (s != BA_OK) return s;
+  // D pass: t1 -> dst; masked-out elements copy copy_src
+  a.in = j.t1;
+  a.out = j.dst;
+  a.out_dtype = j.out_dtype;
+  a.taps = j.taps[2];
+  a.K = (int32_t)j.K[2];
+  a.mask = j.mask;
+  a.copy_src = j.mask ? j.copy_src : nullptr;
+  a.sharp_blur = j.sharp_blur;
+  a.alpha = j.alpha;
+  return launch_axis(2, a, j.planes, st);
+}
+
+ba_status check_taps(const char* who, const int64_t* K, int64_t H, int64_t W, int64_t D,
+                     int32_t padding) {
+  for (int i = 0; i < 3; ++i)
+    BA_REQUIRE(K[i] >= 1 && K[i] <= MAX_TAPS && (K[i] % 2) == 1, "%s: K=%lld must be odd, 1..%d",
+               who, (long long)K[i], MAX_TAPS);
+  if (padding == BA_SMOOTH_REFLECT) {
+    // F.pad(mode="reflect") needs the pad to be smaller than the axis
+    BA_REQUIRE(K[0] / 2 < H && K[1] / 2 < W && K[2] / 2 < D,
+               "%s: reflect padding needs K/2 < size along every axis", who);
+  }
+  return BA_OK;
+}
+
+size_t align16(size_t n) { return (n + 15) & ~(size_t)15; }
+
+}  // namespace
+}  // namespace ba
+
 extern "C" ba_status ba_smooth3d(const void* src, void* dst, int32_t dtype, int64_t batch,
                                  int64_t channels, int64_t H, int64_t W, int64_t D,
                                  const float* taps_h, int64_t Kh, const float* taps_w, int64_t Kw,
@@ -523,18 +667,12 @@ extern "C" ba_status ba_smooth3d(const void* src, void* dst, int32_t dtype, int6
   BA_REQUIRE(dtype == BA_F32 || dtype == BA_BF16, "ba_smooth3d: bad dtype %d", dtype);
   BA_REQUIRE(batch >= 0 && channels >= 0 && H > 0 && W > 0 && D > 0, "ba_smooth3d: bad shape");
   BA_REQUIRE(batch * channels <= 65535, "ba_smooth3d: batch*channels exceeds 65535");
-  for (int64_t K : {Kh, Kw, Kd})
-    BA_REQUIRE(K >= 1 && K <= MAX_TAPS && (K % 2) == 1, "ba_smooth3d: K=%lld must be odd, 1..%d",
-               (long long)K, MAX_TAPS);
   BA_REQUIRE(padding >= BA_SMOOTH_ZEROS && padding <= BA_SMOOTH_REPLICATE,
              "ba_smooth3d: unknown padding %d", padding);
-  if (padding == BA_SMOOTH_REFLECT) {
-    // F.pad(mode="reflect") needs the pad to be smaller than the axis
-    BA_REQUIRE(Kh / 2 < H && Kw / 2 < W && Kd / 2 < D,
-               "ba_smooth3d: reflect padding needs K/2 < size along every axis");
-  }
-  const int64_t HWD = H * W * D;
-  const int64_t n = batch * channels * HWD;
+  const int64_t K[3] = {Kh, Kw, Kd};
+  ba_status s = check_taps("ba_smooth3d", K, H, W, D, padding);
+  if (s != BA_OK) return s;
+  const int64_t n = batch * channels * H * W * D;
   if (n == 0) return BA_OK;
   BA_REQUIRE(src && dst && taps_h && taps_w && taps_d, "ba_smooth3d: NULL pointer");
   const size_t need = ba_smooth_workspace_bytes(batch, channels, H, W, D);
@@ -544,68 +682,105 @@ extern "C" ba_status ba_smooth3d(const void* src, void* dst, int32_t dtype, int6
   BA_REQUIRE((const char*)src + n * esz <= (const char*)dst ||
                  (const char*)dst + n * esz <= (const char*)src,
              "ba_smooth3d: dst overlaps src");
+  SmoothJob j;
+  memset(&j, 0, sizeof(j));
+  j.src = src;
+  j.in_dtype = dtype;
+  j.dst = dst;
+  j.out_dtype = dtype;
+  j.P = channels;
+  j.planes = batch * channels;
+  j.H = H;
+  j.W = W;
+  j.D = D;
+  j.taps[0] = taps_h;
+  j.taps[1] = taps_w;
+  j.taps[2] = taps_d;
+  for (int i = 0; i < 3; ++i) j.K[i] = K[i];
+  j.padding = padding;
+  j.mask = mask;
+  j.copy_src = src;
+  j.t0 = (float*)workspace;
+  j.t1 = j.t0 + n;
+  return run_smooth(j, (cudaStream_t)stream);
+}
+
+extern "C" size_t ba_sharpen_workspace_bytes(const ba_sharpen_desc* d) {
+  using namespace ba;
+  if (d == nullptr || d->batch < 0 || d->channels < 0 || d->H < 0 || d->W < 0 || d->D < 0)
+    return 0;
+  const size_t n = (size_t)(d->batch * d->channels * d->H * d->W * d->D);
+  const size_t esz = d->dtype == BA_BF16 ? 2 : 4;
+  return align16(2 * n * sizeof(float)) + n * esz;
+}
+
+extern "C" ba_status ba_sharpen3d(const ba_sharpen_desc* d, void* workspace,
+                                  size_t workspace_bytes, ba_stream_t stream) {
+  using namespace ba;
+  clear_error();
+  BA_REQUIRE(d != nullptr, "ba_sharpen3d: desc is NULL");
+  BA_REQUIRE(d->dtype == BA_F32 || d->dtype == BA_BF16, "ba_sharpen3d: bad dtype %d", d->dtype);
+  BA_REQUIRE(d->batch >= 0 && d->channels >= 0 && d->H > 0 && d->W > 0 && d->D > 0,
+             "ba_sharpen3d: bad shape");
+  BA_REQUIRE(d->batch * d->channels <= 65535, "ba_sharpen3d: batch*channels exceeds 65535");
+  BA_REQUIRE(d->padding >= BA_SMOOTH_ZEROS && d->padding <= BA_SMOOTH_REPLICATE,
+             "ba_sharpen3d: unknown padding %d", d->padding);
+  ba_status s = check_taps("ba_sharpen3d", d->K1, d->H, d->W, d->D, d->padding);
+  if (s != BA_OK) return s;
+  s = check_taps("ba_sharpen3d", d->K2, d->H, d->W, d->D, d->padding);
+  if (s != BA_OK) return s;
+  const int64_t n = d->batch * d->channels * d->H * d->W * d->D;
+  if (n == 0) return BA_OK;
+  BA_REQUIRE(d->src && d->dst && d->alpha, "ba_sharpen3d: NULL pointer");
+  for (int i = 0; i < 3; ++i)
+    BA_REQUIRE(d->taps1[i] && d->taps2[i], "ba_sharpen3d: NULL taps");
+  const size_t need = ba_sharpen_workspace_bytes(d);
+  BA_REQUIRE(workspace && workspace_bytes >= need,
+             "ba_sharpen3d: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+  BA_REQUIRE((uintptr_t)workspace % 16 == 0, "ba_sharpen3d: workspace not 16-byte aligned");
+  const size_t esz = d->dtype == BA_BF16 ? 2 : 4;
+  BA_REQUIRE((const char*)d->src + n * esz <= (const char*)d->dst ||
+                 (const char*)d->dst + n * esz <= (const char*)d->src,
+             "ba_sharpen3d: dst overlaps src");
+  cudaStream_t st = (cudaStream_t)stream;
   float* t0 = (float*)workspace;
   float* t1 = t0 + n;
-  cudaStream_t st = (cudaStream_t)stream;
-  const int64_t planes = batch * channels;
-  if (tiled_kmax((int)std::max(Kh, std::max(Kw, Kd))) != 0 && H <= 65535 && W <= 65535) {
-    TiledArgs t;
-    memset(&t, 0, sizeof(t));
-    t.in = src;
-    t.in_dtype = dtype;
-    t.mid = t0;
-    t.out = dst;
-    t.out_dtype = dtype;
-    t.taps_h = taps_h;
-    t.taps_w = taps_w;
-    t.taps_d = taps_d;
-    t.Kh = (int32_t)Kh;
-    t.Kw = (int32_t)Kw;
-    t.Kd = (int32_t)Kd;
-    t.padding = padding;
-    t.P = channels;
-    t.H = H;
-    t.W = W;
-    t.D = D;
-    t.HWD = HWD;
-    t.mask = mask;
-    t.copy_src = src;
-    return launch_tiled(t, planes, st);
+  void* blurred = (char*)workspace + align16(2 * (size_t)n * sizeof(float));
+  SmoothJob j;
+  memset(&j, 0, sizeof(j));
+  j.in_dtype = d->dtype;
+  j.out_dtype = d->dtype;
+  j.P = d->channels;
+  j.planes = d->batch * d->channels;
+  j.H = d->H;
+  j.W = d->W;
+  j.D = d->D;
+  j.padding = d->padding;
+  j.t0 = t0;
+  j.t1 = t1;
+  // blurred = smooth(src, taps1), cast to dtype; masked-out elements are not
+  // needed (the second blur copies src for them)
+  j.src = d->src;
+  j.dst = blurred;
+  for (int i = 0; i < 3; ++i) {
+    j.taps[i] = d->taps1[i];
+    j.K[i] = d->K1[i];
   }
-  AxisArgs a;
-  memset(&a, 0, sizeof(a));
-  a.P = channels;
-  a.H = H;
-  a.W = W;
-  a.D = D;
-  a.HWD = HWD;
-  a.padding = padding;
-  // H pass: src (dtype) -> t0
-  a.in = src;
-  a.in_dtype = dtype;
-  a.out = t0;
-  a.out_dtype = BA_F32;
-  a.taps = taps_h;
-  a.K = (int32_t)Kh;
-  ba_status s = launch_axis(0, a, planes, st);
+  j.mask = d->mask;
+  j.copy_src = nullptr;
+  s = run_smooth(j, st);
   if (s != BA_OK) return s;
-  // W pass: t0 -> t1
-  a.in = t0;
-  a.in_dtype = BA_F32;
-  a.out = t1;
-  a.taps = taps_w;
-  a.K = (int32_t)Kw;
-  s = launch_axis(1, a, planes, st);
-  if (s != BA_OK) return s;
-  // D pass: t1 -> dst (dtype); masked-out elements copy src
-  a.in = t1;
-  a.out = dst;
-  a.out_dtype = dtype;
-  a.taps = taps_d;
-  a.K = (int32_t)Kd;
-  a.mask = mask;
-  a.copy_src = mask ? src : nullptr;
-  return launch_axis(2, a, planes, st);
+  // dst = combine(blurred, smooth(blurred, taps2)); masked-out elements copy src
+  j.src = blurred;
+  j.dst = d->dst;
+  for (int i = 0; i < 3; ++i) {
+    j.taps[i] = d->taps2[i];
+    j.K[i] = d->K2[i];
+  }
+  j.copy_src = d->src;
+  j.sharp_blur = blurred;
+  j.alpha = d->alpha;
+  return run_smooth(j, st);
 }
 
 extern "C" size_t ba_elastic_workspace_bytes(int64_t batch, int64_t H, int64_t W, int64_t D) {

@@ -1,7 +1,7 @@
 """Intensity transforms: RandGaussianNoise, RandRicianNoise,
 RandAdjustContrast, RandScaleIntensity, RandShiftIntensity,
 RandStdShiftIntensity, RandScaleIntensityFixedMean, RandBiasField,
-ScaleIntensity, RandGaussianSmooth (+ dict wrappers).
+ScaleIntensity, RandGaussianSmooth, RandGaussianSharpen (+ dict wrappers).
 
 Constructors, params keys and results follow the reference PyTorch backend
 (batchaug/pytorch/intensity/*.py), op by op in the tensor dtype.  Each
@@ -401,6 +401,73 @@ class RandGaussianSmooth(BatchTransform):
                             mask=params["mask"], padding_mode=self.padding_mode)
 
 
+class RandGaussianSharpen(BatchTransform):
+    """Unsharp masking blurred + alpha * (blurred - double_blurred) with two
+    separable Gaussian blurs (sharpen.py:9-136).  A scalar sigma2 samples
+    from [sigma2, sigma1] per element, a tuple from its range.  One
+    ``ba_sharpen3d`` call: the second blur's last pass writes the
+    combination."""
+
+    _stream = _rng.S_SHARPEN
+
+    def __init__(self, prob: float = 0.1, sigma1_x=(0.5, 1.0), sigma1_y=(0.5, 1.0),
+                 sigma1_z=(0.5, 1.0), sigma2_x=0.5, sigma2_y=0.5, sigma2_z=0.5,
+                 alpha=(10.0, 30.0), padding_mode=None):
+        super().__init__(prob=prob)
+        self.sigma1_x, self.sigma1_y, self.sigma1_z = sigma1_x, sigma1_y, sigma1_z
+        self.sigma2_x, self.sigma2_y, self.sigma2_z = sigma2_x, sigma2_y, sigma2_z
+        self.alpha = alpha
+        self.padding_mode = padding_mode
+
+    @staticmethod
+    def _range(col: np.ndarray, rng) -> np.ndarray:
+        lo, hi = rng
+        return (col * np.float32(hi - lo) + np.float32(lo)).astype(np.float32)
+
+    @staticmethod
+    def _sigma2(col: np.ndarray, param, sigma1: np.ndarray) -> np.ndarray:
+        """sharpen.py:61-75: scalar -> U(param, sigma1), tuple -> U(lo, hi)."""
+        if isinstance(param, (int, float)):
+            lo = np.float32(param)
+            return (col * (sigma1 - lo) + lo).astype(np.float32)
+        return RandGaussianSharpen._range(col, param)
+
+    def sample_host(self, batch_size, shape):
+        # draw order of sharpen.py:77-113: mask, sigma1 x/y/z, sigma2 x/y/z, alpha
+        seed = _rng.draw_seed()
+        u_all, row = _rng.global_uniforms(seed, self._stream, batch_size, 8)
+        full = {"mask": u_all[:, 0] < self.prob}
+        for i, a in enumerate("xyz"):
+            full[f"sigma1_{a}"] = self._range(u_all[:, 1 + i], getattr(self, f"sigma1_{a}"))
+        for i, a in enumerate("xyz"):
+            full[f"sigma2_{a}"] = self._sigma2(u_all[:, 4 + i], getattr(self, f"sigma2_{a}"),
+                                               full[f"sigma1_{a}"])
+        full["alpha"] = self._range(u_all[:, 7], self.alpha)
+        host = {k: v[row:row + batch_size] for k, v in full.items()}
+        # gaussian_1d_batch sizes each kernel set by its batch-max sigma
+        for k in ("sigma1_x", "sigma1_y", "sigma1_z", "sigma2_x", "sigma2_y", "sigma2_z"):
+            s_all = full[k]
+            host["K_" + k] = ops.gauss_taps_len(
+                float(np.maximum(s_all, np.float32(1e-6)).max()) if len(s_all) else 1e-6, 4.0)
+        return host
+
+    def sample_params(self, batch_size, shape, device):
+        host = self.sample_host(batch_size, shape)
+        keys = ("mask", "alpha", "sigma1_x", "sigma1_y", "sigma1_z", "sigma2_x", "sigma2_y",
+                "sigma2_z")
+        p = upload({k: host[k] for k in keys}, device)
+        for n in "12":
+            for a, ax in zip("xyz", "hwd"):
+                p[f"kernel{n}_{ax}"] = ops.gauss_taps(p[f"sigma{n}_{a}"], host[f"K_sigma{n}_{a}"])
+        p["_host"] = host
+        return p
+
+    def apply(self, tensor, params):
+        return ops.sharpen3d(tensor, [params[f"kernel1_{a}"] for a in "hwd"],
+                             [params[f"kernel2_{a}"] for a in "hwd"], params["alpha"],
+                             mask=params["mask"], padding_mode=self.padding_mode)
+
+
 # ---------------------------------------------------------------------------
 # Dict wrappers (same keys/params sharing as the reference)
 # ---------------------------------------------------------------------------
@@ -465,4 +532,16 @@ class RandGaussianSmoothd(BatchDictTransform):
                  sigma_z=(0.25, 1.5), padding_mode=None):
         super().__init__(keys=keys, transform=RandGaussianSmooth(
             prob=prob, sigma_x=sigma_x, sigma_y=sigma_y, sigma_z=sigma_z,
+            padding_mode=padding_mode))
+
+
+class RandGaussianSharpend(BatchDictTransform):
+    """Every key gets the same sharpening params (sharpen.py:139-169)."""
+
+    def __init__(self, keys, prob: float = 0.1, sigma1_x=(0.5, 1.0), sigma1_y=(0.5, 1.0),
+                 sigma1_z=(0.5, 1.0), sigma2_x=0.5, sigma2_y=0.5, sigma2_z=0.5,
+                 alpha=(10.0, 30.0), padding_mode=None):
+        super().__init__(keys=keys, transform=RandGaussianSharpen(
+            prob=prob, sigma1_x=sigma1_x, sigma1_y=sigma1_y, sigma1_z=sigma1_z,
+            sigma2_x=sigma2_x, sigma2_y=sigma2_y, sigma2_z=sigma2_z, alpha=alpha,
             padding_mode=padding_mode))

@@ -223,6 +223,40 @@ def smooth3d(x: torch.Tensor, taps_h, taps_w, taps_d, mask=None,
     return out
 
 
+def sharpen3d(x: torch.Tensor, taps1, taps2, alpha, mask=None,
+              padding_mode=None) -> torch.Tensor:
+    """Unsharp masking blurred + alpha * (blurred - double_blurred) with
+    per-element taps: taps1 / taps2 are (H, W, D) triples of (B, K) for the
+    first and second blur."""
+    if padding_mode not in L.SMOOTH_PADS:
+        raise ValueError(f"unsupported padding_mode {padding_mode!r}")
+    x = _contig(x, "tensor")
+    B, C, H, W, D = x.shape
+    t1 = [_dev_f32(t, x.device, "taps1") for t in taps1]
+    t2 = [_dev_f32(t, x.device, "taps2") for t in taps2]
+    for t in t1 + t2:
+        if t.dim() != 2 or t.shape[0] != B:
+            raise ValueError(f"taps must be (B={B}, K), got {tuple(t.shape)}")
+    al = _dev_f32(alpha, x.device, "alpha").reshape(-1)
+    if al.numel() != B:
+        raise ValueError(f"alpha has {al.numel()} values for a batch of {B}")
+    m = _dev_mask(mask, B, x.device)
+    out = torch.empty_like(x)
+    d = L.SharpenDesc()
+    d.src, d.dst = x.data_ptr(), out.data_ptr()
+    d.dtype, d.padding = L.dtype_code(x), L.SMOOTH_PADS[padding_mode]
+    d.batch, d.channels, d.H, d.W, d.D = B, C, H, W, D
+    for i in range(3):
+        d.taps1[i], d.K1[i] = t1[i].data_ptr(), t1[i].shape[1]
+        d.taps2[i], d.K2[i] = t2[i].data_ptr(), t2[i].shape[1]
+    d.alpha, d.mask = al.data_ptr(), L.ptr(m)
+    nbytes = L.lib.ba_sharpen_workspace_bytes(ctypes.byref(d))
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+    L.check(L.lib.ba_sharpen3d(ctypes.byref(d), ws.data_ptr(), nbytes, L.stream_ptr(x.device)),
+            "ba_sharpen3d")
+    return out
+
+
 def elastic_grid(shape, taps, magnitude, *, u=None, seed=0, elem_offset=0,
                  device=None) -> torch.Tensor:
     """grid_sample grid (B,H,W,D,3) of Rand3DElastic from taps (B,K) and

@@ -451,6 +451,24 @@ def _secondary(name, torch, ba, device, rank):
         n = vol.numel()
         return ("RandGaussianSmooth(prob=1, sigma 0.5..1.5) on config 5's vol shard "
                 "(8x2x160^3 bf16)", lambda i: sm.apply(vol, p), n, n * 4)
+    if name == "stats":
+        xs = [(0.5 + 0.2 * torch.randn(16, 4, 128, 128, 128, device=device, generator=g))
+              .clamp(0, 1).bfloat16() for _ in range(2)]
+        c = ba.Compose([ba.RandStdShiftIntensityd(["v"], prob=1.0, nonzero=True),
+                        ba.RandRicianNoised(["v"], prob=1.0, std=0.1, relative=True),
+                        ba.RandScaleIntensityFixedMeand(["v"], prob=1.0, channel_wise=True)],
+                       lazy=True)
+        n = xs[0].numel()
+        return ("std shift (nonzero std) -> relative Rician noise -> fixed-mean scaling "
+                "(channel-wise), prob 1, B=16 C=4 128^3 bf16", lambda i: c({"v": xs[i % 2]}),
+                n, n * 4)
+    if name == "sharpen":
+        vol = torch.rand(8, 2, 160, 160, 160, device=device, generator=g).bfloat16()
+        sh = ba.RandGaussianSharpen(prob=1.0)
+        p = sh.sample_params(8, vol.shape, device)
+        n = vol.numel()
+        return ("RandGaussianSharpen(prob=1, sigma1 0.5..1, sigma2 0.5..sigma1, alpha 10..30) "
+                "on config 5's vol shard (8x2x160^3 bf16)", lambda i: sh.apply(vol, p), n, n * 4)
     if name == "config5-elastic":
         el = ba.Rand3DElastic(prob=1.0, sigma_range=(5, 7), magnitude_range=(50, 150))
         shape = (8, 2, 160, 160, 160)
@@ -530,7 +548,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="config2",
                     choices=["config2", "config3", "config4", "config5", "config5-smooth",
-                             "config5-elastic"],
+                             "config5-elastic", "stats", "sharpen"],
                     help="config2 is the headline; the others time one whole step of that "
                          "configuration (for profiling and per-config numbers)")
     args = ap.parse_args()

@@ -252,6 +252,36 @@ BA_API ba_status ba_smooth3d(const void* src, void* dst, int32_t dtype, int64_t 
                       size_t workspace_bytes, ba_stream_t stream);
 
 /*
+ * Unsharp masking of (B,C,H,W,D) with per-element taps and strength
+ * (RandGaussianSharpen.apply, sharpen.py:117-136):
+ *   blurred        = smooth(src, taps1)      cast to dtype
+ *   double_blurred = smooth(blurred, taps2)  cast to dtype
+ *   dst = blurred + alpha * (blurred - double_blurred), one op at a time in
+ *         dtype (alpha cast to dtype first); masked-out elements copy src.
+ * The combination is computed in the last pass of the second blur, so
+ * double_blurred is never stored.  Replaces the Triton path
+ * batchaug/triton/intensity/sharpen.py:18-38 (two separable blurs, then the
+ * combination in torch).  workspace: ba_sharpen_workspace_bytes bytes, 16-byte
+ * aligned; dst must not overlap src.
+ */
+typedef struct ba_sharpen_desc {
+  const void* src;
+  void* dst;
+  int32_t dtype;
+  int32_t padding; /* ba_smooth_pad, for both blurs */
+  int64_t batch, channels, H, W, D;
+  const float* taps1[3]; /* first blur, (B, K1[i]) for H, W, D */
+  int64_t K1[3];
+  const float* taps2[3]; /* second blur */
+  int64_t K2[3];
+  const float* alpha;    /* (B,) */
+  const uint8_t* mask;   /* (B,) or NULL = every element */
+} ba_sharpen_desc;
+BA_API size_t ba_sharpen_workspace_bytes(const ba_sharpen_desc* desc);
+BA_API ba_status ba_sharpen3d(const ba_sharpen_desc* desc, void* workspace, size_t workspace_bytes,
+                              ba_stream_t stream);
+
+/*
  * Rand3DElastic.sample_params (elastic.py:37-99) from its uniform draw: grid
  * (B,H,W,D,3) = ((smooth(u*2-1) * magnitude) + centred grid) / ((N-1)/2),
  * reordered to grid_sample's xyz.  u is (B,3,H,W,D) fp32 in [0,1); when u is

@@ -90,6 +90,7 @@ def _declare(L):
     L.ora_std_shift.argtypes = [P, P, I, P, P, I64, I64, I64, I, I, I]
     L.ora_fixed_mean.argtypes = [P, P, I, P, P, I64, I64, I64, I, I]
     L.ora_rician.argtypes = [P, P, I, P, P, P, D, I, P, I64, I64, I]
+    L.ora_sharpen_combine.argtypes = [P, P, P, P, I, P, P, I64, I64, I]
 
 
 # ---------------------------------------------------------------------------
@@ -340,3 +341,25 @@ def rician(x, u1, u2, noise_std, mean=0.0, relative=False, mask=None, nthreads=0
                      sd.ctypes.data, float(mean), int(bool(relative)), _p(m), B,
                      x.size // B if B else 0, int(nthreads))
     return out
+
+
+def sharpen_combine(blurred, double_blurred, x, alpha, mask=None, nthreads=0):
+    """blurred + alpha * (blurred - double_blurred) in the dtype, masked-out
+    elements keep x (sharpen.py:117-136)."""
+    bl, db, x = _c(blurred), _c(double_blurred), _c(x)
+    B = x.shape[0]
+    al = _c(np.asarray(alpha, np.float32).reshape(B))
+    out = np.empty_like(x)
+    m = _mask(mask, B)
+    lib().ora_sharpen_combine(bl.ctypes.data, db.ctypes.data, x.ctypes.data, out.ctypes.data,
+                              _dt(x), al.ctypes.data, _p(m), B, x.size // max(B, 1),
+                              int(nthreads))
+    return out
+
+
+def sharpen(x, kernels1, kernels2, alpha, mask=None, padding_mode=None, nthreads=0):
+    """RandGaussianSharpen.apply (sharpen.py:117-136): two separable blurs,
+    each cast to the dtype, then the unsharp-mask combination."""
+    bl = separable_gauss(x, *kernels1, padding_mode=padding_mode, nthreads=nthreads)
+    db = separable_gauss(bl, *kernels2, padding_mode=padding_mode, nthreads=nthreads)
+    return sharpen_combine(bl, db, x, alpha, mask, nthreads=nthreads)

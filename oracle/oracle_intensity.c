@@ -538,3 +538,29 @@ void ora_rician(const void* x, void* out, int dtype, const float* u1, const floa
   free(ss);
   free(nz);
 }
+
+/* sharpen.py:117-136, after the two blurs: out = blurred + alpha * (blurred -
+ * double_blurred), one op at a time in the tensor dtype (alpha cast to it
+ * first); masked-out elements keep x.  bl and db hold the two blurs already
+ * cast to the dtype. */
+void ora_sharpen_combine(const void* bl, const void* db, const void* x, void* out, int dtype,
+                         const float* alpha, const uint8_t* mask, int64_t B, int64_t n_per_b,
+                         int nthreads) {
+  set_threads(nthreads);
+#ifdef _OPENMP
+#pragma omp parallel for collapse(2) schedule(static)
+#endif
+  for (int64_t b = 0; b < B; ++b)
+    for (int64_t i = 0; i < n_per_b; ++i) {
+      const int64_t k = b * n_per_b + i;
+      if (mask && !mask[b]) {
+        st(out, dtype, k, ld(x, dtype, k));
+        continue;
+      }
+      const float a = rnd(dtype, alpha[b]);
+      const float u = ld(bl, dtype, k);
+      const float d = rnd(dtype, u - ld(db, dtype, k));
+      const float t = rnd(dtype, a * d);
+      st(out, dtype, k, u + t);
+    }
+}

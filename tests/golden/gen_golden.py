@@ -42,7 +42,7 @@ def save(name: str, **arrays):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("BATCHAUG_REFERENCE", ""))
-    ap.add_argument("--only", choices=["stats"], default=None,
+    ap.add_argument("--only", choices=["stats", "sharpen"], default=None,
                     help="write only this group of fixtures")
     args = ap.parse_args()
     if args.reference:
@@ -52,6 +52,9 @@ def main():
     import batchaug.pytorch as P
     if args.only == "stats":
         gen_stats_ops(P)
+        return
+    if args.only == "sharpen":
+        gen_sharpen(P)
         return
     from batchaug.pytorch.geometric.affine import monai_affine_to_theta
     from batchaug.pytorch.intensity.smooth import gaussian_1d_batch
@@ -211,6 +214,7 @@ def main():
     save("pipeline_cfg1", vol=vol, seg=seg, affine=A, mask=m, noise=pn["noise"],
          noise_mask=pn["mask"], vol_out=vo, seg_out=so)
     gen_stats_ops(P)
+    gen_sharpen(P)
 
 
 def gen_stats_ops(P):
@@ -248,6 +252,41 @@ def gen_stats_ops(P):
             rec.update({f"{k}_mask": pf["mask"], f"{k}_factor": pf["factor"],
                         f"{k}_out": tf.apply(x, pf)})
         save(f"intensity_stats_{tag}", **rec)
+
+
+def gen_sharpen(P):
+    """RandGaussianSharpen: the two blurs, the unsharp-mask combination and
+    the sampled params (scalar sigma2 -> [sigma2, sigma1] and tuple sigma2),
+    for padding None / reflect / replicate."""
+    from batchaug.pytorch.intensity.smooth import separable_gaussian_conv3d
+    dev = torch.device("cpu")
+    torch.set_num_threads(1)
+    for dt, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
+        torch.manual_seed(109)
+        B, C, H, W, D = 3, 2, 11, 12, 13
+        x = (0.5 + 0.2 * torch.randn(B, C, H, W, D)).clamp(0, 1).to(dt)
+        rec = {"x": x}
+        cases = (("none", None, 0.5), ("reflect", "reflect", (0.3, 0.6)),
+                 ("replicate", "replicate", 0.5))
+        for name, pm, s2 in cases:
+            t = P.RandGaussianSharpen(prob=0.7, sigma2_x=s2, sigma2_y=s2, sigma2_z=s2,
+                                      padding_mode=pm)
+            p = t.sample_params(B, x.shape, dev)
+            p["mask"][0] = True
+            k1 = [p[f"kernel1_{a}"] for a in "hwd"]
+            k2 = [p[f"kernel2_{a}"] for a in "hwd"]
+            bl = separable_gaussian_conv3d(x, *k1, padding_mode=pm)
+            db = separable_gaussian_conv3d(bl, *k2, padding_mode=pm)
+            rec.update({f"{name}_mask": p["mask"], f"{name}_alpha": p["alpha"],
+                        f"{name}_blurred": bl, f"{name}_double_blurred": db,
+                        f"{name}_out": t.apply(x, p)})
+            for a in "xyz":
+                rec[f"{name}_sigma1_{a}"] = p[f"sigma1_{a}"]
+                rec[f"{name}_sigma2_{a}"] = p[f"sigma2_{a}"]
+            for a in "hwd":
+                rec[f"{name}_kernel1_{a}"] = p[f"kernel1_{a}"]
+                rec[f"{name}_kernel2_{a}"] = p[f"kernel2_{a}"]
+        save(f"sharpen_{tag}", **rec)
 
 
 if __name__ == "__main__":

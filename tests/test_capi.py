@@ -38,7 +38,7 @@ def test_struct_layouts_match_header(ba, tmp_path):
     if cc is None:
         pytest.skip("no C compiler")
     structs = {"ba_resample_key": L.ResampleKey, "ba_resample_desc": L.ResampleDesc,
-               "ba_op": L.Op, "ba_chain_desc": L.ChainDesc}
+               "ba_op": L.Op, "ba_chain_desc": L.ChainDesc, "ba_sharpen_desc": L.SharpenDesc}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "batchaug_b200.h"',
              "int main(void) {"]
     for cname, ct in structs.items():
@@ -89,6 +89,20 @@ def test_validation_without_gpu(ba):
     assert L.lib.ba_intensity_chain(ctypes.byref(c), None, 0, None) == L.BA_EUNSUPPORTED
     assert L.lib.ba_minmax(None, 5, 1, 1, None, None) == L.BA_EINVAL
     assert L.lib.ba_gauss_taps(None, 1, 4, None, None) == L.BA_EINVAL  # even K
+    sd = L.SharpenDesc()
+    sd.batch, sd.channels, sd.H, sd.W, sd.D, sd.dtype = 2, 3, 5, 6, 7, 1
+    for i in range(3):
+        sd.K1[i], sd.K2[i] = 9, 5
+    # two fp32 scratch volumes (16-byte rounded) plus the first blur in bf16
+    n = 2 * 3 * 5 * 6 * 7
+    assert L.lib.ba_sharpen_workspace_bytes(ctypes.byref(sd)) == ((8 * n + 15) // 16) * 16 + 2 * n
+    assert L.lib.ba_sharpen3d(ctypes.byref(sd), None, 0, None) == L.BA_EINVAL  # NULL src
+    sd.K2[1] = 4
+    assert L.lib.ba_sharpen3d(ctypes.byref(sd), None, 0, None) == L.BA_EINVAL
+    assert b"must be odd" in L.lib.ba_last_error()
+    sd.K2[1], sd.padding, sd.K1[0] = 5, 1, 11  # reflect needs K/2 < H
+    assert L.lib.ba_sharpen3d(ctypes.byref(sd), None, 0, None) == L.BA_EINVAL
+    assert b"reflect" in L.lib.ba_last_error()
 
 
 def test_gauss_taps_len_matches_reference_rule(ba):

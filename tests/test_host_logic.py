@@ -269,3 +269,28 @@ def test_stats_transforms_host_params_and_ops(ba):
     op = ba.RandScaleIntensityFixedMean(channel_wise=True).chain_op(pf, x)
     assert op.kind == L.BA_OP_FIXED_MEAN and op.flags == L.BA_STAT_CHANNEL
     assert ba.RandRicianNoised(["a"]).transform.std == 0.1
+
+
+def test_sharpen_host_params(ba):
+    """RandGaussianSharpen params (sharpen.py:61-113): sigma1 in its range,
+    a scalar sigma2 in [sigma2, sigma1], a tuple sigma2 in its range, alpha
+    in its range, and each kernel set sized by its batch-max sigma."""
+    torch.manual_seed(2)
+    t = ba.RandGaussianSharpen(prob=0.4, sigma1_x=(1.0, 2.0), sigma2_y=(0.2, 0.3))
+    h = t.sample_host(3000, (3000, 1, 4, 4, 4))
+    assert abs(h["mask"].mean() - 0.4) < 0.03
+    assert h["sigma1_x"].min() >= 1.0 and h["sigma1_x"].max() < 2.0
+    assert np.all(h["sigma2_x"] >= 0.5) and np.all(h["sigma2_x"] <= h["sigma1_x"])
+    assert h["sigma2_y"].min() >= 0.2 and h["sigma2_y"].max() < 0.3
+    assert h["alpha"].min() >= 10.0 and h["alpha"].max() < 30.0
+    assert h["K_sigma1_x"] == ba.ops.gauss_taps_len(float(h["sigma1_x"].max()), 4.0) == 17
+    assert h["K_sigma2_y"] == 3
+    # a shard of the global batch draws exactly that slice of the params
+    torch.manual_seed(3)
+    full = t.sample_host(8, (8, 1, 4, 4, 4))
+    torch.manual_seed(3)
+    with ba.shard(4, 8):
+        part = t.sample_host(4, (4, 1, 4, 4, 4))
+    for k in ("mask", "sigma1_x", "sigma2_z", "alpha"):
+        assert np.array_equal(part[k], full[k][4:])
+    assert part["K_sigma1_x"] == full["K_sigma1_x"]

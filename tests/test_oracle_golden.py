@@ -171,3 +171,40 @@ def test_stats_ops(oracle_lib, tag):
         k = f"fixedmean_cw{cw}"
         out = oracle_lib.fixed_mean(x, g[f"{k}_factor"], mask=g[f"{k}_mask"], channel_wise=cw)
         _close(out, g[f"{k}_out"])
+
+
+@pytest.mark.parametrize("tag", ["f32", "bf16"])
+def test_sharpen(oracle_lib, tag):
+    """RandGaussianSharpen: the combination step is bit-exact on the
+    reference's own blurs; each blur is within the smoothing bar, and the
+    whole op within that bar amplified by the unsharp mask, (1 + 2 alpha)."""
+    O = oracle_lib
+    g = load_golden(f"sharpen_{tag}")
+    x = g["x"]
+    for name, pm in (("none", None), ("reflect", "reflect"), ("replicate", "replicate")):
+        k1 = [g[f"{name}_kernel1_{a}"] for a in "hwd"]
+        k2 = [g[f"{name}_kernel2_{a}"] for a in "hwd"]
+        alpha, mask = g[f"{name}_alpha"], g[f"{name}_mask"]
+        comb = O.sharpen_combine(g[f"{name}_blurred"], g[f"{name}_double_blurred"], x, alpha,
+                                 mask)
+        assert np.array_equal(comb, g[f"{name}_out"])
+        blur_tol = 2e-7 if tag == "f32" else 2.0 ** -8
+        bl = O.separable_gauss(x, *k1, padding_mode=pm)
+        np.testing.assert_allclose(f32(bl), f32(g[f"{name}_blurred"]), rtol=0, atol=blur_tol)
+        db = O.separable_gauss(g[f"{name}_blurred"], *k2, padding_mode=pm)
+        np.testing.assert_allclose(f32(db), f32(g[f"{name}_double_blurred"]), rtol=0,
+                                   atol=blur_tol)
+        full = O.sharpen(x, k1, k2, alpha, mask, padding_mode=pm)
+        amp = 1.0 + 2.0 * float(np.max(alpha))
+        np.testing.assert_allclose(f32(full), f32(g[f"{name}_out"]), rtol=0, atol=amp * blur_tol)
+        # the sampled params: sigma2 in [sigma2, sigma1] (scalar) or its range
+        for a in "xyz":
+            s1, s2 = g[f"{name}_sigma1_{a}"], g[f"{name}_sigma2_{a}"]
+            assert np.all((s1 >= 0.5) & (s1 < 1.0))
+            if name == "reflect":
+                assert np.all((s2 >= 0.3) & (s2 < 0.6))
+            else:
+                assert np.all((s2 >= 0.5) & (s2 <= s1))
+        for a, s in zip("hwd", "xyz"):
+            np.testing.assert_allclose(O.gaussian_1d_batch(g[f"{name}_sigma1_{s}"]),
+                                       g[f"{name}_kernel1_{a}"], rtol=0, atol=1e-7)
