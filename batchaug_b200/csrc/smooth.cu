@@ -485,6 +485,420 @@ ba_status launch_tiled(const TiledArgs& a, int64_t planes, cudaStream_t st) {
   }
 }
 
+// ===========================================================================
+// Streaming separable smoothing (used for KMAX <= SS_KMAX_MAX).
+//
+// One CTA owns an SS_TW (W) x SS_TD (D) column block of one (element,
+// channel) plane stack and walks its H range plane by plane:
+//   1. the plane's tile with its W/D halo arrives one plane ahead: as whole
+//      16-byte chunks copied by cp.async into a double-buffered raw stage
+//      (rows 16-byte aligned), then converted once into the padded fp32 tile
+//      with the D padding rule applied through a per-thread column map; or,
+//      for unaligned rows, element by element through registers;
+//   2. D correlation of every tile row (SS_RD outputs per thread unit);
+//   3. W correlation (SS_RW outputs per thread), the result V of the plane
+//      written to a per-thread ring of the last RING planes in shared memory;
+//   4. every SS_RH planes, the H correlation of SS_RH output planes from the
+//      ring, and the epilogue (cast, or the unsharp-mask combination).
+// The ring holds one float4 (the thread's SS_RW columns) per plane and
+// thread; a thread only reads back the entries it wrote, so the ring needs no
+// barrier.  After each flush the slots of planes no later window reads are
+// zeroed, so a window that runs past the fed planes (taps beyond the runtime
+// K) meets exact zeros.  HBM sees one read of the input (plus the H halo of
+// each chunk) and one write of the output; nothing intermediate leaves the
+// SM.  Tile entries beyond the runtime halo are zero-filled likewise.
+// ===========================================================================
+constexpr int SS_THREADS = 128;
+constexpr int SS_TD = 32;  // D extent of the block: one warp's lanes
+constexpr int SS_TW = 16;  // W extent: 4 warps x SS_RW rows
+constexpr int SS_RD = 8;   // D outputs per thread unit in step 2
+constexpr int SS_RW = 4;   // W outputs per thread in step 3
+constexpr int SS_RH = 4;   // H outputs per thread and column per flush
+constexpr int SS_KMAX_MAX = 23;
+static_assert(SS_TW == (SS_THREADS / SS_TD) * SS_RW, "step 3: one run of SS_RW rows per warp");
+
+template <int KMAX>
+struct SsGeom {
+  static constexpr int ROWS = SS_TW + KMAX - 1;  // tile rows (W with halo)
+  static constexpr int COLS = SS_TD + KMAX - 1;  // tile columns (D with halo)
+  static constexpr int RS = COLS | 1;  // odd row stride: the step-2 reads hit 32 banks
+  static constexpr int NLOAD = (ROWS * COLS + SS_THREADS - 1) / SS_THREADS;
+  static constexpr int BS = SS_TD + 1;  // step-2 output row stride (conflict-free writes)
+  static constexpr int DUNITS = ROWS * (SS_TD / SS_RD);
+  static constexpr int RING = SS_RH + KMAX - 1;
+  static constexpr int TILE_FLOATS = (ROWS * RS + 3) / 4 * 4;
+  static constexpr int BM_FLOATS = (ROWS * BS + 3) / 4 * 4;
+  static constexpr int RING_FLOATS = RING * SS_TW * SS_TD;
+  static constexpr size_t SMEM = (size_t)(TILE_FLOATS + BM_FLOATS + RING_FLOATS) * sizeof(float);
+};
+
+// Raw staging of a plane's tile for the cp.async path: whole 16-byte chunks,
+// the D window widened to chunk boundaries (XO elements each side).
+template <int KMAX, int DT>
+struct SsRaw {
+  static constexpr int ESZ = DT == BA_BF16 ? 2 : 4;
+  static constexpr int CH = 16 / ESZ;  // elements per chunk
+  static constexpr int PMAX = (KMAX - 1) / 2;
+  static constexpr int XO = (PMAX + CH - 1) / CH * CH;
+  static constexpr int RP = SS_TD + 2 * XO;  // row pitch, elements (a whole number of chunks)
+  static constexpr int CPR = RP / CH;
+  static constexpr int ROWS = SS_TW + KMAX - 1;
+  static constexpr int NCHUNK = ROWS * CPR;
+  static constexpr int CPT = (NCHUNK + SS_THREADS - 1) / SS_THREADS;
+  static constexpr int STAGE_BYTES = ROWS * RP * ESZ;
+  static constexpr size_t SMEM = 2 * (size_t)STAGE_BYTES;
+};
+
+// R outputs acc[i] = sum_k w[k] * x(i + k), taps in registers.
+template <int R, int KMAX, typename Load>
+__device__ __forceinline__ void conv_regs(Load x, const float (&w)[KMAX], float* acc) {
+  float xw[R + KMAX - 1];
+#pragma unroll
+  for (int i = 0; i < R; ++i) acc[i] = 0.0f;
+#pragma unroll
+  for (int j = 0; j < R - 1; ++j) xw[j] = x(j);
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) {
+    xw[k + R - 1] = x(k + R - 1);
+#pragma unroll
+    for (int i = 0; i < R; ++i) acc[i] = __fmaf_rn(w[k], xw[i + k], acc[i]);
+  }
+}
+
+template <int KMAX>
+__device__ __forceinline__ void load_taps_regs(const float* taps, int64_t b, int K, float (&w)[KMAX]) {
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) w[k] = k < K ? __ldg(taps + b * K + k) : 0.0f;
+}
+
+template <int DT>
+__device__ __forceinline__ float ld_dt(const void* p, int64_t i) {
+  return DT == BA_BF16 ? bf16_bits_to_f32(__ldg((const unsigned short*)p + i))
+                       : __ldg((const float*)p + i);
+}
+
+template <int DT>
+__device__ __forceinline__ void st_dt(void* p, int64_t i, float v) {
+  if (DT == BA_BF16)
+    ((uint16_t*)p)[i] = f32_to_bf16_bits(v);
+  else
+    ((float*)p)[i] = v;
+}
+
+// Grid (tiles_d * tiles_w, n_chunks, B*P); chunk c covers output planes
+// [c * h_chunk, min(H, (c+1) * h_chunk)).
+template <int KMAX, int DT, bool ASYNC>
+__global__ void __launch_bounds__(SS_THREADS, 4)
+    smooth_stream_kernel(const __grid_constant__ TiledArgs a, int32_t h_chunk) {
+  using G = SsGeom<KMAX>;
+  using RW = SsRaw<KMAX, DT>;
+  extern __shared__ float sm[];
+  float* tile = sm;
+  float* bm = sm + G::TILE_FLOATS;
+  float4* ring4 = reinterpret_cast<float4*>(bm + G::BM_FLOATS);
+  const int tid = threadIdx.x;
+  const int64_t bp = blockIdx.z;
+  const int64_t b = bp / a.P;
+  const int H = (int)a.H, W = (int)a.W, D = (int)a.D;
+  const int tiles_d = (D + SS_TD - 1) / SS_TD;
+  const int d0 = (blockIdx.x % tiles_d) * SS_TD;
+  const int w0 = (blockIdx.x / tiles_d) * SS_TW;
+  const int hs = blockIdx.y * h_chunk;
+  const int he = min(H, hs + h_chunk);
+  const int lane_d = tid % SS_TD, wg = tid / SS_TD;
+  const int64_t plane_sz = (int64_t)W * D;
+  const int64_t stack = bp * (int64_t)H * plane_sz;  // offset of plane 0 of this stack
+
+  if (a.mask != nullptr && a.mask[b] == 0) {
+    // the reference's torch.where: masked-out elements keep the input
+    if (a.copy_src == nullptr) return;
+    const int d = d0 + lane_d;
+    if (d >= D) return;
+    for (int h = hs; h < he; ++h)
+#pragma unroll
+      for (int c = 0; c < SS_RW; ++c) {
+        const int w = w0 + wg * SS_RW + c;
+        if (w < W) {
+          const int64_t o = stack + h * plane_sz + (int64_t)w * D + d;
+          st_dt<DT>(a.out, o, ld_dt<DT>(a.copy_src, o));
+        }
+      }
+    return;
+  }
+
+  const int ph = a.Kh / 2, pw = a.Kw / 2, pd = a.Kd / 2;
+  float wd[KMAX], ww[KMAX], wh[KMAX];
+  load_taps_regs<KMAX>(a.taps_d, b, a.Kd, wd);
+  load_taps_regs<KMAX>(a.taps_w, b, a.Kw, ww);
+  load_taps_regs<KMAX>(a.taps_h, b, a.Kh, wh);
+
+  // Register path: in-plane source offset of each tile entry this thread
+  // loads (-1: zero).  cp.async path: the in-plane source offset of each
+  // raw chunk this thread copies (-1: none, the stage stays zero there) and
+  // the raw column that feeds each of its two conversion columns.
+  constexpr int NOFF = ASYNC ? RW::CPT : G::NLOAD;
+  int32_t off[NOFF];
+  int32_t rcol[2];
+  unsigned char* raw = reinterpret_cast<unsigned char*>(ring4 + G::RING_FLOATS / 4);
+  if constexpr (ASYNC) {
+#pragma unroll
+    for (int i = 0; i < RW::CPT; ++i) {
+      const int c = tid + i * SS_THREADS;
+      const int rr = c / RW::CPR, k = c % RW::CPR;
+      const int r = rr - (RW::PMAX - pw);  // tile row fed by raw row rr
+      int32_t o = -1;
+      if (c < RW::NCHUNK && r >= 0 && r < SS_TW + 2 * pw) {
+        const int64_t wi = pad_index(w0 - pw + r, W, a.padding);
+        const int x = d0 - RW::XO + k * RW::CH;
+        if (wi >= 0 && x >= 0 && x + RW::CH <= D) o = (int32_t)(wi * D + x);
+      }
+      off[i] = o;
+    }
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      const int col = lane_d + SS_TD * cc;
+      int32_t rc = -1;
+      if (col < G::COLS && col < SS_TD + 2 * pd) {
+        const int64_t dd = pad_index(d0 - pd + col, D, a.padding);
+        if (dd >= 0) rc = (int32_t)(dd - (d0 - RW::XO));
+      }
+      rcol[cc] = rc;
+    }
+    // entries the conversion never writes stay zero; chunks never copied too
+    for (int i = tid; i < G::TILE_FLOATS; i += SS_THREADS) tile[i] = 0.0f;
+    for (int i = tid; i < (int)(RW::SMEM / 16); i += SS_THREADS)
+      reinterpret_cast<float4*>(raw)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  } else {
+#pragma unroll
+    for (int i = 0; i < G::NLOAD; ++i) {
+      const int e = tid + i * SS_THREADS;
+      const int row = e / G::COLS, col = e % G::COLS;
+      int32_t o = -1;
+      if (e < G::ROWS * G::COLS && row < SS_TW + 2 * pw && col < SS_TD + 2 * pd) {
+        const int64_t wi = pad_index(w0 - pw + row, W, a.padding);
+        const int64_t di = pad_index(d0 - pd + col, D, a.padding);
+        if (wi >= 0 && di >= 0) o = (int32_t)(wi * D + di);
+      }
+      off[i] = o;
+    }
+    rcol[0] = rcol[1] = -1;
+  }
+  // zero ring: taps beyond K and not-yet-fed planes meet zeros
+  for (int i = tid; i < G::RING_FLOATS / 4; i += SS_THREADS)
+    ring4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  int64_t obase[SS_RW];
+  uint32_t col_ok = 0;
+#pragma unroll
+  for (int c = 0; c < SS_RW; ++c) {
+    const int w = w0 + wg * SS_RW + c, d = d0 + lane_d;
+    obase[c] = stack + (int64_t)w * D + d;
+    if (w < W && d < D) col_ok |= 1u << c;
+  }
+
+  const int q_begin = hs - ph, q_end = he + ph;  // padded plane range fed through
+  // source plane of padded index q (-1: a zero plane)
+  auto src_plane = [&](int q) -> int { return (int)pad_index(q, H, a.padding); };
+  float pre[ASYNC ? 1 : G::NLOAD];
+  auto fetch = [&](int q) {
+    const int sp = src_plane(q);
+    if constexpr (ASYNC) {
+      if (sp >= 0) {
+        const char* pb = (const char*)a.in + (stack + sp * plane_sz) * RW::ESZ;
+        unsigned char* st = raw + ((q - q_begin) & 1) * RW::STAGE_BYTES;
+#pragma unroll
+        for (int i = 0; i < RW::CPT; ++i) {
+          const int c = tid + i * SS_THREADS;
+          if (off[i] >= 0)
+            cp_async16(st + (c / RW::CPR * RW::RP + c % RW::CPR * RW::CH) * RW::ESZ,
+                       pb + (int64_t)off[i] * RW::ESZ);
+        }
+      }
+      cp_async_commit();
+    } else {
+#pragma unroll
+      for (int i = 0; i < G::NLOAD; ++i)
+        pre[i] = (sp >= 0 && off[i] >= 0) ? ld_dt<DT>(a.in, stack + sp * plane_sz + off[i]) : 0.0f;
+    }
+  };
+  if constexpr (ASYNC) __syncthreads();  // the zeroed stages before any copy lands
+  fetch(q_begin);
+  int next_out = hs;
+  const float al = a.sharp_blur != nullptr ? a.alpha[b] : 0.0f;
+  for (int q = q_begin; q < q_end; ++q) {
+    const int slot = (q - q_begin) % G::RING;
+    const bool zero_plane = src_plane(q) < 0;
+    if constexpr (ASYNC) {
+      // 1. copies of plane q+1 in flight; plane q's have landed (this
+      //    thread's), the barrier makes every thread's visible
+      if (q + 1 < q_end)
+        fetch(q + 1);
+      else
+        cp_async_commit();
+      cp_async_wait<1>();
+      __syncthreads();
+      if (!zero_plane) {
+        const unsigned char* st = raw + ((q - q_begin) & 1) * RW::STAGE_BYTES;
+        const int rofs = RW::PMAX - pw;
+#pragma unroll
+        for (int i = 0; i < (G::ROWS + 3) / 4; ++i) {
+          const int r = wg + 4 * i;
+          if (r < SS_TW + 2 * pw) {
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+              if (rcol[cc] >= 0) {
+                const int ri = (r + rofs) * RW::RP + rcol[cc];
+                tile[r * G::RS + lane_d + SS_TD * cc] =
+                    DT == BA_BF16 ? bf16_bits_to_f32(((const uint16_t*)st)[ri])
+                                  : ((const float*)st)[ri];
+              }
+            }
+          }
+        }
+      }
+      __syncthreads();
+    } else {
+      if (!zero_plane) {
+        // 1. prefetched plane -> shared tile (the previous plane's step 2 is done)
+#pragma unroll
+        for (int i = 0; i < G::NLOAD; ++i) {
+          const int e = tid + i * SS_THREADS;
+          if (e < G::ROWS * G::COLS) tile[e + e / G::COLS * (G::RS - G::COLS)] = pre[i];
+        }
+      }
+      __syncthreads();
+      if (q + 1 < q_end) fetch(q + 1);
+    }
+    if (!zero_plane) {
+      // 2. D correlation of every tile row
+      for (int u = tid; u < G::DUNITS; u += SS_THREADS) {
+        const int r = u / (SS_TD / SS_RD), q0 = (u % (SS_TD / SS_RD)) * SS_RD;
+        const float* rowp = tile + r * G::RS + q0;
+        float acc[SS_RD];
+        conv_regs<SS_RD, KMAX>([&](int j) { return rowp[j]; }, wd, acc);
+#pragma unroll
+        for (int i = 0; i < SS_RD; ++i) bm[r * G::BS + q0 + i] = acc[i];
+      }
+    }
+    __syncthreads();
+    // 3. W correlation -> ring slot of plane q (own columns only)
+    float v[SS_RW];
+    if (!zero_plane) {
+      conv_regs<SS_RW, KMAX>([&](int j) { return bm[(wg * SS_RW + j) * G::BS + lane_d]; }, ww,
+                             v);
+    } else {
+#pragma unroll
+      for (int c = 0; c < SS_RW; ++c) v[c] = 0.0f;
+    }
+    ring4[slot * SS_THREADS + tid] = make_float4(v[0], v[1], v[2], v[3]);
+    // 4. flush SS_RH output planes once their last input plane is in
+    const bool last = q + 1 == q_end;
+    if (next_out + SS_RH - 1 + ph <= q || (last && next_out < he)) {
+      const int base = (next_out - hs) % G::RING;
+      const float4* p0 = ring4 + base * SS_THREADS + tid;
+      float acc[SS_RW][SS_RH];
+#pragma unroll
+      for (int c = 0; c < SS_RW; ++c)
+#pragma unroll
+        for (int i = 0; i < SS_RH; ++i) acc[c][i] = 0.0f;
+      auto xslot = [&](int j) {
+        const float4* p = p0 + j * SS_THREADS;
+        return *(j >= G::RING - base ? p - G::RING * SS_THREADS : p);
+      };
+      float4 xw[SS_RH + KMAX - 1];
+#pragma unroll
+      for (int j = 0; j < SS_RH - 1; ++j) xw[j] = xslot(j);
+#pragma unroll
+      for (int k = 0; k < KMAX; ++k) {
+        xw[k + SS_RH - 1] = xslot(k + SS_RH - 1);
+#pragma unroll
+        for (int i = 0; i < SS_RH; ++i) {
+          acc[0][i] = __fmaf_rn(wh[k], xw[i + k].x, acc[0][i]);
+          acc[1][i] = __fmaf_rn(wh[k], xw[i + k].y, acc[1][i]);
+          acc[2][i] = __fmaf_rn(wh[k], xw[i + k].z, acc[2][i]);
+          acc[3][i] = __fmaf_rn(wh[k], xw[i + k].w, acc[3][i]);
+        }
+      }
+      // planes before the next window are never read again: zero their slots
+#pragma unroll
+      for (int i = 0; i < SS_RH; ++i) {
+        float4* p = const_cast<float4*>(p0) + i * SS_THREADS;
+        *(i >= G::RING - base ? p - G::RING * SS_THREADS : p) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int c = 0; c < SS_RW; ++c) {
+        if (!(col_ok & (1u << c))) continue;
+#pragma unroll
+        for (int i = 0; i < SS_RH; ++i) {
+          const int h = next_out + i;
+          if (h < he) {
+            const int64_t o = obase[c] + h * plane_sz;
+            float r = acc[c][i];
+            if (a.sharp_blur != nullptr)
+              r = sharpen_combine(ld_dt<DT>(a.sharp_blur, o), r, al, DT);
+            st_dt<DT>(a.out, o, r);
+          }
+        }
+      }
+      next_out += SS_RH;
+    }
+  }
+}
+
+int sm_count_smooth() {
+  static int cached = 0;
+  if (cached == 0) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+      cached = n;
+    else
+      cached = 148;
+  }
+  return cached;
+}
+
+template <int KMAX, int DT, bool ASYNC>
+ba_status launch_stream_kmax(const TiledArgs& a, int64_t planes, cudaStream_t st) {
+  using G = SsGeom<KMAX>;
+  const size_t smem = G::SMEM + (ASYNC ? SsRaw<KMAX, DT>::SMEM : 0);
+  cudaFuncSetAttribute(smooth_stream_kernel<KMAX, DT, ASYNC>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int tiles_d = (int)((a.D + SS_TD - 1) / SS_TD);
+  const int tiles_w = (int)((a.W + SS_TW - 1) / SS_TW);
+  // chunk H until the grid covers the resident CTAs about twice
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, smooth_stream_kernel<KMAX, DT, ASYNC>,
+                                                    SS_THREADS, smem) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int64_t slots = (int64_t)per_sm * sm_count_smooth();
+  const int64_t blocks = (int64_t)tiles_d * tiles_w * planes;
+  int64_t chunk = a.H;
+  while (blocks * ((a.H + chunk - 1) / chunk) < 2 * slots && chunk / 2 >= 4 * KMAX) chunk /= 2;
+  chunk = (chunk + SS_RH - 1) / SS_RH * SS_RH;
+  dim3 g((unsigned)(tiles_d * tiles_w), (unsigned)((a.H + chunk - 1) / chunk), (unsigned)planes);
+  smooth_stream_kernel<KMAX, DT, ASYNC><<<g, SS_THREADS, smem, st>>>(a, (int32_t)chunk);
+  return check_launch("smooth stream");
+}
+
+// The cp.async path needs 16-byte aligned rows (D * element size a multiple
+// of 16) and a 16-byte aligned source.
+template <int DT, bool ASYNC>
+ba_status launch_stream_a(const TiledArgs& a, int64_t planes, cudaStream_t st) {
+  const int K = std::max(a.Kh, std::max(a.Kw, a.Kd));
+  if (K <= 7) return launch_stream_kmax<7, DT, ASYNC>(a, planes, st);
+  if (K <= 15) return launch_stream_kmax<15, DT, ASYNC>(a, planes, st);
+  return launch_stream_kmax<23, DT, ASYNC>(a, planes, st);
+}
+
+template <int DT>
+ba_status launch_stream(const TiledArgs& a, int64_t planes, cudaStream_t st) {
+  const int esz = DT == BA_BF16 ? 2 : 4;
+  const bool aligned = (a.D * esz) % 16 == 0 && ((uintptr_t)a.in % 16) == 0;
+  return aligned ? launch_stream_a<DT, true>(a, planes, st)
+                 : launch_stream_a<DT, false>(a, planes, st);
+}
+
 // Uniform draw of the elastic field mapped to [-1,1), four values per thread
 // from one Philox block (requires HWD % 4 == 0).
 __global__ void elastic_draw4_kernel(uint32_t seed_lo, uint32_t seed_hi, uint64_t elem_offset,
@@ -574,7 +988,10 @@ struct SmoothJob {
 ba_status run_smooth(const SmoothJob& j, cudaStream_t st) {
   const int64_t HWD = j.H * j.W * j.D;
   const int64_t kmax = std::max(j.K[0], std::max(j.K[1], j.K[2]));
-  if (tiled_kmax((int)kmax) != 0 && j.H <= 65535 && j.W <= 65535) {
+  const bool streamable = kmax <= SS_KMAX_MAX && j.in_dtype == j.out_dtype &&
+                          j.W * j.D < ((int64_t)1 << 31) &&
+                          ((j.D + SS_TD - 1) / SS_TD) * ((j.W + SS_TW - 1) / SS_TW) <= 0x7FFFFFFF;
+  if (streamable || (tiled_kmax((int)kmax) != 0 && j.H <= 65535 && j.W <= 65535)) {
     TiledArgs t;
     memset(&t, 0, sizeof(t));
     t.in = j.src;
@@ -598,6 +1015,9 @@ ba_status run_smooth(const SmoothJob& j, cudaStream_t st) {
     t.copy_src = j.copy_src;
     t.sharp_blur = j.sharp_blur;
     t.alpha = j.alpha;
+    if (streamable)
+      return j.out_dtype == BA_BF16 ? launch_stream<BA_BF16>(t, j.planes, st)
+                                    : launch_stream<BA_F32>(t, j.planes, st);
     return launch_tiled(t, j.planes, st);
   }
   AxisArgs a;

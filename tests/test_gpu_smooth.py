@@ -7,7 +7,7 @@ import pytest
 import torch
 
 from conftest import load_golden
-from helpers import assert_close_dtype, to_dev, to_np
+from helpers import as_f32, assert_close_dtype, to_dev, to_np
 
 pytestmark = pytest.mark.gpu
 
@@ -78,3 +78,40 @@ def test_elastic_transform_end_to_end(ba):
     p0 = t0.sample_params(2, x.shape, x.device)
     out0 = t0.apply(x, p0, mode="nearest")
     assert torch.equal(out0, x)
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+@pytest.mark.parametrize("pm", [None, "reflect", "replicate"])
+@pytest.mark.parametrize("shape,sig", [
+    ((2, 2, 130, 20, 40), (0.3, 1.2)),   # K <= 7, H split into chunks
+    ((1, 3, 136, 35, 33), (1.0, 2.8)),   # K 9..23, ragged W/D, H in chunks for K <= 15
+    ((3, 1, 24, 16, 32), (2.0, 2.7)),    # K = 23, one chunk, exact tiles
+])
+def test_smooth_stream_vs_oracle(ba, oracle_lib, dt, pm, shape, sig):
+    """The streaming smoother (taps up to 23) across padding modes, ragged
+    W/D blocks and H chunks, with a masked-out element.  Intensities in
+    [0, 1): with positive taps nothing cancels, so the bf16 bar (2 ulp)
+    applies to every voxel; zero-mean data is covered in fp32 above."""
+    from batchaug_b200 import ops
+    O = oracle_lib
+    rng = np.random.default_rng(sum(shape) + len(str(pm)))
+    x = rng.random(shape).astype(np.float32)
+    if dt == "bf16":
+        x = O.to_bf16_bits(x)
+    B = shape[0]
+    s = rng.uniform(*sig, (3, B)).astype(np.float32)
+    taps = [O.gaussian_1d_batch(si, 4.0) for si in s]
+    mask = np.ones(B, bool)
+    mask[0] = False
+    ref = O.separable_gauss(x, *taps, padding_mode=pm)
+    ref[0] = x[0]
+    out = ops.smooth3d(to_dev(x), *[to_dev(t) for t in taps], mask=to_dev(mask),
+                       padding_mode=pm)
+    o = to_np(out)
+    diff = np.abs(as_f32(o).astype(np.float64) - as_f32(ref))
+    try:
+        assert_close_dtype(o, ref)
+    except AssertionError:
+        at = np.unravel_index(diff.argmax(), diff.shape)
+        raise AssertionError(f"max |diff| {diff.max()} at {at}: {as_f32(o)[at]} vs "
+                             f"{as_f32(ref)[at]}") from None
