@@ -53,6 +53,8 @@ from .intensity import (
     RandScaleIntensityFixedMeand,
     RandShiftIntensity,
     RandShiftIntensityd,
+    RandSimulateLowResolution,
+    RandSimulateLowResolutiond,
     RandStdShiftIntensity,
     RandStdShiftIntensityd,
     ScaleIntensity,
@@ -87,6 +89,7 @@ __all__ = [
     "RandGaussianSmooth", "RandGaussianSmoothd",
     "RandRicianNoise", "RandRicianNoised", "RandScaleIntensity", "RandScaleIntensityd",
     "RandScaleIntensityFixedMean", "RandScaleIntensityFixedMeand", "RandShiftIntensity",
-    "RandShiftIntensityd", "RandStdShiftIntensity", "RandStdShiftIntensityd",
+    "RandShiftIntensityd", "RandSimulateLowResolution", "RandSimulateLowResolutiond",
+    "RandStdShiftIntensity", "RandStdShiftIntensityd",
     "ScaleIntensity", "ScaleIntensityd",
 ]

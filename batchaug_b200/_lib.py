@@ -77,6 +77,16 @@ class SharpenDesc(ctypes.Structure):
                 ("alpha", _P), ("mask", _P)]
 
 
+class LowresDesc(ctypes.Structure):
+    _fields_ = [("src", _P), ("dst", _P), ("dtype", _I32), ("down_mode", _I32),
+                ("up_mode", _I32), ("align_corners", _I32), ("batch", _I64), ("channels", _I64),
+                ("H", _I64), ("W", _I64), ("D", _I64), ("zoom", _P), ("mask", _P),
+                ("max_zoom", ctypes.c_double)]
+
+
+INTERP_MODES = {"nearest": 0, "nearest-exact": 1, "trilinear": 2, "area": 3}
+
+
 # Every symbol include/batchaug_b200.h declares, with its ctypes signature.
 SIGNATURES = {
     "ba_resample3d": (_I32, [ctypes.POINTER(ResampleDesc), _P]),
@@ -91,6 +101,8 @@ SIGNATURES = {
                            _I64, _I32, _P, _P, ctypes.c_size_t, _P]),
     "ba_sharpen_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SharpenDesc)]),
     "ba_sharpen3d": (_I32, [ctypes.POINTER(SharpenDesc), _P, ctypes.c_size_t, _P]),
+    "ba_lowres_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(LowresDesc)]),
+    "ba_lowres3d": (_I32, [ctypes.POINTER(LowresDesc), _P, ctypes.c_size_t, _P]),
     "ba_elastic_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _I64]),
     "ba_elastic_grid": (_I32, [_P, _U64, _U64, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P,
                                ctypes.c_size_t, _P]),

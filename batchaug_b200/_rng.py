@@ -42,6 +42,7 @@ S_RICIAN = 13
 S_STD_SHIFT = 14
 S_FIXED_MEAN = 15
 S_SHARPEN = 16
+S_LOWRES = 17
 
 
 def set_shard(element_offset: int = 0, global_batch: int | None = None) -> None:

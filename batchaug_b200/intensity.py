@@ -1,7 +1,8 @@
 """Intensity transforms: RandGaussianNoise, RandRicianNoise,
 RandAdjustContrast, RandScaleIntensity, RandShiftIntensity,
 RandStdShiftIntensity, RandScaleIntensityFixedMean, RandBiasField,
-ScaleIntensity, RandGaussianSmooth, RandGaussianSharpen (+ dict wrappers).
+ScaleIntensity, RandGaussianSmooth, RandGaussianSharpen,
+RandSimulateLowResolution (+ dict wrappers).
 
 Constructors, params keys and results follow the reference PyTorch backend
 (batchaug/pytorch/intensity/*.py), op by op in the tensor dtype.  Each
@@ -468,6 +469,43 @@ class RandGaussianSharpen(BatchTransform):
                              mask=params["mask"], padding_mode=self.padding_mode)
 
 
+class RandSimulateLowResolution(BatchTransform):
+    """Downsample each element by a zoom factor ~ U(zoom_range) and upsample
+    back (resolution.py:9-118); any of the 5-D F.interpolate modes
+    ("nearest", "nearest-exact", "trilinear", "area") for either step,
+    align_corners on a trilinear step.  One ``ba_lowres3d`` call; the
+    per-target-size groups of the reference need no grouping here."""
+
+    _stream = _rng.S_LOWRES
+
+    def __init__(self, prob: float = 0.1, zoom_range=(0.5, 1.0), downsample_mode="nearest",
+                 upsample_mode="trilinear", align_corners: bool = False):
+        super().__init__(prob=prob)
+        self.zoom_range = zoom_range
+        self.downsample_mode = downsample_mode
+        self.upsample_mode = upsample_mode
+        self.align_corners = align_corners
+
+    def _n_uniforms(self, shape):
+        return 2
+
+    def _host_params(self, B, shape, u, seed):
+        lo, hi = self.zoom_range
+        return {"mask": u[:, 0] < self.prob,
+                "zoom_factor": (u[:, 1] * np.float32(hi - lo) + np.float32(lo)).astype(np.float32)}
+
+    def _device_params(self, host, shape, device):
+        p = upload({"mask": host["mask"], "zoom_factor": host["zoom_factor"]}, device)
+        p["_max_zoom"] = float(host["zoom_factor"].max()) if len(host["zoom_factor"]) else 1.0
+        return p
+
+    def apply(self, tensor, params):
+        return ops.lowres3d(tensor, params["zoom_factor"], mask=params["mask"],
+                            downsample_mode=self.downsample_mode,
+                            upsample_mode=self.upsample_mode, align_corners=self.align_corners,
+                            max_zoom=params.get("_max_zoom"))
+
+
 # ---------------------------------------------------------------------------
 # Dict wrappers (same keys/params sharing as the reference)
 # ---------------------------------------------------------------------------
@@ -545,3 +583,13 @@ class RandGaussianSharpend(BatchDictTransform):
             prob=prob, sigma1_x=sigma1_x, sigma1_y=sigma1_y, sigma1_z=sigma1_z,
             sigma2_x=sigma2_x, sigma2_y=sigma2_y, sigma2_z=sigma2_z, alpha=alpha,
             padding_mode=padding_mode))
+
+
+class RandSimulateLowResolutiond(BatchDictTransform):
+    """Every key gets the same zoom factor and mask (resolution.py:121-147)."""
+
+    def __init__(self, keys, prob: float = 0.1, zoom_range=(0.5, 1.0), downsample_mode="nearest",
+                 upsample_mode="trilinear", align_corners: bool = False):
+        super().__init__(keys=keys, transform=RandSimulateLowResolution(
+            prob=prob, zoom_range=zoom_range, downsample_mode=downsample_mode,
+            upsample_mode=upsample_mode, align_corners=align_corners))

@@ -257,6 +257,37 @@ def sharpen3d(x: torch.Tensor, taps1, taps2, alpha, mask=None,
     return out
 
 
+def lowres3d(x: torch.Tensor, zoom, mask=None, downsample_mode="nearest",
+             upsample_mode="trilinear", align_corners=False, max_zoom=None) -> torch.Tensor:
+    """Down to max(1, rint(s * zoom[b])) per axis and back up, per element
+    (RandSimulateLowResolution.apply).  max_zoom bounds zoom (read from it
+    when None, which costs a device-to-host copy for a device tensor)."""
+    for m in (downsample_mode, upsample_mode):
+        if m not in L.INTERP_MODES:
+            raise ValueError(f"unsupported interpolation mode {m!r} for a 5-D tensor "
+                             f"(expected one of {sorted(L.INTERP_MODES)})")
+    x = _contig(x, "tensor")
+    B, C, H, W, D = x.shape
+    z = _dev_f32(zoom, x.device, "zoom").reshape(-1)
+    if z.numel() != B:
+        raise ValueError(f"zoom has {z.numel()} values for a batch of {B}")
+    if max_zoom is None:
+        max_zoom = float(z.max()) if B else 1.0
+    m = _dev_mask(mask, B, x.device)
+    out = torch.empty_like(x)
+    d = L.LowresDesc()
+    d.src, d.dst, d.dtype = x.data_ptr(), out.data_ptr(), L.dtype_code(x)
+    d.down_mode, d.up_mode = L.INTERP_MODES[downsample_mode], L.INTERP_MODES[upsample_mode]
+    d.align_corners = int(bool(align_corners))
+    d.batch, d.channels, d.H, d.W, d.D = B, C, H, W, D
+    d.zoom, d.mask, d.max_zoom = z.data_ptr(), L.ptr(m), float(max(max_zoom, 1e-30))
+    nbytes = L.lib.ba_lowres_workspace_bytes(ctypes.byref(d))
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+    L.check(L.lib.ba_lowres3d(ctypes.byref(d), ws.data_ptr(), nbytes, L.stream_ptr(x.device)),
+            "ba_lowres3d")
+    return out
+
+
 def elastic_grid(shape, taps, magnitude, *, u=None, seed=0, elem_offset=0,
                  device=None) -> torch.Tensor:
     """grid_sample grid (B,H,W,D,3) of Rand3DElastic from taps (B,K) and

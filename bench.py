@@ -469,6 +469,12 @@ def _secondary(name, torch, ba, device, rank):
         n = vol.numel()
         return ("RandGaussianSharpen(prob=1, sigma1 0.5..1, sigma2 0.5..sigma1, alpha 10..30) "
                 "on config 5's vol shard (8x2x160^3 bf16)", lambda i: sh.apply(vol, p), n, n * 4)
+    if name == "lowres":
+        xs = [torch.rand(8, 1, 128, 128, 128, device=device, generator=g) for _ in range(4)]
+        lr = ba.RandSimulateLowResolution(prob=1.0, zoom_range=(0.5, 1.0))
+        n = xs[0].numel()
+        return ("RandSimulateLowResolution(prob=1, zoom 0.5..1, nearest down, trilinear up), "
+                "B=8 C=1 128^3 fp32", lambda i: lr(xs[i % 4]), n, n * 8)
     if name == "config5-elastic":
         el = ba.Rand3DElastic(prob=1.0, sigma_range=(5, 7), magnitude_range=(50, 150))
         shape = (8, 2, 160, 160, 160)
@@ -548,7 +554,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="config2",
                     choices=["config2", "config3", "config4", "config5", "config5-smooth",
-                             "config5-elastic", "stats", "sharpen"],
+                             "config5-elastic", "stats", "sharpen", "lowres"],
                     help="config2 is the headline; the others time one whole step of that "
                          "configuration (for profiling and per-config numbers)")
     args = ap.parse_args()

@@ -282,6 +282,41 @@ BA_API ba_status ba_sharpen3d(const ba_sharpen_desc* desc, void* workspace, size
                               ba_stream_t stream);
 
 /*
+ * RandSimulateLowResolution.apply (resolution.py:74-118): per element a
+ * target size t = max(1, rint(float(s) * zoom[b])) per axis, then
+ * F.interpolate down to t with down_mode and back to (H, W, D) with up_mode,
+ * each result cast to dtype; masked-out elements copy src.  Modes are
+ * BA_INTERP_*; align_corners applies to a trilinear step.  Bit-identical to
+ * torch's CPU interpolate in fp32 and bf16.  A nearest or nearest-exact
+ * downsample is folded into the upsample (one pass, no scratch); trilinear
+ * or area downsampling stages each element's small volume in workspace.
+ * max_zoom bounds every zoom[b] (zoom values above it are clamped to it) and
+ * sizes that scratch.  Replaces the per-target-size F.interpolate loop of
+ * the reference (:94-116); the reference has no Triton path for it.
+ */
+typedef enum ba_interp_mode {
+  BA_INTERP_NEAREST = 0,
+  BA_INTERP_NEAREST_EXACT = 1,
+  BA_INTERP_TRILINEAR = 2,
+  BA_INTERP_AREA = 3
+} ba_interp_mode;
+
+typedef struct ba_lowres_desc {
+  const void* src;
+  void* dst; /* must not overlap src */
+  int32_t dtype;
+  int32_t down_mode, up_mode;
+  int32_t align_corners;
+  int64_t batch, channels, H, W, D;
+  const float* zoom;    /* (B,) fp32 */
+  const uint8_t* mask;  /* (B,) or NULL = every element */
+  double max_zoom;      /* >= every zoom[b] */
+} ba_lowres_desc;
+BA_API size_t ba_lowres_workspace_bytes(const ba_lowres_desc* desc);
+BA_API ba_status ba_lowres3d(const ba_lowres_desc* desc, void* workspace, size_t workspace_bytes,
+                             ba_stream_t stream);
+
+/*
  * Rand3DElastic.sample_params (elastic.py:37-99) from its uniform draw: grid
  * (B,H,W,D,3) = ((smooth(u*2-1) * magnitude) + centred grid) / ((N-1)/2),
  * reordered to grid_sample's xyz.  u is (B,3,H,W,D) fp32 in [0,1); when u is

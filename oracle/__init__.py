@@ -91,6 +91,8 @@ def _declare(L):
     L.ora_fixed_mean.argtypes = [P, P, I, P, P, I64, I64, I64, I, I]
     L.ora_rician.argtypes = [P, P, I, P, P, P, D, I, P, I64, I64, I]
     L.ora_sharpen_combine.argtypes = [P, P, P, P, I, P, P, I64, I64, I]
+    L.ora_lowres.argtypes = [P, P, I, I64, I64, I64, I64, I64, P, P, I, I, I, I]
+    L.ora_lowres.restype = I
 
 
 # ---------------------------------------------------------------------------
@@ -363,3 +365,22 @@ def sharpen(x, kernels1, kernels2, alpha, mask=None, padding_mode=None, nthreads
     bl = separable_gauss(x, *kernels1, padding_mode=padding_mode, nthreads=nthreads)
     db = separable_gauss(bl, *kernels2, padding_mode=padding_mode, nthreads=nthreads)
     return sharpen_combine(bl, db, x, alpha, mask, nthreads=nthreads)
+
+
+LOWRES_MODES = {"nearest": 0, "nearest-exact": 1, "trilinear": 2, "area": 3}
+
+
+def lowres(x, zoom, mask=None, downsample_mode="nearest", upsample_mode="trilinear",
+           align_corners=False, nthreads=0):
+    """RandSimulateLowResolution.apply (resolution.py:74-118)."""
+    x = _c(x)
+    B, C, H, W, D = x.shape
+    z = _c(np.asarray(zoom, np.float32).reshape(B))
+    out = np.empty_like(x)
+    m = _mask(mask, B)
+    rc = lib().ora_lowres(x.ctypes.data, out.ctypes.data, _dt(x), B, C, H, W, D, z.ctypes.data,
+                          _p(m), LOWRES_MODES[downsample_mode], LOWRES_MODES[upsample_mode],
+                          int(bool(align_corners)), int(nthreads))
+    if rc:
+        raise ValueError("lowres: unsupported mode")
+    return out

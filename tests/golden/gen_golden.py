@@ -42,7 +42,7 @@ def save(name: str, **arrays):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("BATCHAUG_REFERENCE", ""))
-    ap.add_argument("--only", choices=["stats", "sharpen"], default=None,
+    ap.add_argument("--only", choices=["stats", "sharpen", "lowres"], default=None,
                     help="write only this group of fixtures")
     args = ap.parse_args()
     if args.reference:
@@ -55,6 +55,9 @@ def main():
         return
     if args.only == "sharpen":
         gen_sharpen(P)
+        return
+    if args.only == "lowres":
+        gen_lowres(P)
         return
     from batchaug.pytorch.geometric.affine import monai_affine_to_theta
     from batchaug.pytorch.intensity.smooth import gaussian_1d_batch
@@ -215,6 +218,7 @@ def main():
          noise_mask=pn["mask"], vol_out=vo, seg_out=so)
     gen_stats_ops(P)
     gen_sharpen(P)
+    gen_lowres(P)
 
 
 def gen_stats_ops(P):
@@ -287,6 +291,34 @@ def gen_sharpen(P):
                 rec[f"{name}_kernel1_{a}"] = p[f"kernel1_{a}"]
                 rec[f"{name}_kernel2_{a}"] = p[f"kernel2_{a}"]
         save(f"sharpen_{tag}", **rec)
+
+
+LOWRES_MODES = (("nearest", "trilinear", False), ("nearest-exact", "trilinear", False),
+                ("nearest", "trilinear", True), ("trilinear", "trilinear", False),
+                ("trilinear", "nearest", True), ("area", "trilinear", False),
+                ("nearest-exact", "area", False), ("area", "nearest-exact", False))
+
+
+def gen_lowres(P):
+    """RandSimulateLowResolution for every (downsample, upsample,
+    align_corners) combination above, with the sampled zoom factors and
+    masks; odd sizes so the targets round both ways."""
+    dev = torch.device("cpu")
+    torch.set_num_threads(1)
+    for dt, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
+        torch.manual_seed(110)
+        B, C, H, W, D = 4, 1, 11, 14, 17
+        x = torch.rand(B, C, H, W, D).to(dt)
+        rec = {"x": x}
+        for i, (dm, um, ac) in enumerate(LOWRES_MODES):
+            t = P.RandSimulateLowResolution(prob=0.8, zoom_range=(0.3, 1.0), downsample_mode=dm,
+                                            upsample_mode=um, align_corners=ac)
+            p = t.sample_params(B, x.shape, dev)
+            p["mask"][0] = True
+            p["mask"][1] = False
+            rec.update({f"m{i}_mask": p["mask"], f"m{i}_zoom": p["zoom_factor"],
+                        f"m{i}_out": t.apply(x, p)})
+        save(f"lowres_{tag}", **rec)
 
 
 if __name__ == "__main__":

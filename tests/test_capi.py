@@ -38,7 +38,8 @@ def test_struct_layouts_match_header(ba, tmp_path):
     if cc is None:
         pytest.skip("no C compiler")
     structs = {"ba_resample_key": L.ResampleKey, "ba_resample_desc": L.ResampleDesc,
-               "ba_op": L.Op, "ba_chain_desc": L.ChainDesc, "ba_sharpen_desc": L.SharpenDesc}
+               "ba_op": L.Op, "ba_chain_desc": L.ChainDesc, "ba_sharpen_desc": L.SharpenDesc,
+               "ba_lowres_desc": L.LowresDesc}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "batchaug_b200.h"',
              "int main(void) {"]
     for cname, ct in structs.items():
@@ -103,6 +104,14 @@ def test_validation_without_gpu(ba):
     sd.K2[1], sd.padding, sd.K1[0] = 5, 1, 11  # reflect needs K/2 < H
     assert L.lib.ba_sharpen3d(ctypes.byref(sd), None, 0, None) == L.BA_EINVAL
     assert b"reflect" in L.lib.ba_last_error()
+    ld = L.LowresDesc()
+    ld.batch, ld.channels, ld.H, ld.W, ld.D, ld.dtype, ld.max_zoom = 2, 3, 10, 11, 12, 0, 0.6
+    assert L.lib.ba_lowres_workspace_bytes(ctypes.byref(ld)) == 0  # nearest downsample: none
+    ld.down_mode = 2  # trilinear: scratch for the largest target, rint(s * 0.6)
+    assert L.lib.ba_lowres_workspace_bytes(ctypes.byref(ld)) == 2 * 3 * 6 * 7 * 7 * 4
+    ld.up_mode = 9
+    assert L.lib.ba_lowres3d(ctypes.byref(ld), None, 0, None) == L.BA_EINVAL
+    assert b"mode" in L.lib.ba_last_error()
 
 
 def test_gauss_taps_len_matches_reference_rule(ba):

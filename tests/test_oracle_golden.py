@@ -208,3 +208,19 @@ def test_sharpen(oracle_lib, tag):
         for a, s in zip("hwd", "xyz"):
             np.testing.assert_allclose(O.gaussian_1d_batch(g[f"{name}_sigma1_{s}"]),
                                        g[f"{name}_kernel1_{a}"], rtol=0, atol=1e-7)
+
+
+LOWRES_MODES = (("nearest", "trilinear", False), ("nearest-exact", "trilinear", False),
+                ("nearest", "trilinear", True), ("trilinear", "trilinear", False),
+                ("trilinear", "nearest", True), ("area", "trilinear", False),
+                ("nearest-exact", "area", False), ("area", "nearest-exact", False))
+
+
+@pytest.mark.parametrize("tag", ["f32", "bf16"])
+def test_lowres(oracle_lib, tag):
+    """RandSimulateLowResolution for every downsample/upsample pair: bit-exact
+    against the reference's outputs in fp32 and bf16."""
+    g = load_golden(f"lowres_{tag}")
+    for i, (dm, um, ac) in enumerate(LOWRES_MODES):
+        out = oracle_lib.lowres(g["x"], g[f"m{i}_zoom"], g[f"m{i}_mask"], dm, um, ac)
+        assert np.array_equal(out, g[f"m{i}_out"]), (dm, um, ac)
