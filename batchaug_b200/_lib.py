@@ -90,6 +90,7 @@ INTERP_MODES = {"nearest": 0, "nearest-exact": 1, "trilinear": 2, "area": 3}
 # Every symbol include/batchaug_b200.h declares, with its ctypes signature.
 SIGNATURES = {
     "ba_resample3d": (_I32, [ctypes.POINTER(ResampleDesc), _P]),
+    "ba_compose_field": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P]),
     "ba_intensity_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(ChainDesc)]),
     "ba_intensity_chain": (_I32, [ctypes.POINTER(ChainDesc), _P, ctypes.c_size_t, _P]),
     "ba_intensity_chain_noalloc": (_I32, [ctypes.POINTER(ChainDesc), _P]),

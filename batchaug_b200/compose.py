@@ -21,6 +21,17 @@ B200 execution:
   bias field, ScaleIntensity) becomes one ``ba_intensity_chain`` per key —
   the same ops in the same order as applying them one by one, so results are
   unchanged, in fewer HBM passes.  This applies in eager mode too.
+
+Extension (``fuse_elastic=True``, lazy mode only; off by default, which keeps
+the reference's order): a Rand3DElasticd followed by geometric transforms is
+resampled once instead of twice.  Pending affines before the elastic
+transform are materialised first, as the reference does; the elastic grid is
+then held, the affines after it accumulate as usual, and at the next
+materialisation ``ba_compose_field`` folds them into the grid
+(I(field(A(p))), the displacement extended by clamping) and one
+``ba_resample3d`` samples each key with the elastic transform's per-key mode
+and padding.  The result differs from the two resamples by the second
+interpolation they perform (less blur), not by the geometry.
 """
 from __future__ import annotations
 
@@ -34,9 +45,10 @@ from .intensity import _FusibleIntensity
 
 class Compose:
     def __init__(self, transforms: list, lazy: bool = False, mode="bilinear",
-                 padding_mode="zeros"):
+                 padding_mode="zeros", fuse_elastic: bool = False):
         self.transforms = transforms
         self.lazy = lazy
+        self.fuse_elastic = fuse_elastic
         self._mode = mode
         self._padding_mode = padding_mode
 
@@ -45,6 +57,11 @@ class Compose:
     def _is_geometric(t) -> bool:
         inner = getattr(t, "transform", None)
         return inner is not None and hasattr(inner, "to_affine")
+
+    @staticmethod
+    def _is_elastic(t) -> bool:
+        from .geometric import Rand3DElastic
+        return isinstance(getattr(t, "transform", None), Rand3DElastic) and hasattr(t, "_mode")
 
     @staticmethod
     def _is_fusible(t) -> bool:
@@ -98,9 +115,45 @@ class Compose:
                 i += 1
         return d
 
+    # -- held elastic field composed with the affines after it (extension) ---
+    def _materialize_fields(self, d: dict, pending: dict, fields: dict) -> dict:
+        from .geometric import monai_affine_to_theta
+        groups: dict[tuple, tuple] = {}
+        for key, (fstate, _, _) in fields.items():
+            if key in d:
+                astate = pending.get(key)
+                t = d[key]
+                gk = (id(fstate), id(astate), t.shape[0], tuple(t.shape[2:]), t.device)
+                groups.setdefault(gk, (fstate, astate, []))[2].append(key)
+        for fstate, astate, keys in groups.values():
+            grid, mask_f = fstate
+            B = grid.shape[0]
+            spatial = tuple(d[keys[0]].shape[2:])
+            if astate is not None:
+                affine, mask_a = astate
+                theta = monai_affine_to_theta(affine, spatial)
+            else:
+                mask_a = np.zeros(B, bool)
+                theta = np.tile(np.eye(4, dtype=np.float32), (B, 1, 1))
+            mask = mask_f | mask_a
+            if not mask.any():
+                continue
+            g = ops.compose_field(grid, theta, mask_field=mask_f, mask_affine=mask_a)
+            for i in range(0, len(keys), L.BA_MAX_KEYS):
+                chunk = keys[i:i + L.BA_MAX_KEYS]
+                outs = ops.resample3d([d[k] for k in chunk], grid=g, mask=mask, align_corners=True,
+                                      modes=[fields[k][1] for k in chunk],
+                                      paddings=[fields[k][2] for k in chunk])
+                for k, o in zip(chunk, outs):
+                    d[k] = o
+        return d
+
     # -- lazy materialisation (compose.py:71-110) ---------------------------
-    def _materialize(self, d: dict, pending: dict) -> dict:
+    def _materialize(self, d: dict, pending: dict, fields: dict | None = None) -> dict:
         d = dict(d)
+        if fields:
+            d = self._materialize_fields(d, pending, fields)
+            pending = {k: v for k, v in pending.items() if k not in fields}
         groups: dict[int, tuple] = {}
         for key, state in pending.items():
             if key in d:
@@ -134,10 +187,26 @@ class Compose:
         # key -> (affine (B,4,4) f32, mask (B,) bool); keys with one history
         # share one state object, so they materialise in one launch.
         pending: dict[str, tuple] = {}
+        # key -> ((grid, field mask), mode, padding) of a held elastic field
+        fields: dict[str, tuple] = {}
         i = 0
         ts = list(self.transforms)
         while i < len(ts):
             t = ts[i]
+            if self.fuse_elastic and self._is_elastic(t):
+                if pending or fields:
+                    d = self._materialize(d, pending, fields)
+                    pending.clear()
+                    fields.clear()
+                src = d[t.keys[0]]
+                p = t.transform.sample_params(src.shape[0], src.shape, src.device)
+                fstate = (p["grid"], np.asarray(p["_host"]["mask"], bool))
+                for key in t.keys:
+                    if key in d:
+                        fields[key] = (fstate, t._mode.get(key, "bilinear"),
+                                       t._padding_mode.get(key, t._default_padding))
+                i += 1
+                continue
             if self._is_geometric(t):
                 inner = t.transform
                 host = inner.sample_host(B, shape)
@@ -156,9 +225,10 @@ class Compose:
                     pending[key] = new
                 i += 1
                 continue
-            if pending:
-                d = self._materialize(d, pending)
+            if pending or fields:
+                d = self._materialize(d, pending, fields)
                 pending.clear()
+                fields.clear()
             if self._is_fusible(t):
                 j = i
                 while j < len(ts) and self._is_fusible(ts[j]):
@@ -168,6 +238,6 @@ class Compose:
             else:
                 d = t(d)
                 i += 1
-        if pending:
-            d = self._materialize(d, pending)
+        if pending or fields:
+            d = self._materialize(d, pending, fields)
         return d

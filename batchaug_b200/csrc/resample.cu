@@ -792,6 +792,95 @@ bool overlaps(const void* a, size_t na, const void* b, size_t nb) {
   return pa < pb + nb && pb < pa + na;
 }
 
+// ---------------------------------------------------------------------------
+// Elastic field composed with a following affine (an extension: the
+// reference resamples twice, elastic then affine).  For output voxel p the
+// affine maps p into the elastic output's voxel space exactly as
+// affine_grid + grid_sample(align_corners=False) would (u); the elastic grid
+// F (grid_sample coordinates, align_corners=True, xyz order) is read there
+// by trilinear interpolation at u clamped to the volume (uc), and the
+// displacement is extended beyond the volume by clamping:
+//   G(p) = F~(uc) + (u - uc) / half,   half = max((N-1)/2, 1e-6),
+// so a voxel the affine moves out of view still lands outside and takes the
+// key's padding when G is sampled.  Elements without the affine take
+// G = F; elements without the elastic field take the identity grid for F.
+// One thread per output voxel; grid (ceil(HWD / 256), B).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float lerp_rn(float a, float b, float g, float f) {
+  return __fadd_rn(__fmul_rn(a, g), __fmul_rn(b, f));
+}
+
+// identity grid value of index q along an axis of n (elastic convention)
+__device__ __forceinline__ float ident_coord(int q, int n) {
+  const float half_lo = __fdiv_rn(__fsub_rn((float)n, 1.0f), 2.0f);
+  const float step = __fdiv_rn(__fsub_rn(half_lo, -half_lo), __fsub_rn((float)n, 1.0f));
+  const float c0 = linspace_at(-half_lo, half_lo, step, q, n);
+  return __fdiv_rn(c0, half_lo < 1e-6f ? 1e-6f : half_lo);
+}
+
+__global__ void __launch_bounds__(256)
+    compose_field_kernel(const float* __restrict__ field, const float* __restrict__ theta,
+                         const uint8_t* __restrict__ mask_field,
+                         const uint8_t* __restrict__ mask_affine, int H, int W, int D,
+                         float* __restrict__ out) {
+  const int64_t b = blockIdx.y;
+  const int64_t hwd = (int64_t)H * W * D;
+  const int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= hwd) return;
+  const int h = (int)(s / ((int64_t)W * D)), w = (int)((s / D) % W), d = (int)(s % D);
+  const bool has_field = mask_field == nullptr || mask_field[b] != 0;
+  const bool has_affine = mask_affine == nullptr || mask_affine[b] != 0;
+  const int n[3] = {D, W, H};  // x, y, z extents
+  float* o = out + (b * hwd + s) * 3;
+  auto F = [&](int z, int y, int x, int r) -> float {
+    if (has_field) return __ldg(field + ((b * H + z) * (int64_t)W * D + (int64_t)y * D + x) * 3 + r);
+    return ident_coord(r == 0 ? x : (r == 1 ? y : z), n[r]);
+  };
+  if (!has_affine) {
+#pragma unroll
+    for (int r = 0; r < 3; ++r) o[r] = F(h, w, d, r);
+    return;
+  }
+  // affine_grid's coordinates (align_corners=False) and the bmm as the
+  // resample kernel computes them: x*t0, fused y and z terms, translation
+  const float bx = base_coord(d, D, 0), by = base_coord(w, W, 0), bz = base_coord(h, H, 0);
+  const float* t = theta + b * 12;
+  float u[3], uc[3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    const float g = __fadd_rn(
+        __fmaf_rn(bz, __ldg(t + r * 4 + 2), __fmaf_rn(by, __ldg(t + r * 4 + 1), __fmul_rn(bx, __ldg(t + r * 4)))),
+        __ldg(t + r * 4 + 3));
+    // grid_sampler_unnormalize, align_corners=False
+    u[r] = __fmul_rn(__fsub_rn(__fmul_rn(__fadd_rn(g, 1.0f), (float)n[r]), 1.0f), 0.5f);
+    const float hi = (float)(n[r] - 1);
+    uc[r] = u[r] != u[r] ? 0.0f : fminf(fmaxf(u[r], 0.0f), hi);  // NaN -> 0
+  }
+  int i0[3], i1[3];
+  float f[3], g1[3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    i0[r] = (int)floorf(uc[r]);
+    i1[r] = i0[r] + 1 < n[r] ? i0[r] + 1 : i0[r];
+    f[r] = __fsub_rn(uc[r], (float)i0[r]);
+    g1[r] = __fsub_rn(1.0f, f[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    // x, then y, then z
+    const float c00 = lerp_rn(F(i0[2], i0[1], i0[0], r), F(i0[2], i0[1], i1[0], r), g1[0], f[0]);
+    const float c01 = lerp_rn(F(i0[2], i1[1], i0[0], r), F(i0[2], i1[1], i1[0], r), g1[0], f[0]);
+    const float c10 = lerp_rn(F(i1[2], i0[1], i0[0], r), F(i1[2], i0[1], i1[0], r), g1[0], f[0]);
+    const float c11 = lerp_rn(F(i1[2], i1[1], i0[0], r), F(i1[2], i1[1], i1[0], r), g1[0], f[0]);
+    const float c0 = lerp_rn(c00, c01, g1[1], f[1]);
+    const float c1 = lerp_rn(c10, c11, g1[1], f[1]);
+    const float fi = lerp_rn(c0, c1, g1[2], f[2]);
+    const float half_lo = __fdiv_rn(__fsub_rn((float)n[r], 1.0f), 2.0f);
+    const float half = half_lo < 1e-6f ? 1e-6f : half_lo;
+    o[r] = __fadd_rn(fi, __fdiv_rn(__fsub_rn(u[r], uc[r]), half));
+  }
+}
+
 }  // namespace
 }  // namespace ba
 
@@ -962,4 +1051,22 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
     if (s1 != BA_OK) return s1;
   }
   return BA_OK;
+}
+
+extern "C" ba_status ba_compose_field(const float* field, const float* theta,
+                                      const uint8_t* mask_field, const uint8_t* mask_affine,
+                                      int64_t batch, int64_t H, int64_t W, int64_t D, float* grid,
+                                      ba_stream_t stream) {
+  using namespace ba;
+  clear_error();
+  BA_REQUIRE(batch >= 0 && H > 0 && W > 0 && D > 0, "ba_compose_field: bad shape");
+  BA_REQUIRE(batch <= 65535, "ba_compose_field: batch exceeds 65535");
+  BA_REQUIRE(H * W * D < ((int64_t)1 << 31), "ba_compose_field: volume exceeds 2^31 voxels");
+  if (batch == 0) return BA_OK;
+  BA_REQUIRE(field && theta && grid, "ba_compose_field: NULL pointer");
+  const int64_t hwd = H * W * D;
+  dim3 g((unsigned)((hwd + 255) / 256), (unsigned)batch);
+  compose_field_kernel<<<g, 256, 0, (cudaStream_t)stream>>>(field, theta, mask_field, mask_affine,
+                                                          (int)H, (int)W, (int)D, grid);
+  return check_launch("ba_compose_field");
 }

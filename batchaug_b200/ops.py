@@ -288,6 +288,27 @@ def lowres3d(x: torch.Tensor, zoom, mask=None, downsample_mode="nearest",
     return out
 
 
+def compose_field(field: torch.Tensor, theta, mask_field=None, mask_affine=None) -> torch.Tensor:
+    """Grid (B,H,W,D,3) of the elastic field ``field`` followed by the affine
+    ``theta`` (B,3,4) (see ba_compose_field): one grid_sample with it
+    (align_corners=True) gives I(field(A(p)))."""
+    field = _contig(field.to(torch.float32), "field")
+    if field.dim() != 5 or field.shape[-1] != 3:
+        raise ValueError(f"field must be (B,H,W,D,3), got {tuple(field.shape)}")
+    B, H, W, D, _ = field.shape
+    th = _dev_f32(theta, field.device, "theta").reshape(B, -1)
+    if th.shape[1] == 16:
+        th = th.reshape(B, 4, 4)[:, :3, :].contiguous()
+    th = th.reshape(B, 3, 4).contiguous()
+    mf = _dev_mask(mask_field, B, field.device)
+    ma = _dev_mask(mask_affine, B, field.device)
+    out = torch.empty_like(field)
+    L.check(L.lib.ba_compose_field(field.data_ptr(), th.data_ptr(), L.ptr(mf), L.ptr(ma), B, H, W,
+                                   D, out.data_ptr(), L.stream_ptr(field.device)),
+            "ba_compose_field")
+    return out
+
+
 def elastic_grid(shape, taps, magnitude, *, u=None, seed=0, elem_offset=0,
                  device=None) -> torch.Tensor:
     """grid_sample grid (B,H,W,D,3) of Rand3DElastic from taps (B,K) and

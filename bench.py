@@ -443,6 +443,22 @@ def _secondary(name, torch, ba, device, rank):
         return ("config 5 per-GPU shard: elastic + affine(0.1) -> bias(0.1) -> smooth(0.1) -> "
                 "ScaleIntensity, vol 8x2x160^3 bf16 + seg 8x2x160^3 f32",
                 lambda i: c({"vol": vol, "seg": seg}), n, vol.numel() * 4 + seg.numel() * 8)
+    if name == "config5-fused":
+        vol = torch.rand(8, 2, 160, 160, 160, device=device, generator=g).bfloat16()
+        seg = torch.randint(0, 8, (8, 2, 160, 160, 160), device=device, generator=g).float()
+        c = ba.Compose([ba.Rand3DElasticd(["vol", "seg"], prob=1.0, sigma_range=(5, 7),
+                                          magnitude_range=(50, 150),
+                                          mode={"vol": "bilinear", "seg": "nearest"}),
+                        ba.RandAffined(["vol", "seg"], prob=0.1, rotate_range=0.5),
+                        ba.RandBiasFieldd(["vol"], prob=0.1),
+                        ba.RandGaussianSmoothd(["vol"], prob=0.1, sigma_x=(0.5, 1.5),
+                                               sigma_y=(0.5, 1.5), sigma_z=(0.5, 1.5)),
+                        ba.ScaleIntensityd(["vol"])], lazy=True,
+                       mode={"vol": "bilinear", "seg": "nearest"}, fuse_elastic=True)
+        n = vol.numel() + seg.numel()
+        return ("config 5 per-GPU shard with the elastic∘affine single resample "
+                "(Compose(fuse_elastic=True), an extension), vol 8x2x160^3 bf16 + seg f32",
+                lambda i: c({"vol": vol, "seg": seg}), n, vol.numel() * 4 + seg.numel() * 8)
     if name == "config5-smooth":
         vol = torch.rand(8, 2, 160, 160, 160, device=device, generator=g).bfloat16()
         sm = ba.RandGaussianSmooth(prob=1.0, sigma_x=(0.5, 1.5), sigma_y=(0.5, 1.5),
@@ -554,7 +570,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="config2",
                     choices=["config2", "config3", "config4", "config5", "config5-smooth",
-                             "config5-elastic", "stats", "sharpen", "lowres"],
+                             "config5-elastic", "config5-fused", "stats", "sharpen", "lowres"],
                     help="config2 is the headline; the others time one whole step of that "
                          "configuration (for profiling and per-config numbers)")
     args = ap.parse_args()

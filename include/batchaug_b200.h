@@ -101,6 +101,27 @@ typedef struct ba_resample_desc {
  */
 BA_API ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t stream);
 
+/*
+ * Elastic field composed with the affine that follows it, as one grid
+ * (an extension: the reference resamples twice, Rand3DElastic.apply
+ * elastic.py:101-125 and then Compose._materialize compose.py:71-110).
+ * field: the elastic grid_sample grid (B,H,W,D,3), align_corners=True, xyz
+ * order (Rand3DElastic.sample_params, elastic.py:37-99); theta: affine_grid
+ * theta (B,3,4) of the affine applied after it.  For output voxel p, with u
+ * the affine's source position in voxels of the elastic output
+ * (affine_grid + unnormalise, align_corners=False), uc = u clamped to the
+ * volume and half = max((N-1)/2, 1e-6) per axis:
+ *   grid(p) = trilinear(field, uc) + (u - uc) / half
+ * i.e. the elastic displacement extended by clamping; sampling the input
+ * once with grid (align_corners=True) gives I(field(A(p))).  Elements with
+ * mask_affine[b] == 0 take grid = field; elements with mask_field[b] == 0
+ * use the identity grid for field.  Either mask may be NULL (all set).
+ */
+BA_API ba_status ba_compose_field(const float* field, const float* theta,
+                                  const uint8_t* mask_field, const uint8_t* mask_affine,
+                                  int64_t batch, int64_t H, int64_t W, int64_t D, float* grid,
+                                  ba_stream_t stream);
+
 /* ---------------------------------------------------------------------- */
 /* Intensity chain                                                         */
 /* ---------------------------------------------------------------------- */

@@ -93,6 +93,7 @@ def _declare(L):
     L.ora_sharpen_combine.argtypes = [P, P, P, P, I, P, P, I64, I64, I]
     L.ora_lowres.argtypes = [P, P, I, I64, I64, I64, I64, I64, P, P, I, I, I, I]
     L.ora_lowres.restype = I
+    L.ora_compose_field.argtypes = [P, P, P, P, I64, I64, I64, I64, P]
 
 
 # ---------------------------------------------------------------------------
@@ -383,4 +384,17 @@ def lowres(x, zoom, mask=None, downsample_mode="nearest", upsample_mode="triline
                           int(bool(align_corners)), int(nthreads))
     if rc:
         raise ValueError("lowres: unsupported mode")
+    return out
+
+
+def compose_field(field, theta, mask_field=None, mask_affine=None):
+    """The elastic grid (B,H,W,D,3) composed with the affine theta (B,3,4)
+    that follows it (an extension; see oracle_compose.c)."""
+    field = _c(field, np.float32)
+    B, H, W, D, _ = field.shape
+    th = _c(np.asarray(theta, np.float32).reshape(B, -1)[:, :12])
+    out = np.empty_like(field)
+    mf, ma = _mask(mask_field, B), _mask(mask_affine, B)  # held until the call returns
+    lib().ora_compose_field(field.ctypes.data, th.ctypes.data, _p(mf), _p(ma), B, H, W, D,
+                            out.ctypes.data)
     return out
