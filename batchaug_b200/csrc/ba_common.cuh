@@ -118,6 +118,28 @@ constexpr int32_t KEY_MAX_NAN = (int32_t)0x7FFFFFFF;  // above key(+inf)
 constexpr int32_t KEY_POS_INF = (int32_t)0x7F800000;
 constexpr int32_t KEY_NEG_INF = (int32_t)(0xFF800000u ^ 0x7FFFFFFFu);
 
+// RN(1/b) when a/b can take the reciprocal path of div_rn, else 0.
+__device__ __forceinline__ float recip_for_div(float b) {
+  const float m = fabsf(b);
+  return (m >= 0x1p-120f && m <= 0x1p120f) ? __frcp_rn(b) : 0.0f;
+}
+
+// a / b rounded to nearest, from y = RN(1/b) (recip_for_div): q = RN(a*y),
+// the remainder r = a - b*q is exact in one fma, and RN(q + r*y) is the
+// correctly rounded quotient (P. Markstein, "IA-64 and Elementary Functions",
+// 2000, the correction step for a correctly rounded reciprocal) whenever a, b
+// and the quotient are normal.  Zero, tiny, huge and non-finite quotients take
+// the plain division.
+__device__ __forceinline__ float div_rn(float a, float b, float y) {
+  if (y != 0.0f) {
+    const float q = __fmul_rn(a, y);
+    const float aq = fabsf(q);
+    if (a == 0.0f) return q;
+    if (aq >= 0x1p-100f && aq <= 0x1p100f) return __fmaf_rn(__fmaf_rn(-q, b, a), y, q);
+  }
+  return __fdiv_rn(a, b);
+}
+
 __device__ __forceinline__ float decode_min_key(int32_t k) {
   return k == KEY_MIN_NAN ? __int_as_float(0x7FC00000) : fkey_inv(k);
 }

@@ -168,28 +168,6 @@ struct OpConst {
 __device__ __forceinline__ bool is_bf16_value(float f) { return round_bf16(f) == f; }
 __device__ __forceinline__ uint32_t splat_bf16(float f) { return pack_bf16x2(f, f); }
 
-// RN(1/b) when a/b can take the reciprocal path of div_rn, else 0.
-__device__ __forceinline__ float recip_for_div(float b) {
-  const float m = fabsf(b);
-  return (m >= 0x1p-120f && m <= 0x1p120f) ? __frcp_rn(b) : 0.0f;
-}
-
-// a / b rounded to nearest, from y = RN(1/b) (recip_for_div): q = RN(a*y),
-// the remainder r = a - b*q is exact in one fma, and RN(q + r*y) is the
-// correctly rounded quotient (P. Markstein, "IA-64 and Elementary Functions",
-// 2000, the correction step for a correctly rounded reciprocal) whenever a, b
-// and the quotient are normal.  Zero, tiny, huge and non-finite quotients take
-// the plain division.
-__device__ __forceinline__ float div_rn(float a, float b, float y) {
-  if (y != 0.0f) {
-    const float q = __fmul_rn(a, y);
-    const float aq = fabsf(q);
-    if (a == 0.0f) return q;
-    if (aq >= 0x1p-100f && aq <= 0x1p100f) return __fmaf_rn(__fmaf_rn(-q, b, a), y, q);
-  }
-  return __fdiv_rn(a, b);
-}
-
 // a / b rounded to fp32 and then to bf16, for bf16 values a and b: the
 // bf16 rounding of RN(a * RN(1/b)) already equals it.  Reason: a/b of two
 // 8-bit significands is never a bf16 midpoint and, when not exact, is at

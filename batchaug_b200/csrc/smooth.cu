@@ -565,6 +565,18 @@ __device__ __forceinline__ void conv_regs(Load x, const float (&w)[KMAX], float*
   }
 }
 
+// Taps of length K (odd, <= KMAX) centred in a KMAX array with zeros on both
+// sides: correlating a window whose centre sits at PMAX = (KMAX-1)/2 then
+// equals the K-tap correlation, the extra taps adding exact zeros.
+template <int KMAX>
+__device__ __forceinline__ void load_taps_centred(const float* taps, int64_t b, int K,
+                                                  float (&w)[KMAX]) {
+  const int off = (KMAX - K) / 2;
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k)
+    w[k] = (k >= off && k < off + K) ? __ldg(taps + b * K + (k - off)) : 0.0f;
+}
+
 template <int KMAX>
 __device__ __forceinline__ void load_taps_regs(const float* taps, int64_t b, int K, float (&w)[KMAX]) {
 #pragma unroll
@@ -927,6 +939,319 @@ ba_status launch_axis(int axis, const AxisArgs& a, int64_t planes, cudaStream_t 
   return check_launch("axis pass");
 }
 
+// ===========================================================================
+// Wide-tap separable smoothing (taps 24..63; the elastic field's K=43).
+//
+// Three coalesced passes, D then W then H, fp32 intermediates in scratch:
+//   - D: a CTA stages RL_ROWS rows with their padded halo in shared memory
+//     (for the elastic field the Philox draw is generated right there, so
+//     the uniform field is never written) and correlates SS_RD outputs per
+//     thread unit from a register window;
+//   - W and H: each thread walks one line along the axis, lanes along D
+//     (every load is coalesced and read once).  The line's outputs
+//     accumulate in a ring of KMAX registers: the input at padded step q
+//     adds w[k] * x to output q - k, and output q - (KMAX-1) is complete and
+//     stored.  The walk is unrolled by KMAX, so every ring slot is a
+//     compile-time register.  Outputs accumulate in tap order, as every
+//     other smoothing path does.
+// Taps are centred in KMAX-wide arrays (zeros outside the runtime K).  The
+// H pass writes the output dtype (masked-out elements copy the input) or,
+// for the elastic field, the grid_sample grid.
+// ===========================================================================
+constexpr int RL_THREADS = 128;
+constexpr int RL_ROWS = 32;  // D pass: rows staged per CTA
+
+// 4-byte cp.async (a thread stages its own inputs; no other thread reads them)
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(gmem) : "memory");
+}
+
+enum { RL_SRC_DT = 0, RL_SRC_PHILOX = 1, RL_SRC_UNIFORM = 2 };
+enum { RL_OUT_F32 = 0, RL_OUT_DT = 1, RL_OUT_GRID = 2 };
+
+struct RollArgs {
+  const void* src;      // RL_SRC_DT: volume (in_dtype); RL_SRC_UNIFORM: u fp32
+  int32_t in_dtype;
+  void* dst;            // fp32 scratch, the output volume (out_dtype) or the grid
+  int32_t out_dtype;
+  const float* taps;    // (B, K) taps of this axis
+  int32_t K;
+  int32_t padding;
+  int64_t batch, P, H, W, D;  // P planes per element
+  const uint8_t* mask;  // RL_OUT_DT: masked-out elements copy copy_src (or are skipped)
+  const void* copy_src;
+  const void* sharp_blur;     // RL_OUT_DT: unsharp-mask combination with this blur
+  const float* alpha;
+  const float* magnitude;   // RL_OUT_GRID
+  uint32_t seed_lo, seed_hi;  // RL_SRC_PHILOX
+  uint64_t elem_offset;
+};
+
+// D pass: grid (ceil(B*P*H*W / RL_ROWS)); each row is one line along D.
+template <int KMAX, int SRC>
+__global__ void __launch_bounds__(RL_THREADS) roll_d_kernel(const __grid_constant__ RollArgs a) {
+  constexpr int PMAX = (KMAX - 1) / 2;
+  extern __shared__ float srow[];
+  const int D = (int)a.D;
+  const int LS = D + KMAX - 1;  // staged row length
+  // one pad word every 8 entries (the R=8 units of a row read distinct banks)
+  // and SS_RD - 1 zero entries past the row, so a unit's window never needs
+  // a bounds check
+  const int LSP = pidx(LS + SS_RD - 2) + 1;
+  const int64_t rows_per_elem = a.P * a.H * a.W;
+  const int64_t total = a.batch * rows_per_elem;
+  const int64_t row0 = (int64_t)blockIdx.x * RL_ROWS;
+  const int tid = threadIdx.x;
+  for (int r = 0; r < RL_ROWS; ++r) {
+    const int64_t row = row0 + r;
+    if (row >= total) break;  // the same for every thread
+    float* sr = srow + r * LSP;
+    if (SRC == RL_SRC_PHILOX) {
+      // the elastic draw u*2-1 keyed as the standalone draw kernel keys it:
+      // flat position p = comp*HWD + s of element b, four per Philox block
+      // (D % 4 == 0, so a row starts a block); zero padding around it
+      const int64_t b = row / rows_per_elem;
+      const int64_t p = (row - b * rows_per_elem) * D;
+      const uint64_t eb = a.elem_offset + (uint64_t)b;
+      for (int j = tid; j < PMAX; j += RL_THREADS) sr[pidx(j)] = 0.0f;
+      for (int j = PMAX + D + tid; j < LS + SS_RD - 1; j += RL_THREADS) sr[pidx(j)] = 0.0f;
+      for (int q4 = tid; q4 < D / 4; q4 += RL_THREADS) {
+        const uint64_t q = (uint64_t)(p >> 2) + (uint64_t)q4;
+        const U4 ctr = {(uint32_t)q, (uint32_t)eb, (uint32_t)(eb >> 32),
+                        STREAM_ELASTIC | (uint32_t)(q >> 32)};
+        const U4 rr = philox4x32_10(ctr, a.seed_lo, a.seed_hi);
+        const int j0 = PMAX + 4 * q4;
+        sr[pidx(j0)] = u01(rr.x) * 2.0f - 1.0f;
+        sr[pidx(j0 + 1)] = u01(rr.y) * 2.0f - 1.0f;
+        sr[pidx(j0 + 2)] = u01(rr.z) * 2.0f - 1.0f;
+        sr[pidx(j0 + 3)] = u01(rr.w) * 2.0f - 1.0f;
+      }
+    } else {
+      const int64_t base = row * D;
+      for (int j = tid; j < LS + SS_RD - 1; j += RL_THREADS) {
+        const int64_t di = j < LS ? pad_index(j - PMAX, D, a.padding) : -1;
+        float v = 0.0f;
+        if (di >= 0) {
+          if (SRC == RL_SRC_UNIFORM)
+            v = __ldg((const float*)a.src + base + di) * 2.0f - 1.0f;
+          else
+            v = load_in(a.src, a.in_dtype, base + di);
+        }
+        sr[pidx(j)] = v;
+      }
+    }
+  }
+  __syncthreads();
+  float w[KMAX];
+  const int nseg = (D + SS_RD - 1) / SS_RD;
+  int64_t cur_b = -1;
+  for (int u = tid; u < RL_ROWS * nseg; u += RL_THREADS) {
+    const int r = u / nseg, q0 = (u % nseg) * SS_RD;
+    const int64_t row = row0 + r;
+    if (row >= total) break;
+    const int64_t b = row / rows_per_elem;
+    if (b != cur_b) {
+      load_taps_centred<KMAX>(a.taps, b, a.K, w);
+      cur_b = b;
+    }
+    // q0 is a multiple of 8: pidx(q0 + j) = pidx(q0) + j + j / 8
+    const float* x = srow + r * LSP + pidx(q0);
+    float acc[SS_RD];
+    conv_regs<SS_RD, KMAX>([&](int j) { return x[j + (j >> 3)]; }, w, acc);
+    float* o = (float*)a.dst + row * D + q0;
+    if ((D & 3) == 0 && q0 + SS_RD <= D) {
+      reinterpret_cast<float4*>(o)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      reinterpret_cast<float4*>(o)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < SS_RD; ++i)
+        if (q0 + i < D) o[i] = acc[i];
+    }
+  }
+}
+
+// W (AXIS 1) or H (AXIS 0) pass: grid (ceil(O*D / RL_THREADS), B*P); a
+// thread owns line (plane, o, d) with o the other in-plane axis and walks
+// the axis of length N.
+template <int KMAX, int AXIS, int OUT>
+__global__ void __launch_bounds__(RL_THREADS, KMAX > 47 ? 2 : (KMAX > 31 ? 3 : 4))
+    roll_axis_kernel(const __grid_constant__ RollArgs a) {
+  constexpr int PMAX = (KMAX - 1) / 2;
+  const int H = (int)a.H, W = (int)a.W, D = (int)a.D;
+  const int64_t plane = blockIdx.y;  // b * P + p
+  const int64_t b = plane / a.P;
+  const int O = AXIS == 1 ? H : W;
+  const int N = AXIS == 1 ? W : H;
+  const int64_t idx = (int64_t)blockIdx.x * RL_THREADS + threadIdx.x;
+  if (idx >= (int64_t)O * D) return;
+  const int o_ax = (int)(idx / D), d = (int)(idx % D);
+  const int64_t HWD = (int64_t)H * W * D;
+  const int64_t stride = AXIS == 1 ? D : (int64_t)W * D;  // step along the walked axis
+  const int64_t base = plane * HWD + (AXIS == 1 ? (int64_t)o_ax * W * D : (int64_t)o_ax * D) + d;
+  if (OUT == RL_OUT_DT && a.mask != nullptr && a.mask[b] == 0) {
+    if (a.copy_src != nullptr)
+      for (int n = 0; n < N; ++n) {
+        const int64_t i = base + n * stride;
+        if (a.out_dtype == BA_BF16)
+          ((uint16_t*)a.dst)[i] = ((const uint16_t*)a.copy_src)[i];
+        else
+          ((float*)a.dst)[i] = ((const float*)a.copy_src)[i];
+      }
+    return;
+  }
+  float w[KMAX];
+  load_taps_centred<KMAX>(a.taps, b, a.K, w);
+  float acc[KMAX];
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) acc[k] = 0.0f;
+  // grid epilogue constants (elastic): component = plane % 3
+  const int comp = OUT == RL_OUT_GRID ? (int)(plane % 3) : 0;
+  float mag = 0.0f, half = 1.0f, rhalf = 0.0f, half_lo = 0.0f, step = 0.0f;
+  int64_t csz = 1;
+  if (OUT == RL_OUT_GRID) {
+    mag = a.magnitude[b];
+    csz = comp == 0 ? H : (comp == 1 ? W : D);
+    const float n = (float)csz;
+    half_lo = (n - 1.0f) / 2.0f;
+    step = (half_lo - (-half_lo)) / (n - 1.0f);
+    half = half_lo < 1e-6f ? 1e-6f : half_lo;
+    rhalf = recip_for_div(half);
+  }
+  // grid coordinate of the components that do not vary along the walk
+  float c_fixed = 0.0f;
+  if (OUT == RL_OUT_GRID) {
+    const int64_t cidx = comp == 2 ? d : o_ax;  // comp 1 (W) on the H walk, 0 (H) on a W walk
+    c_fixed = linspace_at(-half_lo, half_lo, step, cidx, csz);
+  }
+  const float* src = (const float*)a.src;
+  // Walk of nblk full blocks of KMAX padded steps; steps past the last input
+  // read zeros and their outputs (past N) are not stored.
+  const int T = N + KMAX - 1;
+  const int nblk = (T + KMAX - 1) / KMAX;
+  extern __shared__ float xs[];  // 2 x KMAX x RL_THREADS: this thread's column
+  auto stage_block = [&](int blk, int buf) {
+    float* col = xs + buf * KMAX * RL_THREADS + threadIdx.x;
+    const int p0 = blk * KMAX - PMAX;  // input position of step 0
+    if (p0 >= 0 && p0 + KMAX <= N) {
+      const float* g = src + base + (int64_t)p0 * stride;
+#pragma unroll
+      for (int s = 0; s < KMAX; ++s) cp_async4(col + s * RL_THREADS, g + (int64_t)s * stride);
+    } else {
+      for (int s = 0; s < KMAX; ++s) {
+        const int64_t pos = p0 + s < N + PMAX ? pad_index(p0 + s, N, a.padding) : -1;
+        if (pos >= 0)
+          cp_async4(col + s * RL_THREADS, src + base + pos * stride);
+        else
+          col[s * RL_THREADS] = 0.0f;
+      }
+    }
+    cp_async_commit();
+  };
+  auto store = [&](int o, float v) {
+    const int64_t oi = base + (int64_t)o * stride;
+    if (OUT == RL_OUT_F32) {
+      ((float*)a.dst)[oi] = v;
+    } else if (OUT == RL_OUT_DT) {
+      float r = v;
+      if (a.sharp_blur != nullptr)
+        r = sharpen_combine(load_in(a.sharp_blur, a.out_dtype, oi), v, a.alpha[b], a.out_dtype);
+      if (a.out_dtype == BA_BF16)
+        ((uint16_t*)a.dst)[oi] = f32_to_bf16_bits(r);
+      else
+        ((float*)a.dst)[oi] = r;
+    } else {
+      const int hh = AXIS == 0 ? o : o_ax, ww = AXIS == 0 ? o_ax : o;
+      const int64_t sidx = ((int64_t)hh * W + ww) * D + d;
+      const bool walked = comp == (AXIS == 0 ? 0 : 1);
+      const float c0 = walked ? linspace_at(-half_lo, half_lo, step, o, csz) : c_fixed;
+      ((float*)a.dst)[((b * HWD) + sidx) * 3 + (2 - comp)] = div_rn(c0 + v * mag, half, rhalf);
+    }
+  };
+  stage_block(0, 0);
+  for (int blk = 0; blk < nblk; ++blk) {
+    if (blk + 1 < nblk)
+      stage_block(blk + 1, (blk + 1) & 1);
+    else
+      cp_async_commit();
+    cp_async_wait<1>();
+    const float* xb = xs + (blk & 1) * KMAX * RL_THREADS + threadIdx.x;
+    const int o0 = blk * KMAX - (KMAX - 1);  // output completed at step 0
+    const bool all_out = o0 >= 0 && o0 + KMAX <= N;
+#pragma unroll
+    for (int s = 0; s < KMAX; ++s) {
+      const float x = xb[s * RL_THREADS];
+#pragma unroll
+      for (int k = 0; k < KMAX; ++k) {
+        const int slot = (s - k + KMAX) % KMAX;
+        acc[slot] = __fmaf_rn(w[k], x, acc[slot]);
+      }
+      const int slot_done = (s + 1) % KMAX;
+      const int o = o0 + s;
+      if (all_out || (o >= 0 && o < N)) store(o, acc[slot_done]);
+      acc[slot_done] = 0.0f;
+    }
+  }
+}
+
+int roll_kmax(int K) {
+  for (int k : {23, 31, 47, 63})
+    if (K <= k) return k;
+  return 0;
+}
+
+template <int KMAX>
+ba_status launch_roll_kmax(int src_kind, int out_kind, const RollArgs& ad, const RollArgs& aw,
+                           const RollArgs& ah, int64_t batch, cudaStream_t st) {
+  const int64_t rows = batch * ad.P * ad.H * ad.W;
+  const size_t smem =
+      (size_t)RL_ROWS * (pidx((int)ad.D + KMAX - 1 + SS_RD - 2) + 1) * sizeof(float);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(roll_d_kernel<KMAX, RL_SRC_DT>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+        cudaFuncSetAttribute(roll_d_kernel<KMAX, RL_SRC_PHILOX>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+        cudaFuncSetAttribute(roll_d_kernel<KMAX, RL_SRC_UNIFORM>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 gd((unsigned)((rows + RL_ROWS - 1) / RL_ROWS));
+  if (src_kind == RL_SRC_PHILOX)
+    roll_d_kernel<KMAX, RL_SRC_PHILOX><<<gd, RL_THREADS, smem, st>>>(ad);
+  else if (src_kind == RL_SRC_UNIFORM)
+    roll_d_kernel<KMAX, RL_SRC_UNIFORM><<<gd, RL_THREADS, smem, st>>>(ad);
+  else
+    roll_d_kernel<KMAX, RL_SRC_DT><<<gd, RL_THREADS, smem, st>>>(ad);
+  ba_status s = check_launch("wide smooth D pass");
+  if (s != BA_OK) return s;
+  const int64_t planes = batch * aw.P;
+  const size_t xs = (size_t)2 * KMAX * RL_THREADS * sizeof(float);
+  cudaFuncSetAttribute(roll_axis_kernel<KMAX, 1, RL_OUT_F32>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xs);
+  cudaFuncSetAttribute(roll_axis_kernel<KMAX, 0, RL_OUT_GRID>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xs);
+  cudaFuncSetAttribute(roll_axis_kernel<KMAX, 0, RL_OUT_DT>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xs);
+  dim3 gw((unsigned)((aw.H * aw.D + RL_THREADS - 1) / RL_THREADS), (unsigned)planes);
+  roll_axis_kernel<KMAX, 1, RL_OUT_F32><<<gw, RL_THREADS, xs, st>>>(aw);
+  s = check_launch("wide smooth W pass");
+  if (s != BA_OK) return s;
+  dim3 gh((unsigned)((ah.W * ah.D + RL_THREADS - 1) / RL_THREADS), (unsigned)planes);
+  if (out_kind == RL_OUT_GRID)
+    roll_axis_kernel<KMAX, 0, RL_OUT_GRID><<<gh, RL_THREADS, xs, st>>>(ah);
+  else
+    roll_axis_kernel<KMAX, 0, RL_OUT_DT><<<gh, RL_THREADS, xs, st>>>(ah);
+  return check_launch("wide smooth H pass");
+}
+
+ba_status launch_roll(int kmax, int src_kind, int out_kind, const RollArgs& ad, const RollArgs& aw,
+                      const RollArgs& ah, int64_t batch, cudaStream_t st) {
+  switch (kmax) {
+    case 23: return launch_roll_kmax<23>(src_kind, out_kind, ad, aw, ah, batch, st);
+    case 31: return launch_roll_kmax<31>(src_kind, out_kind, ad, aw, ah, batch, st);
+    case 47: return launch_roll_kmax<47>(src_kind, out_kind, ad, aw, ah, batch, st);
+    default: return launch_roll_kmax<63>(src_kind, out_kind, ad, aw, ah, batch, st);
+  }
+}
+
 }  // namespace
 }  // namespace ba
 
@@ -991,6 +1316,38 @@ ba_status run_smooth(const SmoothJob& j, cudaStream_t st) {
   const bool streamable = kmax <= SS_KMAX_MAX && j.in_dtype == j.out_dtype &&
                           j.W * j.D < ((int64_t)1 << 31) &&
                           ((j.D + SS_TD - 1) / SS_TD) * ((j.W + SS_TW - 1) / SS_TW) <= 0x7FFFFFFF;
+  const bool rollable = !streamable && roll_kmax((int)kmax) != 0 &&
+                        j.H * j.D <= ((int64_t)1 << 31) && j.W * j.D <= ((int64_t)1 << 31);
+  if (rollable) {
+    RollArgs r;
+    memset(&r, 0, sizeof(r));
+    r.batch = j.planes / j.P;
+    r.P = j.P;
+    r.H = j.H;
+    r.W = j.W;
+    r.D = j.D;
+    r.padding = j.padding;
+    RollArgs rd = r, rw = r, rh = r;
+    rd.src = j.src;
+    rd.in_dtype = j.in_dtype;
+    rd.dst = j.t0;
+    rd.taps = j.taps[2];
+    rd.K = (int32_t)j.K[2];
+    rw.src = j.t0;
+    rw.dst = j.t1;
+    rw.taps = j.taps[1];
+    rw.K = (int32_t)j.K[1];
+    rh.src = j.t1;
+    rh.dst = j.dst;
+    rh.out_dtype = j.out_dtype;
+    rh.taps = j.taps[0];
+    rh.K = (int32_t)j.K[0];
+    rh.mask = j.mask;
+    rh.copy_src = j.copy_src;
+    rh.sharp_blur = j.sharp_blur;
+    rh.alpha = j.alpha;
+    return launch_roll(roll_kmax((int)kmax), RL_SRC_DT, RL_OUT_DT, rd, rw, rh, r.batch, st);
+  }
   if (streamable || (tiled_kmax((int)kmax) != 0 && j.H <= 65535 && j.W <= 65535)) {
     TiledArgs t;
     memset(&t, 0, sizeof(t));
@@ -1230,6 +1587,46 @@ extern "C" ba_status ba_elastic_grid(const float* u, uint64_t seed, uint64_t ele
   float* t1 = t0 + batch * 3 * HWD;
   const int64_t total = batch * 3 * HWD;
   ba_status s;
+  if (roll_kmax((int)K) != 0 && H * D <= ((int64_t)1 << 31) && W * D <= ((int64_t)1 << 31)) {
+    // D pass straight from the Philox draw (or the injected u); W; H into
+    // the grid.  An unaligned D takes the draw through scratch first.
+    RollArgs r;
+    memset(&r, 0, sizeof(r));
+    r.batch = batch;
+    r.P = 3;
+    r.H = H;
+    r.W = W;
+    r.D = D;
+    r.padding = BA_SMOOTH_ZEROS;
+    r.taps = taps;
+    r.K = (int32_t)K;
+    RollArgs rd = r, rw = r, rh = r;
+    int src_kind;
+    if (u != nullptr) {
+      src_kind = RL_SRC_UNIFORM;
+      rd.src = u;
+    } else if ((D % 4) == 0) {
+      src_kind = RL_SRC_PHILOX;
+      rd.seed_lo = (uint32_t)seed;
+      rd.seed_hi = (uint32_t)(seed >> 32);
+      rd.elem_offset = elem_offset;
+    } else {
+      elastic_draw_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+          nullptr, (uint32_t)seed, (uint32_t)(seed >> 32), elem_offset, HWD, total, t1);
+      s = check_launch("ba_elastic_grid");
+      if (s != BA_OK) return s;
+      src_kind = RL_SRC_DT;
+      rd.src = t1;
+      rd.in_dtype = BA_F32;
+    }
+    rd.dst = t0;
+    rw.src = t0;
+    rw.dst = t1;
+    rh.src = t1;
+    rh.dst = grid;
+    rh.magnitude = magnitude;
+    return launch_roll(roll_kmax((int)K), src_kind, RL_OUT_GRID, rd, rw, rh, batch, st);
+  }
   if (u == nullptr && (HWD % 4) == 0) {
     const int64_t total4 = total / 4;
     elastic_draw4_kernel<<<(unsigned)((total4 + 255) / 256), 256, 0, st>>>(

@@ -83,6 +83,7 @@ def test_golden_via_transform_api(ba, tag):
 @pytest.mark.parametrize("shape,sig1,pm", [
     ((3, 2, 20, 24, 28), (0.5, 1.0), "reflect"),     # tiled smoother, small taps
     ((2, 3, 17, 9, 40), (2.0, 5.0), "replicate"),    # tiled, K up to 41
+    ((2, 2, 30, 28, 36), (5.0, 6.0), "replicate"),   # K up to 49: wide-tap passes
     ((2, 1, 12, 10, 70), (15.0, 16.0), None),        # K = 129: axis-pass smoother
 ])
 def test_sharpen_vs_oracle(ba, oracle_lib, dt, shape, sig1, pm):
