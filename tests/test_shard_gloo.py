@@ -32,10 +32,17 @@ def _sample_all(ba, B):
                           magnitude_range=(50.0, 150.0)).sample_host(B, (B, 1, 16, 16, 16))
     sm = ba.RandGaussianSmooth(prob=0.5, sigma_x=(0.5, 1.5)).sample_host(B, (B, 1, 16, 16, 16))
     nz = ba.RandGaussianNoise(prob=0.5, std=(0.1, 0.5)).sample_host(B, (B, 1, 16, 16, 16))
+    ri = ba.RandRicianNoise(prob=0.5, std=0.3).sample_host(B, (B, 1, 16, 16, 16))
+    ss = ba.RandStdShiftIntensity(prob=0.5).sample_host(B, (B, 1, 16, 16, 16))
+    sh = ba.RandGaussianSharpen(prob=0.5, sigma1_x=(1.0, 3.0)).sample_host(B, (B, 1, 16, 16, 16))
+    lr = ba.RandSimulateLowResolution(prob=0.5).sample_host(B, (B, 1, 16, 16, 16))
     return {"mask": aff["mask"].astype(np.float32), "affine": aff["affine"].reshape(B, -1),
             "el_sigma": el["sigma"], "el_max": np.full(B, el["max_sigma"], np.float32),
             "sm_K": np.full(B, sm["K_sigma_x"], np.float32), "sm_sigma": sm["sigma_x"],
-            "nz_std": nz["std"], "nz_seed": np.full(B, nz["noise_seed"] % 2**24, np.float32)}
+            "nz_std": nz["std"], "nz_seed": np.full(B, nz["noise_seed"] % 2**24, np.float32),
+            "ri_std": ri["noise_std"], "ri_mask": ri["mask"].astype(np.float32),
+            "ss_factor": ss["factor"], "sh_sigma2": sh["sigma2_x"], "sh_alpha": sh["alpha"],
+            "sh_K": np.full(B, sh["K_sigma1_x"], np.float32), "lr_zoom": lr["zoom_factor"]}
 
 
 def _worker(rank, world, port, out_path):
