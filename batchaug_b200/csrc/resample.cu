@@ -538,21 +538,35 @@ __global__ void __launch_bounds__(ST_THREADS, BA_ST_MINBLOCKS)
   const size_t esz = DT == BA_BF16 ? 2 : 4;
   const bool active = (a.mask == nullptr) || (a.mask[b] != 0);
   if (!active) {
-    for (int pp = 0; pp < ST_PW * ST_PH; ++pp) {
-      const int pw = pp % ST_PW, ph = pp / ST_PW;
-      const int w = w0 + ty + 2 * pw, h = h0 + tz + 2 * wp + 8 * ph;
-      if (w >= W || h >= H) continue;
-      for (int j = 0; j < 2; ++j) {
-        const int d = d0 + tx + 8 * j;
-        if (d >= D) continue;
-        for (int ki = 0; ki < a.n_keys; ++ki) {
-          const KeyArgs& kc = a.keys[ki];
-          for (int c = 0; c < kc.channels; ++c) {
-            const int64_t i = (b * kc.channels + c) * (int64_t)hwd + ((int64_t)h * W + w) * D + d;
-            if (kc.dtype == BA_BF16)
-              ((uint16_t*)kc.dst)[i] = __ldg((const uint16_t*)kc.src + i);
+    // the reference's torch.where keeps a masked-out element: copy the
+    // tile, one 16-element D row per thread, 16-byte vectors where the row
+    // is whole and aligned
+    static_assert(ST_TW * ST_TH == ST_THREADS, "one tile row per thread");
+    const int w = w0 + t % ST_TW, h = h0 + t / ST_TW;
+    if (w >= W || h >= H) return;
+    const int n = min(ST_TD, D - d0);
+    for (int ki = 0; ki < a.n_keys; ++ki) {
+      const KeyArgs& kc = a.keys[ki];
+      const int ke = kc.dtype == BA_BF16 ? 2 : 4;
+      for (int c = 0; c < kc.channels; ++c) {
+        const int64_t i0 = (b * kc.channels + c) * (int64_t)hwd + ((int64_t)h * W + w) * D + d0;
+        const char* sp = (const char*)kc.src + i0 * ke;
+        char* dp = (char*)kc.dst + i0 * ke;
+        if (n == ST_TD && ((uintptr_t)sp % 16) == 0 && ((uintptr_t)dp % 16) == 0) {
+          uint4 v[4];
+          const int nv = ST_TD * ke / 16;  // 4 (fp32) or 2 (bf16)
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (q < nv) v[q] = __ldg(reinterpret_cast<const uint4*>(sp) + q);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (q < nv) reinterpret_cast<uint4*>(dp)[q] = v[q];
+        } else {
+          for (int q = 0; q < n; ++q) {
+            if (ke == 2)
+              ((uint16_t*)dp)[q] = __ldg((const uint16_t*)sp + q);
             else
-              ((float*)kc.dst)[i] = __ldg((const float*)kc.src + i);
+              ((float*)dp)[q] = __ldg((const float*)sp + q);
           }
         }
       }

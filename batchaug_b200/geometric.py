@@ -12,6 +12,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
+from . import _lib as L
 from . import _rng, ops
 from .base import BatchDictTransform, BatchTransform, upload
 
@@ -102,6 +103,12 @@ class _AffineFamily(BatchTransform):
         return ops.resample3d(tensor, theta=params["theta"], mask=params["mask"],
                               modes=mode or self.mode,
                               paddings=padding_mode or self.padding_mode)
+
+    def apply_keys(self, tensors, params, modes, paddings):
+        """``apply`` of several tensors (same batch and spatial shape) with
+        one launch: the coordinates are computed once for all of them."""
+        return ops.resample3d(list(tensors), theta=params["theta"], mask=params["mask"],
+                              modes=list(modes), paddings=list(paddings))
 
 
 class RandAffine(_AffineFamily):
@@ -373,6 +380,12 @@ class Rand3DElastic(BatchTransform):
                               modes=mode or self.mode,
                               paddings=padding_mode or self.padding_mode, align_corners=True)
 
+    def apply_keys(self, tensors, params, modes, paddings):
+        """``apply`` of several tensors (same batch and spatial shape) with
+        one launch reading the grid once."""
+        return ops.resample3d(list(tensors), grid=params["grid"], mask=params["mask"],
+                              modes=list(modes), paddings=list(paddings), align_corners=True)
+
 
 def _to_host(params: dict, keys) -> dict:
     """Host copies of injected device params (a device read; only used when
@@ -401,11 +414,27 @@ class _PerKeyModes:
         d = dict(data)
         first = d[self.keys[0]]
         params = self.transform.sample_params(first.shape[0], first.shape, first.device)
-        for key in self.keys:
-            if key in d:
-                d[key] = self.transform.apply(
-                    d[key], params, mode=self._mode.get(key, "bilinear"),
-                    padding_mode=self._padding_mode.get(key, self._default_padding))
+        mode = lambda k: self._mode.get(k, "bilinear")  # noqa: E731
+        pad = lambda k: self._padding_mode.get(k, self._default_padding)  # noqa: E731
+        keys = [k for k in self.keys if k in d]
+        if hasattr(self.transform, "apply_keys"):
+            # keys with one batch and spatial shape share one launch (the
+            # same per-key arithmetic as applying them one at a time)
+            groups: dict[tuple, list] = {}
+            for k in keys:
+                t = d[k]
+                groups.setdefault((t.shape[0], tuple(t.shape[2:]), t.device), []).append(k)
+            for ks in groups.values():
+                for i in range(0, len(ks), L.BA_MAX_KEYS):
+                    chunk = ks[i:i + L.BA_MAX_KEYS]
+                    outs = self.transform.apply_keys([d[k] for k in chunk], params,
+                                                     [mode(k) for k in chunk],
+                                                     [pad(k) for k in chunk])
+                    for k, o in zip(chunk, outs):
+                        d[k] = o
+            return d
+        for key in keys:
+            d[key] = self.transform.apply(d[key], params, mode=mode(key), padding_mode=pad(key))
         return d
 
 
