@@ -986,6 +986,7 @@ struct RollArgs {
   const float* magnitude;   // RL_OUT_GRID
   uint32_t seed_lo, seed_hi;  // RL_SRC_PHILOX
   uint64_t elem_offset;
+  int32_t plane_major;  // W/H passes: planes along blockIdx.x
 };
 
 // D pass: grid (ceil(B*P*H*W / RL_ROWS)); each row is one line along D.
@@ -1002,33 +1003,59 @@ __global__ void __launch_bounds__(RL_THREADS) roll_d_kernel(const __grid_constan
   const int64_t rows_per_elem = a.P * a.H * a.W;
   const int64_t total = a.batch * rows_per_elem;
   const int64_t row0 = (int64_t)blockIdx.x * RL_ROWS;
+  const int nrows = (int)(total - row0 < RL_ROWS ? total - row0 : RL_ROWS);
   const int tid = threadIdx.x;
-  for (int r = 0; r < RL_ROWS; ++r) {
-    const int64_t row = row0 + r;
-    if (row >= total) break;  // the same for every thread
-    float* sr = srow + r * LSP;
-    if (SRC == RL_SRC_PHILOX) {
-      // the elastic draw u*2-1 keyed as the standalone draw kernel keys it:
-      // flat position p = comp*HWD + s of element b, four per Philox block
-      // (D % 4 == 0, so a row starts a block); zero padding around it
-      const int64_t b = row / rows_per_elem;
-      const int64_t p = (row - b * rows_per_elem) * D;
-      const uint64_t eb = a.elem_offset + (uint64_t)b;
-      for (int j = tid; j < PMAX; j += RL_THREADS) sr[pidx(j)] = 0.0f;
-      for (int j = PMAX + D + tid; j < LS + SS_RD - 1; j += RL_THREADS) sr[pidx(j)] = 0.0f;
-      for (int q4 = tid; q4 < D / 4; q4 += RL_THREADS) {
-        const uint64_t q = (uint64_t)(p >> 2) + (uint64_t)q4;
-        const U4 ctr = {(uint32_t)q, (uint32_t)eb, (uint32_t)(eb >> 32),
-                        STREAM_ELASTIC | (uint32_t)(q >> 32)};
-        const U4 rr = philox4x32_10(ctr, a.seed_lo, a.seed_hi);
-        const int j0 = PMAX + 4 * q4;
-        sr[pidx(j0)] = u01(rr.x) * 2.0f - 1.0f;
-        sr[pidx(j0 + 1)] = u01(rr.y) * 2.0f - 1.0f;
-        sr[pidx(j0 + 2)] = u01(rr.z) * 2.0f - 1.0f;
-        sr[pidx(j0 + 3)] = u01(rr.w) * 2.0f - 1.0f;
+  // element and row-within-element of each staged row: one 64-bit division
+  // per row for the whole CTA, none in the loops below
+  __shared__ int32_t s_elem[RL_ROWS];
+  __shared__ int64_t s_erow[RL_ROWS];
+  if (tid < nrows) {
+    const int64_t row = row0 + tid;
+    const int64_t b = row / rows_per_elem;
+    s_elem[tid] = (int32_t)b;
+    s_erow[tid] = row - b * rows_per_elem;
+  }
+  if (SRC == RL_SRC_PHILOX) {
+    // zero padding: PMAX entries before the row, PMAX + SS_RD - 1 after it
+    const int npad = LS + SS_RD - 1 - D;
+    {
+      int r = tid / npad, j = tid % npad;
+      const int step_r = RL_THREADS / npad, step_j = RL_THREADS % npad;
+      while (r < nrows) {
+        srow[r * LSP + pidx(j < PMAX ? j : D + j)] = 0.0f;
+        j += step_j;
+        r += step_r;
+        if (j >= npad) j -= npad, ++r;
       }
-    } else {
-      const int64_t base = row * D;
+    }
+    __syncthreads();  // s_elem, s_erow
+    // the elastic draw u*2-1 keyed as the standalone draw kernel keys it:
+    // flat position p = comp*HWD + s of element b, four per Philox block
+    // (D % 4 == 0, so a row starts a block); (row, block) pairs spread over
+    // every thread of the CTA
+    const int q4n = D / 4;
+    int r = tid / q4n, q4 = tid % q4n;
+    const int step_r = RL_THREADS / q4n, step_q = RL_THREADS % q4n;
+    while (r < nrows) {
+      const uint64_t q = (uint64_t)((s_erow[r] * D) >> 2) + (uint64_t)q4;
+      const uint64_t eb = a.elem_offset + (uint64_t)s_elem[r];
+      const U4 ctr = {(uint32_t)q, (uint32_t)eb, (uint32_t)(eb >> 32),
+                      STREAM_ELASTIC | (uint32_t)(q >> 32)};
+      const U4 rr = philox4x32_10(ctr, a.seed_lo, a.seed_hi);
+      float* sr = srow + r * LSP;
+      const int j0 = PMAX + 4 * q4;
+      sr[pidx(j0)] = u01(rr.x) * 2.0f - 1.0f;
+      sr[pidx(j0 + 1)] = u01(rr.y) * 2.0f - 1.0f;
+      sr[pidx(j0 + 2)] = u01(rr.z) * 2.0f - 1.0f;
+      sr[pidx(j0 + 3)] = u01(rr.w) * 2.0f - 1.0f;
+      q4 += step_q;
+      r += step_r;
+      if (q4 >= q4n) q4 -= q4n, ++r;
+    }
+  } else {
+    for (int r = 0; r < nrows; ++r) {
+      float* sr = srow + r * LSP;
+      const int64_t base = (row0 + r) * D;
       for (int j = tid; j < LS + SS_RD - 1; j += RL_THREADS) {
         const int64_t di = j < LS ? pad_index(j - PMAX, D, a.padding) : -1;
         float v = 0.0f;
@@ -1045,12 +1072,13 @@ __global__ void __launch_bounds__(RL_THREADS) roll_d_kernel(const __grid_constan
   __syncthreads();
   float w[KMAX];
   const int nseg = (D + SS_RD - 1) / SS_RD;
-  int64_t cur_b = -1;
-  for (int u = tid; u < RL_ROWS * nseg; u += RL_THREADS) {
-    const int r = u / nseg, q0 = (u % nseg) * SS_RD;
+  int cur_b = -1;
+  int r = tid / nseg, seg = tid % nseg;
+  const int step_r = RL_THREADS / nseg, step_s = RL_THREADS % nseg;
+  while (r < nrows) {
+    const int q0 = seg * SS_RD;
     const int64_t row = row0 + r;
-    if (row >= total) break;
-    const int64_t b = row / rows_per_elem;
+    const int b = s_elem[r];
     if (b != cur_b) {
       load_taps_centred<KMAX>(a.taps, b, a.K, w);
       cur_b = b;
@@ -1068,27 +1096,40 @@ __global__ void __launch_bounds__(RL_THREADS) roll_d_kernel(const __grid_constan
       for (int i = 0; i < SS_RD; ++i)
         if (q0 + i < D) o[i] = acc[i];
     }
+    seg += step_s;
+    r += step_r;
+    if (seg >= nseg) seg -= nseg, ++r;
   }
 }
 
-// W (AXIS 1) or H (AXIS 0) pass: grid (ceil(O*D / RL_THREADS), B*P); a
-// thread owns line (plane, o, d) with o the other in-plane axis and walks
-// the axis of length N.
-template <int KMAX, int AXIS, int OUT>
+// W (AXIS 1) or H (AXIS 0) pass: a thread owns line (plane, o, d) with o
+// the other in-plane axis and walks the axis of length N.  Grid
+// (ceil(O*D / RL_THREADS), B*P), or (B*P, ceil(O*D / RL_THREADS)) with
+// plane_major set, so that the CTAs writing the three interleaved
+// components of one grid region run together.
+//
+// ZPAD (zero padding): the walk starts at the first real input (the PMAX
+// padded steps before it would only add zeros to outputs below 0) and the
+// steps past the last input skip their FMAs; skipping the addition of an
+// exact zero product leaves every sum unchanged.
+template <int KMAX, int AXIS, int OUT, bool ZPAD>
 __global__ void __launch_bounds__(RL_THREADS, KMAX > 47 ? 2 : (KMAX > 31 ? 3 : 4))
     roll_axis_kernel(const __grid_constant__ RollArgs a) {
   constexpr int PMAX = (KMAX - 1) / 2;
+  constexpr int LEAD = ZPAD ? PMAX : 0;  // first walked step
   const int H = (int)a.H, W = (int)a.W, D = (int)a.D;
-  const int64_t plane = blockIdx.y;  // b * P + p
-  const int64_t b = plane / a.P;
+  const unsigned plane = a.plane_major ? blockIdx.x : blockIdx.y;  // b * P + p
+  const unsigned lblk = a.plane_major ? blockIdx.y : blockIdx.x;
+  const int b = (int)(plane / (unsigned)a.P);
   const int O = AXIS == 1 ? H : W;
   const int N = AXIS == 1 ? W : H;
-  const int64_t idx = (int64_t)blockIdx.x * RL_THREADS + threadIdx.x;
-  if (idx >= (int64_t)O * D) return;
-  const int o_ax = (int)(idx / D), d = (int)(idx % D);
+  const unsigned idx = lblk * RL_THREADS + threadIdx.x;  // O * D < 2^31 (host check)
+  if (idx >= (unsigned)O * (unsigned)D) return;
+  const int o_ax = (int)(idx / (unsigned)D), d = (int)(idx - (unsigned)o_ax * (unsigned)D);
   const int64_t HWD = (int64_t)H * W * D;
   const int64_t stride = AXIS == 1 ? D : (int64_t)W * D;  // step along the walked axis
-  const int64_t base = plane * HWD + (AXIS == 1 ? (int64_t)o_ax * W * D : (int64_t)o_ax * D) + d;
+  const int64_t inplane = AXIS == 1 ? (int64_t)o_ax * W * D + d : (int64_t)o_ax * D + d;
+  const int64_t base = (int64_t)plane * HWD + inplane;
   if (OUT == RL_OUT_DT && a.mask != nullptr && a.mask[b] == 0) {
     if (a.copy_src != nullptr)
       for (int n = 0; n < N; ++n) {
@@ -1106,7 +1147,7 @@ __global__ void __launch_bounds__(RL_THREADS, KMAX > 47 ? 2 : (KMAX > 31 ? 3 : 4
 #pragma unroll
   for (int k = 0; k < KMAX; ++k) acc[k] = 0.0f;
   // grid epilogue constants (elastic): component = plane % 3
-  const int comp = OUT == RL_OUT_GRID ? (int)(plane % 3) : 0;
+  const int comp = OUT == RL_OUT_GRID ? (int)(plane % 3u) : 0;
   float mag = 0.0f, half = 1.0f, rhalf = 0.0f, half_lo = 0.0f, step = 0.0f;
   int64_t csz = 1;
   if (OUT == RL_OUT_GRID) {
@@ -1124,15 +1165,17 @@ __global__ void __launch_bounds__(RL_THREADS, KMAX > 47 ? 2 : (KMAX > 31 ? 3 : 4
     const int64_t cidx = comp == 2 ? d : o_ax;  // comp 1 (W) on the H walk, 0 (H) on a W walk
     c_fixed = linspace_at(-half_lo, half_lo, step, cidx, csz);
   }
+  const bool walked = OUT == RL_OUT_GRID && comp == (AXIS == 0 ? 0 : 1);
+  // grid element of output 0 of this line and the step between outputs
+  const int64_t g0 = ((int64_t)b * HWD + inplane) * 3 + (2 - comp), gstep = 3 * stride;
   const float* src = (const float*)a.src;
-  // Walk of nblk full blocks of KMAX padded steps; steps past the last input
-  // read zeros and their outputs (past N) are not stored.
-  const int T = N + KMAX - 1;
-  const int nblk = (T + KMAX - 1) / KMAX;
+  // Walk over padded steps t = LEAD .. N + KMAX - 2 in blocks of KMAX: step t
+  // reads input t - PMAX and completes output t - (KMAX - 1).
+  const int nblk = (N + KMAX - 1 - LEAD + KMAX - 1) / KMAX;
   extern __shared__ float xs[];  // 2 x KMAX x RL_THREADS: this thread's column
   auto stage_block = [&](int blk, int buf) {
     float* col = xs + buf * KMAX * RL_THREADS + threadIdx.x;
-    const int p0 = blk * KMAX - PMAX;  // input position of step 0
+    const int p0 = LEAD + blk * KMAX - PMAX;  // input position of step 0
     if (p0 >= 0 && p0 + KMAX <= N) {
       const float* g = src + base + (int64_t)p0 * stride;
 #pragma unroll
@@ -1149,10 +1192,10 @@ __global__ void __launch_bounds__(RL_THREADS, KMAX > 47 ? 2 : (KMAX > 31 ? 3 : 4
     cp_async_commit();
   };
   auto store = [&](int o, float v) {
-    const int64_t oi = base + (int64_t)o * stride;
     if (OUT == RL_OUT_F32) {
-      ((float*)a.dst)[oi] = v;
+      ((float*)a.dst)[base + (int64_t)o * stride] = v;
     } else if (OUT == RL_OUT_DT) {
+      const int64_t oi = base + (int64_t)o * stride;
       float r = v;
       if (a.sharp_blur != nullptr)
         r = sharpen_combine(load_in(a.sharp_blur, a.out_dtype, oi), v, a.alpha[b], a.out_dtype);
@@ -1161,11 +1204,8 @@ __global__ void __launch_bounds__(RL_THREADS, KMAX > 47 ? 2 : (KMAX > 31 ? 3 : 4
       else
         ((float*)a.dst)[oi] = r;
     } else {
-      const int hh = AXIS == 0 ? o : o_ax, ww = AXIS == 0 ? o_ax : o;
-      const int64_t sidx = ((int64_t)hh * W + ww) * D + d;
-      const bool walked = comp == (AXIS == 0 ? 0 : 1);
       const float c0 = walked ? linspace_at(-half_lo, half_lo, step, o, csz) : c_fixed;
-      ((float*)a.dst)[((b * HWD) + sidx) * 3 + (2 - comp)] = div_rn(c0 + v * mag, half, rhalf);
+      ((float*)a.dst)[g0 + (int64_t)o * gstep] = div_rn(c0 + v * mag, half, rhalf);
     }
   };
   stage_block(0, 0);
@@ -1176,28 +1216,47 @@ __global__ void __launch_bounds__(RL_THREADS, KMAX > 47 ? 2 : (KMAX > 31 ? 3 : 4
       cp_async_commit();
     cp_async_wait<1>();
     const float* xb = xs + (blk & 1) * KMAX * RL_THREADS + threadIdx.x;
-    const int o0 = blk * KMAX - (KMAX - 1);  // output completed at step 0
+    const int o0 = LEAD + blk * KMAX - (KMAX - 1);  // output completed at step 0
+    const int p0 = LEAD + blk * KMAX - PMAX;        // input read at step 0
     const bool all_out = o0 >= 0 && o0 + KMAX <= N;
+    const int s_end = N - o0;                 // steps s < s_end complete an output
+    const int s_in = ZPAD ? N - p0 : KMAX;    // steps s < s_in read a real input
 #pragma unroll
     for (int s = 0; s < KMAX; ++s) {
-      const float x = xb[s * RL_THREADS];
-#pragma unroll
-      for (int k = 0; k < KMAX; ++k) {
-        const int slot = (s - k + KMAX) % KMAX;
-        acc[slot] = __fmaf_rn(w[k], x, acc[slot]);
-      }
-      const int slot_done = (s + 1) % KMAX;
       const int o = o0 + s;
-      if (all_out || (o >= 0 && o < N)) store(o, acc[slot_done]);
+      if (s >= s_end) break;  // past the last output
+      if (!ZPAD || s < s_in) {
+        const float x = xb[s * RL_THREADS];
+#pragma unroll
+        for (int k = 0; k < KMAX; ++k) {
+          const int slot = (LEAD + s - k + KMAX) % KMAX;
+          acc[slot] = __fmaf_rn(w[k], x, acc[slot]);
+        }
+      }
+      const int slot_done = (LEAD + s + 1) % KMAX;
+      if (all_out || o >= 0) store(o, acc[slot_done]);
       acc[slot_done] = 0.0f;
     }
   }
 }
 
 int roll_kmax(int K) {
-  for (int k : {23, 31, 47, 63})
+  // 43 is the elastic field's K (sigma 7, truncated 3): no zero taps
+  for (int k : {23, 31, 43, 47, 63})
     if (K <= k) return k;
   return 0;
+}
+
+template <int KMAX, int AXIS, int OUT, bool ZPAD>
+ba_status launch_axis_roll(const RollArgs& a, int64_t planes, cudaStream_t st, const char* what) {
+  const size_t xs = (size_t)2 * KMAX * RL_THREADS * sizeof(float);
+  cudaFuncSetAttribute(roll_axis_kernel<KMAX, AXIS, OUT, ZPAD>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xs);
+  const int64_t lines = (AXIS == 1 ? a.H : a.W) * a.D;
+  const unsigned lb = (unsigned)((lines + RL_THREADS - 1) / RL_THREADS);
+  const dim3 g = a.plane_major ? dim3((unsigned)planes, lb) : dim3(lb, (unsigned)planes);
+  roll_axis_kernel<KMAX, AXIS, OUT, ZPAD><<<g, RL_THREADS, xs, st>>>(a);
+  return check_launch(what);
 }
 
 template <int KMAX>
@@ -1223,23 +1282,14 @@ ba_status launch_roll_kmax(int src_kind, int out_kind, const RollArgs& ad, const
   ba_status s = check_launch("wide smooth D pass");
   if (s != BA_OK) return s;
   const int64_t planes = batch * aw.P;
-  const size_t xs = (size_t)2 * KMAX * RL_THREADS * sizeof(float);
-  cudaFuncSetAttribute(roll_axis_kernel<KMAX, 1, RL_OUT_F32>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xs);
-  cudaFuncSetAttribute(roll_axis_kernel<KMAX, 0, RL_OUT_GRID>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xs);
-  cudaFuncSetAttribute(roll_axis_kernel<KMAX, 0, RL_OUT_DT>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xs);
-  dim3 gw((unsigned)((aw.H * aw.D + RL_THREADS - 1) / RL_THREADS), (unsigned)planes);
-  roll_axis_kernel<KMAX, 1, RL_OUT_F32><<<gw, RL_THREADS, xs, st>>>(aw);
-  s = check_launch("wide smooth W pass");
+  const bool zp = aw.padding == BA_SMOOTH_ZEROS;
+  s = zp ? launch_axis_roll<KMAX, 1, RL_OUT_F32, true>(aw, planes, st, "wide smooth W pass")
+         : launch_axis_roll<KMAX, 1, RL_OUT_F32, false>(aw, planes, st, "wide smooth W pass");
   if (s != BA_OK) return s;
-  dim3 gh((unsigned)((ah.W * ah.D + RL_THREADS - 1) / RL_THREADS), (unsigned)planes);
-  if (out_kind == RL_OUT_GRID)
-    roll_axis_kernel<KMAX, 0, RL_OUT_GRID><<<gh, RL_THREADS, xs, st>>>(ah);
-  else
-    roll_axis_kernel<KMAX, 0, RL_OUT_DT><<<gh, RL_THREADS, xs, st>>>(ah);
-  return check_launch("wide smooth H pass");
+  if (out_kind == RL_OUT_GRID)  // the elastic field is zero-padded
+    return launch_axis_roll<KMAX, 0, RL_OUT_GRID, true>(ah, planes, st, "wide smooth H pass");
+  return zp ? launch_axis_roll<KMAX, 0, RL_OUT_DT, true>(ah, planes, st, "wide smooth H pass")
+            : launch_axis_roll<KMAX, 0, RL_OUT_DT, false>(ah, planes, st, "wide smooth H pass");
 }
 
 ba_status launch_roll(int kmax, int src_kind, int out_kind, const RollArgs& ad, const RollArgs& aw,
@@ -1247,6 +1297,7 @@ ba_status launch_roll(int kmax, int src_kind, int out_kind, const RollArgs& ad, 
   switch (kmax) {
     case 23: return launch_roll_kmax<23>(src_kind, out_kind, ad, aw, ah, batch, st);
     case 31: return launch_roll_kmax<31>(src_kind, out_kind, ad, aw, ah, batch, st);
+    case 43: return launch_roll_kmax<43>(src_kind, out_kind, ad, aw, ah, batch, st);
     case 47: return launch_roll_kmax<47>(src_kind, out_kind, ad, aw, ah, batch, st);
     default: return launch_roll_kmax<63>(src_kind, out_kind, ad, aw, ah, batch, st);
   }
@@ -1625,6 +1676,7 @@ extern "C" ba_status ba_elastic_grid(const float* u, uint64_t seed, uint64_t ele
     rh.src = t1;
     rh.dst = grid;
     rh.magnitude = magnitude;
+    rh.plane_major = (W * D + RL_THREADS - 1) / RL_THREADS <= 65535;
     return launch_roll(roll_kmax((int)K), src_kind, RL_OUT_GRID, rd, rw, rh, batch, st);
   }
   if (u == nullptr && (HWD % 4) == 0) {

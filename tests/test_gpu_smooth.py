@@ -121,7 +121,8 @@ def test_smooth_stream_vs_oracle(ba, oracle_lib, dt, pm, shape, sig):
 @pytest.mark.parametrize("pm", [None, "reflect", "replicate"])
 @pytest.mark.parametrize("shape,sig", [
     ((2, 2, 40, 36, 44), (3.0, 3.8)),    # K 25..31: KMAX 31
-    ((1, 3, 30, 50, 33), (4.5, 5.5)),    # K 37..45: KMAX 47, ragged D
+    ((2, 2, 34, 40, 36), (4.0, 5.2)),    # K 33..43: KMAX 43 (39 and 41 pad it)
+    ((1, 3, 30, 50, 33), (4.5, 5.5)),    # K 37..45: KMAX 43 or 47, ragged D
     ((2, 1, 70, 64, 66), (7.0, 7.8)),    # K 57..63: KMAX 63
 ])
 def test_smooth_wide_vs_oracle(ba, oracle_lib, dt, pm, shape, sig):
