@@ -1102,6 +1102,12 @@ __global__ void __launch_bounds__(RL_THREADS) roll_d_kernel(const __grid_constan
   }
 }
 
+// Resident CTAs per SM the register budget is set for: the grid-writing H
+// pass fits 4 at KMAX 43 without spills, the others 3.
+constexpr int rl_axis_min_blocks(int kmax, int out) {
+  return kmax > 47 ? 2 : (kmax > 43 ? 3 : (kmax > 31 && out != RL_OUT_GRID ? 3 : 4));
+}
+
 // W (AXIS 1) or H (AXIS 0) pass: a thread owns line (plane, o, d) with o
 // the other in-plane axis and walks the axis of length N.  Grid
 // (ceil(O*D / RL_THREADS), B*P), or (B*P, ceil(O*D / RL_THREADS)) with
@@ -1113,7 +1119,7 @@ __global__ void __launch_bounds__(RL_THREADS) roll_d_kernel(const __grid_constan
 // steps past the last input skip their FMAs; skipping the addition of an
 // exact zero product leaves every sum unchanged.
 template <int KMAX, int AXIS, int OUT, bool ZPAD>
-__global__ void __launch_bounds__(RL_THREADS, KMAX > 47 ? 2 : (KMAX > 31 ? 3 : 4))
+__global__ void __launch_bounds__(RL_THREADS, rl_axis_min_blocks(KMAX, OUT))
     roll_axis_kernel(const __grid_constant__ RollArgs a) {
   constexpr int PMAX = (KMAX - 1) / 2;
   constexpr int LEAD = ZPAD ? PMAX : 0;  // first walked step
