@@ -947,13 +947,16 @@ ba_status launch_axis(int axis, const AxisArgs& a, int64_t planes, cudaStream_t 
 //     (for the elastic field the Philox draw is generated right there, so
 //     the uniform field is never written) and correlates SS_RD outputs per
 //     thread unit from a register window;
-//   - W and H: each thread walks one line along the axis, lanes along D
-//     (every load is coalesced and read once).  The line's outputs
-//     accumulate in a ring of KMAX registers: the input at padded step q
-//     adds w[k] * x to output q - k, and output q - (KMAX-1) is complete and
-//     stored.  The walk is unrolled by KMAX, so every ring slot is a
-//     compile-time register.  Outputs accumulate in tap order, as every
-//     other smoothing path does.
+//   - W and H: a CTA stages the whole padded line of 32 D columns in
+//     shared memory (roll_col_kernel) and each warp correlates chunks of
+//     RC_R outputs from a register window, lanes along D.  Lines too long
+//     to stage take a walk instead (roll_axis_kernel): each thread walks
+//     one line, its outputs accumulating in a ring of KMAX registers (the
+//     input at padded step q adds w[k] * x to output q - k, and output
+//     q - (KMAX-1) is complete and stored), unrolled by KMAX so every ring
+//     slot is a compile-time register.
+// Every path accumulates the outputs in tap order, as the other smoothing
+// paths do, so the two W/H forms give identical results.
 // Taps are centred in KMAX-wide arrays (zeros outside the runtime K).  The
 // H pass writes the output dtype (masked-out elements copy the input) or,
 // for the elastic field, the grid_sample grid.
@@ -1246,6 +1249,128 @@ __global__ void __launch_bounds__(RL_THREADS, rl_axis_min_blocks(KMAX, OUT))
   }
 }
 
+// W (AXIS 1) or H (AXIS 0) pass as a column tile: a CTA stages the whole
+// padded line (N + KMAX - 1 positions) of RC_LANES consecutive D columns of
+// one (plane, o) in shared memory, and each warp correlates chunks of RC_R
+// consecutive outputs from a register window, lanes along D.  No input is
+// staged twice and the loop body is one chunk, so the code stays small.
+// Grid (B*P, O * ceil(D / RC_LANES)): planes fastest, so the CTAs writing
+// the three interleaved components of one grid region run together.
+constexpr int RC_LANES = 32;
+constexpr int RC_WARPS = 4;
+constexpr int RC_R = 8;
+
+__host__ __device__ constexpr int rc_rows(int N, int kmax) { return N + kmax - 1 + RC_R - 1; }
+
+template <int KMAX, int AXIS, int OUT>
+__global__ void __launch_bounds__(RC_WARPS * 32) roll_col_kernel(const __grid_constant__ RollArgs a) {
+  constexpr int PMAX = (KMAX - 1) / 2;
+  extern __shared__ __align__(16) float col[];  // [rc_rows][RC_LANES]
+  const int H = (int)a.H, W = (int)a.W, D = (int)a.D;
+  const int N = AXIS == 1 ? W : H;
+  const int dblocks = (D + RC_LANES - 1) / RC_LANES;
+  const unsigned plane = blockIdx.x;  // b * P + p
+  const int o_ax = (int)(blockIdx.y / (unsigned)dblocks);
+  const int d0 = (int)(blockIdx.y - (unsigned)o_ax * (unsigned)dblocks) * RC_LANES;
+  const int nd = min(RC_LANES, D - d0);
+  const int b = (int)(plane / (unsigned)a.P);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t HWD = (int64_t)H * W * D;
+  const int64_t stride = AXIS == 1 ? D : (int64_t)W * D;  // step along the walked axis
+  const int64_t inplane = (AXIS == 1 ? (int64_t)o_ax * W * D : (int64_t)o_ax * D) + d0;
+  const int64_t base = (int64_t)plane * HWD + inplane;  // position 0 of column d0
+  if (OUT == RL_OUT_DT && a.mask != nullptr && a.mask[b] == 0) {
+    if (a.copy_src != nullptr && lane < nd)
+      for (int n = warp; n < N; n += RC_WARPS) {
+        const int64_t i = base + n * stride + lane;
+        if (a.out_dtype == BA_BF16)
+          ((uint16_t*)a.dst)[i] = ((const uint16_t*)a.copy_src)[i];
+        else
+          ((float*)a.dst)[i] = ((const float*)a.copy_src)[i];
+      }
+    return;
+  }
+  // stage rows r = padded position (input r - PMAX); rows past the padded
+  // line and lanes past D are zero
+  const float* src = (const float*)a.src;
+  const int rows = rc_rows(N, KMAX);
+  if ((D & 3) == 0) {
+    // 16-byte copies: 8 per row, 16 rows per pass of the CTA
+    const int q = threadIdx.x & 7;
+    for (int r = threadIdx.x >> 3; r < rows; r += RC_WARPS * 4) {
+      const int64_t pos = r < N + KMAX - 1 ? pad_index(r - PMAX, N, a.padding) : -1;
+      float* dstp = col + r * RC_LANES + 4 * q;
+      if (pos >= 0 && 4 * q < nd)
+        cp_async16(dstp, src + base + pos * stride + 4 * q);
+      else
+        *reinterpret_cast<float4*>(dstp) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+  } else {
+    for (int r = warp; r < rows; r += RC_WARPS) {
+      const int64_t pos = r < N + KMAX - 1 ? pad_index(r - PMAX, N, a.padding) : -1;
+      if (pos >= 0 && lane < nd)
+        cp_async4(col + r * RC_LANES + lane, src + base + pos * stride + lane);
+      else
+        col[r * RC_LANES + lane] = 0.0f;
+    }
+  }
+  cp_async_commit();
+  float w[KMAX];
+  load_taps_centred<KMAX>(a.taps, b, a.K, w);
+  // grid epilogue constants (elastic): component = plane % 3
+  const int comp = OUT == RL_OUT_GRID ? (int)(plane % 3u) : 0;
+  float mag = 0.0f, half = 1.0f, rhalf = 0.0f, half_lo = 0.0f, step = 0.0f, c_fixed = 0.0f;
+  int64_t csz = 1;
+  if (OUT == RL_OUT_GRID) {
+    mag = a.magnitude[b];
+    csz = comp == 0 ? H : (comp == 1 ? W : D);
+    const float n = (float)csz;
+    half_lo = (n - 1.0f) / 2.0f;
+    step = (half_lo - (-half_lo)) / (n - 1.0f);
+    half = half_lo < 1e-6f ? 1e-6f : half_lo;
+    rhalf = recip_for_div(half);
+    // the coordinate of a component that does not vary along the walk
+    const int64_t cidx = comp == 2 ? d0 + lane : o_ax;
+    c_fixed = linspace_at(-half_lo, half_lo, step, cidx, csz);
+  }
+  const bool walked = OUT == RL_OUT_GRID && comp == (AXIS == 0 ? 0 : 1);
+  const int64_t g0 = ((int64_t)b * HWD + inplane + lane) * 3 + (2 - comp), gstep = 3 * stride;
+  cp_async_wait<0>();
+  __syncthreads();
+  const int nchunk = (N + RC_R - 1) / RC_R;
+  for (int c = warp; c < nchunk; c += RC_WARPS) {
+    const int q0 = c * RC_R;
+    const float* x = col + q0 * RC_LANES + lane;
+    float acc[RC_R];
+    conv_regs<RC_R, KMAX>([&](int j) { return x[j * RC_LANES]; }, w, acc);
+    if (lane < nd) {
+#pragma unroll
+      for (int i = 0; i < RC_R; ++i) {
+        const int o = q0 + i;
+        if (o < N) {
+          const float v = acc[i];
+          const int64_t oi = base + (int64_t)o * stride + lane;
+          if (OUT == RL_OUT_F32) {
+            ((float*)a.dst)[oi] = v;
+          } else if (OUT == RL_OUT_DT) {
+            float r = v;
+            if (a.sharp_blur != nullptr)
+              r = sharpen_combine(load_in(a.sharp_blur, a.out_dtype, oi), v, a.alpha[b],
+                                  a.out_dtype);
+            if (a.out_dtype == BA_BF16)
+              ((uint16_t*)a.dst)[oi] = f32_to_bf16_bits(r);
+            else
+              ((float*)a.dst)[oi] = r;
+          } else {
+            const float c0 = walked ? linspace_at(-half_lo, half_lo, step, o, csz) : c_fixed;
+            ((float*)a.dst)[g0 + (int64_t)o * gstep] = div_rn(c0 + v * mag, half, rhalf);
+          }
+        }
+      }
+    }
+  }
+}
+
 int roll_kmax(int K) {
   // 43 is the elastic field's K (sigma 7, truncated 3): no zero taps
   for (int k : {23, 31, 43, 47, 63})
@@ -1253,8 +1378,24 @@ int roll_kmax(int K) {
   return 0;
 }
 
+// The column-tile pass when its staged line fits in shared memory and the
+// (O, D-block) count fits grid.y; the ring walk otherwise.
+template <int KMAX, int AXIS, int OUT>
+bool launch_axis_col(const RollArgs& a, int64_t planes, cudaStream_t st) {
+  const int64_t N = AXIS == 1 ? a.W : a.H, O = AXIS == 1 ? a.H : a.W;
+  const int64_t yblocks = O * ((a.D + RC_LANES - 1) / RC_LANES);
+  const size_t smem = (size_t)rc_rows((int)N, KMAX) * RC_LANES * sizeof(float);
+  if (smem > 96 * 1024 || yblocks > 65535 || planes > 65535) return false;
+  cudaFuncSetAttribute(roll_col_kernel<KMAX, AXIS, OUT>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  roll_col_kernel<KMAX, AXIS, OUT>
+      <<<dim3((unsigned)planes, (unsigned)yblocks), RC_WARPS * 32, smem, st>>>(a);
+  return true;
+}
+
 template <int KMAX, int AXIS, int OUT, bool ZPAD>
 ba_status launch_axis_roll(const RollArgs& a, int64_t planes, cudaStream_t st, const char* what) {
+  if (launch_axis_col<KMAX, AXIS, OUT>(a, planes, st)) return check_launch(what);
   const size_t xs = (size_t)2 * KMAX * RL_THREADS * sizeof(float);
   cudaFuncSetAttribute(roll_axis_kernel<KMAX, AXIS, OUT, ZPAD>,
                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xs);

@@ -124,10 +124,12 @@ def test_smooth_stream_vs_oracle(ba, oracle_lib, dt, pm, shape, sig):
     ((2, 2, 34, 40, 36), (4.0, 5.2)),    # K 33..43: KMAX 43 (39 and 41 pad it)
     ((1, 3, 30, 50, 33), (4.5, 5.5)),    # K 37..45: KMAX 43 or 47, ragged D
     ((2, 1, 70, 64, 66), (7.0, 7.8)),    # K 57..63: KMAX 63
+    ((1, 2, 760, 20, 20), (3.0, 3.8)),   # H line too long to stage: the ring walk
 ])
 def test_smooth_wide_vs_oracle(ba, oracle_lib, dt, pm, shape, sig):
-    """The wide-tap path (three coalesced passes, register-ring H and W
-    correlation) across padding modes, sizes and a masked-out element."""
+    """The wide-tap path (D rows, then W and H as staged column tiles, or
+    the register-ring walk for lines too long to stage) across padding
+    modes, sizes and a masked-out element."""
     from batchaug_b200 import ops
     O = oracle_lib
     rng = np.random.default_rng(sum(shape) * 3 + len(str(pm)))
