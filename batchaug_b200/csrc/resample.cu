@@ -895,6 +895,225 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// ===========================================================================
+// Grid-driven resample (a grid_sample grid B x H x W x D x 3, the elastic
+// path).  A warp takes 128 consecutive output voxels (flat index), each lane
+// 4 of them 32 apart, so every gather instruction reads 32 consecutive
+// voxels' taps (a few sectors for a near-identity map).  The lane's voxels
+// are sampled as two packed pairs; every channel of each key is sampled at
+// them with one tap base pointer per voxel (constant deltas inside the
+// volume).  The arithmetic is resample3d_kernel's operation for operation,
+// so results are identical.
+// ===========================================================================
+constexpr int G4_THREADS = 128;
+constexpr int G4_VOX = 4;  // voxels per thread, 32 apart
+
+template <int DT>
+__device__ __forceinline__ float ldp(const char* p) {
+  if (DT == BA_BF16) return bf16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t*>(p)));
+  return __ldg(reinterpret_cast<const float*>(p));
+}
+
+// taps8 with one base pointer and constant deltas for an interior footprint
+template <int DT>
+__device__ __forceinline__ void taps8p(const char* cs, int x0, int y0, int z0, int H, int W, int D,
+                                       bool interior, float* v) {
+  constexpr int E = DT == BA_BF16 ? 2 : 4;
+  if (interior) {
+    const char* p = cs + (size_t)((z0 * W + y0) * D + x0) * E;
+    const char* py = p + (size_t)D * E;
+    const char* pz = p + (size_t)W * D * E;
+    const char* pzy = pz + (size_t)D * E;
+    v[0] = ldp<DT>(p);
+    v[1] = ldp<DT>(p + E);
+    v[2] = ldp<DT>(py);
+    v[3] = ldp<DT>(py + E);
+    v[4] = ldp<DT>(pz);
+    v[5] = ldp<DT>(pz + E);
+    v[6] = ldp<DT>(pzy);
+    v[7] = ldp<DT>(pzy + E);
+    return;
+  }
+  taps8<DT>(cs, x0, y0, z0, H, W, D, false, v);
+}
+
+// Trilinear set-up of a voxel pair, as sample_pair forms it.
+struct Pair8 {
+  Floor2 fx, fy, fz;
+  float2 w[8];
+  bool ia, ib;
+};
+
+template <int PAD, bool ALIGN>
+__device__ __forceinline__ Pair8 pair_setup(float2 ix, float2 iy, float2 iz, int H, int W, int D) {
+  const float2 px = pad2<PAD, ALIGN>(ix, D);
+  const float2 py = pad2<PAD, ALIGN>(iy, W);
+  const float2 pz = pad2<PAD, ALIGN>(iz, H);
+  Pair8 q;
+  q.fx = floor2(px);
+  q.fy = floor2(py);
+  q.fz = floor2(pz);
+  const float2 one = f2(1.0f);
+  const float2 wx1 = sub2(px, q.fx.f), wx0 = sub2(add2(q.fx.f, one), px);
+  const float2 wy1 = sub2(py, q.fy.f), wy0 = sub2(add2(q.fy.f, one), py);
+  const float2 wz1 = sub2(pz, q.fz.f), wz0 = sub2(add2(q.fz.f, one), pz);
+  const float2 xy00 = mul2(wx0, wy0), xy10 = mul2(wx1, wy0);
+  const float2 xy01 = mul2(wx0, wy1), xy11 = mul2(wx1, wy1);
+  q.w[0] = mul2(xy00, wz0);
+  q.w[1] = mul2(xy10, wz0);
+  q.w[2] = mul2(xy01, wz0);
+  q.w[3] = mul2(xy11, wz0);
+  q.w[4] = mul2(xy00, wz1);
+  q.w[5] = mul2(xy10, wz1);
+  q.w[6] = mul2(xy01, wz1);
+  q.w[7] = mul2(xy11, wz1);
+  q.ia = (unsigned)q.fx.lo < (unsigned)(D - 1) && (unsigned)q.fy.lo < (unsigned)(W - 1) &&
+         (unsigned)q.fz.lo < (unsigned)(H - 1);
+  q.ib = (unsigned)q.fx.hi < (unsigned)(D - 1) && (unsigned)q.fy.hi < (unsigned)(W - 1) &&
+         (unsigned)q.fz.hi < (unsigned)(H - 1);
+  return q;
+}
+
+template <int DT>
+__device__ __forceinline__ float2 pair_interp(const Pair8& q, const char* cs, int H, int W, int D) {
+  float va[8], vb[8];
+  taps8p<DT>(cs, q.fx.lo, q.fy.lo, q.fz.lo, H, W, D, q.ia, va);
+  taps8p<DT>(cs, q.fx.hi, q.fy.hi, q.fz.hi, H, W, D, q.ib, vb);
+  // products packed, sums scalar, in torch's tap order
+  float2 acc = f2(0.0f);
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const float2 pr = mul2(f2(va[t], vb[t]), q.w[t]);
+    acc.x = __fadd_rn(acc.x, pr.x);
+    acc.y = __fadd_rn(acc.y, pr.y);
+  }
+  return acc;
+}
+
+// Every channel of key k at the lane's voxels fv[0..3]: pairs (0,1), (2,3),
+// coordinates (ix, iy, iz)[p]; a voxel with ok[v] false is not stored.
+template <int S, bool ALIGN>
+__device__ __forceinline__ void sample_lane(const KeyArgs& k, int64_t b, int H, int W, int D,
+                                            int hwd, const int* fv, const bool* ok,
+                                            const float2* ix, const float2* iy,
+                                            const float2* iz) {
+  constexpr int MODE = spec_mode(S), PAD = spec_pad(S), DT = spec_dt(S);
+  constexpr int E = DT == BA_BF16 ? 2 : 4;
+  const size_t cstride = (size_t)hwd * E;
+  const char* src_e = (const char*)k.src + (size_t)b * k.channels * cstride;
+  char* dst_e = (char*)k.dst + (size_t)b * k.channels * cstride;
+  if (MODE == BA_NEAREST) {
+    int o[G4_VOX];
+    bool in[G4_VOX];
+#pragma unroll
+    for (int v = 0; v < G4_VOX; ++v) {
+      const int p = v / 2;
+      const float2 px = pad2<PAD, ALIGN>(ix[p], D), py = pad2<PAD, ALIGN>(iy[p], W),
+                   pz = pad2<PAD, ALIGN>(iz[p], H);
+      // nearbyint (round half to even) in one conversion
+      const int x = __float2int_rn(v & 1 ? px.y : px.x), y = __float2int_rn(v & 1 ? py.y : py.x),
+                z = __float2int_rn(v & 1 ? pz.y : pz.x);
+      in[v] = (unsigned)x < (unsigned)D && (unsigned)y < (unsigned)W && (unsigned)z < (unsigned)H;
+      o[v] = in[v] ? ((z * W + y) * D + x) * E : 0;
+    }
+    for (int c = 0; c < k.channels; ++c) {
+      const char* cs = src_e + c * cstride;
+      char* cd = dst_e + c * cstride;
+      float r[G4_VOX];
+#pragma unroll
+      for (int v = 0; v < G4_VOX; ++v) r[v] = in[v] ? ldp<DT>(cs + o[v]) : 0.0f;
+#pragma unroll
+      for (int v = 0; v < G4_VOX; ++v)
+        if (ok[v]) st<DT>(cd, fv[v], r[v]);
+    }
+    return;
+  }
+  // one pair's set-up live at a time: the kernel runs 8 CTAs per SM (64
+  // registers), the occupancy that hides the gathers' latency best
+  static_assert(G4_VOX == 4, "two pairs per lane");
+#pragma unroll 1
+  for (int p = 0; p < 2; ++p) {
+    // selects, not indexing, so the lane's values stay in registers
+    const Pair8 q = pair_setup<PAD, ALIGN>(p ? ix[1] : ix[0], p ? iy[1] : iy[0],
+                                           p ? iz[1] : iz[0], H, W, D);
+    const int fa = p ? fv[2] : fv[0], fb = p ? fv[3] : fv[1];
+    const bool oa = p ? ok[2] : ok[0], ob = p ? ok[3] : ok[1];
+    for (int c = 0; c < k.channels; ++c) {
+      const float2 r = pair_interp<DT>(q, src_e + c * cstride, H, W, D);
+      char* cd = dst_e + c * cstride;
+      if (oa) st<DT>(cd, fa, r.x);
+      if (ob) st<DT>(cd, fb, r.y);
+    }
+  }
+}
+
+template <int S0, int S1>
+__global__ void __launch_bounds__(G4_THREADS, 8) resample3d_grid4_kernel(const __grid_constant__ ResampleArgs a) {
+  const int H = a.H, W = a.W, D = a.D;
+  const int hwd = H * W * D;
+  const int lane = threadIdx.x & 31;
+  const int f0 = (int)blockIdx.x * (G4_THREADS * G4_VOX) + (int)(threadIdx.x >> 5) * 32 * G4_VOX + lane;
+  if (f0 >= hwd) return;
+  const int64_t b = blockIdx.y;
+  int fv[G4_VOX];
+  bool ok[G4_VOX];
+#pragma unroll
+  for (int v = 0; v < G4_VOX; ++v) {
+    ok[v] = f0 + 32 * v < hwd;
+    fv[v] = ok[v] ? f0 + 32 * v : f0;  // a voxel past the end recomputes f0, unstored
+  }
+  if (a.mask != nullptr && a.mask[b] == 0) {
+    // the reference's torch.where keeps a masked-out element
+    for (int ki = 0; ki < a.n_keys; ++ki) {
+      const KeyArgs& k = a.keys[ki];
+      for (int c = 0; c < k.channels; ++c) {
+        const int64_t base = ((int64_t)b * k.channels + c) * hwd;
+#pragma unroll
+        for (int v = 0; v < G4_VOX; ++v)
+          if (ok[v]) {
+            if (k.dtype == BA_BF16)
+              ((uint16_t*)k.dst)[base + fv[v]] = __ldg((const uint16_t*)k.src + base + fv[v]);
+            else
+              ((float*)k.dst)[base + fv[v]] = __ldg((const float*)k.src + base + fv[v]);
+          }
+      }
+    }
+    return;
+  }
+  float g[3][G4_VOX];
+#pragma unroll
+  for (int v = 0; v < G4_VOX; ++v) {
+    const float* gp = a.xform + ((int64_t)b * hwd + fv[v]) * 3;
+#pragma unroll
+    for (int r = 0; r < 3; ++r) g[r][v] = __ldg(gp + r);
+  }
+  const float fD = (float)D, fW = (float)W, fH = (float)H;
+  float2 ix[G4_VOX / 2], iy[G4_VOX / 2], iz[G4_VOX / 2];
+  if (a.align_corners) {
+#pragma unroll
+    for (int p = 0; p < G4_VOX / 2; ++p) {
+      ix[p] = unnormalize2<true>(f2(g[0][2 * p], g[0][2 * p + 1]), fD);
+      iy[p] = unnormalize2<true>(f2(g[1][2 * p], g[1][2 * p + 1]), fW);
+      iz[p] = unnormalize2<true>(f2(g[2][2 * p], g[2][2 * p + 1]), fH);
+    }
+    sample_lane<S0, true>(a.keys[0], b, H, W, D, hwd, fv, ok, ix, iy, iz);
+    if (S1 >= 0) sample_lane<(S1 < 0 ? 0 : S1), true>(a.keys[1], b, H, W, D, hwd, fv, ok, ix, iy, iz);
+  } else {
+    const bool pD = (D & (D - 1)) == 0, pW = (W & (W - 1)) == 0, pH = (H & (H - 1)) == 0;
+    auto un = [](float2 c, float size, bool pow2) {
+      return pow2 ? unnormalize2_pow2(c, size) : unnormalize2<false>(c, size);
+    };
+#pragma unroll
+    for (int p = 0; p < G4_VOX / 2; ++p) {
+      ix[p] = un(f2(g[0][2 * p], g[0][2 * p + 1]), fD, pD);
+      iy[p] = un(f2(g[1][2 * p], g[1][2 * p + 1]), fW, pW);
+      iz[p] = un(f2(g[2][2 * p], g[2][2 * p + 1]), fH, pH);
+    }
+    sample_lane<S0, false>(a.keys[0], b, H, W, D, hwd, fv, ok, ix, iy, iz);
+    if (S1 >= 0) sample_lane<(S1 < 0 ? 0 : S1), false>(a.keys[1], b, H, W, D, hwd, fv, ok, ix, iy, iz);
+  }
+}
+
 }  // namespace
 }  // namespace ba
 
@@ -1008,6 +1227,10 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
         return false;
     }
   };
+  // Grid maps take the lane-per-voxel grid kernel.
+  const bool grid4 = a.xform_kind == BA_XFORM_GRID;
+  const dim3 g4_grid((unsigned)((hwd + G4_THREADS * G4_VOX - 1) / (G4_THREADS * G4_VOX)),
+                     (unsigned)d.batch);
   // vol (bilinear) + seg (nearest) with one padding: one fused launch
   if (a.n_keys == 2) {
     KeyArgs k0 = a.keys[0], k1 = a.keys[1];
@@ -1025,8 +1248,12 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
       switch (code(k0) * 16 + code(k1)) {
 #define BA_PAIR(P, T0, T1)                                                                 \
   case spec_code(BA_BILINEAR, P, T0) * 16 + spec_code(BA_NEAREST, P, T1):                  \
-    resample3d_kernel<spec_code(BA_BILINEAR, P, T0), spec_code(BA_NEAREST, P, T1)>         \
-        <<<grid, NTHREADS, 0, st>>>(a);                                                    \
+    if (grid4)                                                                             \
+      resample3d_grid4_kernel<spec_code(BA_BILINEAR, P, T0), spec_code(BA_NEAREST, P, T1)> \
+          <<<g4_grid, G4_THREADS, 0, st>>>(a);                                             \
+    else                                                                                   \
+      resample3d_kernel<spec_code(BA_BILINEAR, P, T0), spec_code(BA_NEAREST, P, T1)>       \
+          <<<grid, NTHREADS, 0, st>>>(a);                                                  \
     break;
 #define BA_PAIRS(P) BA_PAIR(P, 0, 0) BA_PAIR(P, 0, 1) BA_PAIR(P, 1, 0) BA_PAIR(P, 1, 1)
         BA_PAIRS(BA_PAD_ZEROS)
@@ -1053,7 +1280,10 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
     switch (code(one.keys[0])) {
 #define BA_ONE(S)                                                      \
   case S:                                                              \
-    resample3d_kernel<S, -1><<<grid, NTHREADS, 0, st>>>(one);          \
+    if (grid4)                                                         \
+      resample3d_grid4_kernel<S, -1><<<g4_grid, G4_THREADS, 0, st>>>(one); \
+    else                                                               \
+      resample3d_kernel<S, -1><<<grid, NTHREADS, 0, st>>>(one);        \
     break;
       BA_ONE(0) BA_ONE(1) BA_ONE(2) BA_ONE(3) BA_ONE(4) BA_ONE(5)
       BA_ONE(6) BA_ONE(7) BA_ONE(8) BA_ONE(9) BA_ONE(10) BA_ONE(11)

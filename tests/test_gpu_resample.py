@@ -102,6 +102,46 @@ def test_grid_mode_align_corners(ba, oracle_lib):
     assert np.array_equal(to_np(so), g["seg_out"])
 
 
+@pytest.mark.parametrize("pad", PADS)
+@pytest.mark.parametrize("align", [True, False])
+@pytest.mark.parametrize("shape", [(3, 12, 10, 16), (2, 9, 11, 14)])
+def test_grid_map_keys_vs_oracle(ba, oracle_lib, pad, align, shape):
+    """Grid maps (the lane-per-voxel grid kernel, whole and partial last
+    CTAs): a bf16 bilinear key and an fp32 nearest key in one launch, an
+    fp32 bilinear key alone, a masked-out element, displacements that leave
+    the volume near its faces."""
+    from batchaug_b200 import ops
+    B, H, W, D = shape
+    rng = np.random.default_rng(H * W + D + len(pad) + int(align))
+    lin = [np.linspace(-1, 1, n, dtype=np.float32) for n in (H, W, D)]
+    zz, yy, xx = np.meshgrid(*lin, indexing="ij")
+    grid = np.empty((B, H, W, D, 3), np.float32)
+    for b in range(B):
+        ph = rng.uniform(0, np.pi, 3)
+        grid[b, ..., 0] = xx + 0.2 * np.sin(3 * zz + ph[0])
+        grid[b, ..., 1] = yy + 0.2 * np.cos(2 * xx + ph[1])
+        grid[b, ..., 2] = zz + 0.2 * np.sin(2 * yy + ph[2])
+    vol = rng.random((B, 2, H, W, D)).astype(np.float32)
+    vol_bf = oracle_lib.to_bf16_bits(vol)
+    seg = rng.integers(0, 6, (B, 1, H, W, D)).astype(np.float32)
+    mask = np.ones(B, bool)
+    mask[1] = False
+    m = mask.astype(np.uint8)
+    gd = to_dev(grid)
+    vo, so = ops.resample3d([to_dev(vol_bf), to_dev(seg)], grid=gd, modes=["bilinear", "nearest"],
+                            paddings=pad, align_corners=align, mask=to_dev(mask))
+    assert np.array_equal(to_np(vo), oracle_lib.resample3d(vol_bf, grid=grid, mode="bilinear",
+                                                           padding=pad, align_corners=align,
+                                                           mask=m))
+    assert np.array_equal(to_np(so), oracle_lib.resample3d(seg, grid=grid, mode="nearest",
+                                                           padding=pad, align_corners=align,
+                                                           mask=m))
+    v32 = ops.resample3d(to_dev(vol), grid=gd, modes="bilinear", paddings=pad,
+                         align_corners=align)
+    assert np.array_equal(to_np(v32), oracle_lib.resample3d(vol, grid=grid, mode="bilinear",
+                                                            padding=pad, align_corners=align))
+
+
 def test_golden_compose_materialize(ba):
     from batchaug_b200 import ops
     g = load_golden("compose_materialize")
