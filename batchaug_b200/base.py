@@ -63,9 +63,32 @@ class BatchTransform:
     """
 
     _stream = _rng.S_MASK_ONLY
+    # True when apply() on a subset of the batch with subset_params() gives
+    # those elements' results: every per-element parameter has the batch as
+    # its first dimension and nothing else depends on an element's index
+    # (in-kernel Philox draws are keyed on the global element index, so
+    # noise transforms are not subsettable).
+    _subsettable = False
 
     def __init__(self, prob: float = 1.0):
         self.prob = prob
+
+    def subset_params(self, params: dict, idx: np.ndarray, idx_t: torch.Tensor) -> dict:
+        """``params`` restricted to the elements ``idx`` (host) / ``idx_t``
+        (device): every tensor or array whose first dimension is the batch is
+        indexed, everything else is kept."""
+        B = len(params["_host"]["mask"])
+
+        def pick(v):
+            if isinstance(v, torch.Tensor) and v.dim() >= 1 and v.shape[0] == B:
+                return v.index_select(0, idx_t.to(v.device))
+            if isinstance(v, np.ndarray) and v.ndim >= 1 and v.shape[0] == B:
+                return v[idx]
+            return v
+
+        out = {k: pick(v) for k, v in params.items() if k != "_host"}
+        out["_host"] = {k: pick(v) for k, v in params["_host"].items()}
+        return out
 
     # -- parameter sampling ------------------------------------------------
     def _n_uniforms(self, shape) -> int:

@@ -22,6 +22,16 @@ B200 execution:
   the same ops in the same order as applying them one by one, so results are
   unchanged, in fewer HBM passes.  This applies in eager mode too.
 
+* a key whose tensor the pipeline itself created (its storage shared with
+  no input tensor and no other key) is updated in place when a transform
+  selects under a third of the elements: the selected elements are gathered,
+  transformed and scattered back, and the others are not touched (the
+  reference's torch.where copies them).  This covers the geometric materialisation and
+  the transforms whose parameters are all per element (Gaussian smoothing
+  and sharpening, bias field); a transform that selects no element leaves
+  such a key as it is.  Results are unchanged; input tensors are never
+  written.
+
 Extension (``fuse_elastic=True``, lazy mode only; off by default, which keeps
 the reference's order): a Rand3DElasticd followed by geometric transforms is
 resampled once instead of twice.  Pending affines before the elastic
@@ -40,6 +50,7 @@ import torch
 
 from . import _lib as L
 from . import ops
+from .base import to_device
 from .intensity import _FusibleIntensity
 
 
@@ -78,28 +89,104 @@ class Compose:
             return self._padding_mode.get(key, "zeros")
         return self._padding_mode
 
-    # -- intensity fusion ---------------------------------------------------
+    # -- pipeline-owned keys, updated in place on the selected elements -----
     @staticmethod
-    def _run_intensity(d: dict, run: list) -> dict:
+    def _storage(x) -> int:
+        return x.untyped_storage().data_ptr() if isinstance(x, torch.Tensor) else 0
+
+    def _owned(self, d: dict, keys, inputs: set) -> bool:
+        """True when every key's tensor was created by the pipeline: its
+        storage is shared with no input tensor and no other key of ``d``."""
+        counts: dict[int, int] = {}
+        for v in d.values():
+            p = self._storage(v)
+            counts[p] = counts.get(p, 0) + 1
+        for k in keys:
+            p = self._storage(d[k])
+            if p == 0 or p in inputs or counts[p] != 1:
+                return False
+        return True
+
+    @staticmethod
+    def _subset_index(mask: np.ndarray, device):
+        idx = np.flatnonzero(mask)
+        # pinned, non-blocking: a pageable upload would synchronise the stream
+        return idx, to_device(idx.astype(np.int64), device)
+
+    @staticmethod
+    def _sparse(mask: np.ndarray) -> bool:
+        """Selected elements few enough that gathering them and scattering the
+        results back (two copies of the selection) moves less than copying
+        the unselected ones: under a third of the batch."""
+        return 3 * int(np.count_nonzero(mask)) < len(mask)
+
+    def _apply_dict(self, d: dict, t, inputs: set) -> dict:
+        """One non-fused dict transform; owned keys of a subsettable
+        transform are updated on the selected elements only."""
+        inner = getattr(t, "transform", None)
+        keys = [k for k in getattr(t, "keys", ()) if k in d]
+        if (inputs is None or not getattr(inner, "_subsettable", False) or not keys
+                or t.keys[0] not in d or not self._owned(d, keys, inputs)):
+            return t(d)
+        d = dict(d)
+        first = d[t.keys[0]]
+        params = inner.sample_params(first.shape[0], first.shape, first.device)
+        mask = np.asarray(params["_host"]["mask"], bool)
+        if mask.any() and not self._sparse(mask):
+            for k in keys:
+                d[k] = inner.apply(d[k], params)
+        elif mask.any():
+            idx, it = self._subset_index(mask, first.device)
+            sub = inner.subset_params(params, idx, it)
+            for k in keys:
+                x = d[k]
+                x.index_copy_(0, it, inner.apply(x.index_select(0, it), sub))
+        return d
+
+    # -- intensity fusion ---------------------------------------------------
+    def _run_intensity(self, d: dict, run: list, inputs: set | None = None) -> dict:
         """Apply consecutive fusible dict transforms as one chain per key."""
         d = dict(d)
-        per_key: dict[str, list] = {}
+        sampled = []
         for t in run:
             first = d.get(t.keys[0])
             if first is None:  # the reference would raise KeyError here too
                 raise KeyError(t.keys[0])
-            params = t.transform.sample_params(first.shape[0], first.shape, first.device)
+            sampled.append((t, t.transform.sample_params(first.shape[0], first.shape,
+                                                         first.device)))
+        keys = list(dict.fromkeys(k for t in run for k in t.keys if k in d))
+        sel = None  # owned keys, subsettable run: the elements any op selects
+        if inputs is not None and keys and self._owned(d, keys, inputs) and all(
+                getattr(t.transform, "_subsettable", False) for t in run):
+            sel = np.zeros(len(sampled[0][1]["_host"]["mask"]), bool)
+            for _, p in sampled:
+                sel |= np.asarray(p["_host"]["mask"], bool)
+            if not sel.any():
+                return d
+            if not self._sparse(sel):
+                sel = None
+        if sel is not None:
+            idx, it = self._subset_index(sel, d[keys[0]].device)
+            sampled = [(t, t.transform.subset_params(p, idx, it)) for t, p in sampled]
+            views = {k: d[k].index_select(0, it) for k in keys}
+        else:
+            views = {k: d[k] for k in keys}
+        per_key: dict[str, list] = {}
+        for t, params in sampled:
             for key in t.keys:
-                if key in d:
-                    per_key.setdefault(key, []).append(t.transform.chain_op(params, d[key]))
+                if key in views:
+                    per_key.setdefault(key, []).append(t.transform.chain_op(params, views[key]))
         for key, chain in per_key.items():
-            x = d[key]
+            x = views[key]
             for i in range(0, len(chain), L.BA_MAX_OPS):
                 x = ops.intensity_chain(x, chain[i:i + L.BA_MAX_OPS])
-            d[key] = x
+            if sel is not None:
+                d[key].index_copy_(0, it, x)
+            else:
+                d[key] = x
         return d
 
-    def _apply_rest(self, d: dict, transforms: list) -> dict:
+    def _apply_rest(self, d: dict, transforms: list, inputs: set | None = None) -> dict:
         """Eager pass over ``transforms`` with intensity runs fused."""
         i = 0
         while i < len(transforms):
@@ -108,10 +195,10 @@ class Compose:
                 j = i
                 while j < len(transforms) and self._is_fusible(transforms[j]):
                     j += 1
-                d = self._run_intensity(d, transforms[i:j])
+                d = self._run_intensity(d, transforms[i:j], inputs)
                 i = j
             else:
-                d = t(d)
+                d = self._apply_dict(d, t, inputs)
                 i += 1
         return d
 
@@ -149,7 +236,8 @@ class Compose:
         return d
 
     # -- lazy materialisation (compose.py:71-110) ---------------------------
-    def _materialize(self, d: dict, pending: dict, fields: dict | None = None) -> dict:
+    def _materialize(self, d: dict, pending: dict, fields: dict | None = None,
+                     inputs: set | None = None) -> dict:
         d = dict(d)
         if fields:
             d = self._materialize_fields(d, pending, fields)
@@ -169,16 +257,28 @@ class Compose:
             for ks in by_shape.values():
                 for i in range(0, len(ks), L.BA_MAX_KEYS):
                     chunk = ks[i:i + L.BA_MAX_KEYS]
+                    modes = [self._get_mode(k) for k in chunk]
+                    paddings = [self._get_padding_mode(k) for k in chunk]
+                    if (inputs is not None and self._sparse(mask)
+                            and self._owned(d, chunk, inputs)):
+                        # the selected elements only, written back in place
+                        idx, it = self._subset_index(mask, d[chunk[0]].device)
+                        outs = ops.resample3d([d[k].index_select(0, it) for k in chunk],
+                                              affine=affine[idx], modes=modes, paddings=paddings)
+                        for k, o in zip(chunk, outs):
+                            d[k].index_copy_(0, it, o)
+                        continue
                     outs = ops.resample3d([d[k] for k in chunk], affine=affine, mask=mask,
-                                          modes=[self._get_mode(k) for k in chunk],
-                                          paddings=[self._get_padding_mode(k) for k in chunk])
+                                          modes=modes, paddings=paddings)
                     for k, o in zip(chunk, outs):
                         d[k] = o
         return d
 
     def __call__(self, data: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
+        # storages of the caller's tensors: never written in place
+        inputs = {self._storage(v) for v in data.values()}
         if not self.lazy:
-            return self._apply_rest(dict(data), list(self.transforms))
+            return self._apply_rest(dict(data), list(self.transforms), inputs)
         d = dict(data)
         if not d:
             return d
@@ -195,7 +295,7 @@ class Compose:
             t = ts[i]
             if self.fuse_elastic and self._is_elastic(t):
                 if pending or fields:
-                    d = self._materialize(d, pending, fields)
+                    d = self._materialize(d, pending, fields, inputs)
                     pending.clear()
                     fields.clear()
                 src = d[t.keys[0]]
@@ -226,18 +326,18 @@ class Compose:
                 i += 1
                 continue
             if pending or fields:
-                d = self._materialize(d, pending, fields)
+                d = self._materialize(d, pending, fields, inputs)
                 pending.clear()
                 fields.clear()
             if self._is_fusible(t):
                 j = i
                 while j < len(ts) and self._is_fusible(ts[j]):
                     j += 1
-                d = self._run_intensity(d, ts[i:j])
+                d = self._run_intensity(d, ts[i:j], inputs)
                 i = j
             else:
-                d = t(d)
+                d = self._apply_dict(d, t, inputs)
                 i += 1
         if pending or fields:
-            d = self._materialize(d, pending, fields)
+            d = self._materialize(d, pending, fields, inputs)
         return d

@@ -185,6 +185,7 @@ class RandBiasField(_FusibleIntensity):
     (bias_field.py:56-112)."""
 
     _stream = _rng.S_BIAS
+    _subsettable = True
 
     def __init__(self, prob: float = 0.1, degree: int = 3, coeff_range=(0.0, 0.1)):
         super().__init__(prob=prob)
@@ -367,6 +368,7 @@ class RandGaussianSmooth(BatchTransform):
     (smooth.py:91-143)."""
 
     _stream = _rng.S_SMOOTH
+    _subsettable = True
 
     def __init__(self, prob: float = 0.1, sigma_x=(0.25, 1.5), sigma_y=(0.25, 1.5),
                  sigma_z=(0.25, 1.5), padding_mode=None):
@@ -410,6 +412,7 @@ class RandGaussianSharpen(BatchTransform):
     combination."""
 
     _stream = _rng.S_SHARPEN
+    _subsettable = True
 
     def __init__(self, prob: float = 0.1, sigma1_x=(0.5, 1.0), sigma1_y=(0.5, 1.0),
                  sigma1_z=(0.5, 1.0), sigma2_x=0.5, sigma2_y=0.5, sigma2_z=0.5,

@@ -230,3 +230,58 @@ def test_config_pipelines_run(ba):
     r5 = c5({"vol": v5, "seg": s5})
     assert r5["vol"].dtype == torch.bfloat16 and torch.isfinite(r5["vol"].float()).all()
     assert set(r5["seg"].unique().tolist()) <= set(float(i) for i in range(8))
+
+
+def _owned_pipeline(ba):
+    return [ba.RandAffined(["vol", "seg"], prob=1.0, rotate_range=0.3, translate_range=2),
+            ba.RandGaussianSmoothd(["vol"], prob=0.2, sigma_x=(0.5, 1.5), sigma_y=(0.5, 1.5),
+                                   sigma_z=(0.5, 1.5)),
+            ba.RandBiasFieldd(["vol"], prob=0.2),
+            ba.RandGaussianSharpend(["vol"], prob=0.2),
+            ba.RandAffined(["vol", "seg"], prob=0.2, rotate_range=0.5),
+            ba.RandGaussianSmoothd(["vol"], prob=0.7),
+            ba.RandGaussianSmoothd(["vol"], prob=0.0),
+            ba.ScaleIntensityd(["vol"])]
+
+
+@pytest.mark.parametrize("lazy", [False, True])
+def test_owned_keys_in_place_equal_copying(ba, monkeypatch, lazy):
+    """Keys the pipeline created are updated on the selected elements only
+    (gather, transform, scatter back); the result equals the copying path
+    (every transform writing a new tensor), and the inputs are untouched."""
+    B = 6
+    g = torch.Generator(device="cuda").manual_seed(3)
+    vol = torch.rand(B, 2, 18, 20, 16, device="cuda", generator=g).bfloat16()
+    seg = torch.randint(0, 4, (B, 1, 18, 20, 16), device="cuda", generator=g).float()
+    v0, s0 = vol.clone(), seg.clone()
+    subsets = []
+    orig = ba.Compose._subset_index
+    monkeypatch.setattr(ba.Compose, "_subset_index",
+                        staticmethod(lambda m, dev: subsets.append(1) or orig(m, dev)))
+    outs = []
+    for in_place in (True, False):
+        if not in_place:
+            monkeypatch.setattr(ba.Compose, "_owned", lambda self, d, keys, inputs: False)
+        for seed in range(4):
+            torch.manual_seed(seed)
+            r = ba.Compose(_owned_pipeline(ba), lazy=lazy,
+                           mode={"vol": "bilinear", "seg": "nearest"})({"vol": vol, "seg": seg})
+            outs.append((r["vol"], r["seg"]))
+    for (a, b), (c, e) in zip(outs[:4], outs[4:]):
+        assert torch.equal(a, c) and torch.equal(b, e)
+    assert torch.equal(vol, v0) and torch.equal(seg, s0)
+    assert subsets, "the in-place subset path never ran"
+
+
+def test_owned_keys_never_the_inputs(ba):
+    """A transform selecting no element, or keys sharing one tensor, never
+    write in place into the caller's tensors."""
+    x = torch.rand(3, 1, 8, 8, 8, device="cuda")
+    x0 = x.clone()
+    c = ba.Compose([ba.RandGaussianSmoothd(["a", "b"], prob=0.5),
+                    ba.RandBiasFieldd(["a", "b"], prob=0.5)], lazy=True)
+    for seed in range(4):
+        torch.manual_seed(seed)
+        r = c({"a": x, "b": x})
+        assert torch.equal(x, x0)
+        assert torch.equal(r["a"], r["b"])
