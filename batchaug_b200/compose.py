@@ -114,6 +114,37 @@ class Compose:
         return idx, to_device(idx.astype(np.int64), device)
 
     @staticmethod
+    def _runs(idx: np.ndarray):
+        """(first element, count) of each run of consecutive indices."""
+        runs, i = [], 0
+        while i < len(idx):
+            j = i
+            while j + 1 < len(idx) and idx[j + 1] == idx[j] + 1:
+                j += 1
+            runs.append((int(idx[i]), j - i + 1))
+            i = j + 1
+        return runs
+
+    @classmethod
+    def _gather(cls, x: torch.Tensor, idx: np.ndarray) -> torch.Tensor:
+        """x[idx] by one device copy per run of consecutive elements (an
+        element is one contiguous block)."""
+        out = torch.empty((len(idx),) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+        j = 0
+        for b, n in cls._runs(idx):
+            out[j:j + n].copy_(x[b:b + n])
+            j += n
+        return out
+
+    @classmethod
+    def _scatter(cls, x: torch.Tensor, idx: np.ndarray, y: torch.Tensor) -> None:
+        """x[idx] = y in place, one device copy per run."""
+        j = 0
+        for b, n in cls._runs(idx):
+            x[b:b + n].copy_(y[j:j + n])
+            j += n
+
+    @staticmethod
     def _sparse(mask: np.ndarray) -> bool:
         """Selected elements few enough that gathering them and scattering the
         results back (two copies of the selection) moves less than copying
@@ -139,8 +170,7 @@ class Compose:
             idx, it = self._subset_index(mask, first.device)
             sub = inner.subset_params(params, idx, it)
             for k in keys:
-                x = d[k]
-                x.index_copy_(0, it, inner.apply(x.index_select(0, it), sub))
+                self._scatter(d[k], idx, inner.apply(self._gather(d[k], idx), sub))
         return d
 
     # -- intensity fusion ---------------------------------------------------
@@ -168,7 +198,7 @@ class Compose:
         if sel is not None:
             idx, it = self._subset_index(sel, d[keys[0]].device)
             sampled = [(t, t.transform.subset_params(p, idx, it)) for t, p in sampled]
-            views = {k: d[k].index_select(0, it) for k in keys}
+            views = {k: self._gather(d[k], idx) for k in keys}
         else:
             views = {k: d[k] for k in keys}
         per_key: dict[str, list] = {}
@@ -181,7 +211,7 @@ class Compose:
             for i in range(0, len(chain), L.BA_MAX_OPS):
                 x = ops.intensity_chain(x, chain[i:i + L.BA_MAX_OPS])
             if sel is not None:
-                d[key].index_copy_(0, it, x)
+                self._scatter(d[key], idx, x)
             else:
                 d[key] = x
         return d
@@ -262,11 +292,11 @@ class Compose:
                     if (inputs is not None and self._sparse(mask)
                             and self._owned(d, chunk, inputs)):
                         # the selected elements only, written back in place
-                        idx, it = self._subset_index(mask, d[chunk[0]].device)
-                        outs = ops.resample3d([d[k].index_select(0, it) for k in chunk],
+                        idx = np.flatnonzero(mask)
+                        outs = ops.resample3d([self._gather(d[k], idx) for k in chunk],
                                               affine=affine[idx], modes=modes, paddings=paddings)
                         for k, o in zip(chunk, outs):
-                            d[k].index_copy_(0, it, o)
+                            self._scatter(d[k], idx, o)
                         continue
                     outs = ops.resample3d([d[k] for k in chunk], affine=affine, mask=mask,
                                           modes=modes, paddings=paddings)
