@@ -84,6 +84,13 @@ __device__ __forceinline__ float linspace_at(float start, float end, float step,
   if (i < n / 2) return __fmaf_rn(step, (float)i, start);
   return __fmaf_rn(-step, (float)(n - 1 - i), end);
 }
+// linspace_at for 32-bit indices (the same values: the conversions are exact
+// below 2^24)
+__device__ __forceinline__ float linspace_at32(float start, float end, float step, int i, int n) {
+  if (n == 1) return start;
+  if (i < n / 2) return __fmaf_rn(step, (float)i, start);
+  return __fmaf_rn(-step, (float)(n - 1 - i), end);
+}
 
 // ---------------------------------------------------------------------------
 // Order-preserving int32 keys for float min/max with atomics.  NaN maps to

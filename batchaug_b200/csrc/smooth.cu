@@ -1343,7 +1343,36 @@ __global__ void __launch_bounds__(RC_WARPS * 32) roll_col_kernel(const __grid_co
     const float* x = col + q0 * RC_LANES + lane;
     float acc[RC_R];
     conv_regs<RC_R, KMAX>([&](int j) { return x[j * RC_LANES]; }, w, acc);
-    if (lane < nd) {
+    if (lane < nd && q0 + RC_R <= N && OUT != RL_OUT_DT) {
+      // a whole chunk: stores by pointer steps, no per-output bounds
+      if (OUT == RL_OUT_F32) {
+        float* op = (float*)a.dst + base + (int64_t)q0 * stride + lane;
+#pragma unroll
+        for (int i = 0; i < RC_R; ++i, op += stride) *op = acc[i];
+      } else {
+        // the grid: c0 + field * mag divided by half; every quotient takes
+        // div_rn's fast path (RN(a*y) corrected by one fma) unless one of
+        // the chunk's needs its slow path, then all go through div_rn
+        float av[RC_R], r[RC_R];
+        bool fast = rhalf != 0.0f;
+#pragma unroll
+        for (int i = 0; i < RC_R; ++i) {
+          const float cw = walked ? linspace_at32(-half_lo, half_lo, step, q0 + i, (int)csz)
+                                  : c_fixed;
+          av[i] = cw + acc[i] * mag;
+          const float q = __fmul_rn(av[i], rhalf);
+          const float aq = fabsf(q);
+          fast = fast && av[i] != 0.0f && aq >= 0x1p-100f && aq <= 0x1p100f;
+          r[i] = __fmaf_rn(__fmaf_rn(-q, half, av[i]), rhalf, q);
+        }
+        if (!fast)
+#pragma unroll
+          for (int i = 0; i < RC_R; ++i) r[i] = div_rn(av[i], half, rhalf);
+        float* gp = (float*)a.dst + g0 + (int64_t)q0 * gstep;
+#pragma unroll
+        for (int i = 0; i < RC_R; ++i, gp += gstep) *gp = r[i];
+      }
+    } else if (lane < nd) {
 #pragma unroll
       for (int i = 0; i < RC_R; ++i) {
         const int o = q0 + i;
