@@ -46,23 +46,31 @@ __device__ __forceinline__ float sharpen_combine(float blurred, float db, float 
   return __fadd_rn(blurred, __fmul_rn(alpha, __fsub_rn(blurred, db)));
 }
 
+// One warp per element: the lanes evaluate the taps, lane 0 sums them in
+// tap order (the order the normalisation has always used), every lane
+// divides its taps by the sum.
+constexpr int GT_THREADS = 128;
+
 __global__ void gauss_taps_kernel(const float* sigmas, int64_t B, int64_t K, float* taps) {
-  const int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t b = blockIdx.x * (int64_t)(GT_THREADS / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
   if (b >= B) return;
   const int64_t tail = K / 2;
   float s = sigmas[b];
   s = s < 1e-6f ? 1e-6f : s;
   const float t = 0.70710678f / s;
   float* o = taps + b * K;
-  float sum = 0.0f;
-  for (int64_t k = 0; k < K; ++k) {
+  for (int64_t k = lane; k < K; k += 32) {
     const float x = (float)(k - tail);
     float v = 0.5f * (erff(t * (x + 0.5f)) - erff(t * (x - 0.5f)));
-    v = v < 0.0f ? 0.0f : v;
-    o[k] = v;
-    sum += v;
+    o[k] = v < 0.0f ? 0.0f : v;
   }
-  for (int64_t k = 0; k < K; ++k) o[k] = o[k] / sum;
+  __syncwarp();  // the warp's tap stores are visible to lane 0
+  float sum = 0.0f;
+  if (lane == 0)
+    for (int64_t k = 0; k < K; ++k) sum += o[k];
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+  for (int64_t k = lane; k < K; k += 32) o[k] = o[k] / sum;
 }
 
 // One zero-padded correlation along AXIS (0=H, 1=W, 2=D) of planes
@@ -1501,8 +1509,8 @@ extern "C" ba_status ba_gauss_taps(const float* sigmas, int64_t batch, int64_t K
              (long long)K, MAX_TAPS);
   if (batch == 0) return BA_OK;
   BA_REQUIRE(sigmas && taps, "ba_gauss_taps: NULL pointer");
-  gauss_taps_kernel<<<(unsigned)((batch + 127) / 128), 128, 0, (cudaStream_t)stream>>>(
-      sigmas, batch, K, taps);
+  gauss_taps_kernel<<<(unsigned)((batch + GT_THREADS / 32 - 1) / (GT_THREADS / 32)), GT_THREADS, 0,
+                      (cudaStream_t)stream>>>(sigmas, batch, K, taps);
   return check_launch("ba_gauss_taps");
 }
 
