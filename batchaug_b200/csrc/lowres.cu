@@ -232,6 +232,113 @@ __global__ void __launch_bounds__(256) lowres_kernel(const __grid_constant__ Low
     ((float*)a.dst)[oo] = v;
 }
 
+// Trilinear direct and up passes by output rows: CTA (ceil(H * W /
+// LR_ROW_ROWS), B * C) takes LR_ROW_ROWS consecutive (h, w) rows, threads
+// along D.  The D map (tap indices, through the folded nearest downsample
+// of a direct pass, and weights) is tabulated once per CTA in shared memory;
+// per row, the H and W maps and the four source rows they select are
+// resolved once, and each thread gathers its D positions' 8 taps from those
+// rows.  The arithmetic is interp_voxel's, so results are identical to
+// lowres_kernel's.
+constexpr int LR_ROW_THREADS = 128;
+constexpr int LR_ROW_ROWS = 16;
+
+// The D map of a row pass, the same for every row of an element: source
+// indices of the two taps (through the folded nearest downsample of a
+// direct pass) and their weights.
+struct DTap {
+  int32_t e0, e1;
+  float l0, l1;
+};
+
+template <int DT, bool DIRECT>
+__device__ __forceinline__ void lowres_row(const LowresArgs& a, const PassConst& k,
+                                           const int32_t (&S)[3], int32_t row,
+                                           const DTap* dmap) {
+  const int32_t h = row / S[1], w = row - h * S[1];
+  const int64_t orow = k.out_base + (int64_t)row * S[2];
+  if (k.off) {
+    for (int32_t d = threadIdx.x; d < S[2]; d += LR_ROW_THREADS) {
+      if (DT == BA_BF16)
+        ((uint16_t*)a.dst)[orow + d] = ((const uint16_t*)a.copy_src)[orow + d];
+      else
+        ((float*)a.dst)[orow + d] = ((const float*)a.copy_src)[orow + d];
+    }
+    return;
+  }
+  const bool align = a.align != 0;
+  const int dm = a.down_mode;
+  auto fold = [&](int ax, int32_t i) {
+    return DIRECT ? near_index(dm, S[ax], k.t[ax], i, k.sd[ax]) : i;
+  };
+  const Lin A = lin_map<DT>(k.n[0], k.m[0], h, align, k.s[0]);
+  const Lin Bw = lin_map<DT>(k.n[1], k.m[1], w, align, k.s[1]);
+  const int32_t a0 = fold(0, A.i0), a1 = fold(0, A.i1), b0 = fold(1, Bw.i0), b1 = fold(1, Bw.i1);
+  // source rows (a, b): sizes S for a direct pass (x itself), the target for up
+  const int64_t N1 = DIRECT ? S[1] : k.n[1], N2 = DIRECT ? S[2] : k.n[2];
+  const int64_t r00 = k.in_base + ((int64_t)a0 * N1 + b0) * N2;
+  const int64_t r01 = k.in_base + ((int64_t)a0 * N1 + b1) * N2;
+  const int64_t r10 = k.in_base + ((int64_t)a1 * N1 + b0) * N2;
+  const int64_t r11 = k.in_base + ((int64_t)a1 * N1 + b1) * N2;
+  for (int32_t d = threadIdx.x; d < S[2]; d += LR_ROW_THREADS) {
+    const DTap t = dmap[d];
+    auto tw = [&](int64_t r) {
+      return __fmaf_rn(ld<DT>(a.src, r + t.e0), t.l0, __fmul_rn(ld<DT>(a.src, r + t.e1), t.l1));
+    };
+    const float th0 = __fmaf_rn(tw(r00), Bw.l0, __fmul_rn(tw(r01), Bw.l1));
+    const float th1 = __fmaf_rn(tw(r10), Bw.l0, __fmul_rn(tw(r11), Bw.l1));
+    const float v = __fmaf_rn(th0, A.l0, __fmul_rn(th1, A.l1));
+    if (DT == BA_BF16)
+      ((uint16_t*)a.dst)[orow + d] = f32_to_bf16_bits(v);
+    else
+      ((float*)a.dst)[orow + d] = v;
+  }
+}
+
+template <int DT, bool DIRECT>
+__global__ void __launch_bounds__(LR_ROW_THREADS) lowres_row_kernel(const __grid_constant__ LowresArgs a) {
+  __shared__ PassConst k;
+  extern __shared__ DTap dmap[];  // D entries
+  const int64_t bc = blockIdx.y;
+  const int64_t b = bc / a.C, c = bc % a.C;
+  const int32_t S[3] = {(int32_t)a.H, (int32_t)a.W, (int32_t)a.D};
+  const int64_t HWD = a.H * a.W * a.D;
+  if (threadIdx.x < 3) {  // one axis per thread
+    const int ax = threadIdx.x;
+    const float z = fminf(a.zoom[b], a.max_zoom);
+    k.t[ax] = target_size(S[ax], z);
+    k.n[ax] = k.t[ax];
+    k.m[ax] = S[ax];
+    k.s[ax] = map_scale(a.mode, a.align != 0, k.n[ax], k.m[ax]);
+    k.sd[ax] = __fdiv_rn((float)S[ax], (float)k.t[ax]);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int64_t tv = (int64_t)k.t[0] * k.t[1] * k.t[2];
+    k.in_base = DIRECT ? bc * HWD : b * a.ws_elem + c * tv;
+    k.out_base = bc * HWD;
+    k.off = a.mask != nullptr && a.mask[b] == 0;
+  }
+  __syncthreads();
+  if (!k.off) {
+    const bool align = a.align != 0;
+    for (int32_t d = threadIdx.x; d < S[2]; d += LR_ROW_THREADS) {
+      const Lin Dd = lin_map<DT>(k.n[2], k.m[2], d, align, k.s[2]);
+      DTap t;
+      t.e0 = DIRECT ? near_index(a.down_mode, S[2], k.t[2], Dd.i0, k.sd[2]) : Dd.i0;
+      t.e1 = DIRECT ? near_index(a.down_mode, S[2], k.t[2], Dd.i1, k.sd[2]) : Dd.i1;
+      t.l0 = Dd.l0;
+      t.l1 = Dd.l1;
+      dmap[d] = t;
+    }
+    __syncthreads();
+  }
+  const int32_t rows = S[0] * S[1];
+  const int32_t first = (int32_t)blockIdx.x * LR_ROW_ROWS;
+  const int32_t last = min(rows, first + LR_ROW_ROWS);
+  for (int32_t row = first; row < last; ++row) lowres_row<DT, DIRECT>(a, k, S, row, dmap);
+}
+
 int64_t host_target(int64_t s, double zoom) {
   const int64_t v = (int64_t)std::nearbyint((double)((float)s * (float)zoom));
   return v < 1 ? 1 : v;
@@ -239,6 +346,20 @@ int64_t host_target(int64_t s, double zoom) {
 
 ba_status launch(const LowresArgs& a, int64_t voxels, int64_t planes, cudaStream_t st) {
   if (voxels <= 0) return BA_OK;
+  const size_t dmap_bytes = (size_t)a.D * sizeof(DTap);
+  if (a.mode == LR_TRILINEAR && a.pass != LR_PASS_DOWN && dmap_bytes <= 48 * 1024) {
+    const dim3 g((unsigned)((a.H * a.W + LR_ROW_ROWS - 1) / LR_ROW_ROWS), (unsigned)planes);
+    const bool bf = a.dtype == BA_BF16, direct = a.pass == LR_PASS_DIRECT;
+    if (bf && direct)
+      lowres_row_kernel<BA_BF16, true><<<g, LR_ROW_THREADS, dmap_bytes, st>>>(a);
+    else if (bf)
+      lowres_row_kernel<BA_BF16, false><<<g, LR_ROW_THREADS, dmap_bytes, st>>>(a);
+    else if (direct)
+      lowres_row_kernel<BA_F32, true><<<g, LR_ROW_THREADS, dmap_bytes, st>>>(a);
+    else
+      lowres_row_kernel<BA_F32, false><<<g, LR_ROW_THREADS, dmap_bytes, st>>>(a);
+    return check_launch("ba_lowres3d");
+  }
   dim3 g((unsigned)((voxels + 255) / 256), (unsigned)planes);
   if (a.dtype == BA_BF16)
     lowres_kernel<BA_BF16><<<g, 256, 0, st>>>(a);
