@@ -906,7 +906,12 @@ ba_status launch_stream_kmax(const TiledArgs& a, int64_t planes, cudaStream_t st
 template <int DT, bool ASYNC>
 ba_status launch_stream_a(const TiledArgs& a, int64_t planes, cudaStream_t st) {
   const int K = std::max(a.Kh, std::max(a.Kw, a.Kd));
+  // an exact KMAX for the common sigma ranges (1.0 -> 9, 1.25 -> 11, 1.5 -> 13
+  // taps at truncation 4): every zero tap is an FMA per voxel and axis
   if (K <= 7) return launch_stream_kmax<7, DT, ASYNC>(a, planes, st);
+  if (K <= 9) return launch_stream_kmax<9, DT, ASYNC>(a, planes, st);
+  if (K <= 11) return launch_stream_kmax<11, DT, ASYNC>(a, planes, st);
+  if (K <= 13) return launch_stream_kmax<13, DT, ASYNC>(a, planes, st);
   if (K <= 15) return launch_stream_kmax<15, DT, ASYNC>(a, planes, st);
   return launch_stream_kmax<23, DT, ASYNC>(a, planes, st);
 }

@@ -83,7 +83,9 @@ def test_elastic_transform_end_to_end(ba):
 @pytest.mark.parametrize("dt", ["f32", "bf16"])
 @pytest.mark.parametrize("pm", [None, "reflect", "replicate"])
 @pytest.mark.parametrize("shape,sig", [
-    ((2, 2, 130, 20, 40), (0.3, 1.2)),   # K <= 7, H split into chunks
+    ((2, 2, 130, 20, 40), (0.3, 1.2)),   # K <= 11, H split into chunks
+    ((2, 1, 50, 18, 20), (0.6, 1.0)),    # K 7..9: KMAX 9
+    ((2, 2, 40, 24, 36), (1.2, 1.5)),    # K 11..13: KMAX 13
     ((1, 3, 136, 35, 33), (1.0, 2.8)),   # K 9..23, ragged W/D, H in chunks for K <= 15
     ((3, 1, 24, 16, 32), (2.0, 2.7)),    # K = 23, one chunk, exact tiles
 ])
