@@ -21,7 +21,9 @@ its input from HBM.  ``value`` = voxels of all ranks / max-over-ranks time.
 ``e2e`` is the same step through the public API from pinned host memory:
 H2D of the input, the transform, D2H of the augmented volume, every step,
 with the two copies on their own streams (double-buffered) so they overlap
-the neighbouring steps' work.
+the neighbouring steps' work.  ``e2e.copy_bound`` times the same copies with
+no transform between them: the host link's concurrent rate, which bounds
+``e2e`` (``frac_of_copy_bound`` is e2e over that bound).
 
 --impl reference times the reference algorithm on the host CPU cores (the C
 oracle, a restatement of the reference's PyTorch path; the Python reference
@@ -274,12 +276,30 @@ def run_b200(args):
     barrier()
     e2e_ms = e0.elapsed_time(e1)
 
+    # The e2e roofline: the same double-buffered uploads and downloads with
+    # no transform between them (the host link's concurrent copy rate).
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(stream)
+    s_in.wait_stream(stream)
+    s_out.wait_stream(stream)
+    for i in range(e2e_steps):
+        buf = i % 2
+        with torch.cuda.stream(s_in):
+            x_devs[buf].copy_(hosts[buf], non_blocking=True)
+        with torch.cuda.stream(s_out):
+            host_outs[buf].copy_(x_devs[1 - buf], non_blocking=True)
+    stream.wait_stream(s_in)
+    stream.wait_stream(s_out)
+    c1.record(stream)
+    barrier()
+    copy_ms = c0.elapsed_time(c1)
+
     # max over ranks
-    vals = torch.tensor([total_ms, statistics.mean(kern_ms), e2e_ms], device=device,
+    vals = torch.tensor([total_ms, statistics.mean(kern_ms), e2e_ms, copy_ms], device=device,
                         dtype=torch.float64)
     if ws > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    total_ms, kern_mean_ms, e2e_ms = vals.tolist()
+    total_ms, kern_mean_ms, e2e_ms, copy_ms = vals.tolist()
 
     if rank == 0:
         peak, peak_kind = _peaks()
@@ -307,7 +327,9 @@ def run_b200(args):
                     "h2d_bytes_per_step": VOXELS * 4 + param_bytes,
                     "d2h_bytes_per_step": VOXELS * 4, "steps": e2e_steps,
                     "copies": "pinned host buffers, upload/download on their own streams, "
-                              "double-buffered"},
+                              "double-buffered",
+                    "copy_bound": ws * VOXELS * e2e_steps / (copy_ms * 1e-3),
+                    "frac_of_copy_bound": copy_ms / e2e_ms},
             "roofline": {"bound": "hbm", "kernel": "resample3d_staged_kernel",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
