@@ -492,14 +492,16 @@ __global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
 #define BA_ST_TH 8
 #endif
 #ifndef BA_ST_MAX_FLOATS
-#define BA_ST_MAX_FLOATS 12288
+#define BA_ST_MAX_FLOATS 11264
 #endif
 #ifndef BA_ST_MINBLOCKS
 #define BA_ST_MINBLOCKS 4
 #endif
 constexpr int ST_TD = 16, ST_TW = BA_ST_TW, ST_TH = BA_ST_TH;
 constexpr int ST_THREADS = 128;
-constexpr int ST_MAX_FLOATS = BA_ST_MAX_FLOATS;  // 48 KB of staged source
+// 44 KB of staged source: five CTAs (with their static shared memory and the
+// per-CTA reserve) fit in an SM's 228 KB; at 46-48 KB only four do
+constexpr int ST_MAX_FLOATS = BA_ST_MAX_FLOATS;
 constexpr int ST_PW = ST_TW / 2, ST_PH = ST_TH / 8;
 static_assert(ST_TW % 2 == 0 && ST_TH % 8 == 0, "tile covered by the thread layout");
 
