@@ -233,13 +233,13 @@ __global__ void __launch_bounds__(256) lowres_kernel(const __grid_constant__ Low
 }
 
 // Trilinear direct and up passes by output rows: CTA (ceil(H * W /
-// LR_ROW_ROWS), B * C) takes LR_ROW_ROWS consecutive (h, w) rows, threads
-// along D.  The D map (tap indices, through the folded nearest downsample
-// of a direct pass, and weights) is tabulated once per CTA in shared memory;
-// per row, the H and W maps and the four source rows they select are
-// resolved once, and each thread gathers its D positions' 8 taps from those
-// rows.  The arithmetic is interp_voxel's, so results are identical to
-// lowres_kernel's.
+// LR_ROW_ROWS), B * C) takes LR_ROW_ROWS consecutive (h, w) rows, one warp
+// per row, lanes along D.  The D map (tap indices, through the folded
+// nearest downsample of a direct pass, and weights) is tabulated once per
+// CTA in shared memory; per row, the H and W maps and the four source rows
+// they select are resolved once by its warp, and each lane gathers its D
+// positions' 8 taps from those rows.  The arithmetic is interp_voxel's, so
+// results are identical to lowres_kernel's.
 constexpr int LR_ROW_THREADS = 128;
 constexpr int LR_ROW_ROWS = 16;
 
@@ -258,7 +258,7 @@ __device__ __forceinline__ void lowres_row(const LowresArgs& a, const PassConst&
   const int32_t h = row / S[1], w = row - h * S[1];
   const int64_t orow = k.out_base + (int64_t)row * S[2];
   if (k.off) {
-    for (int32_t d = threadIdx.x; d < S[2]; d += LR_ROW_THREADS) {
+    for (int32_t d = (int32_t)(threadIdx.x & 31); d < S[2]; d += 32) {
       if (DT == BA_BF16)
         ((uint16_t*)a.dst)[orow + d] = ((const uint16_t*)a.copy_src)[orow + d];
       else
@@ -280,7 +280,7 @@ __device__ __forceinline__ void lowres_row(const LowresArgs& a, const PassConst&
   const int64_t r01 = k.in_base + ((int64_t)a0 * N1 + b1) * N2;
   const int64_t r10 = k.in_base + ((int64_t)a1 * N1 + b0) * N2;
   const int64_t r11 = k.in_base + ((int64_t)a1 * N1 + b1) * N2;
-  for (int32_t d = threadIdx.x; d < S[2]; d += LR_ROW_THREADS) {
+  for (int32_t d = (int32_t)(threadIdx.x & 31); d < S[2]; d += 32) {
     const DTap t = dmap[d];
     auto tw = [&](int64_t r) {
       return __fmaf_rn(ld<DT>(a.src, r + t.e0), t.l0, __fmul_rn(ld<DT>(a.src, r + t.e1), t.l1));
@@ -336,7 +336,10 @@ __global__ void __launch_bounds__(LR_ROW_THREADS) lowres_row_kernel(const __grid
   const int32_t rows = S[0] * S[1];
   const int32_t first = (int32_t)blockIdx.x * LR_ROW_ROWS;
   const int32_t last = min(rows, first + LR_ROW_ROWS);
-  for (int32_t row = first; row < last; ++row) lowres_row<DT, DIRECT>(a, k, S, row, dmap);
+  // one warp per row: a row's H/W maps and source rows are resolved once per
+  // warp and amortised over its D / 32 voxels per lane
+  for (int32_t row = first + (int32_t)(threadIdx.x >> 5); row < last; row += LR_ROW_THREADS / 32)
+    lowres_row<DT, DIRECT>(a, k, S, row, dmap);
 }
 
 int64_t host_target(int64_t s, double zoom) {
