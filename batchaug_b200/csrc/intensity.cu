@@ -587,13 +587,29 @@ __device__ __forceinline__ void apply_ops_bf16x8(const ChainArgs& a, const OpCon
         }
         {
           const bool both = (op.flags & BA_RESCALE_MINV) && (op.flags & BA_RESCALE_MAXV);
+          // (x - mn) / den in bf16, then * (maxv - minv) + minv in bf16; the
+          // 8 quotients take div_for_bf16's reciprocal path unless one of
+          // them needs its division, then all go through div_for_bf16
+          float nv[8], q[8];
+          bool fast = k.k3 != 0.0f;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            // (x - mn) / den in bf16, then * (maxv - minv) + minv in bf16
             const uint32_t num = as_u32(__hsub2_rn(as_bf2(w[j]), as_bf2(k.h0)));
-            const float q0 = div_for_bf16(__uint_as_float(num << 16), k.k1, k.k3);
-            const float q1 = div_for_bf16(__uint_as_float(num & 0xFFFF0000u), k.k1, k.k3);
-            __nv_bfloat162 r = __floats2bfloat162_rn(q0, q1);
+            nv[2 * j] = __uint_as_float(num << 16);
+            nv[2 * j + 1] = __uint_as_float(num & 0xFFFF0000u);
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            q[i] = __fmul_rn(nv[i], k.k3);
+            const float aq = fabsf(q[i]);
+            fast = fast && (nv[i] == 0.0f || (aq >= 0x1p-100f && aq <= 0x1p100f));
+          }
+          if (!fast)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) q[i] = div_for_bf16(nv[i], k.k1, k.k3);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            __nv_bfloat162 r = __floats2bfloat162_rn(q[2 * j], q[2 * j + 1]);
             if (both) r = __hadd2_rn(__hmul2_rn(r, as_bf2(k.h1)), as_bf2(k.h2));
             w[j] = as_u32(r);
           }
