@@ -23,7 +23,6 @@ BA_PAD_ZEROS, BA_PAD_BORDER, BA_PAD_REFLECTION = 0, 1, 2
 BA_XFORM_AFFINE, BA_XFORM_THETA, BA_XFORM_GRID = 0, 1, 2
 BA_MAX_KEYS = 8
 BA_MAX_OPS = 8
-BA_NOALLOC_CHAIN_SCRATCH = 262144  # bytes of the static scratch of ba_intensity_chain_noalloc
 
 BA_OP_NOISE, BA_OP_CONTRAST, BA_OP_SCALE, BA_OP_SHIFT, BA_OP_BIAS_FIELD, BA_OP_RESCALE = 1, 2, 3, 4, 5, 6
 BA_OP_RICIAN, BA_OP_STD_SHIFT, BA_OP_FIXED_MEAN = 7, 8, 9
@@ -94,6 +93,7 @@ SIGNATURES = {
     "ba_intensity_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(ChainDesc)]),
     "ba_intensity_chain": (_I32, [ctypes.POINTER(ChainDesc), _P, ctypes.c_size_t, _P]),
     "ba_intensity_chain_noalloc": (_I32, [ctypes.POINTER(ChainDesc), _P]),
+    "ba_noalloc_chain_scratch_bytes": (ctypes.c_size_t, []),
     "ba_minmax": (_I32, [_P, _I32, _I64, _I64, _P, _P]),
     "ba_gauss_taps_len": (_I64, [ctypes.c_double, ctypes.c_double]),
     "ba_gauss_taps": (_I32, [_P, _I64, _I64, _P, _P]),
@@ -130,6 +130,9 @@ def _load():
 
 
 lib = _load()
+
+# bytes of the static scratch of ba_intensity_chain_noalloc, from the library
+BA_NOALLOC_CHAIN_SCRATCH = int(lib.ba_noalloc_chain_scratch_bytes())
 
 
 def check(status: int, what: str) -> None:

@@ -70,8 +70,31 @@ class BatchTransform:
     # noise transforms are not subsettable).
     _subsettable = False
 
+    # keys of injected params that host-side code reads (see adopt_params)
+    _host_keys: tuple = ()
+
     def __init__(self, prob: float = 1.0):
         self.prob = prob
+
+    def adopt_params(self, params: dict) -> dict:
+        """Params made elsewhere (the reference's own ``sample_params``, or a
+        test's) in this class's form: the same dict plus, under ``"_host"``,
+        host copies of the mask and of the other keys that host-side code
+        reads (``_host_keys``).  Params from this class's ``sample_params``
+        are returned unchanged.  Costs one device read per copied key."""
+        if "_host" in params:
+            return params
+        p = dict(params)
+        host = {}
+        for k in ("mask",) + tuple(self._host_keys):
+            if k in p:
+                v = p[k]
+                host[k] = v.detach().cpu().numpy() if isinstance(v, torch.Tensor) else np.asarray(v)
+        if "mask" not in host:
+            raise ValueError("injected params need a 'mask'")
+        host["mask"] = np.asarray(host["mask"]).astype(bool).reshape(-1)
+        p["_host"] = host
+        return p
 
     def subset_params(self, params: dict, idx: np.ndarray, idx_t: torch.Tensor) -> dict:
         """``params`` restricted to the elements ``idx`` (host) / ``idx_t``
@@ -132,10 +155,16 @@ class BatchDictTransform:
         self.keys = keys
         self.transform = transform
 
-    def __call__(self, data: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
+    def __call__(self, data: dict[str, torch.Tensor], params: dict | None = None
+                 ) -> dict[str, torch.Tensor]:
+        """``params``: optional injected params (as ``sample_params`` returns
+        them, e.g. the reference's own) instead of sampling."""
         d = dict(data)
-        first = d[self.keys[0]]
-        params = self.transform.sample_params(first.shape[0], first.shape, first.device)
+        if params is None:
+            first = d[self.keys[0]]
+            params = self.transform.sample_params(first.shape[0], first.shape, first.device)
+        else:
+            params = self.transform.adopt_params(params)
         for key in self.keys:
             if key in d:
                 d[key] = self.transform.apply(d[key], params)

@@ -54,6 +54,20 @@ from .base import to_device
 from .intensity import _FusibleIntensity
 
 
+def compose_affines(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Batched (B,4,4) fp32 product a @ b rounded as the reference's
+    ``per_key_affines[key] @ affine`` (compose.py:145-151) is on torch's CPU
+    path: for each entry the four products, each rounded to fp32, summed
+    left to right with a rounding after every addition (no fused
+    multiply-add).  numpy's matmul rounds differently."""
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    acc = a[:, :, 0, None] * b[:, None, 0, :]
+    for k in range(1, 4):
+        acc = acc + a[:, :, k, None] * b[:, None, k, :]
+    return acc.astype(np.float32)
+
+
 class Compose:
     def __init__(self, transforms: list, lazy: bool = False, mode="bilinear",
                  padding_mode="zeros", fuse_elastic: bool = False):
@@ -151,17 +165,20 @@ class Compose:
         the unselected ones: under a third of the batch."""
         return 3 * int(np.count_nonzero(mask)) < len(mask)
 
-    def _apply_dict(self, d: dict, t, inputs: set) -> dict:
+    def _apply_dict(self, d: dict, t, inputs: set, injected: dict | None = None) -> dict:
         """One non-fused dict transform; owned keys of a subsettable
         transform are updated on the selected elements only."""
         inner = getattr(t, "transform", None)
         keys = [k for k in getattr(t, "keys", ()) if k in d]
         if (inputs is None or not getattr(inner, "_subsettable", False) or not keys
                 or t.keys[0] not in d or not self._owned(d, keys, inputs)):
-            return t(d)
+            return t(d) if injected is None else t(d, params=injected)
         d = dict(d)
         first = d[t.keys[0]]
-        params = inner.sample_params(first.shape[0], first.shape, first.device)
+        if injected is None:
+            params = inner.sample_params(first.shape[0], first.shape, first.device)
+        else:
+            params = inner.adopt_params(injected)
         mask = np.asarray(params["_host"]["mask"], bool)
         if mask.any() and not self._sparse(mask):
             for k in keys:
@@ -174,16 +191,21 @@ class Compose:
         return d
 
     # -- intensity fusion ---------------------------------------------------
-    def _run_intensity(self, d: dict, run: list, inputs: set | None = None) -> dict:
+    def _run_intensity(self, d: dict, run: list, inputs: set | None = None,
+                       injected: list | None = None) -> dict:
         """Apply consecutive fusible dict transforms as one chain per key."""
         d = dict(d)
         sampled = []
-        for t in run:
+        for i, t in enumerate(run):
             first = d.get(t.keys[0])
             if first is None:  # the reference would raise KeyError here too
                 raise KeyError(t.keys[0])
-            sampled.append((t, t.transform.sample_params(first.shape[0], first.shape,
-                                                         first.device)))
+            p = injected[i] if injected is not None else None
+            if p is None:
+                p = t.transform.sample_params(first.shape[0], first.shape, first.device)
+            else:
+                p = t.transform.adopt_params(p)
+            sampled.append((t, p))
         keys = list(dict.fromkeys(k for t in run for k in t.keys if k in d))
         sel = None  # owned keys, subsettable run: the elements any op selects
         if inputs is not None and keys and self._owned(d, keys, inputs) and all(
@@ -216,8 +238,10 @@ class Compose:
                 d[key] = x
         return d
 
-    def _apply_rest(self, d: dict, transforms: list, inputs: set | None = None) -> dict:
+    def _apply_rest(self, d: dict, transforms: list, inputs: set | None = None,
+                    injected: list | None = None) -> dict:
         """Eager pass over ``transforms`` with intensity runs fused."""
+        injected = injected if injected is not None else [None] * len(transforms)
         i = 0
         while i < len(transforms):
             t = transforms[i]
@@ -225,10 +249,10 @@ class Compose:
                 j = i
                 while j < len(transforms) and self._is_fusible(transforms[j]):
                     j += 1
-                d = self._run_intensity(d, transforms[i:j], inputs)
+                d = self._run_intensity(d, transforms[i:j], inputs, injected[i:j])
                 i = j
             else:
-                d = self._apply_dict(d, t, inputs)
+                d = self._apply_dict(d, t, inputs, injected[i])
                 i += 1
         return d
 
@@ -304,11 +328,28 @@ class Compose:
                         d[k] = o
         return d
 
-    def __call__(self, data: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
+    def __call__(self, data: dict[str, torch.Tensor],
+                 params: list | None = None) -> dict[str, torch.Tensor]:
+        """Run the pipeline on ``data``.
+
+        ``params`` (optional, an addition to the reference's signature): one
+        entry per transform, in order — a params dict as that transform's
+        ``sample_params`` returns it (the reference's own params inject
+        unchanged: same keys), or None to sample as usual.  Each transform
+        samples its params exactly once per call in the reference, so this
+        replays a recorded run of the reference's Compose.
+        """
+        ts = list(self.transforms)
+        if params is None:
+            injected = [None] * len(ts)
+        else:
+            injected = list(params)
+            if len(injected) != len(ts):
+                raise ValueError(f"params has {len(injected)} entries for {len(ts)} transforms")
         # storages of the caller's tensors: never written in place
         inputs = {self._storage(v) for v in data.values()}
         if not self.lazy:
-            return self._apply_rest(dict(data), list(self.transforms), inputs)
+            return self._apply_rest(dict(data), ts, inputs, injected)
         d = dict(data)
         if not d:
             return d
@@ -320,7 +361,6 @@ class Compose:
         # key -> ((grid, field mask), mode, padding) of a held elastic field
         fields: dict[str, tuple] = {}
         i = 0
-        ts = list(self.transforms)
         while i < len(ts):
             t = ts[i]
             if self.fuse_elastic and self._is_elastic(t):
@@ -329,7 +369,10 @@ class Compose:
                     pending.clear()
                     fields.clear()
                 src = d[t.keys[0]]
-                p = t.transform.sample_params(src.shape[0], src.shape, src.device)
+                if injected[i] is None:
+                    p = t.transform.sample_params(src.shape[0], src.shape, src.device)
+                else:
+                    p = t.transform.adopt_params(injected[i])
                 fstate = (p["grid"], np.asarray(p["_host"]["mask"], bool))
                 for key in t.keys:
                     if key in d:
@@ -339,7 +382,10 @@ class Compose:
                 continue
             if self._is_geometric(t):
                 inner = t.transform
-                host = inner.sample_host(B, shape)
+                if injected[i] is None:
+                    host = inner.sample_host(B, shape)
+                else:
+                    host = inner.adopt_params(injected[i])["_host"]
                 a_t = inner.host_affine({"_host": host})
                 m_t = host["mask"]
                 updated: dict[int, tuple] = {}
@@ -350,7 +396,7 @@ class Compose:
                     else:
                         new = updated.get(id(old))
                         if new is None:
-                            new = ((old[0] @ a_t).astype(np.float32), old[1] | m_t)
+                            new = (compose_affines(old[0], a_t), old[1] | m_t)
                             updated[id(old)] = new
                     pending[key] = new
                 i += 1
@@ -363,10 +409,10 @@ class Compose:
                 j = i
                 while j < len(ts) and self._is_fusible(ts[j]):
                     j += 1
-                d = self._run_intensity(d, ts[i:j], inputs)
+                d = self._run_intensity(d, ts[i:j], inputs, injected[i:j])
                 i = j
             else:
-                d = self._apply_dict(d, t, inputs)
+                d = self._apply_dict(d, t, inputs, injected[i])
                 i += 1
         if pending or fields:
             d = self._materialize(d, pending, fields, inputs)

@@ -22,6 +22,10 @@ void set_error(const char* fmt, ...);
 void clear_error();
 ba_status check_launch(const char* what);
 
+// Checks of an intensity-chain descriptor (shape, dtype, ops, pointers);
+// defined in intensity.cu.
+ba_status validate_chain(const ba_chain_desc* d);
+
 #define BA_REQUIRE(cond, ...)        \
   do {                               \
     if (!(cond)) {                   \

@@ -1025,6 +1025,44 @@ struct Segment {
   int64_t stats_offset;  // int32 offset of those stats in the workspace (8-byte aligned)
 };
 
+void plan_segments(const ba_chain_desc* d, std::vector<Segment>& segs, int64_t& ws_ints) {
+  segs.clear();
+  ws_ints = 0;
+  int first = 0;
+  for (int i = 0; i <= d->n_ops; ++i) {
+    const bool cut = (i == d->n_ops) || needs_stats(d->ops[i]);
+    if (!cut) continue;
+    Segment s;
+    s.first = first;
+    s.last = i;
+    s.stats_for = (i < d->n_ops) ? i : -1;
+    s.stats_offset = 0;
+    if (s.stats_for >= 0) {
+      ws_ints = (ws_ints + 1) & ~(int64_t)1;  // doubles stay 8-byte aligned
+      s.stats_offset = ws_ints;
+      ws_ints += stats_words(d->ops[i]) * stats_groups(d->ops[i], d->batch, d->channels);
+    }
+    segs.push_back(s);
+    first = i;
+  }
+}
+
+template <int DT, int VEC>
+ba_status launch_segment(ChainArgs& a, int64_t nb, bool write, cudaStream_t st) {
+  const int64_t tile = pick_tile(a.HWD, nb * a.C, VEC);
+  a.tile = tile;
+  dim3 grid((unsigned)((a.HWD + tile - 1) / tile), (unsigned)(nb * a.C));
+  if (write)
+    chain_kernel<DT, VEC, true><<<grid, CHAIN_THREADS, 0, st>>>(a);
+  else
+    chain_kernel<DT, VEC, false><<<grid, CHAIN_THREADS, 0, st>>>(a);
+  return check_launch("ba_intensity_chain");
+}
+
+}  // namespace
+
+// Shape, dtype, op and pointer checks of a chain descriptor, shared with
+// ba_intensity_chain_noalloc (noalloc.cu).
 ba_status validate_chain(const ba_chain_desc* d) {
   BA_REQUIRE(d != nullptr, "ba_intensity_chain: desc is NULL");
   BA_REQUIRE(d->batch >= 0 && d->channels >= 0 && d->H > 0 && d->W > 0 && d->D > 0,
@@ -1088,46 +1126,13 @@ ba_status validate_chain(const ba_chain_desc* d) {
   return BA_OK;
 }
 
-void plan_segments(const ba_chain_desc* d, std::vector<Segment>& segs, int64_t& ws_ints) {
-  segs.clear();
-  ws_ints = 0;
-  int first = 0;
-  for (int i = 0; i <= d->n_ops; ++i) {
-    const bool cut = (i == d->n_ops) || needs_stats(d->ops[i]);
-    if (!cut) continue;
-    Segment s;
-    s.first = first;
-    s.last = i;
-    s.stats_for = (i < d->n_ops) ? i : -1;
-    s.stats_offset = 0;
-    if (s.stats_for >= 0) {
-      ws_ints = (ws_ints + 1) & ~(int64_t)1;  // doubles stay 8-byte aligned
-      s.stats_offset = ws_ints;
-      ws_ints += stats_words(d->ops[i]) * stats_groups(d->ops[i], d->batch, d->channels);
-    }
-    segs.push_back(s);
-    first = i;
-  }
-}
-
-template <int DT, int VEC>
-ba_status launch_segment(ChainArgs& a, int64_t nb, bool write, cudaStream_t st) {
-  const int64_t tile = pick_tile(a.HWD, nb * a.C, VEC);
-  a.tile = tile;
-  dim3 grid((unsigned)((a.HWD + tile - 1) / tile), (unsigned)(nb * a.C));
-  if (write)
-    chain_kernel<DT, VEC, true><<<grid, CHAIN_THREADS, 0, st>>>(a);
-  else
-    chain_kernel<DT, VEC, false><<<grid, CHAIN_THREADS, 0, st>>>(a);
-  return check_launch("ba_intensity_chain");
-}
-
-}  // namespace
 }  // namespace ba
 
 extern "C" size_t ba_intensity_workspace_bytes(const ba_chain_desc* desc) {
   using namespace ba;
   if (desc == nullptr || desc->n_ops < 1 || desc->n_ops > BA_MAX_OPS) return 0;
+  // a malformed shape has no workspace size (ba_intensity_chain rejects it)
+  if (desc->batch < 0 || desc->channels < 0 || desc->batch * desc->channels > 65535) return 0;
   std::vector<Segment> segs;
   int64_t ints = 0;
   plan_segments(desc, segs, ints);

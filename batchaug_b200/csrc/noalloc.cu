@@ -63,6 +63,10 @@ extern "C" ba_status ba_intensity_chain_noalloc(const ba_chain_desc* desc, ba_st
   using namespace ba;
   clear_error();
   BA_REQUIRE(desc != nullptr, "ba_intensity_chain_noalloc: desc is NULL");
+  // the descriptor first, so a malformed shape reports itself and not a
+  // scratch size derived from it
+  const ba_status v = validate_chain(desc);
+  if (v != BA_OK) return v;
   const size_t need = ba_intensity_workspace_bytes(desc);
   BA_REQUIRE(need <= (size_t)BA_NOALLOC_CHAIN_SCRATCH,
              "ba_intensity_chain_noalloc: this chain needs %zu bytes of scratch, more than the "
@@ -77,3 +81,5 @@ extern "C" ba_status ba_intensity_chain_noalloc(const ba_chain_desc* desc, ba_st
   // the call, so nothing left in the array by an earlier call is read.
   return ba_intensity_chain(desc, scratch, need, stream);
 }
+
+extern "C" size_t ba_noalloc_chain_scratch_bytes(void) { return (size_t)BA_NOALLOC_CHAIN_SCRATCH; }

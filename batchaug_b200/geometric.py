@@ -79,6 +79,7 @@ class _AffineFamily(BatchTransform):
 
     mode = "bilinear"
     padding_mode = "zeros"
+    _host_keys = ("affine",)
 
     def _device_params(self, host, shape, device):
         theta = host.get("theta")
@@ -217,6 +218,7 @@ class RandAxisFlip(BatchTransform):
     """Flip one random spatial axis per element (flip.py:8-66)."""
 
     _stream = _rng.S_FLIP
+    _host_keys = ("axes",)
 
     def __init__(self, prob: float = 0.1):
         super().__init__(prob=prob)
@@ -287,6 +289,7 @@ class RandRotate90(BatchTransform):
     """k*90 degree rotation, k in 1..max_k, in spatial_axes (rotate90.py:10-112)."""
 
     _stream = _rng.S_ROT90
+    _host_keys = ("k",)
 
     def __init__(self, prob: float = 0.1, max_k: int = 3, spatial_axes=(0, 1)):
         super().__init__(prob=prob)
@@ -410,10 +413,15 @@ class _PerKeyModes:
         self._padding_mode = ({k: padding_mode for k in keys} if isinstance(padding_mode, str)
                               else padding_mode)
 
-    def __call__(self, data):
+    def __call__(self, data, params: dict | None = None):
+        """``params``: optional injected params (as ``sample_params`` returns
+        them, e.g. the reference's own) instead of sampling."""
         d = dict(data)
-        first = d[self.keys[0]]
-        params = self.transform.sample_params(first.shape[0], first.shape, first.device)
+        if params is None:
+            first = d[self.keys[0]]
+            params = self.transform.sample_params(first.shape[0], first.shape, first.device)
+        else:
+            params = self.transform.adopt_params(params)
         mode = lambda k: self._mode.get(k, "bilinear")  # noqa: E731
         pad = lambda k: self._padding_mode.get(k, self._default_padding)  # noqa: E731
         keys = [k for k in self.keys if k in d]
@@ -474,8 +482,8 @@ class RandRotated:
         self._inner = RandAffined(keys=keys, prob=prob, rotate_range=[range_x, range_y, range_z],
                                   mode=mode, padding_mode=padding_mode)
 
-    def __call__(self, data):
-        return self._inner(data)
+    def __call__(self, data, params: dict | None = None):
+        return self._inner(data, params=params)
 
 
 class RandAxisFlipd(BatchDictTransform):

@@ -13,6 +13,7 @@ import numpy as np
 import torch
 
 from . import _lib as L
+from . import _timing
 
 
 def _contig(t: torch.Tensor, name: str) -> torch.Tensor:
@@ -112,7 +113,10 @@ def resample3d(tensors, *, affine=None, theta=None, grid=None, modes="bilinear",
         k.dtype = L.dtype_code(t)
         k.mode = L.MODES[modes[i]]
         k.padding = L.PADDINGS[paddings[i]]
+    tok = _timing.begin("ba_resample3d", sum(2 * t.numel() * t.element_size() for t in ts),
+                        device)
     L.check(L.lib.ba_resample3d(ctypes.byref(d), L.stream_ptr(device)), "ba_resample3d")
+    _timing.end(tok)
     return outs[0] if single else outs
 
 
@@ -167,8 +171,10 @@ def intensity_chain(x: torch.Tensor, ops, out: torch.Tensor | None = None,
         o.c0, o.c1 = float(op.c0), float(op.c1)
     nbytes = L.lib.ba_intensity_workspace_bytes(ctypes.byref(d))
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device) if nbytes else None
+    tok = _timing.begin("ba_intensity_chain", 2 * x.numel() * x.element_size(), x.device)
     L.check(L.lib.ba_intensity_chain(ctypes.byref(d), L.ptr(ws), nbytes, L.stream_ptr(x.device)),
             "ba_intensity_chain")
+    _timing.end(tok)
     return out
 
 
@@ -178,9 +184,11 @@ def minmax(x: torch.Tensor, n_groups: int):
     if x.numel() % max(n_groups, 1):
         raise ValueError("minmax: numel is not a multiple of n_groups")
     stats = torch.empty(n_groups, 2, dtype=torch.float32, device=x.device)
+    tok = _timing.begin("ba_minmax", x.numel() * x.element_size(), x.device)
     L.check(L.lib.ba_minmax(x.data_ptr(), L.dtype_code(x), n_groups,
                             x.numel() // max(n_groups, 1), stats.data_ptr(),
                             L.stream_ptr(x.device)), "ba_minmax")
+    _timing.end(tok)
     return stats[:, 0], stats[:, 1]
 
 
@@ -215,11 +223,13 @@ def smooth3d(x: torch.Tensor, taps_h, taps_w, taps_d, mask=None,
     out = torch.empty_like(x)
     nbytes = L.lib.ba_smooth_workspace_bytes(B, C, H, W, D)
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+    tok = _timing.begin("ba_smooth3d", 2 * x.numel() * x.element_size(), x.device)
     L.check(L.lib.ba_smooth3d(x.data_ptr(), out.data_ptr(), L.dtype_code(x), B, C, H, W, D,
                               th.data_ptr(), th.shape[1], tw.data_ptr(), tw.shape[1],
                               td.data_ptr(), td.shape[1], L.SMOOTH_PADS[padding_mode], L.ptr(m),
                               ws.data_ptr(), nbytes,
                               L.stream_ptr(x.device)), "ba_smooth3d")
+    _timing.end(tok)
     return out
 
 
@@ -252,8 +262,10 @@ def sharpen3d(x: torch.Tensor, taps1, taps2, alpha, mask=None,
     d.alpha, d.mask = al.data_ptr(), L.ptr(m)
     nbytes = L.lib.ba_sharpen_workspace_bytes(ctypes.byref(d))
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+    tok = _timing.begin("ba_sharpen3d", 2 * x.numel() * x.element_size(), x.device)
     L.check(L.lib.ba_sharpen3d(ctypes.byref(d), ws.data_ptr(), nbytes, L.stream_ptr(x.device)),
             "ba_sharpen3d")
+    _timing.end(tok)
     return out
 
 
@@ -283,8 +295,10 @@ def lowres3d(x: torch.Tensor, zoom, mask=None, downsample_mode="nearest",
     d.zoom, d.mask, d.max_zoom = z.data_ptr(), L.ptr(m), float(max(max_zoom, 1e-30))
     nbytes = L.lib.ba_lowres_workspace_bytes(ctypes.byref(d))
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+    tok = _timing.begin("ba_lowres3d", 2 * x.numel() * x.element_size(), x.device)
     L.check(L.lib.ba_lowres3d(ctypes.byref(d), ws.data_ptr(), nbytes, L.stream_ptr(x.device)),
             "ba_lowres3d")
+    _timing.end(tok)
     return out
 
 
@@ -303,9 +317,11 @@ def compose_field(field: torch.Tensor, theta, mask_field=None, mask_affine=None)
     mf = _dev_mask(mask_field, B, field.device)
     ma = _dev_mask(mask_affine, B, field.device)
     out = torch.empty_like(field)
+    tok = _timing.begin("ba_compose_field", 2 * field.numel() * 4, field.device)
     L.check(L.lib.ba_compose_field(field.data_ptr(), th.data_ptr(), L.ptr(mf), L.ptr(ma), B, H, W,
                                    D, out.data_ptr(), L.stream_ptr(field.device)),
             "ba_compose_field")
+    _timing.end(tok)
     return out
 
 
@@ -322,10 +338,12 @@ def elastic_grid(shape, taps, magnitude, *, u=None, seed=0, elem_offset=0,
     grid = torch.empty(B, H, W, D, 3, dtype=torch.float32, device=device)
     nbytes = L.lib.ba_elastic_workspace_bytes(B, H, W, D)
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+    tok = _timing.begin("ba_elastic_grid", grid.numel() * 4, device)
     L.check(L.lib.ba_elastic_grid(L.ptr(uu), int(seed) & 0xFFFFFFFFFFFFFFFF, int(elem_offset),
                                   B, H, W, D, tp.data_ptr(), tp.shape[1], mg.data_ptr(),
                                   grid.data_ptr(), ws.data_ptr(), nbytes,
                                   L.stream_ptr(device)), "ba_elastic_grid")
+    _timing.end(tok)
     return grid
 
 

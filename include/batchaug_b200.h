@@ -224,6 +224,9 @@ BA_API ba_status ba_intensity_chain(const ba_chain_desc* desc, void* workspace, 
  */
 #define BA_NOALLOC_CHAIN_SCRATCH 262144
 BA_API ba_status ba_intensity_chain_noalloc(const ba_chain_desc* desc, ba_stream_t stream);
+/* The size of that static array, BA_NOALLOC_CHAIN_SCRATCH, as the library
+ * was built with it (for bindings that do not read this header). */
+BA_API size_t ba_noalloc_chain_scratch_bytes(void);
 
 /*
  * Per-group min and max of a contiguous (n_groups, group_size) view, fp32

@@ -43,7 +43,7 @@ def build(force: bool = False) -> str:
 
 def _stale() -> bool:
     lib_t = os.path.getmtime(_LIB_PATH)
-    for f in ("oracle.c", "oracle_intensity.c", "Makefile"):
+    for f in ("oracle.c", "oracle_intensity.c", "oracle_lowres.c", "oracle_compose.c", "Makefile"):
         p = os.path.join(_HERE, f)
         if os.path.exists(p) and os.path.getmtime(p) > lib_t:
             return True

@@ -21,6 +21,8 @@ import numpy as np
 import torch
 
 OUT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, OUT)
+import inputs  # noqa: E402  (tests/golden/inputs.py: seeded regenerable inputs)
 
 
 def npy(t: torch.Tensor) -> np.ndarray:
@@ -42,7 +44,7 @@ def save(name: str, **arrays):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("BATCHAUG_REFERENCE", ""))
-    ap.add_argument("--only", choices=["stats", "sharpen", "lowres"], default=None,
+    ap.add_argument("--only", choices=["stats", "sharpen", "lowres", "compose"], default=None,
                     help="write only this group of fixtures")
     args = ap.parse_args()
     if args.reference:
@@ -50,6 +52,9 @@ def main():
     import torch.nn.functional as F
 
     import batchaug.pytorch as P
+    if args.only == "compose":
+        gen_compose(P)
+        return
     if args.only == "stats":
         gen_stats_ops(P)
         return
@@ -219,6 +224,7 @@ def main():
     gen_stats_ops(P)
     gen_sharpen(P)
     gen_lowres(P)
+    gen_compose(P)
 
 
 def gen_stats_ops(P):
@@ -319,6 +325,221 @@ def gen_lowres(P):
             rec.update({f"m{i}_mask": p["mask"], f"m{i}_zoom": p["zoom_factor"],
                         f"m{i}_out": t.apply(x, p)})
         save(f"lowres_{tag}", **rec)
+
+
+# ---------------------------------------------------------------------------
+# Compose itself: the reference's batchaug.compose.Compose on recorded params
+# ---------------------------------------------------------------------------
+
+def _sampler_of(t):
+    """The object whose sample_params a Compose step calls for ``t``."""
+    inner = getattr(t, "transform", None)
+    if inner is not None:
+        return inner
+    wrapped = getattr(t, "_inner", None)  # RandRotated wraps a RandAffined
+    if wrapped is not None:
+        return wrapped.transform
+    return t
+
+
+def _record(transforms, overrides):
+    """Wrap every transform's sample_params: apply the override for its
+    index (forced masks, regenerated large tensors) and log the params."""
+    log = {}
+    for i, t in enumerate(transforms):
+        obj = _sampler_of(t)
+        orig = obj.sample_params
+
+        def wrapped(B, shape, device, _i=i, _orig=orig):
+            p = _orig(B, shape, device)
+            ov = overrides.get(_i)
+            if ov is not None:
+                p = ov(p, tuple(shape))
+            log[_i] = p
+            return p
+        obj.sample_params = wrapped
+    return log
+
+
+# params regenerated by the tests from a recipe instead of being stored
+_REGENERATED = {"noise", "grid", "basis"}
+
+
+def _params_arrays(log, n):
+    out = {}
+    for i in range(n):
+        for k, v in log.get(i, {}).items():
+            if k in _REGENERATED or not isinstance(v, torch.Tensor):
+                continue
+            out[f"p{i}_{k}"] = v
+    return out
+
+
+def _summary(name, a):
+    """A large output kept as: one H plane, a strided subsample and the
+    per-(element, channel) sums and sums of squares (float64)."""
+    a = np.asarray(a)
+    vals = a.astype(np.float32) if a.dtype != np.uint16 else inputs.bf16_to_f32(a)
+    H = a.shape[2]
+    flat = vals.reshape(a.shape[0] * a.shape[1], -1).astype(np.float64)
+    return {f"{name}_plane": a[:, :, (H * 3) // 5], f"{name}_stride": a[:, :, ::9, ::9, ::9],
+            f"{name}_sum": flat.sum(1), f"{name}_sumsq": (flat * flat).sum(1)}
+
+
+def _force(mask_values, extra=None):
+    def ov(p, shape):
+        p["mask"] = torch.tensor(mask_values)
+        if extra is not None:
+            p = extra(p, shape)
+        return p
+    return ov
+
+
+def _noise_from(seed):
+    """Replace the reference's randn noise by the seeded one (same formula:
+    z * std + mean in fp32, per element)."""
+    def ov(p, shape):
+        z = inputs.normal(seed, shape)
+        std = p["std"].numpy().astype(np.float32).reshape(-1, 1, 1, 1, 1)
+        mean = p["mean"].numpy().astype(np.float32).reshape(-1, 1, 1, 1, 1)
+        p["noise"] = torch.from_numpy((z * std + mean).astype(np.float32))
+        return p
+    return ov
+
+
+def _grid_from(seed, max_disp):
+    def ov(p, shape):
+        B, _, H, W, D = shape
+        p["grid"] = torch.from_numpy(inputs.elastic_grid(seed, B, (H, W, D), max_disp))
+        return p
+    return ov
+
+
+def gen_compose(P):
+    """Compose(lazy=True) of the reference at configs 1, 4 and 5 (full size
+    for config 1, two-element slices of configs 4 and 5), the
+    different-key-sets and mask cases of the reference's tests, and
+    RandZoom / RandFlip / RandRotate eager and inside Compose."""
+    from batchaug.compose import Compose
+    torch.set_num_threads(8)
+    dev = torch.device("cpu")
+
+    def run(name, transforms, data, overrides, mode, padding="zeros", seeds=None,
+            big=(), lazy=True):
+        log = _record(transforms, overrides)
+        c = Compose(transforms, lazy=lazy, mode=mode, padding_mode=padding)
+        out = c({k: torch.from_numpy(v.copy()) if v.dtype != np.uint16 else
+                 torch.from_numpy(v.view(np.int16).copy()).view(torch.bfloat16)
+                 for k, v in data.items()})
+        rec = _params_arrays(log, len(transforms))
+        rec["n_transforms"] = np.int64(len(transforms))
+        for k, v in out.items():
+            a = npy(v)
+            if k in big:
+                rec.update(_summary(f"out_{k}", a))
+            else:
+                rec[f"out_{k}"] = a
+        rec.update({f"seed_{k}": np.int64(v) for k, v in (seeds or {}).items()})
+        rec["input_digest"] = np.array(inputs.digest(*[data[k] for k in sorted(data)]))
+        save(name, **rec)
+        return out
+
+    # --- config 1, full size: 2 x 1 x 64^3, flip + affine fused, noise, scale
+    shp = (2, 1, 64, 64, 64)
+    vol, seg = inputs.normal(201, shp), inputs.labels(202, shp, 5, block=10)
+    run("compose_cfg1", [P.RandAxisFlipd(["vol", "seg"], prob=0.5),
+                         P.RandAffined(["vol", "seg"], prob=1.0, rotate_range=0.785,
+                                       shear_range=0.3, translate_range=5),
+                         P.RandGaussianNoised(["vol"], std=0.1),
+                         P.ScaleIntensityd(["vol"])],
+        {"vol": vol, "seg": seg},
+        {0: _force([True, False]), 2: _force([True, False], _noise_from(203))},
+        {"vol": "bilinear", "seg": "nearest"}, seeds={"vol": 201, "seg": 202, "noise": 203})
+
+    # --- config 4 slice: 2 x 4 x 128^3, {rot90, flip} -> noise -> {affine} -> scale
+    shp = (2, 4, 128, 128, 128)
+    vol = inputs.normal(401, shp)
+    seg = (inputs.labels(402, shp, 2, block=16) > 0).astype(np.float32)
+    run("compose_cfg4", [P.RandRotate90d(["vol", "seg"], prob=0.5, max_k=3, spatial_axes=(0, 1)),
+                         P.RandAxisFlipd(["vol", "seg"], prob=0.5),
+                         P.RandGaussianNoised(["vol"], std=0.5),
+                         P.RandAffined(["vol", "seg"], prob=0.5, rotate_range=0.785,
+                                       shear_range=0.3, translate_range=5),
+                         P.ScaleIntensityd(["vol"])],
+        {"vol": vol, "seg": seg},
+        {0: _force([True, False]), 1: _force([True, True]),
+         2: _force([False, True], _noise_from(403)), 3: _force([True, False])},
+        {"vol": "bilinear", "seg": "nearest"}, seeds={"vol": 401, "seg": 402, "noise": 403},
+        big=("vol", "seg"))
+
+    # --- config 5 slice: 2 x 2 x 160^3, vol bf16 + seg f32; elastic (grid
+    # injected) -> {affine} -> bias -> smooth -> scale
+    shp = (2, 2, 160, 160, 160)
+    vol = inputs.bf16_bits(inputs.uniform(501, shp))
+    seg = inputs.labels(502, shp, 8, block=20)
+    run("compose_cfg5", [P.Rand3DElasticd(["vol", "seg"], prob=1.0, sigma_range=(5, 7),
+                                          magnitude_range=(50, 150),
+                                          mode={"vol": "bilinear", "seg": "nearest"}),
+                         P.RandAffined(["vol", "seg"], prob=0.1, rotate_range=0.5),
+                         P.RandBiasFieldd(["vol"], prob=0.1),
+                         P.RandGaussianSmoothd(["vol"], prob=0.1, sigma_x=(0.5, 1.5),
+                                               sigma_y=(0.5, 1.5), sigma_z=(0.5, 1.5)),
+                         P.ScaleIntensityd(["vol"])],
+        {"vol": vol, "seg": seg},
+        {0: _grid_from(503, 4.0), 1: _force([True, False]), 2: _force([False, True]),
+         3: _force([True, False])},
+        {"vol": "bilinear", "seg": "nearest"}, seeds={"vol": 501, "seg": 502, "grid": 503},
+        big=("vol", "seg"))
+
+    # --- the reference's own Compose cases (tests/test_compose.py) --------
+    shp = (4, 3, 16, 16, 16)
+    vol, seg = inputs.uniform(601, shp), inputs.labels(602, shp, 5, block=3)
+    run("compose_keysets", [P.RandAxisFlipd(["vol", "seg"], prob=1.0),
+                            P.RandRotate90d(["vol"], prob=1.0)],
+        {"vol": vol, "seg": seg}, {}, "nearest", seeds={"vol": 601, "seg": 602})
+    run("compose_partial_mask", [P.RandAxisFlipd(["vol"], prob=0.5)], {"vol": vol},
+        {0: _force([True, False, True, False])}, "nearest", seeds={"vol": 601})
+    run("compose_mixed", [P.RandAxisFlipd(["vol", "seg"], prob=1.0),
+                          P.RandGaussianNoised(["vol"], prob=1.0, std=0.1),
+                          P.RandRotate90d(["vol", "seg"], prob=1.0)],
+        {"vol": vol, "seg": seg}, {1: _noise_from(603)},
+        {"vol": "bilinear", "seg": "nearest"}, seeds={"vol": 601, "seg": 602, "noise": 603})
+
+    # --- RandZoom / RandFlip / RandRotate: eager, and inside Compose -----
+    shp = (3, 2, 12, 14, 16)
+    vol, seg = inputs.normal(701, shp), inputs.labels(702, shp, 6, block=4)
+    mask3 = [True, False, True]
+    run("compose_zoom_flip_rotate",
+        [P.RandZoomd(["vol", "seg"], prob=0.7, min_zoom=0.7, max_zoom=1.3),
+         P.RandFlipd(["vol", "seg"], prob=0.7),
+         P.RandRotated(["vol", "seg"], prob=0.7, range_x=0.4, range_y=0.3, range_z=0.2,
+                       mode={"vol": "bilinear", "seg": "nearest"}),
+         P.RandFlipd(["vol", "seg"], prob=0.7, spatial_axis=[0, 2])],
+        {"vol": vol, "seg": seg},
+        {0: _force(mask3), 1: _force([False, True, True]), 2: _force(mask3),
+         3: _force([True, True, False])},
+        {"vol": "bilinear", "seg": "nearest"}, seeds={"vol": 701, "seg": 702})
+    x = torch.from_numpy(vol)
+    rec = {}
+    z = P.RandZoom(prob=0.7, min_zoom=0.7, max_zoom=1.3)
+    pz = z.sample_params(3, x.shape, dev)
+    pz["mask"] = torch.tensor(mask3)
+    rec.update(zoom_mask=pz["mask"], zoom_zoom=pz["zoom"], zoom_affine=pz["affine"],
+               zoom_theta=pz["theta"], zoom_out=z.apply(x, pz),
+               zoom_nearest_zeros_out=z.apply(x, pz, mode="nearest", padding_mode="zeros"))
+    for tag, axis in (("all", None), ("h", 0), ("wd", [1, 2])):
+        f = P.RandFlip(prob=0.7, spatial_axis=axis)
+        pf = f.sample_params(3, x.shape, dev)
+        pf["mask"] = torch.tensor(mask3)
+        rec[f"flip_{tag}_mask"] = pf["mask"]
+        rec[f"flip_{tag}_out"] = f.apply(x, pf)
+    r = P.RandRotate(prob=0.7, range_x=0.4, range_y=(0.1, 0.3), range_z=0.2)
+    pr = r.sample_params(3, x.shape, dev)
+    pr["mask"] = torch.tensor(mask3)
+    rec.update(rotate_mask=pr["mask"], rotate_affine=pr["affine"], rotate_theta=pr["theta"],
+               rotate_out=r.apply(x, pr))
+    rec["x"] = x
+    save("zoom_flip_rotate_eager", **rec)
 
 
 if __name__ == "__main__":

@@ -66,14 +66,43 @@ def test_noalloc_rejects_oversized_scratch():
     from batchaug_b200 import _lib as L
     limit = L.BA_NOALLOC_CHAIN_SCRATCH
     groups = limit // 8 + 1  # 2 int32 keys per group per min/max barrier
-    x = torch.zeros(1, device="cuda")
+    # src and dst hold every voxel the descriptor describes (1 x groups x 1^3
+    # fp32), so the call stays in bounds even if the size check regressed
+    x = torch.arange(groups, dtype=torch.float32, device="cuda")
+    before = x.clone()
     d = L.ChainDesc()
     d.src = d.dst = x.data_ptr()
     d.batch, d.channels, d.H, d.W, d.D = 1, groups, 1, 1, 1
     d.dtype, d.n_ops = L.BA_F32, 1
     d.ops[0].kind = L.BA_OP_RESCALE
     d.ops[0].flags = L.BA_RESCALE_MINV | L.BA_RESCALE_MAXV | L.BA_RESCALE_CHANNEL
+    assert L.lib.ba_intensity_workspace_bytes(ctypes.byref(d)) > limit
     st = L.lib.ba_intensity_chain_noalloc(ctypes.byref(d), torch.cuda.current_stream().cuda_stream)
     assert st == L.BA_EINVAL
     assert b"static array" in L.lib.ba_last_error()
-    assert np.isfinite(float(x.cpu()[0]))
+    torch.cuda.synchronize()
+    assert torch.equal(x, before)  # rejected before any kernel ran
+
+
+def test_noalloc_reports_bad_shape_first():
+    """A malformed descriptor is reported as such, not as a scratch size
+    computed from its shape."""
+    from batchaug_b200 import _lib as L
+    d = L.ChainDesc()
+    d.batch, d.channels, d.H, d.W, d.D = -1, 1, 4, 4, 4
+    d.dtype, d.n_ops = L.BA_F32, 1
+    d.ops[0].kind = L.BA_OP_RESCALE
+    d.ops[0].flags = L.BA_RESCALE_MINV | L.BA_RESCALE_MAXV
+    st = L.lib.ba_intensity_chain_noalloc(ctypes.byref(d), torch.cuda.current_stream().cuda_stream)
+    assert st == L.BA_EINVAL
+    assert b"bad shape" in L.lib.ba_last_error()
+
+
+def test_noalloc_limit_matches_header():
+    from batchaug_b200 import _lib as L
+    import os
+    import re
+    hdr = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                       "batchaug_b200.h")
+    m = re.search(r"#define BA_NOALLOC_CHAIN_SCRATCH (\d+)", open(hdr).read())
+    assert m and int(m.group(1)) == L.BA_NOALLOC_CHAIN_SCRATCH
