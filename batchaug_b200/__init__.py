@@ -18,6 +18,7 @@ from . import _lib  # noqa: F401  (loads libbatchaug_b200.so or raises ImportErr
 from ._rng import get_shard, set_shard, shard
 from .base import BatchDictTransform, BatchTransform
 from .compose import Compose
+from .ops import resample_exact, set_resample_exact
 from .geometric import (
     Rand3DElastic,
     Rand3DElasticd,
@@ -80,7 +81,7 @@ def resolve_backend() -> str:
 
 __all__ = [
     "BatchTransform", "BatchDictTransform", "Compose", "set_backend", "get_backend",
-    "resolve_backend", "set_shard", "get_shard", "shard",
+    "resolve_backend", "set_shard", "get_shard", "shard", "resample_exact", "set_resample_exact",
     "Rand3DElastic", "Rand3DElasticd", "RandAffine", "RandAffined", "RandAxisFlip",
     "RandAxisFlipd", "RandFlip", "RandFlipd", "RandRotate", "RandRotated", "RandRotate90",
     "RandRotate90d", "RandZoom", "RandZoomd",

@@ -21,6 +21,7 @@ BA_F32, BA_BF16 = 0, 1
 BA_BILINEAR, BA_NEAREST = 0, 1
 BA_PAD_ZEROS, BA_PAD_BORDER, BA_PAD_REFLECTION = 0, 1, 2
 BA_XFORM_AFFINE, BA_XFORM_THETA, BA_XFORM_GRID = 0, 1, 2
+BA_RESAMPLE_EXACT, BA_RESAMPLE_HOST_PARAMS = 0x1, 0x2
 BA_MAX_KEYS = 8
 BA_MAX_OPS = 8
 
@@ -53,7 +54,7 @@ class ResampleKey(ctypes.Structure):
 class ResampleDesc(ctypes.Structure):
     _fields_ = [("batch", _I64), ("H", _I64), ("W", _I64), ("D", _I64),
                 ("xform_kind", _I32), ("align_corners", _I32), ("n_keys", _I32),
-                ("reserved", _I32), ("xform", _P), ("xform_stride", _I64), ("mask", _P),
+                ("flags", _I32), ("xform", _P), ("xform_stride", _I64), ("mask", _P),
                 ("keys", ResampleKey * BA_MAX_KEYS)]
 
 

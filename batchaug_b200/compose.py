@@ -68,6 +68,25 @@ def compose_affines(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     return acc.astype(np.float32)
 
 
+def _slice_params(params: dict, b: int, n: int) -> dict:
+    """``params`` for elements b .. b+n-1 as a view of the batch: every
+    tensor or array whose first dimension is the batch is sliced, the
+    element offset of in-kernel random streams (keyed on the global element
+    index) advances by b, everything else is kept."""
+    B = len(params["_host"]["mask"])
+
+    def cut(v):
+        if isinstance(v, (torch.Tensor, np.ndarray)) and v.ndim >= 1 and v.shape[0] == B:
+            return v[b:b + n]
+        return v
+
+    out = {k: cut(v) for k, v in params.items() if k != "_host"}
+    out["_host"] = {k: cut(v) for k, v in params["_host"].items()}
+    if "elem_offset" in params:
+        out["elem_offset"] = params["elem_offset"] + b
+    return out
+
+
 class Compose:
     def __init__(self, transforms: list, lazy: bool = False, mode="bilinear",
                  padding_mode="zeros", fuse_elastic: bool = False):
@@ -202,41 +221,47 @@ class Compose:
                 raise KeyError(t.keys[0])
             p = injected[i] if injected is not None else None
             if p is None:
-                p = t.transform.sample_params(first.shape[0], first.shape, first.device)
+                p = t.transform.chain_params(first.shape[0], first.shape, first.device)
             else:
                 p = t.transform.adopt_params(p)
             sampled.append((t, p))
         keys = list(dict.fromkeys(k for t in run for k in t.keys if k in d))
-        sel = None  # owned keys, subsettable run: the elements any op selects
-        if inputs is not None and keys and self._owned(d, keys, inputs) and all(
-                getattr(t.transform, "_subsettable", False) for t in run):
+        owned = inputs is not None and bool(keys) and self._owned(d, keys, inputs)
+        if owned:
+            # pipeline-owned keys: the chain runs in place on the runs of
+            # elements some op selects; an element no op selects is left as
+            # it is (every op of a chain is the identity on an unselected
+            # element, up to the sign of a zero that adds noise * 0)
             sel = np.zeros(len(sampled[0][1]["_host"]["mask"]), bool)
             for _, p in sampled:
                 sel |= np.asarray(p["_host"]["mask"], bool)
-            if not sel.any():
+            if not sel.all():
+                for b, n in self._runs(np.flatnonzero(sel)):
+                    sub = [(t, _slice_params(p, b, n)) for t, p in sampled]
+                    self._chain_keys({k: d[k][b:b + n] for k in keys}, sub, inplace=True)
                 return d
-            if not self._sparse(sel):
-                sel = None
-        if sel is not None:
-            idx, it = self._subset_index(sel, d[keys[0]].device)
-            sampled = [(t, t.transform.subset_params(p, idx, it)) for t, p in sampled]
-            views = {k: self._gather(d[k], idx) for k in keys}
-        else:
-            views = {k: d[k] for k in keys}
+        out = self._chain_keys({k: d[k] for k in keys}, sampled, inplace=owned)
+        d.update(out)
+        return d
+
+    @staticmethod
+    def _chain_keys(views: dict, sampled: list, inplace: bool) -> dict:
+        """One ba_intensity_chain per key over the ops that list it; an op
+        that selects no element is the identity and is left out."""
         per_key: dict[str, list] = {}
         for t, params in sampled:
+            if not np.asarray(params["_host"]["mask"]).any():
+                continue
             for key in t.keys:
                 if key in views:
                     per_key.setdefault(key, []).append(t.transform.chain_op(params, views[key]))
+        out = {}
         for key, chain in per_key.items():
             x = views[key]
             for i in range(0, len(chain), L.BA_MAX_OPS):
-                x = ops.intensity_chain(x, chain[i:i + L.BA_MAX_OPS])
-            if sel is not None:
-                self._scatter(d[key], idx, x)
-            else:
-                d[key] = x
-        return d
+                x = ops.intensity_chain(x, chain[i:i + L.BA_MAX_OPS], inplace=inplace)
+            out[key] = x
+        return out
 
     def _apply_rest(self, d: dict, transforms: list, inputs: set | None = None,
                     injected: list | None = None) -> dict:

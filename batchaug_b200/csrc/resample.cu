@@ -29,6 +29,9 @@
 // scalar code rounds (this file is compiled with -fmad=false; fused or packed
 // operations appear only where written explicitly).
 #include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
 
 #include "ba_common.cuh"
 
@@ -72,6 +75,10 @@ struct KeyArgs {
   int32_t padding;
 };
 
+// Elements per launch whose transform and mask ride in the kernel's
+// parameters (BA_RESAMPLE_HOST_PARAMS): 16 floats and a mask byte each.
+constexpr int RS_INLINE_B = 32;
+
 struct ResampleArgs {
   int64_t batch;
   int32_t H, W, D;
@@ -84,7 +91,24 @@ struct ResampleArgs {
   float sn[3];  // fl32(2/H), fl32(2/W), fl32(2/D)
   float si[3];  // H/2, W/2, D/2
   KeyArgs keys[BA_MAX_KEYS];
+  // elements b0 .. b0 + gridDim.z - 1 (the launch's blocks z, or y for the
+  // grid kernel); with inline_params the affine / theta and mask of element
+  // b are inl_xform[(b - b0) * xform_stride ..] and inl_mask[b - b0]
+  int64_t b0;
+  int32_t inline_params;
+  float inl_xform[RS_INLINE_B * 16];
+  uint8_t inl_mask[RS_INLINE_B];
 };
+
+__device__ __forceinline__ bool elem_active(const ResampleArgs& a, int64_t b) {
+  if (a.inline_params) return a.inl_mask[b - a.b0] != 0;
+  return a.mask == nullptr || a.mask[b] != 0;
+}
+
+// the element's affine / theta rows (AFFINE and THETA maps)
+__device__ __forceinline__ const float* elem_xform(const ResampleArgs& a, int64_t b) {
+  return a.inline_params ? a.inl_xform + (b - a.b0) * a.xform_stride : a.xform + b * a.xform_stride;
+}
 
 // ---------------------------------------------------------------------------
 // Packed fp32x2 arithmetic (sm_100), two voxels per instruction.  A packed
@@ -252,7 +276,24 @@ __device__ __forceinline__ void sample_pair(const KeyArgs& k, int64_t b, int H, 
                      (unsigned)zb < (unsigned)H;
     const int oa = oka ? (za * W + ya) * D + xa : 0;
     const int ob = okb ? (zb * W + yb) * D + xb : 0;
-    for (int c = 0; c < k.channels; ++c) {
+    // four channels' gathers in flight before their stores
+    int c = 0;
+    for (; c + 4 <= k.channels; c += 4) {
+      float va[4], vb[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const void* cs = src_e + (size_t)(c + j) * hwd * esz;
+        va[j] = oka ? ld<DT>(cs, oa) : 0.0f;
+        vb[j] = okb ? ld<DT>(cs, ob) : 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        void* cd = dst_e + (size_t)(c + j) * hwd * esz;
+        st<DT>(cd, sa, va[j]);
+        if (has_b) st<DT>(cd, sb, vb[j]);
+      }
+    }
+    for (; c < k.channels; ++c) {
       const void* cs = src_e + (size_t)c * hwd * esz;
       void* cd = dst_e + (size_t)c * hwd * esz;
       const float va = oka ? ld<DT>(cs, oa) : 0.0f;
@@ -340,9 +381,9 @@ __global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
   const int w_brick = (blockIdx.x / tiles_d) * TY;
   const int h_first = blockIdx.y * (TZ * NB);
   const int w = w_brick + ty;
-  const int64_t b = blockIdx.z;
+  const int64_t b = a.b0 + blockIdx.z;
   const int hwd = H * W * D;
-  const bool active = (a.mask == nullptr) || (a.mask[b] != 0);
+  const bool active = elem_active(a, b);
   const bool affine = a.xform_kind != BA_XFORM_GRID;
 
   // Prologue: theta, then the base coordinates of the CTA's rows and
@@ -354,7 +395,7 @@ __global__ void __launch_bounds__(NTHREADS, BA_RS_MINBLOCKS)
     const int t = threadIdx.x;
     if (t < 12) {
       const int i = t / 4, j = t % 4;
-      const float* x = a.xform + b * a.xform_stride;
+      const float* x = elem_xform(a, b);
       if (a.xform_kind == BA_XFORM_AFFINE) {
         // monai_affine_to_theta: theta = P S_norm A S_inv P, P swapping 0 and 2.
         const int pi = 2 - i, pj = (j == 3) ? 3 : 2 - j;
@@ -502,6 +543,11 @@ constexpr int ST_THREADS = 128;
 // 44 KB of staged source: five CTAs (with their static shared memory and the
 // per-CTA reserve) fit in an SM's 228 KB; at 46-48 KB only four do
 constexpr int ST_MAX_FLOATS = BA_ST_MAX_FLOATS;
+#ifndef BA_FS_MAX_FLOATS
+#define BA_FS_MAX_FLOATS 11264
+#endif
+// the fast kernel re-checks its box with the padded pitches
+constexpr int FS_MAX_SETUP_FLOATS = BA_FS_MAX_FLOATS;
 constexpr int ST_PW = ST_TW / 2, ST_PH = ST_TH / 8;
 static_assert(ST_TW % 2 == 0 && ST_TH % 8 == 0, "tile covered by the thread layout");
 
@@ -515,83 +561,89 @@ __device__ __forceinline__ float4 ld4(const void* base, int64_t i) {
   return __ldg(reinterpret_cast<const float4*>((const float*)base + i));
 }
 
-template <int S0, int S1>
-__global__ void __launch_bounds__(ST_THREADS, BA_ST_MINBLOCKS)
-    resample3d_staged_kernel(const __grid_constant__ ResampleArgs a) {
-  extern __shared__ float4 s_dyn4[];
-  float* s_src = reinterpret_cast<float*>(s_dyn4);
-  __shared__ float s_theta[12];
-  __shared__ float s_by[ST_TW], s_bz[ST_TH];
-  __shared__ float2 s_px[3][8];
-  __shared__ int s_lo[3], s_hi[3];
-  __shared__ int s_box[6];
-  constexpr int MODE = spec_mode(S0), PAD = spec_pad(S0), DT = spec_dt(S0);
-  const bool ALIGN = a.align_corners != 0;
+
+// Shared-memory state of a staged CTA: theta, the base coordinates of the
+// tile's W and H positions, bx * theta[r][0] for its 16 D positions (packed
+// as the thread layout pairs them), and the staged box.
+struct StagedShared {
+  float theta[12];
+  float by[ST_TW], bz[ST_TH];
+  float2 px[3][8];
+  int lo[3], hi[3];
+  int box[6];  // lx4, ly, lz, 16-byte chunks per row (0: not staged), ey, ez
+};
+
+// The reference's torch.where keeps a masked-out element: copy the tile, one
+// 16-element D row per thread, 16-byte vectors where the row is whole and
+// aligned.
+__device__ __forceinline__ void staged_copy_masked(const ResampleArgs& a, int64_t b, int d0, int w0,
+                                                   int h0, int hwd, int t) {
+  static_assert(ST_TW * ST_TH == ST_THREADS, "one tile row per thread");
   const int H = a.H, W = a.W, D = a.D;
-  const int tiles_d = (D + ST_TD - 1) / ST_TD;
-  const int d0 = (blockIdx.x % tiles_d) * ST_TD;
-  const int w0 = (blockIdx.x / tiles_d) * ST_TW;
-  const int h0 = blockIdx.y * ST_TH;
-  const int64_t b = blockIdx.z;
-  const int hwd = H * W * D;
-  const int t = threadIdx.x;
-  const int tx = t & 7, ty = (t >> 3) & 1, tz = (t >> 4) & 1, wp = t >> 5;
-  const KeyArgs& k = a.keys[0];
-  const size_t esz = DT == BA_BF16 ? 2 : 4;
-  const bool active = (a.mask == nullptr) || (a.mask[b] != 0);
-  if (!active) {
-    // the reference's torch.where keeps a masked-out element: copy the
-    // tile, one 16-element D row per thread, 16-byte vectors where the row
-    // is whole and aligned
-    static_assert(ST_TW * ST_TH == ST_THREADS, "one tile row per thread");
-    const int w = w0 + t % ST_TW, h = h0 + t / ST_TW;
-    if (w >= W || h >= H) return;
-    const int n = min(ST_TD, D - d0);
-    for (int ki = 0; ki < a.n_keys; ++ki) {
-      const KeyArgs& kc = a.keys[ki];
-      const int ke = kc.dtype == BA_BF16 ? 2 : 4;
-      for (int c = 0; c < kc.channels; ++c) {
-        const int64_t i0 = (b * kc.channels + c) * (int64_t)hwd + ((int64_t)h * W + w) * D + d0;
-        const char* sp = (const char*)kc.src + i0 * ke;
-        char* dp = (char*)kc.dst + i0 * ke;
-        if (n == ST_TD && ((uintptr_t)sp % 16) == 0 && ((uintptr_t)dp % 16) == 0) {
-          uint4 v[4];
-          const int nv = ST_TD * ke / 16;  // 4 (fp32) or 2 (bf16)
+  const int w = w0 + t % ST_TW, h = h0 + t / ST_TW;
+  if (w >= W || h >= H) return;
+  const int n = min(ST_TD, D - d0);
+  for (int ki = 0; ki < a.n_keys; ++ki) {
+    const KeyArgs& kc = a.keys[ki];
+    const int ke = kc.dtype == BA_BF16 ? 2 : 4;
+    for (int c = 0; c < kc.channels; ++c) {
+      const int64_t i0 = (b * kc.channels + c) * (int64_t)hwd + ((int64_t)h * W + w) * D + d0;
+      const char* sp = (const char*)kc.src + i0 * ke;
+      char* dp = (char*)kc.dst + i0 * ke;
+      if (n == ST_TD && ((uintptr_t)sp % 16) == 0 && ((uintptr_t)dp % 16) == 0) {
+        uint4 v[4];
+        const int nv = ST_TD * ke / 16;  // 4 (fp32) or 2 (bf16)
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            if (q < nv) v[q] = __ldg(reinterpret_cast<const uint4*>(sp) + q);
+        for (int q = 0; q < 4; ++q)
+          if (q < nv) v[q] = __ldg(reinterpret_cast<const uint4*>(sp) + q);
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            if (q < nv) reinterpret_cast<uint4*>(dp)[q] = v[q];
-        } else {
-          for (int q = 0; q < n; ++q) {
-            if (ke == 2)
-              ((uint16_t*)dp)[q] = __ldg((const uint16_t*)sp + q);
-            else
-              ((float*)dp)[q] = __ldg((const float*)sp + q);
-          }
+        for (int q = 0; q < 4; ++q)
+          if (q < nv) reinterpret_cast<uint4*>(dp)[q] = v[q];
+      } else {
+        for (int q = 0; q < n; ++q) {
+          if (ke == 2)
+            ((uint16_t*)dp)[q] = __ldg((const uint16_t*)sp + q);
+          else
+            ((float*)dp)[q] = __ldg((const float*)sp + q);
         }
       }
     }
-    return;
   }
+}
+
+// Prologue of a staged CTA: theta, base coordinates, and the source box the
+// tile's taps fall in.  The box is the corners' bounding box of the padded
+// coordinates (every voxel's coordinate is within rounding, < 1e-3 voxel, of
+// the affine image of its index, whose extremes are at the corners; the
+// padding is monotone) with 0.01-voxel slack and one more voxel for the
+// upper taps.  FAST pads as the fast kernel does (fast_pad: every tap of
+// every voxel inside the box); otherwise as torch pads (voxels beyond
+// [-1, size] fall outside the clipped box and gather from global memory).
+template <int PAD>
+__device__ __forceinline__ float fast_pad(float c, float size);
+
+template <int PAD, bool FAST>
+__device__ __forceinline__ void staged_setup(const ResampleArgs& a, int64_t b, int d0, int w0,
+                                             int h0, bool ALIGN, int t, StagedShared& sh) {
+  const int H = a.H, W = a.W, D = a.D;
   if (t < 12) {
     const int i = t / 4, j = t % 4;
-    const float* x = a.xform + b * a.xform_stride;
+    const float* x = elem_xform(a, b);
     if (a.xform_kind == BA_XFORM_AFFINE) {
+      // monai_affine_to_theta: theta = P S_norm A S_inv P, P swapping 0 and 2.
       const int pi = 2 - i, pj = (j == 3) ? 3 : 2 - j;
       const float s_j = (pj == 3) ? 1.0f : a.si[pj];
-      s_theta[t] = (a.sn[pi] * x[pi * 4 + pj]) * s_j;
+      sh.theta[t] = (a.sn[pi] * x[pi * 4 + pj]) * s_j;
     } else {
-      s_theta[t] = x[i * 4 + j];
+      sh.theta[t] = x[i * 4 + j];
     }
   } else if (t >= 32 && t < 32 + ST_TW) {
-    s_by[t - 32] = base_coord(w0 + t - 32, W, ALIGN);
+    sh.by[t - 32] = base_coord(w0 + t - 32, W, ALIGN);
   } else if (t >= 64 && t < 64 + ST_TH) {
-    s_bz[t - 64] = base_coord(h0 + t - 64, H, ALIGN);
+    sh.bz[t - 64] = base_coord(h0 + t - 64, H, ALIGN);
   } else if (t >= 96 && t < 99) {
-    s_lo[t - 96] = 0x7fffffff;
-    s_hi[t - 96] = -0x7fffffff;
+    sh.lo[t - 96] = 0x7fffffff;
+    sh.hi[t - 96] = -0x7fffffff;
   }
   __syncthreads();
   if (t < 16) {
@@ -599,7 +651,7 @@ __global__ void __launch_bounds__(ST_THREADS, BA_ST_MINBLOCKS)
     const float bx = d < D ? base_coord(d, D, ALIGN) : 0.0f;
     const int j = t & 7, q = t >> 3;
 #pragma unroll
-    for (int r = 0; r < 3; ++r) reinterpret_cast<float*>(&s_px[r][j])[q] = bx * s_theta[r * 4];
+    for (int r = 0; r < 3; ++r) reinterpret_cast<float*>(&sh.px[r][j])[q] = bx * sh.theta[r * 4];
   } else if (t >= 32 && t < 40) {
     // bounding box of the tile's corners in source voxels
     const int c = t - 32;
@@ -613,15 +665,14 @@ __global__ void __launch_bounds__(ST_THREADS, BA_ST_MINBLOCKS)
 #pragma unroll
     for (int r = 0; r < 3; ++r) {
       const float g = __fadd_rn(
-          __fmaf_rn(bz, s_theta[r * 4 + 2], __fmaf_rn(by, s_theta[r * 4 + 1], bx * s_theta[r * 4])),
-          s_theta[r * 4 + 3]);
+          __fmaf_rn(bz, sh.theta[r * 4 + 2], __fmaf_rn(by, sh.theta[r * 4 + 1], bx * sh.theta[r * 4])),
+          sh.theta[r * 4 + 3]);
       const float u = ALIGN ? __fmul_rn(__fmul_rn(__fadd_rn(g, 1.0f), 0.5f), sz[r] - 1.0f)
                             : __fmul_rn(__fsub_rn(__fmul_rn(__fadd_rn(g, 1.0f), sz[r]), 1.0f), 0.5f);
-      // every voxel's coordinate is within rounding (< 1e-3 voxel) of the
-      // affine image of its index, whose extremes are at the corners
-      const float p = fminf(fmaxf(pad_coord<PAD, false>(u, isz[r]), -1.0e6f), 1.0e6f);
-      atomicMin(&s_lo[r], (int)floorf(p - 0.01f));
-      atomicMax(&s_hi[r], (int)floorf(p + 0.01f));
+      const float p = FAST ? fast_pad<PAD>(u, sz[r])
+                           : fminf(fmaxf(pad_coord<PAD, false>(u, isz[r]), -1.0e6f), 1.0e6f);
+      atomicMin(&sh.lo[r], (int)floorf(p - 0.01f));
+      atomicMax(&sh.hi[r], (int)floorf(p + 0.01f));
     }
   }
   __syncthreads();
@@ -629,84 +680,118 @@ __global__ void __launch_bounds__(ST_THREADS, BA_ST_MINBLOCKS)
     const int isz[3] = {D, W, H};
     int lo[3], hi[3];
     for (int r = 0; r < 3; ++r) {
-      lo[r] = max(s_lo[r], -1);
-      hi[r] = min(s_hi[r] + 1, isz[r]);  // + 1: the upper taps
+      // FAST: the padded coordinates already lie in [-1, size]
+      lo[r] = FAST ? sh.lo[r] : max(sh.lo[r], -1);
+      hi[r] = FAST ? sh.hi[r] + 1 : min(sh.hi[r] + 1, isz[r]);  // + 1: the upper taps
     }
     const int lx4 = (lo[0] >= 0) ? (lo[0] & ~3) : -4;
     const int ex = ((hi[0] - lx4 + 1) + 3) & ~3;
     const int ey = hi[1] - lo[1] + 1, ez = hi[2] - lo[2] + 1;
     const bool ok = PAD != BA_PAD_REFLECTION && ex >= 4 && ey >= 2 && ez >= 2 &&
-                    ex / 4 <= ST_THREADS && (int64_t)ex * ey * ez <= ST_MAX_FLOATS;
-    s_box[0] = lx4;
-    s_box[1] = lo[1];
-    s_box[2] = lo[2];
-    s_box[3] = ok ? ex / 4 : 0;
-    s_box[4] = ey;
-    s_box[5] = ez;
+                    ex / 4 <= ST_THREADS &&
+                    (int64_t)ex * ey * ez <= (FAST ? FS_MAX_SETUP_FLOATS : ST_MAX_FLOATS);
+    sh.box[0] = lx4;
+    sh.box[1] = lo[1];
+    sh.box[2] = lo[2];
+    sh.box[3] = ok ? ex / 4 : 0;
+    sh.box[4] = ey;
+    sh.box[5] = ez;
   }
   __syncthreads();
-  const int lx4 = s_box[0], ly = s_box[1], lz = s_box[2], nx4 = s_box[3], ey = s_box[4],
-            ez = s_box[5];
+}
+
+// Copy channel c's staged box into shared memory: 16-byte chunks, cp.async
+// for fp32 (chunks outside the volume are zero-filled: source size 0),
+// synchronous widening loads for bf16.  Ends with the block synchronised.
+template <int DT>
+__device__ __forceinline__ void stage_box(float4* s_dyn4, const char* src_c, int lx4, int ly,
+                                          int lz, int nx4, int ey, int ez, int H, int W, int D,
+                                          int t) {
+  const int rows = ey * ez;
+  const int rpp = ST_THREADS / nx4;  // rows per pass (nx4 <= ST_THREADS)
+  const int lc = t % nx4;
+  int row = t / nx4;
+  int y = row % ey, z = row / ey;
+  if (row < rpp) {
+    for (; row < rows; row += rpp) {
+      const int gy = ly + y, gz = lz + z, gx = lx4 + 4 * lc;
+      const bool in = (unsigned)gy < (unsigned)W && (unsigned)gz < (unsigned)H && gx >= 0 && gx < D;
+      const int64_t gi = in ? ((int64_t)gz * W + gy) * D + gx : 0;
+      const unsigned sdst = (unsigned)__cvta_generic_to_shared(&s_dyn4[row * nx4 + lc]);
+      if (DT == BA_F32) {
+        const void* gsrc = (const float*)src_c + gi;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sdst), "l"(gsrc),
+                     "r"(in ? 16 : 0) : "memory");
+      } else {
+        s_dyn4[row * nx4 + lc] = in ? ld4<DT>(src_c, gi) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      y += rpp;
+      while (y >= ey) {
+        y -= ey;
+        ++z;
+      }
+    }
+  }
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+  __syncthreads();
+}
+
+template <int S0, int S1>
+__global__ void __launch_bounds__(ST_THREADS, BA_ST_MINBLOCKS)
+    resample3d_staged_kernel(const __grid_constant__ ResampleArgs a) {
+  extern __shared__ float4 s_dyn4[];
+  float* s_src = reinterpret_cast<float*>(s_dyn4);
+  __shared__ StagedShared sh;
+  constexpr int MODE = spec_mode(S0), PAD = spec_pad(S0), DT = spec_dt(S0);
+  const bool ALIGN = a.align_corners != 0;
+  const int H = a.H, W = a.W, D = a.D;
+  const int tiles_d = (D + ST_TD - 1) / ST_TD;
+  const int d0 = (blockIdx.x % tiles_d) * ST_TD;
+  const int w0 = (blockIdx.x / tiles_d) * ST_TW;
+  const int h0 = blockIdx.y * ST_TH;
+  const int64_t b = a.b0 + blockIdx.z;
+  const int hwd = H * W * D;
+  const int t = threadIdx.x;
+  const int tx = t & 7, ty = (t >> 3) & 1, tz = (t >> 4) & 1, wp = t >> 5;
+  const KeyArgs& k = a.keys[0];
+  const size_t esz = DT == BA_BF16 ? 2 : 4;
+  if (!elem_active(a, b)) {
+    staged_copy_masked(a, b, d0, w0, h0, hwd, t);
+    return;
+  }
+  staged_setup<PAD, false>(a, b, d0, w0, h0, ALIGN, t, sh);
+  const int lx4 = sh.box[0], ly = sh.box[1], lz = sh.box[2], nx4 = sh.box[3], ey = sh.box[4],
+            ez = sh.box[5];
   const int ex = nx4 * 4;
   const bool staged = nx4 > 0;
   float2 t1[3], t2[3], t3[3];
 #pragma unroll
   for (int r = 0; r < 3; ++r) {
-    t1[r] = f2(s_theta[r * 4 + 1]);
-    t2[r] = f2(s_theta[r * 4 + 2]);
-    t3[r] = f2(s_theta[r * 4 + 3]);
+    t1[r] = f2(sh.theta[r * 4 + 1]);
+    t2[r] = f2(sh.theta[r * 4 + 2]);
+    t3[r] = f2(sh.theta[r * 4 + 3]);
   }
   const float fD = (float)D, fW = (float)W, fH = (float)H;
   const bool pD = (D & (D - 1)) == 0, pW = (W & (W - 1)) == 0, pH = (H & (H - 1)) == 0;
   for (int c = 0; c < k.channels; ++c) {
     const char* src_c = (const char*)k.src + ((size_t)b * k.channels + c) * hwd * esz;
     char* dst_c = (char*)k.dst + ((size_t)b * k.channels + c) * hwd * esz;
-    if (staged) {
-      // cp.async 16-byte chunks; chunks outside the volume are zero-filled
-      // (source size 0)
-      const int rows = ey * ez;
-      const int rpp = ST_THREADS / nx4;  // rows per pass (nx4 <= ST_THREADS)
-      const int lc = t % nx4;
-      int row = t / nx4;
-      int y = row % ey, z = row / ey;
-      if (row < rpp) {
-        for (; row < rows; row += rpp) {
-          const int gy = ly + y, gz = lz + z, gx = lx4 + 4 * lc;
-          const bool in = (unsigned)gy < (unsigned)W && (unsigned)gz < (unsigned)H && gx >= 0 && gx < D;
-          const int64_t gi = in ? ((int64_t)gz * W + gy) * D + gx : 0;
-          const unsigned sdst = (unsigned)__cvta_generic_to_shared(&s_dyn4[row * nx4 + lc]);
-          if (DT == BA_F32) {
-            const void* gsrc = (const float*)src_c + gi;
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sdst), "l"(gsrc),
-                         "r"(in ? 16 : 0) : "memory");
-          } else {
-            s_dyn4[row * nx4 + lc] = in ? ld4<DT>(src_c, gi) : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
-          y += rpp;
-          while (y >= ey) {
-            y -= ey;
-            ++z;
-          }
-        }
-      }
-      asm volatile("cp.async.commit_group;\n" ::: "memory");
-      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-      __syncthreads();
-    }
+    if (staged) stage_box<DT>(s_dyn4, src_c, lx4, ly, lz, nx4, ey, ez, H, W, D, t);
     for (int pp = 0; pp < ST_PW * ST_PH; ++pp) {
       const int pw = pp % ST_PW, ph = pp / ST_PW;
       const int h = h0 + tz + 2 * wp + 8 * ph;
-      const float2 bz2 = f2(s_bz[tz + 2 * wp + 8 * ph]);
+      const float2 bz2 = f2(sh.bz[tz + 2 * wp + 8 * ph]);
       const int w = w0 + ty + 2 * pw;
       if (w >= W || h >= H) continue;
       const int da = d0 + tx, db = da + 8;
       if (da >= D) continue;
       const bool has_b = db < D;
-      const float2 by2 = f2(s_by[ty + 2 * pw]);
+      const float2 by2 = f2(sh.by[ty + 2 * pw]);
       float2 g[3];
 #pragma unroll
       for (int r = 0; r < 3; ++r)
-        g[r] = add2(__ffma2_rn(bz2, t2[r], __ffma2_rn(by2, t1[r], s_px[r][tx])), t3[r]);
+        g[r] = add2(__ffma2_rn(bz2, t2[r], __ffma2_rn(by2, t1[r], sh.px[r][tx])), t3[r]);
       float2 ix, iy, iz;
       if (ALIGN) {
         ix = unnormalize2<true>(g[0], fD);
@@ -790,14 +875,251 @@ __global__ void __launch_bounds__(ST_THREADS, BA_ST_MINBLOCKS)
 }
 
 
+// ===========================================================================
+// Fast affine resample: the default for a bilinear key (zeros or border
+// padding) of an affine map; BA_RESAMPLE_EXACT selects the kernels above.
+// Tiles, thread layout, exact source coordinates and staging are
+// resample3d_staged_kernel's; it differs in three ways:
+//  * each coordinate is first clamped to the range its taps can need
+//    (fast_pad): [-1, size] for zeros padding, where every tap outside the
+//    volume reads the zero fill, and torch's [0, size - 1] clip for border.
+//    The box staged from the clamped corners then holds every tap of the
+//    tile, so there is no per-voxel containment test; the shared-memory
+//    index is clamped to the box only to keep every access in bounds;
+//  * trilinear interpolation is seven fused lerps a + t * (b - a) on voxel
+//    pairs (fp32x2), against torch's eight rounded weight products and
+//    sums: within 1e-5 (fp32) / 2 bf16 ulp of them.  Source coordinates are
+//    the exact ones, so a nearest key sampled alongside stays bit-exact;
+//  * a CTA whose box exceeds ST_MAX_FLOATS gathers its taps from global
+//    memory (bounds-checked, zero outside the volume).
+// ===========================================================================
+template <int PAD>
+__device__ __forceinline__ float fast_pad(float c, float size) {
+  if (PAD == BA_PAD_BORDER) return clip_coord(c, size - 1.0f);
+  return fminf(fmaxf(c, -1.0f), size);  // fmaxf(NaN, -1) = -1: a zero tap, as torch
+}
+
+__device__ __forceinline__ float2 lerp2(float2 a, float2 b, float2 t) {
+  return __ffma2_rn(t, sub2(b, a), a);
+}
+
+// trilinear of the taps of two voxels (taps8 order) at fractions (fx, fy, fz)
+__device__ __forceinline__ float2 trilerp2(const float* va, const float* vb, float2 fx, float2 fy,
+                                           float2 fz) {
+  const float2 c00 = lerp2(f2(va[0], vb[0]), f2(va[1], vb[1]), fx);
+  const float2 c10 = lerp2(f2(va[2], vb[2]), f2(va[3], vb[3]), fx);
+  const float2 c01 = lerp2(f2(va[4], vb[4]), f2(va[5], vb[5]), fx);
+  const float2 c11 = lerp2(f2(va[6], vb[6]), f2(va[7], vb[7]), fx);
+  return lerp2(lerp2(c00, c10, fy), lerp2(c01, c11, fy), fz);
+}
+
+constexpr int FS_MAX_FLOATS = BA_FS_MAX_FLOATS;
+
+// Copy the boxes of channels src_c, src_c + cstride, ... (nch of them) into
+// shared memory, channel i at float offset i * box, rows of exp and planes of
+// plp floats: 16-byte chunks, cp.async for fp32 (chunks outside the volume
+// zero-filled: source size 0), synchronous widening loads for bf16.  Ends
+// with the block synchronised.
+template <int DT>
+__device__ __forceinline__ void stage_box_pitched(float4* s_dyn4, const char* src_c,
+                                                  size_t cstride, int nch, int box, int lx4,
+                                                  int ly, int lz, int nx4, int ey, int ez, int exp,
+                                                  int plp, int H, int W, int D, int t) {
+  for (int ci = 0; ci < nch; ++ci, src_c += cstride, s_dyn4 += box / 4) {
+  const int rows = ey * ez;
+  const int rpp = ST_THREADS / nx4;  // rows per pass (nx4 <= ST_THREADS)
+  const int lc = t % nx4;
+  int row = t / nx4;
+  int y = row % ey, z = row / ey;
+  if (row < rpp) {
+    for (; row < rows; row += rpp) {
+      const int gy = ly + y, gz = lz + z, gx = lx4 + 4 * lc;
+      const bool in = (unsigned)gy < (unsigned)W && (unsigned)gz < (unsigned)H && gx >= 0 && gx < D;
+      const int64_t gi = in ? ((int64_t)gz * W + gy) * D + gx : 0;
+      float4* sd = &s_dyn4[(z * plp + y * exp) / 4 + lc];
+      if (DT == BA_F32) {
+        const unsigned sdst = (unsigned)__cvta_generic_to_shared(sd);
+        const void* gsrc = (const float*)src_c + gi;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sdst), "l"(gsrc),
+                     "r"(in ? 16 : 0) : "memory");
+      } else {
+        *sd = in ? ld4<DT>(src_c, gi) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      y += rpp;
+      while (y >= ey) {
+        y -= ey;
+        ++z;
+      }
+    }
+  }
+  }
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+  __syncthreads();
+}
+
+#ifndef BA_FS_MINBLOCKS
+#define BA_FS_MINBLOCKS 4
+#endif
+
+template <int S0, int S1>
+__global__ void __launch_bounds__(ST_THREADS, BA_FS_MINBLOCKS)
+    resample3d_fast_kernel(const __grid_constant__ ResampleArgs a) {
+  extern __shared__ float4 s_dyn4[];
+  const float* s_src = reinterpret_cast<const float*>(s_dyn4);
+  __shared__ StagedShared sh;
+  constexpr int PAD = spec_pad(S0), DT = spec_dt(S0);
+  static_assert(spec_mode(S0) == BA_BILINEAR && PAD != BA_PAD_REFLECTION,
+                "the fast kernel samples a bilinear key with zeros or border padding");
+  const bool ALIGN = a.align_corners != 0;
+  const int H = a.H, W = a.W, D = a.D;
+  const int tiles_d = (D + ST_TD - 1) / ST_TD;
+  const int d0 = (blockIdx.x % tiles_d) * ST_TD;
+  const int w0 = (blockIdx.x / tiles_d) * ST_TW;
+  const int h0 = blockIdx.y * ST_TH;
+  const int64_t b = a.b0 + blockIdx.z;
+  const int hwd = H * W * D;
+  const int t = threadIdx.x;
+  const int tx = t & 7, ty = (t >> 3) & 1, tz = (t >> 4) & 1, wp = t >> 5;
+  const KeyArgs& k = a.keys[0];
+  const size_t esz = DT == BA_BF16 ? 2 : 4;
+  if (!elem_active(a, b)) {
+    staged_copy_masked(a, b, d0, w0, h0, hwd, t);
+    return;
+  }
+  staged_setup<PAD, true>(a, b, d0, w0, h0, ALIGN, t, sh);
+  const int lx4 = sh.box[0], ly = sh.box[1], lz = sh.box[2], ey = sh.box[4], ez = sh.box[5];
+  const int nx4 = sh.box[3];
+  const int exp = nx4 * 4, plp = ey * exp, box = ez * plp;
+  const bool staged = nx4 > 0 && box <= FS_MAX_FLOATS;
+  // channels staged together: all of them when their boxes fit side by
+  // side, so each voxel's coordinates serve every channel
+  const int cstack = staged && (int64_t)box * k.channels <= FS_MAX_FLOATS ? k.channels : 1;
+  // a voxel's first tap, relative to the box: (z0 - lz) * plp + (y0 - ly) * exp
+  // + x0 - lx4; clamped to [0, smax] so that even a wrong index stays inside
+  const int s_off = -(lz * plp + ly * exp + lx4);
+  const int smax = staged ? ez * plp - plp - exp - 2 : 0;
+  float2 t1[3], t2[3], t3[3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    t1[r] = f2(sh.theta[r * 4 + 1]);
+    t2[r] = f2(sh.theta[r * 4 + 2]);
+    t3[r] = f2(sh.theta[r * 4 + 3]);
+  }
+  const float fD = (float)D, fW = (float)W, fH = (float)H;
+  const bool pD = (D & (D - 1)) == 0, pW = (W & (W - 1)) == 0, pH = (H & (H - 1)) == 0;
+  const size_t cstride = (size_t)hwd * esz;
+  for (int c0 = 0; c0 < k.channels; c0 += cstack) {
+    const int nch = min(cstack, k.channels - c0);
+    const char* src_c = (const char*)k.src + ((size_t)b * k.channels + c0) * cstride;
+    char* dst_c = (char*)k.dst + ((size_t)b * k.channels + c0) * cstride;
+    if (staged)
+      stage_box_pitched<DT>(s_dyn4, src_c, cstride, nch, box, lx4, ly, lz, nx4, ey, ez, exp, plp,
+                            H, W, D, t);
+    for (int pw = 0; pw < ST_PW; ++pw) {
+      const int h = h0 + tz + 2 * wp;
+      const int w = w0 + ty + 2 * pw;
+      const int da = d0 + tx, db = da + 8;
+      // every lane runs the iteration (the one-tap vote below is warp-wide);
+      // a lane outside the volume computes but neither loads nor stores
+      const bool valid = w < W && h < H && da < D;
+      const bool has_b = db < D;
+      const float2 bz2 = f2(sh.bz[tz + 2 * wp]);
+      const float2 by2 = f2(sh.by[ty + 2 * pw]);
+      float2 g[3];
+#pragma unroll
+      for (int r = 0; r < 3; ++r)
+        g[r] = add2(__ffma2_rn(bz2, t2[r], __ffma2_rn(by2, t1[r], sh.px[r][tx])), t3[r]);
+      float2 ix, iy, iz;
+      if (ALIGN) {
+        ix = unnormalize2<true>(g[0], fD);
+        iy = unnormalize2<true>(g[1], fW);
+        iz = unnormalize2<true>(g[2], fH);
+      } else {
+        ix = pD ? unnormalize2_pow2(g[0], fD) : unnormalize2<false>(g[0], fD);
+        iy = pW ? unnormalize2_pow2(g[1], fW) : unnormalize2<false>(g[1], fW);
+        iz = pH ? unnormalize2_pow2(g[2], fH) : unnormalize2<false>(g[2], fH);
+      }
+      const int row = (h * W + w) * D;
+      if (S1 >= 0 && c0 == 0 && valid) {
+        if (ALIGN)
+          sample_spec<(S1 < 0 ? 0 : S1), true>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da,
+                                               row + db, has_b);
+        else
+          sample_spec<(S1 < 0 ? 0 : S1), false>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da,
+                                                row + db, has_b);
+      }
+      const float2 px = f2(fast_pad<PAD>(ix.x, fD), fast_pad<PAD>(ix.y, fD));
+      const float2 py = f2(fast_pad<PAD>(iy.x, fW), fast_pad<PAD>(iy.y, fW));
+      const float2 pz = f2(fast_pad<PAD>(iz.x, fH), fast_pad<PAD>(iz.y, fH));
+      const Floor2 fx = floor2(px), fy = floor2(py), fz = floor2(pz);
+      const float2 wx = sub2(px, fx.f), wy = sub2(py, fy.f), wz = sub2(pz, fz.f);
+      // voxel b of a pair past the volume's end reuses voxel a's corner
+      const int xb = has_b ? fx.hi : fx.lo, yb = has_b ? fy.hi : fy.lo, zb = has_b ? fz.hi : fz.lo;
+      if (staged) {
+        const int sa = min(max(fz.lo * plp + fy.lo * exp + fx.lo + s_off, 0), smax);
+        const int sb = min(max(zb * plp + yb * exp + xb + s_off, 0), smax);
+        // every voxel of the warp on a source voxel centre (all fractions
+        // zero: a flip or rot90 for ~88 % of warp iterations): the
+        // interpolation is its one tap
+        const bool centre = !valid || ((wx.x == 0.0f && wy.x == 0.0f && wz.x == 0.0f) &&
+                                       (!has_b || (wx.y == 0.0f && wy.y == 0.0f && wz.y == 0.0f)));
+        const bool one_tap = __all_sync(0xFFFFFFFFu, centre);
+        for (int ci = 0; valid && ci < nch; ++ci) {
+          const float* sc = s_src + ci * box;
+          char* dst = dst_c + ci * cstride;
+          float2 r;
+          if (one_tap) {
+            r = f2(sc[sa], sc[sb]);
+          } else {
+            float va[8], vb[8];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const int si = q ? sb : sa;
+              float* v = q ? vb : va;
+              v[0] = sc[si];
+              v[1] = sc[si + 1];
+              v[2] = sc[si + exp];
+              v[3] = sc[si + exp + 1];
+              v[4] = sc[si + plp];
+              v[5] = sc[si + plp + 1];
+              v[6] = sc[si + plp + exp];
+              v[7] = sc[si + plp + exp + 1];
+            }
+            r = trilerp2(va, vb, wx, wy, wz);
+          }
+          st<DT>(dst, row + da, r.x);
+          if (has_b) st<DT>(dst, row + db, r.y);
+        }
+      } else if (valid) {
+        const bool ia = (unsigned)fx.lo < (unsigned)(D - 1) && (unsigned)fy.lo < (unsigned)(W - 1) &&
+                        (unsigned)fz.lo < (unsigned)(H - 1);
+        const bool ib = (unsigned)xb < (unsigned)(D - 1) && (unsigned)yb < (unsigned)(W - 1) &&
+                        (unsigned)zb < (unsigned)(H - 1);
+        float va[8], vb[8];
+        taps8<DT>(src_c, fx.lo, fy.lo, fz.lo, H, W, D, ia, va);
+        taps8<DT>(src_c, xb, yb, zb, H, W, D, ib, vb);
+        const float2 r = trilerp2(va, vb, wx, wy, wz);
+        st<DT>(dst_c, row + da, r.x);
+        if (has_b) st<DT>(dst_c, row + db, r.y);
+      }
+    }
+    if (staged) __syncthreads();
+  }
+}
+
 // Opt the staged kernel in to its dynamic shared memory once per process
 // (needed above 48 KB; idempotent, so concurrent first calls are harmless).
-template <int S0, int S1>
+template <int S0, int S1, bool FAST>
 void allow_staged_smem(int bytes) {
   static bool done = false;
   if (!done) {
-    cudaFuncSetAttribute(resample3d_staged_kernel<S0, S1>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (FAST)
+      cudaFuncSetAttribute(resample3d_fast_kernel<S0, S1>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    else
+      cudaFuncSetAttribute(resample3d_staged_kernel<S0, S1>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     done = true;
   }
 }
@@ -1056,7 +1378,7 @@ __global__ void __launch_bounds__(G4_THREADS, 8) resample3d_grid4_kernel(const _
   const int lane = threadIdx.x & 31;
   const int f0 = (int)blockIdx.x * (G4_THREADS * G4_VOX) + (int)(threadIdx.x >> 5) * 32 * G4_VOX + lane;
   if (f0 >= hwd) return;
-  const int64_t b = blockIdx.y;
+  const int64_t b = a.b0 + blockIdx.y;
   int fv[G4_VOX];
   bool ok[G4_VOX];
 #pragma unroll
@@ -1064,7 +1386,7 @@ __global__ void __launch_bounds__(G4_THREADS, 8) resample3d_grid4_kernel(const _
     ok[v] = f0 + 32 * v < hwd;
     fv[v] = ok[v] ? f0 + 32 * v : f0;  // a voxel past the end recomputes f0, unstored
   }
-  if (a.mask != nullptr && a.mask[b] == 0) {
+  if (!elem_active(a, b)) {
     // the reference's torch.where keeps a masked-out element
     for (int ki = 0; ki < a.n_keys; ++ki) {
       const KeyArgs& k = a.keys[ki];
@@ -1119,83 +1441,19 @@ __global__ void __launch_bounds__(G4_THREADS, 8) resample3d_grid4_kernel(const _
 }  // namespace
 }  // namespace ba
 
-extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t stream) {
-  using namespace ba;
-  clear_error();
-  BA_REQUIRE(desc != nullptr, "ba_resample3d: desc is NULL");
-  const ba_resample_desc& d = *desc;
-  BA_REQUIRE(d.batch >= 0 && d.H > 0 && d.W > 0 && d.D > 0,
-             "ba_resample3d: bad shape B=%lld H=%lld W=%lld D=%lld", (long long)d.batch,
-             (long long)d.H, (long long)d.W, (long long)d.D);
-  BA_REQUIRE(d.H * d.W * d.D < (int64_t)INT32_MAX / 2,
-             "ba_resample3d: spatial size H*W*D=%lld exceeds the 2^30 limit",
-             (long long)(d.H * d.W * d.D));
-  BA_REQUIRE(d.batch <= 65535, "ba_resample3d: batch %lld exceeds 65535", (long long)d.batch);
-  BA_REQUIRE(d.n_keys >= 1 && d.n_keys <= BA_MAX_KEYS, "ba_resample3d: n_keys=%d not in 1..%d",
-             d.n_keys, BA_MAX_KEYS);
-  BA_REQUIRE(d.xform_kind >= BA_XFORM_AFFINE && d.xform_kind <= BA_XFORM_GRID,
-             "ba_resample3d: unknown xform_kind %d", d.xform_kind);
-  BA_REQUIRE(d.xform != nullptr || d.batch == 0, "ba_resample3d: xform is NULL");
-  if (d.xform_kind != BA_XFORM_GRID)
-    BA_REQUIRE(d.xform_stride >= 12, "ba_resample3d: xform_stride %lld < 12",
-               (long long)d.xform_stride);
-  if (d.xform_kind == BA_XFORM_AFFINE)
-    BA_REQUIRE(d.xform_stride >= 16, "ba_resample3d: AFFINE xform_stride %lld < 16",
-               (long long)d.xform_stride);
-
-  ResampleArgs a;
-  memset(&a, 0, sizeof(a));
-  a.batch = d.batch;
-  a.H = (int32_t)d.H;
-  a.W = (int32_t)d.W;
-  a.D = (int32_t)d.D;
-  a.xform_kind = d.xform_kind;
-  a.align_corners = d.align_corners ? 1 : 0;
-  a.n_keys = d.n_keys;
-  a.xform = d.xform;
-  a.xform_stride = d.xform_stride;
-  a.mask = d.mask;
-  a.sn[0] = (float)(2.0 / (double)d.H);
-  a.sn[1] = (float)(2.0 / (double)d.W);
-  a.sn[2] = (float)(2.0 / (double)d.D);
-  a.si[0] = (float)((double)d.H / 2.0);
-  a.si[1] = (float)((double)d.W / 2.0);
-  a.si[2] = (float)((double)d.D / 2.0);
-
+namespace ba {
+namespace {
+// Launches of one resample over elements a.b0 .. a.b0 + nb - 1: the kernel
+// each key group takes (staged / fast for affine maps with a bilinear key,
+// grid kernel for grid maps, global-gather kernel otherwise).
+ba_status launch_resample(const ba_resample_desc& d, ResampleArgs& a, int64_t nb,
+                          cudaStream_t st) {
   const int64_t hwd = d.H * d.W * d.D;
-  for (int i = 0; i < d.n_keys; ++i) {
-    const ba_resample_key& k = d.keys[i];
-    BA_REQUIRE(k.dtype == BA_F32 || k.dtype == BA_BF16, "ba_resample3d: key %d bad dtype %d", i,
-               k.dtype);
-    BA_REQUIRE(k.mode == BA_BILINEAR || k.mode == BA_NEAREST, "ba_resample3d: key %d bad mode %d",
-               i, k.mode);
-    BA_REQUIRE(k.padding >= BA_PAD_ZEROS && k.padding <= BA_PAD_REFLECTION,
-               "ba_resample3d: key %d bad padding %d", i, k.padding);
-    BA_REQUIRE(k.channels >= 0 && k.channels <= 65535, "ba_resample3d: key %d bad channels %lld",
-               i, (long long)k.channels);
-    const size_t esz = k.dtype == BA_BF16 ? 2 : 4;
-    const size_t bytes = (size_t)(d.batch * k.channels * hwd) * esz;
-    if (bytes == 0) continue;
-    BA_REQUIRE(k.src != nullptr && k.dst != nullptr, "ba_resample3d: key %d has a NULL pointer", i);
-    BA_REQUIRE(((uintptr_t)k.src % esz) == 0 && ((uintptr_t)k.dst % esz) == 0,
-               "ba_resample3d: key %d pointers not aligned to the element size", i);
-    BA_REQUIRE(!overlaps(k.src, bytes, k.dst, bytes),
-               "ba_resample3d: key %d dst overlaps src (the resample is out of place)", i);
-    a.keys[i].src = k.src;
-    a.keys[i].dst = k.dst;
-    a.keys[i].channels = (int32_t)k.channels;
-    a.keys[i].dtype = k.dtype;
-    a.keys[i].mode = k.mode;
-    a.keys[i].padding = k.padding;
-  }
-  if (d.batch == 0) return BA_OK;
-
   const int tiles_d = (int)((d.D + BD - 1) / BD);
   const int64_t gx = (int64_t)tiles_d * ((d.W + TY - 1) / TY);
   const int64_t gy = (d.H + TZ * NB - 1) / (TZ * NB);
   BA_REQUIRE(gx <= INT32_MAX && gy <= 65535, "ba_resample3d: spatial extent too large");
-  const dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)d.batch);
-  const cudaStream_t st = (cudaStream_t)stream;
+  const dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)nb);
   auto code = [](const KeyArgs& k) { return spec_code(k.mode, k.padding, k.dtype); };
   // The staged kernel serves a bilinear key (zeros or border padding) of an
   // affine map whose rows start on 16-byte (fp32) or 8-byte (bf16) boundaries.
@@ -1205,15 +1463,22 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
            a.xform_kind != BA_XFORM_GRID && (d.D % 4) == 0 && ((uintptr_t)k.src % align) == 0;
   };
   const int st_tiles = (int)(((d.D + ST_TD - 1) / ST_TD) * ((d.W + ST_TW - 1) / ST_TW));
-  const dim3 st_grid((unsigned)st_tiles, (unsigned)((d.H + ST_TH - 1) / ST_TH), (unsigned)d.batch);
+  const dim3 st_grid((unsigned)st_tiles, (unsigned)((d.H + ST_TH - 1) / ST_TH), (unsigned)nb);
   const int st_smem = ST_MAX_FLOATS * (int)sizeof(float);
+  const int fs_smem = FS_MAX_FLOATS * (int)sizeof(float);
   // returns false when (s0, s1) has no staged instantiation
+  const bool exact = (d.flags & BA_RESAMPLE_EXACT) != 0;
   auto launch_staged = [&](const ResampleArgs& args, int s0, int s1) -> bool {
     switch (s0 * 16 + (s1 + 1)) {
-#define BA_ST(S0, S1)                                                            \
-  case S0 * 16 + (S1 + 1):                                                       \
-    allow_staged_smem<S0, S1>(st_smem);                                          \
-    resample3d_staged_kernel<S0, S1><<<st_grid, ST_THREADS, st_smem, st>>>(args); \
+#define BA_ST(S0, S1)                                                                \
+  case S0 * 16 + (S1 + 1):                                                           \
+    if (exact) {                                                                     \
+      allow_staged_smem<S0, S1, false>(st_smem);                                     \
+      resample3d_staged_kernel<S0, S1><<<st_grid, ST_THREADS, st_smem, st>>>(args);  \
+    } else {                                                                         \
+      allow_staged_smem<S0, S1, true>(fs_smem);                                      \
+      resample3d_fast_kernel<S0, S1><<<st_grid, ST_THREADS, fs_smem, st>>>(args);    \
+    }                                                                                \
     return true;
 #define BA_ST_KEY(P, T0)                                                               \
   BA_ST(spec_code(BA_BILINEAR, P, T0), -1)                                             \
@@ -1232,7 +1497,7 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
   // Grid maps take the lane-per-voxel grid kernel.
   const bool grid4 = a.xform_kind == BA_XFORM_GRID;
   const dim3 g4_grid((unsigned)((hwd + G4_THREADS * G4_VOX - 1) / (G4_THREADS * G4_VOX)),
-                     (unsigned)d.batch);
+                     (unsigned)nb);
   // vol (bilinear) + seg (nearest) with one padding: one fused launch
   if (a.n_keys == 2) {
     KeyArgs k0 = a.keys[0], k1 = a.keys[1];
@@ -1295,6 +1560,103 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
     }
     const ba_status s1 = check_launch("ba_resample3d");
     if (s1 != BA_OK) return s1;
+  }
+  return BA_OK;
+}
+
+}  // namespace
+}  // namespace ba
+
+extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t stream) {
+  using namespace ba;
+  clear_error();
+  BA_REQUIRE(desc != nullptr, "ba_resample3d: desc is NULL");
+  const ba_resample_desc& d = *desc;
+  BA_REQUIRE(d.batch >= 0 && d.H > 0 && d.W > 0 && d.D > 0,
+             "ba_resample3d: bad shape B=%lld H=%lld W=%lld D=%lld", (long long)d.batch,
+             (long long)d.H, (long long)d.W, (long long)d.D);
+  BA_REQUIRE(d.H * d.W * d.D < (int64_t)INT32_MAX / 2,
+             "ba_resample3d: spatial size H*W*D=%lld exceeds the 2^30 limit",
+             (long long)(d.H * d.W * d.D));
+  BA_REQUIRE(d.batch <= 65535, "ba_resample3d: batch %lld exceeds 65535", (long long)d.batch);
+  BA_REQUIRE(d.n_keys >= 1 && d.n_keys <= BA_MAX_KEYS, "ba_resample3d: n_keys=%d not in 1..%d",
+             d.n_keys, BA_MAX_KEYS);
+  BA_REQUIRE(d.xform_kind >= BA_XFORM_AFFINE && d.xform_kind <= BA_XFORM_GRID,
+             "ba_resample3d: unknown xform_kind %d", d.xform_kind);
+  BA_REQUIRE((d.flags & ~(BA_RESAMPLE_EXACT | BA_RESAMPLE_HOST_PARAMS)) == 0,
+             "ba_resample3d: unknown flags 0x%x", d.flags);
+  BA_REQUIRE(d.xform != nullptr || d.batch == 0, "ba_resample3d: xform is NULL");
+  if (d.xform_kind != BA_XFORM_GRID)
+    BA_REQUIRE(d.xform_stride >= 12, "ba_resample3d: xform_stride %lld < 12",
+               (long long)d.xform_stride);
+  if (d.xform_kind == BA_XFORM_AFFINE)
+    BA_REQUIRE(d.xform_stride >= 16, "ba_resample3d: AFFINE xform_stride %lld < 16",
+               (long long)d.xform_stride);
+
+  ResampleArgs a;
+  memset(&a, 0, sizeof(a));
+  a.batch = d.batch;
+  a.H = (int32_t)d.H;
+  a.W = (int32_t)d.W;
+  a.D = (int32_t)d.D;
+  a.xform_kind = d.xform_kind;
+  a.align_corners = d.align_corners ? 1 : 0;
+  a.n_keys = d.n_keys;
+  a.xform = d.xform;
+  a.xform_stride = d.xform_stride;
+  a.mask = d.mask;
+  a.sn[0] = (float)(2.0 / (double)d.H);
+  a.sn[1] = (float)(2.0 / (double)d.W);
+  a.sn[2] = (float)(2.0 / (double)d.D);
+  a.si[0] = (float)((double)d.H / 2.0);
+  a.si[1] = (float)((double)d.W / 2.0);
+  a.si[2] = (float)((double)d.D / 2.0);
+
+  const int64_t hwd = d.H * d.W * d.D;
+  for (int i = 0; i < d.n_keys; ++i) {
+    const ba_resample_key& k = d.keys[i];
+    BA_REQUIRE(k.dtype == BA_F32 || k.dtype == BA_BF16, "ba_resample3d: key %d bad dtype %d", i,
+               k.dtype);
+    BA_REQUIRE(k.mode == BA_BILINEAR || k.mode == BA_NEAREST, "ba_resample3d: key %d bad mode %d",
+               i, k.mode);
+    BA_REQUIRE(k.padding >= BA_PAD_ZEROS && k.padding <= BA_PAD_REFLECTION,
+               "ba_resample3d: key %d bad padding %d", i, k.padding);
+    BA_REQUIRE(k.channels >= 0 && k.channels <= 65535, "ba_resample3d: key %d bad channels %lld",
+               i, (long long)k.channels);
+    const size_t esz = k.dtype == BA_BF16 ? 2 : 4;
+    const size_t bytes = (size_t)(d.batch * k.channels * hwd) * esz;
+    if (bytes == 0) continue;
+    BA_REQUIRE(k.src != nullptr && k.dst != nullptr, "ba_resample3d: key %d has a NULL pointer", i);
+    BA_REQUIRE(((uintptr_t)k.src % esz) == 0 && ((uintptr_t)k.dst % esz) == 0,
+               "ba_resample3d: key %d pointers not aligned to the element size", i);
+    BA_REQUIRE(!overlaps(k.src, bytes, k.dst, bytes),
+               "ba_resample3d: key %d dst overlaps src (the resample is out of place)", i);
+    a.keys[i].src = k.src;
+    a.keys[i].dst = k.dst;
+    a.keys[i].channels = (int32_t)k.channels;
+    a.keys[i].dtype = k.dtype;
+    a.keys[i].mode = k.mode;
+    a.keys[i].padding = k.padding;
+  }
+  if (d.batch == 0) return BA_OK;
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (!(d.flags & BA_RESAMPLE_HOST_PARAMS)) return launch_resample(d, a, d.batch, st);
+  // host parameters: each launch of up to RS_INLINE_B elements carries their
+  // transform and mask in its kernel parameters (read here, before return)
+  BA_REQUIRE(d.xform_kind == BA_XFORM_GRID || d.xform_stride <= 16,
+             "ba_resample3d: host xform_stride %lld > 16", (long long)d.xform_stride);
+  a.inline_params = 1;
+  for (int64_t b0 = 0; b0 < d.batch; b0 += RS_INLINE_B) {
+    const int64_t nb = std::min<int64_t>(RS_INLINE_B, d.batch - b0);
+    a.b0 = b0;
+    for (int64_t i = 0; i < nb; ++i) {
+      a.inl_mask[i] = d.mask == nullptr ? 1 : (d.mask[b0 + i] != 0);
+      if (d.xform_kind != BA_XFORM_GRID)
+        memcpy(a.inl_xform + i * d.xform_stride, d.xform + (b0 + i) * d.xform_stride,
+               (size_t)d.xform_stride * sizeof(float));
+    }
+    const ba_status s = launch_resample(d, a, nb, st);
+    if (s != BA_OK) return s;
   }
   return BA_OK;
 }

@@ -146,27 +146,33 @@ __global__ void __launch_bounds__(SM_THREADS) axis_pass_kernel(const __grid_cons
 }
 
 // Uniform draw of the elastic field, mapped to [-1, 1): u * 2 - 1.
+// One thread per Philox block: the four field values at positions 4q .. 4q+3
+// of an element (p = comp * HWD + s), all four outputs of the block used.
 __global__ void elastic_draw_kernel(const float* u, uint32_t seed_lo, uint32_t seed_hi,
-                                    uint64_t elem_offset, int64_t HWD, int64_t total,
+                                    uint64_t elem_offset, int64_t HWD, int64_t batch,
                                     float* out) {
+  const int64_t per = 3 * HWD;           // values per element
+  const int64_t blocks = (per + 3) / 4;  // Philox blocks per element
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= total) return;
-  float x;
+  if (i >= batch * blocks) return;
+  const int64_t b = i / blocks;
+  const int64_t q = i - b * blocks;
+  const int64_t p0 = 4 * q;
+  const int n = per - p0 < 4 ? (int)(per - p0) : 4;
+  float* o = out + b * per + p0;
   if (u != nullptr) {
-    x = u[i];
-  } else {
-    const int64_t per = 3 * HWD;
-    const int64_t b = i / per;
-    const int64_t p = i - b * per;  // comp * HWD + s
-    const uint64_t eb = elem_offset + (uint64_t)b;
-    const uint64_t q = (uint64_t)p >> 2;
-    const U4 ctr = {(uint32_t)q, (uint32_t)eb, (uint32_t)(eb >> 32),
-                    STREAM_ELASTIC | (uint32_t)(q >> 32)};
-    const U4 r = philox4x32_10(ctr, seed_lo, seed_hi);
-    const int l = (int)(p & 3);
-    x = u01(l == 0 ? r.x : (l == 1 ? r.y : (l == 2 ? r.z : r.w)));
+    const float* x = u + b * per + p0;
+    for (int l = 0; l < n; ++l) o[l] = x[l] * 2.0f - 1.0f;
+    return;
   }
-  out[i] = x * 2.0f - 1.0f;
+  const uint64_t eb = elem_offset + (uint64_t)b;
+  const U4 ctr = {(uint32_t)q, (uint32_t)eb, (uint32_t)(eb >> 32),
+                  STREAM_ELASTIC | (uint32_t)((uint64_t)q >> 32)};
+  const U4 r = philox4x32_10(ctr, seed_lo, seed_hi);
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int l = 0; l < 4; ++l)
+    if (l < n) o[l] = u01(w[l]) * 2.0f - 1.0f;
 }
 
 // Last (D-axis) pass of the elastic field, forming the grid:
@@ -1826,6 +1832,8 @@ extern "C" ba_status ba_elastic_grid(const float* u, uint64_t seed, uint64_t ele
   float* t0 = (float*)workspace;
   float* t1 = t0 + batch * 3 * HWD;
   const int64_t total = batch * 3 * HWD;
+  // elastic_draw_kernel threads: one per Philox block of four field values
+  const int64_t draw_threads = batch * ((3 * HWD + 3) / 4);
   ba_status s;
   if (roll_kmax((int)K) != 0 && H * D <= ((int64_t)1 << 31) && W * D <= ((int64_t)1 << 31)) {
     // D pass straight from the Philox draw (or the injected u); W; H into
@@ -1851,8 +1859,8 @@ extern "C" ba_status ba_elastic_grid(const float* u, uint64_t seed, uint64_t ele
       rd.seed_hi = (uint32_t)(seed >> 32);
       rd.elem_offset = elem_offset;
     } else {
-      elastic_draw_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
-          nullptr, (uint32_t)seed, (uint32_t)(seed >> 32), elem_offset, HWD, total, t1);
+      elastic_draw_kernel<<<(unsigned)((draw_threads + 255) / 256), 256, 0, st>>>(
+          nullptr, (uint32_t)seed, (uint32_t)(seed >> 32), elem_offset, HWD, batch, t1);
       s = check_launch("ba_elastic_grid");
       if (s != BA_OK) return s;
       src_kind = RL_SRC_DT;
@@ -1873,8 +1881,8 @@ extern "C" ba_status ba_elastic_grid(const float* u, uint64_t seed, uint64_t ele
     elastic_draw4_kernel<<<(unsigned)((total4 + 255) / 256), 256, 0, st>>>(
         (uint32_t)seed, (uint32_t)(seed >> 32), elem_offset, HWD, total4, (float4*)t0);
   } else {
-    elastic_draw_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
-        u, (uint32_t)seed, (uint32_t)(seed >> 32), elem_offset, HWD, total, t0);
+    elastic_draw_kernel<<<(unsigned)((draw_threads + 255) / 256), 256, 0, st>>>(
+        u, (uint32_t)seed, (uint32_t)(seed >> 32), elem_offset, HWD, batch, t0);
   }
   s = check_launch("ba_elastic_grid");
   if (s != BA_OK) return s;

@@ -54,6 +54,17 @@ class _FusibleIntensity(BatchTransform):
     def chain_op(self, params: dict, tensor: torch.Tensor) -> ops.ChainOp:
         raise NotImplementedError
 
+    def chain_params(self, batch_size: int, shape, device) -> dict:
+        """``sample_params`` for a Compose chain, which reads the host copies:
+        the same draws, but device tensors only when the op selects some
+        element (a chain leaves an op that selects none out)."""
+        host = self.sample_host(batch_size, shape)
+        if not np.asarray(host["mask"]).any():
+            return {"_host": host}
+        params = self._device_params(host, tuple(shape), device)
+        params["_host"] = host
+        return params
+
     def apply(self, tensor: torch.Tensor, params: dict) -> torch.Tensor:
         return ops.intensity_chain(tensor, [self.chain_op(params, tensor)])
 
@@ -356,6 +367,10 @@ class ScaleIntensity(_FusibleIntensity):
             flags |= L.BA_RESCALE_CHANNEL
         return ops.ChainOp(L.BA_OP_RESCALE, flags=flags, c0=self.minv or 0.0,
                            c1=self.maxv or 0.0)
+
+    def chain_params(self, batch_size, shape, device):
+        # chain_op reads no params: nothing to upload
+        return {"_host": self.sample_host(batch_size, shape)}
 
     def apply(self, tensor, params):
         if self.factor is None and self.minv is None and self.maxv is None:

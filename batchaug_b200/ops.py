@@ -7,7 +7,9 @@ can also be used directly.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
+import os
 
 import numpy as np
 import torch
@@ -49,14 +51,40 @@ def _dev_mask(mask, B, device):
 # Geometric
 # ---------------------------------------------------------------------------
 
+# Trilinear arithmetic of the resample: False (default) interpolates with
+# fused multiply-add lerps, within 1e-5 (fp32) / 2 bf16 ulp of torch's CPU
+# grid_sample; True rounds every weight product and sum as torch's CPU code
+# does (bit for bit).  Coordinates, and so nearest keys, are exact either way.
+# BATCHAUG_B200_EXACT=1 in the environment starts in exact mode.
+_EXACT = [os.environ.get("BATCHAUG_B200_EXACT", "0") == "1"]
+
+
+def set_resample_exact(flag: bool) -> bool:
+    """Set the default trilinear arithmetic (see above); returns the old one."""
+    old, _EXACT[0] = _EXACT[0], bool(flag)
+    return old
+
+
+@contextlib.contextmanager
+def resample_exact(flag: bool = True):
+    """``with resample_exact():`` runs its body's resamples in exact mode."""
+    old = set_resample_exact(flag)
+    try:
+        yield
+    finally:
+        set_resample_exact(old)
+
+
 def resample3d(tensors, *, affine=None, theta=None, grid=None, modes="bilinear",
-               paddings="zeros", align_corners=False, mask=None, out=None):
+               paddings="zeros", align_corners=False, mask=None, out=None, exact=None):
     """Resample one or more (B,C,H,W,D) tensors through one shared map.
 
     Exactly one of ``affine`` (MONAI (B,4,4)), ``theta`` (affine_grid
     (B,3|4,4)) or ``grid`` (grid_sample (B,H,W,D,3)) gives the map.  ``modes``
     and ``paddings`` are a string or one entry per tensor.  Masked-out
-    elements are copied.  Returns a list of new tensors (or fills ``out``).
+    elements are copied.  ``exact`` overrides the default trilinear
+    arithmetic (``set_resample_exact``).  Returns a list of new tensors (or
+    fills ``out``).
     """
     single = isinstance(tensors, torch.Tensor)
     ts = [tensors] if single else list(tensors)
@@ -81,13 +109,19 @@ def resample3d(tensors, *, affine=None, theta=None, grid=None, modes="bilinear",
             raise ValueError(f"unsupported padding_mode {p!r} (zeros, border or reflection)")
     if sum(x is not None for x in (affine, theta, grid)) != 1:
         raise ValueError("resample3d needs exactly one of affine, theta or grid")
+    # host (numpy) transforms and masks ride in the kernels' parameters
+    # (BA_RESAMPLE_HOST_PARAMS): no upload, no device allocation
+    host = not isinstance(affine if affine is not None else theta, torch.Tensor) and \
+        (grid is None or isinstance(grid, torch.Tensor)) and not isinstance(mask, torch.Tensor)
     if affine is not None:
-        xf = _dev_f32(affine, device, "affine").reshape(B, -1)
+        xf = (np.ascontiguousarray(affine, np.float32).reshape(B, -1) if host
+              else _dev_f32(affine, device, "affine").reshape(B, -1))
         kind, stride = L.BA_XFORM_AFFINE, xf.shape[1]
         if stride != 16:
             raise ValueError("affine must be (B,4,4)")
     elif theta is not None:
-        xf = _dev_f32(theta, device, "theta").reshape(B, -1)
+        xf = (np.ascontiguousarray(theta, np.float32).reshape(B, -1) if host
+              else _dev_f32(theta, device, "theta").reshape(B, -1))
         kind, stride = L.BA_XFORM_THETA, xf.shape[1]
         if stride not in (12, 16):
             raise ValueError("theta must be (B,3,4) or (B,4,4)")
@@ -96,16 +130,26 @@ def resample3d(tensors, *, affine=None, theta=None, grid=None, modes="bilinear",
         if tuple(xf.shape) != (B, H, W, D, 3):
             raise ValueError(f"grid must be {(B, H, W, D, 3)}, got {tuple(xf.shape)}")
         kind, stride = L.BA_XFORM_GRID, 0
-    m = _dev_mask(mask, B, device)
+    if host:
+        m = None if mask is None else np.ascontiguousarray(np.asarray(mask).reshape(B) != 0,
+                                                           np.uint8)
+    else:
+        m = _dev_mask(mask, B, device)
     outs = list(out) if out is not None else [torch.empty_like(t) for t in ts]
     d = L.ResampleDesc()
     d.batch, d.H, d.W, d.D = B, H, W, D
     d.xform_kind = kind
     d.align_corners = int(bool(align_corners))
+    d.flags = L.BA_RESAMPLE_EXACT if (_EXACT[0] if exact is None else exact) else 0
     d.n_keys = len(ts)
-    d.xform = xf.data_ptr()
+    if host:
+        d.flags |= L.BA_RESAMPLE_HOST_PARAMS
+        d.xform = xf.ctypes.data if kind != L.BA_XFORM_GRID else xf.data_ptr()
+        d.mask = None if m is None else m.ctypes.data
+    else:
+        d.xform = xf.data_ptr()
+        d.mask = L.ptr(m)
     d.xform_stride = stride
-    d.mask = L.ptr(m)
     for i, (t, o) in enumerate(zip(ts, outs)):
         k = d.keys[i]
         k.src, k.dst = t.data_ptr(), o.data_ptr()

@@ -74,12 +74,26 @@ typedef struct ba_resample_key {
   int32_t reserved;
 } ba_resample_key;
 
+/* ba_resample_desc.flags */
+#define BA_RESAMPLE_EXACT 0x1 /* trilinear weights and sums rounded as torch's CPU
+                                 grid_sample rounds them (bit for bit); without it
+                                 the interpolation uses fused multiply-add lerps,
+                                 within 1e-5 (fp32) / 2 bf16 ulp of it.  Source
+                                 coordinates, and so nearest keys, are exact in
+                                 both modes. */
+#define BA_RESAMPLE_HOST_PARAMS 0x2 /* xform (AFFINE / THETA maps) and mask are host
+                                       pointers, read before the call returns: each
+                                       launch of up to 32 elements carries them in its
+                                       kernel parameters, so no device copy of them is
+                                       needed (xform_stride <= 16; a GRID map's grid
+                                       stays a device pointer) */
+
 typedef struct ba_resample_desc {
   int64_t batch, H, W, D;
   int32_t xform_kind;    /* ba_xform */
   int32_t align_corners; /* grid_sample's align_corners */
   int32_t n_keys;        /* 1..BA_MAX_KEYS keys sharing one coordinate map */
-  int32_t reserved;
+  int32_t flags;         /* BA_RESAMPLE_* */
   const float* xform;   /* see ba_xform */
   int64_t xform_stride; /* floats between consecutive elements of an AFFINE or
                            THETA xform (16 for (B,4,4), 12 for (B,3,4)) */

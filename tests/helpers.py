@@ -37,10 +37,20 @@ def bf16_ulp_diff(a: np.ndarray, b: np.ndarray) -> int:
     return int(np.abs(ia - ib).max()) if ia.size else 0
 
 
-def assert_close_dtype(out: np.ndarray, ref: np.ndarray, atol_f32=1e-5, max_bf16_ulp=2):
-    """The parity bar: fp32 within atol_f32, bf16 within max_bf16_ulp ulps."""
+def assert_close_dtype(out: np.ndarray, ref: np.ndarray, atol_f32=1e-5, max_bf16_ulp=2,
+                       bf16_abs=0.0):
+    """The parity bar: fp32 within atol_f32, bf16 within max_bf16_ulp ulps.
+
+    ``bf16_abs`` > 0 also accepts bf16 values within that absolute distance:
+    for a bf16 result computed in fp32 and rounded once, a value that
+    cancels to near zero (|x| < ~1e-4) has bf16 ulps below the fp32
+    arithmetic's own rounding (~1e-7 of the operands), so a reordered fp32
+    computation can land several bf16 ulps away while being 1e-8 apart."""
     assert out.shape == ref.shape and out.dtype == ref.dtype
     if out.dtype == np.uint16:
+        if bf16_abs > 0:
+            near = np.abs(as_f32(out) - as_f32(ref)) <= bf16_abs
+            out, ref = out[~near], ref[~near]
         assert bf16_ulp_diff(out, ref) <= max_bf16_ulp
     else:
         np.testing.assert_allclose(out, ref, rtol=0, atol=atol_f32)

@@ -194,7 +194,7 @@ def test_golden_pipeline_cfg1(ba):
     from batchaug_b200 import ops
     g = load_golden("pipeline_cfg1")
     vo, so = ops.resample3d([to_dev(g["vol"]), to_dev(g["seg"])], affine=g["affine"],
-                            mask=g["mask"], modes=["bilinear", "nearest"])
+                            mask=g["mask"], modes=["bilinear", "nearest"], exact=True)
     vo = ops.intensity_chain(vo, [
         ops.ChainOp(L.BA_OP_NOISE, mask=to_dev(g["noise_mask"]).to(torch.uint8),
                     noise=to_dev(g["noise"])),
@@ -285,3 +285,25 @@ def test_owned_keys_never_the_inputs(ba):
         r = c({"a": x, "b": x})
         assert torch.equal(x, x0)
         assert torch.equal(r["a"], r["b"])
+
+
+def test_owned_key_noise_runs_equal_full_chain(ba):
+    """A pipeline-owned key gets its intensity run in place on the runs of
+    selected elements only; with the same params, the selected elements get
+    exactly the noise a full-batch chain gives them (Philox keyed on the
+    global element index), the others are untouched."""
+    torch.manual_seed(4)
+    vol = torch.randn(7, 2, 12, 10, 16, device="cuda")
+    flip = ba.RandAxisFlipd(["vol"], prob=1.0)
+    noise = ba.RandGaussianNoised(["vol"], prob=0.5, std=0.3)
+    pf = flip.transform.sample_params(7, vol.shape, vol.device)
+    pn = noise.transform.sample_params(7, vol.shape, vol.device)
+    sel = np.array([True, True, False, True, False, False, True])
+    pn["mask"] = torch.from_numpy(sel).cuda()
+    pn["_host"]["mask"] = sel
+    out = ba.Compose([flip, noise], lazy=True)({"vol": vol}, params=[pf, pn])["vol"]
+    # the Compose's own materialisation of the flip (bilinear, its mode)
+    flipped = ba.Compose([flip], lazy=True)({"vol": vol}, params=[pf])["vol"]
+    full = noise.transform.apply(flipped, pn)
+    assert torch.equal(out[torch.from_numpy(sel)], full[torch.from_numpy(sel)])
+    assert torch.equal(out[torch.from_numpy(~sel)], flipped[torch.from_numpy(~sel)])

@@ -163,7 +163,7 @@ def _check(name, key, out: np.ndarray, z, exact: bool):
         if exact:
             assert np.array_equal(out, ref), f"{name}/{key}: differs from the reference"
         else:
-            assert_close_dtype(out, ref)
+            assert_close_dtype(out, ref, bf16_abs=1e-6)
         return
     plane, stride, s, ss = _summary(out)
     for part, mine in (("plane", plane), ("stride", stride)):
@@ -171,7 +171,7 @@ def _check(name, key, out: np.ndarray, z, exact: bool):
         if exact:
             assert np.array_equal(mine, ref), f"{name}/{key} {part}: differs from the reference"
         else:
-            assert_close_dtype(mine, ref)
+            assert_close_dtype(mine, ref, bf16_abs=1e-6)
     if exact:
         np.testing.assert_array_equal(s, z[f"out_{key}_sum"])
         np.testing.assert_array_equal(ss, z[f"out_{key}_sumsq"])

@@ -116,7 +116,7 @@ def test_compose_plan_config4(ba, rec, oracle_lib):
     seg = (torch.rand(3, 1, 8, 8, 8) > 0.5).float()
     c = ba.Compose([ba.RandRotate90d(["vol", "seg"], prob=1.0, max_k=3),
                     ba.RandAxisFlipd(["vol", "seg"], prob=1.0),
-                    ba.RandGaussianNoised(["vol"], std=0.5),
+                    ba.RandGaussianNoised(["vol"], prob=1.0, std=0.5),
                     ba.RandAffined(["vol", "seg"], prob=1.0, rotate_range=0.785),
                     ba.ScaleIntensityd(["vol"]),
                     ba.RandShiftIntensityd(["vol"], prob=1.0)],
@@ -128,6 +128,28 @@ def test_compose_plan_config4(ba, rec, oracle_lib):
     assert rec.calls[3][2] == [6, 4]  # ScaleIntensity then shift, one chain
     # nearest keeps binary labels
     assert set(np.unique(out["seg"].numpy())) <= {0.0, 1.0}
+
+
+def test_owned_key_chain_runs_on_selected_elements_only(ba, rec, oracle_lib):
+    """On a key the pipeline created (the first resample's output), an
+    intensity run touches only the runs of elements its ops select, in place:
+    no launch when none is selected, one per run of consecutive elements."""
+    torch.manual_seed(0)
+    vol = torch.randn(6, 1, 8, 8, 8)
+    for prob, launches in ((0.0, 0), (1.0, 1)):
+        rec.calls.clear()
+        c = ba.Compose([ba.RandAxisFlipd(["vol"], prob=1.0),
+                        ba.RandGaussianNoised(["vol"], prob=prob, std=0.5)], lazy=True)
+        c({"vol": vol})
+        assert [k[0] for k in rec.calls].count("chain") == launches
+    rec.calls.clear()
+    from batchaug_b200 import compose
+    sel = np.array([True, True, False, True, False, False])
+    assert compose.Compose._runs(np.flatnonzero(sel)) == [(0, 2), (3, 1)]
+    p = {"mask": torch.tensor(sel), "std": torch.arange(6.0), "elem_offset": 10,
+         "_host": {"mask": sel}}
+    q = compose._slice_params(p, 3, 1)
+    assert q["elem_offset"] == 13 and q["std"].tolist() == [3.0] and q["_host"]["mask"].tolist() == [True]
 
 
 def test_compose_accumulates_like_reference(ba, rec, oracle_lib):
