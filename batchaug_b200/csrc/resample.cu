@@ -1108,6 +1108,466 @@ __global__ void __launch_bounds__(ST_THREADS, BA_FS_MINBLOCKS)
   }
 }
 
+// ===========================================================================
+// Signed-permutation resample: theta's 3x3 part holds one +-1 per row and
+// column, and the source x (D) coordinate is driven by the output D index —
+// flips, square-plane rot90s in the (H, W) plane and their products in a
+// Compose.  Each source coordinate then depends on one output index only
+// (the other terms of the affine_grid sum are exact zeros), so the kernel
+// tabulates it per axis with the same arithmetic as the other kernels and
+// copies rows as 16-byte (fp32) / 8-byte (bf16) vectors, forwards or
+// reversed.  A coordinate a few ulp from an integer (torch's linspace base
+// grid puts one position per axis there) takes the fast kernel's fused lerp
+// from the neighbouring source voxel, fetched alongside the vector; the few
+// rows off a centre along y or z lerp 2 or 4 source rows.  Nearest keys read
+// the same voxels as the exact kernels and take this kernel in both modes.
+// A warp covers R consecutive (h, w) rows of one element; a lane takes 4
+// consecutive D positions.  D is a multiple of 4 and at most PM_MAX_D, rows
+// 16-byte (fp32) / 8-byte (bf16) aligned.
+// ===========================================================================
+constexpr int PM_THREADS = 256;
+constexpr int PM_WARPS = PM_THREADS / 32;
+constexpr int PM_MAX_D = 1024;
+
+struct PermAxis {
+  int lo;      // floor of the coordinate clamped as the fast kernel clamps it
+  float frac;  // its fractional part (0: on a voxel centre)
+  int near;    // the nearest key's index, -1 outside the volume
+};
+
+template <int PAD>
+__device__ __forceinline__ PermAxis perm_axis(float u, int size) {
+  PermAxis r;
+  const float p = fast_pad<PAD>(u, (float)size);
+  const float f = floorf(p);
+  r.lo = (int)f;
+  r.frac = __fsub_rn(p, f);
+  const int n = __float2int_rn(pad_coord<PAD, false>(u, size));
+  r.near = (unsigned)n < (unsigned)size ? n : -1;
+  return r;
+}
+
+// source coordinate along axis r for output index i along the axis that
+// drives it: g = sign * base + t3 (the affine_grid sum's other terms are
+// exact zeros), then grid_sampler_unnormalize
+__device__ __forceinline__ float perm_coord(int i, int n_out, float sign, float t3, int size,
+                                            bool align) {
+  const float g = __fadd_rn(__fmul_rn(base_coord(i, n_out, align), sign), t3);
+  return align ? __fmul_rn(__fmul_rn(__fadd_rn(g, 1.0f), 0.5f), (float)(size - 1))
+               : __fmul_rn(__fsub_rn(__fmul_rn(__fadd_rn(g, 1.0f), (float)size), 1.0f), 0.5f);
+}
+
+template <int DT>
+__device__ __forceinline__ void ld4v(const void* base, int64_t i, float* v) {
+  if (DT == BA_BF16) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>((const uint16_t*)base + i));
+    v[0] = __uint_as_float(u.x << 16);
+    v[1] = __uint_as_float(u.x & 0xFFFF0000u);
+    v[2] = __uint_as_float(u.y << 16);
+    v[3] = __uint_as_float(u.y & 0xFFFF0000u);
+  } else {
+    const float4 f = __ldg(reinterpret_cast<const float4*>((const float*)base + i));
+    v[0] = f.x;
+    v[1] = f.y;
+    v[2] = f.z;
+    v[3] = f.w;
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void st4v(void* base, int64_t i, const float* v) {
+  if (DT == BA_BF16) {
+    uint2 u;
+    u.x = pack_bf16x2(v[0], v[1]);
+    u.y = pack_bf16x2(v[2], v[3]);
+    *reinterpret_cast<uint2*>((uint16_t*)base + i) = u;
+  } else {
+    *reinterpret_cast<float4*>((float*)base + i) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+// A voxel off a voxel centre (or on the volume's border): the fast kernel's
+// lerps over its 8 taps, bounds-checked, zero outside the volume.  Rare, so
+// kept out of line to leave the copy loop its registers.
+template <int DT>
+__device__ __noinline__ float perm_interp(const char* cs, PermAxis ax, PermAxis ay, PermAxis az,
+                                          int H, int W, int D) {
+  const int x0 = ax.lo, y0 = ay.lo, z0 = az.lo;
+  float va[8];
+  const bool interior = (unsigned)x0 < (unsigned)(D - 1) && (unsigned)y0 < (unsigned)(W - 1) &&
+                        (unsigned)z0 < (unsigned)(H - 1);
+  taps8<DT>(cs, x0, y0, z0, H, W, D, interior, va);
+  return trilerp2(va, va, f2(ax.frac), f2(ay.frac), f2(az.frac)).x;
+}
+
+// The x side of a lane's 4 voxels (D positions d .. d+3 of a row): the
+// aligned source chunk their nearest indices fill, forwards or reversed, and
+// whether a bilinear lerp along x reaches the source voxel just before or
+// just after that chunk.
+struct PermX {
+  int base;     // first source x of the chunk; -1 when the voxels do not fill one
+  bool rev;     // reversed order (a flip along x)
+  bool off;     // a voxel off a voxel centre along x
+  bool need_l;  // a lerp reads source x base - 1
+  bool need_r;  // a lerp reads source x base + 4
+};
+
+__device__ __forceinline__ PermX perm_x(const PermAxis* sx, int D) {
+  PermX p;
+  const int n0 = sx[0].near, n3 = sx[3].near;
+  p.rev = n0 > n3;
+  const int base = p.rev ? n3 : n0;
+  bool ok = base >= 0 && (base & 3) == 0 && base + 3 < D;
+  p.off = p.need_l = p.need_r = false;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const PermAxis ax = sx[j];
+    ok = ok && ax.near == (p.rev ? base + 3 - j : base + j);
+    if (ax.frac != 0.0f) {
+      p.off = true;
+      p.need_l = p.need_l || ax.lo < base;
+      p.need_r = p.need_r || ax.lo + 1 > base + 3;
+    }
+  }
+  p.base = ok ? base : -1;
+  return p;
+}
+
+// One source row's chunk for a lane: 4 voxels as one vector plus, for x
+// lerps, the voxels on either side (zero outside the volume); every load is
+// issued before any use.
+template <int DT>
+__device__ __forceinline__ void perm_fetch(const char* cs, int64_t row, bool in, const PermX& px,
+                                           int D, float* v, float& l, float& r) {
+  if (in) {
+    ld4v<DT>(cs, row + px.base, v);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = 0.0f;
+  }
+  l = (in && px.need_l && px.base > 0) ? ld<DT>(cs, row + px.base - 1) : 0.0f;
+  r = (in && px.need_r && px.base + 4 < D) ? ld<DT>(cs, row + px.base + 4) : 0.0f;
+}
+
+__device__ __forceinline__ float pick6(const float (&w)[6], int i) {
+  const float a = i == 0 ? w[0] : w[1];
+  const float b = i == 2 ? w[2] : w[3];
+  const float c = i == 4 ? w[4] : w[5];
+  return i < 2 ? a : (i < 4 ? b : c);
+}
+
+// The 4 voxels in output order: the chunk's voxels, and the fast kernel's
+// x lerp fma(f, hi - lo, lo) for the ones off a centre (trilerp2's lerps
+// along y and z at fraction 0 return it unchanged).
+template <bool LERP>
+__device__ __forceinline__ void perm_xlerp(const float* v, float l, float r, const PermX& px,
+                                           const PermAxis* sx, float* out) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) out[j] = px.rev ? v[3 - j] : v[j];
+  if (LERP && px.off) {
+    const float w[6] = {l, v[0], v[1], v[2], v[3], r};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const PermAxis ax = sx[j];
+      if (ax.frac != 0.0f) {
+        const int i = ax.lo - px.base + 1;  // 0 .. 4
+        const float lo = pick6(w, i), hi = pick6(w, i + 1);
+        out[j] = __fmaf_rn(ax.frac, __fsub_rn(hi, lo), lo);
+      }
+    }
+  }
+}
+
+// Where a key's output row reads: its source row (nearest indices, or the
+// floors for a bilinear key) and whether that row lies inside the volume.
+template <int MODE>
+__device__ __forceinline__ void perm_row(PermAxis ay, PermAxis az, int H, int W, int D,
+                                         int64_t& row, bool& in) {
+  const int yi = MODE == BA_NEAREST ? ay.near : ay.lo;
+  const int zi = MODE == BA_NEAREST ? az.near : az.lo;
+  in = (unsigned)yi < (unsigned)W && (unsigned)zi < (unsigned)H;
+  row = ((int64_t)zi * W + yi) * D;
+}
+
+// The common case: rows on voxel centres along y and z (nearest keys always
+// are), lanes whose voxels fill aligned source chunks.  R output rows of the
+// warp and 4 / R channels at a time, both keys' loads issued before any
+// store (a store could alias a later load as far as the compiler knows).
+template <int S0, int S1, int R>
+__device__ __forceinline__ void perm_rows_fast(const ResampleArgs& a, int64_t b, int H, int W,
+                                               int D, int64_t orow0, int nr, int d, bool act,
+                                               const PermX& px, const PermAxis* sy,
+                                               const PermAxis* sz, const PermAxis* sx) {
+  constexpr int CB = 4 / R;
+  constexpr int M0 = spec_mode(S0), DT0 = spec_dt(S0);
+  constexpr int S1K = S1 < 0 ? 0 : S1;
+  constexpr int M1 = spec_mode(S1K), DT1 = spec_dt(S1K);
+  const int64_t hwd = (int64_t)H * W * D;
+  const KeyArgs& k0 = a.keys[0];
+  const KeyArgs& k1 = a.keys[S1 >= 0 ? 1 : 0];
+  const size_t e0 = DT0 == BA_BF16 ? 2 : 4, e1 = DT1 == BA_BF16 ? 2 : 4;
+  int64_t src0[R], src1[R];
+  bool in0[R], in1[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int rr = min(r, nr - 1);  // rows past the group's end repeat its last (not stored)
+    perm_row<M0>(sy[rr], sz[rr], H, W, D, src0[r], in0[r]);
+    in0[r] = in0[r] && act;
+    if (S1 >= 0) {
+      perm_row<M1>(sy[rr], sz[rr], H, W, D, src1[r], in1[r]);
+      in1[r] = in1[r] && act;
+    }
+  }
+  const int nc = max(k0.channels, S1 >= 0 ? k1.channels : 0);
+  for (int c0 = 0; c0 < nc; c0 += CB) {
+    float v0[4][4], l0[4], r0[4], v1[4][4];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int j = 0; j < CB; ++j) {
+        const int s = r * CB + j, c = c0 + j;
+        perm_fetch<DT0>((const char*)k0.src + ((size_t)b * k0.channels + c) * hwd * e0, src0[r],
+                        in0[r] && c < k0.channels, px, D, v0[s], l0[s], r0[s]);
+        if (S1 >= 0) {
+          float dl, dr;
+          PermX p1 = px;
+          p1.need_l = p1.need_r = false;
+          perm_fetch<DT1>((const char*)k1.src + ((size_t)b * k1.channels + c) * hwd * e1, src1[r],
+                          in1[r] && c < k1.channels, p1, D, v1[s], dl, dr);
+        }
+      }
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int j = 0; j < CB; ++j) {
+        const int s = r * CB + j, c = c0 + j;
+        if (!act || r >= nr) continue;
+        const int64_t o = (orow0 + r) * D + d;
+        float out[4];
+        if (c < k0.channels) {
+          perm_xlerp<M0 != BA_NEAREST>(v0[s], l0[s], r0[s], px, sx, out);
+          st4v<DT0>((char*)k0.dst + ((size_t)b * k0.channels + c) * hwd * e0, o, out);
+        }
+        if (S1 >= 0 && c < k1.channels) {
+          perm_xlerp<false>(v1[s], 0.0f, 0.0f, px, sx, out);
+          st4v<DT1>((char*)k1.dst + ((size_t)b * k1.channels + c) * hwd * e1, o, out);
+        }
+      }
+  }
+}
+
+// A voxel whose lane does not fill an aligned chunk: the fast kernel's lerps
+// over its 8 taps, bounds-checked, zero outside the volume.  Not reached by
+// the signed permutations the host selects; kept out of line.
+template <int DT>
+__device__ __noinline__ float perm_interp(const char* cs, PermAxis ax, PermAxis ay, PermAxis az,
+                                          int H, int W, int D) {
+  const int x0 = ax.lo, y0 = ay.lo, z0 = az.lo;
+  float va[8];
+  const bool interior = (unsigned)x0 < (unsigned)(D - 1) && (unsigned)y0 < (unsigned)(W - 1) &&
+                        (unsigned)z0 < (unsigned)(H - 1);
+  taps8<DT>(cs, x0, y0, z0, H, W, D, interior, va);
+  return trilerp2(va, va, f2(ax.frac), f2(ay.frac), f2(az.frac)).x;
+}
+
+// One key, one channel, one output row off voxel centres along y or z (a
+// coordinate a few ulp from an integer: a few rows per volume), or lanes
+// whose voxels do not fill aligned chunks: the 2 or 4 source rows around it
+// fetched together, lerped along x, then along y and z as trilerp2 does.
+template <int S>
+__device__ __forceinline__ void perm_row_slow(const char* cs, char* cd, int H, int W, int D,
+                                              int64_t o, bool act, bool xok, const PermX& px,
+                                              PermAxis ay, PermAxis az, const PermAxis* sx) {
+  constexpr int MODE = spec_mode(S), DT = spec_dt(S);
+  float out[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  if (!xok) {
+    if (act) {
+      if (MODE == BA_NEAREST) {
+        const bool in = ay.near >= 0 && az.near >= 0;
+        const int64_t row = ((int64_t)az.near * W + ay.near) * D;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          out[j] = (in && sx[j].near >= 0) ? ld<DT>(cs, row + sx[j].near) : 0.0f;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) out[j] = perm_interp<DT>(cs, sx[j], ay, az, H, W, D);
+      }
+      st4v<DT>(cd, o, out);
+    }
+    return;
+  }
+  if (MODE == BA_NEAREST) {
+    int64_t row;
+    bool in;
+    perm_row<MODE>(ay, az, H, W, D, row, in);
+    float v[4], l, r;
+    PermX p = px;
+    p.need_l = p.need_r = false;
+    perm_fetch<DT>(cs, row, in && act, p, D, v, l, r);
+    perm_xlerp<false>(v, l, r, px, sx, out);
+  } else {
+    float v[4][4], l[4], r[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int dy = q & 1, dz = q >> 1;
+      const bool need = (dy == 0 || ay.frac != 0.0f) && (dz == 0 || az.frac != 0.0f);
+      const int yy = ay.lo + dy, zz = az.lo + dz;
+      const bool in = act && need && (unsigned)yy < (unsigned)W && (unsigned)zz < (unsigned)H;
+      perm_fetch<DT>(cs, ((int64_t)zz * W + yy) * D, in, px, D, v[q], l[q], r[q]);
+    }
+    float c[4][4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) perm_xlerp<true>(v[q], l[q], r[q], px, sx, c[q]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float c0 = __fmaf_rn(ay.frac, __fsub_rn(c[1][j], c[0][j]), c[0][j]);
+      const float c1 = __fmaf_rn(ay.frac, __fsub_rn(c[3][j], c[2][j]), c[2][j]);
+      out[j] = __fmaf_rn(az.frac, __fsub_rn(c1, c0), c0);
+    }
+  }
+  if (act) st4v<DT>(cd, o, out);
+}
+
+template <int S0, int S1, int R>
+__device__ __forceinline__ void perm_rows_slow(const ResampleArgs& a, int64_t b, int H, int W,
+                                               int D, int64_t orow0, int nr, int d, bool act,
+                                               bool xok, const PermX& px, const PermAxis* sy,
+                                               const PermAxis* sz, const PermAxis* sx) {
+  constexpr int DT0 = spec_dt(S0);
+  constexpr int S1K = S1 < 0 ? 0 : S1;
+  constexpr int DT1 = spec_dt(S1K);
+  const int64_t hwd = (int64_t)H * W * D;
+  const KeyArgs& k0 = a.keys[0];
+  const KeyArgs& k1 = a.keys[S1 >= 0 ? 1 : 0];
+  const size_t e0 = DT0 == BA_BF16 ? 2 : 4, e1 = DT1 == BA_BF16 ? 2 : 4;
+  for (int r = 0; r < nr; ++r) {
+    const int64_t o = (orow0 + r) * D + d;
+    for (int c = 0; c < k0.channels; ++c) {
+      const size_t off = ((size_t)b * k0.channels + c) * hwd * e0;
+      perm_row_slow<S0>((const char*)k0.src + off, (char*)k0.dst + off, H, W, D, o, act, xok, px,
+                        sy[r], sz[r], sx);
+    }
+    if (S1 >= 0)
+      for (int c = 0; c < k1.channels; ++c) {
+        const size_t off = ((size_t)b * k1.channels + c) * hwd * e1;
+        perm_row_slow<S1K>((const char*)k1.src + off, (char*)k1.dst + off, H, W, D, o, act, xok,
+                           px, sy[r], sz[r], sx);
+      }
+  }
+}
+
+// R output rows per warp (4 for single-channel keys, so that each lane keeps
+// four loads in flight; 1 otherwise, with four channels at a time).
+template <int S0, int S1, int R>
+__global__ void __launch_bounds__(PM_THREADS, 2) resample3d_perm_kernel(const __grid_constant__ ResampleArgs a) {
+  constexpr int ROWS = PM_WARPS * R;
+  __shared__ PermAxis s_x[PM_MAX_D];
+  __shared__ PermAxis s_y[ROWS], s_z[ROWS];
+  __shared__ float s_th[12];
+  constexpr int PAD = spec_pad(S0);
+  const bool ALIGN = a.align_corners != 0;
+  const int H = a.H, W = a.W, D = a.D;
+  const int hwd = H * W * D;
+  const int64_t b = a.b0 + blockIdx.y;
+  // the CTA walks groups of ROWS rows, gridDim.x apart
+  const int n_groups = (H * W + ROWS - 1) / ROWS;
+  const int t = threadIdx.x;
+  if (!elem_active(a, b)) {
+    // the reference's torch.where keeps a masked-out element: a group's rows
+    // are one contiguous run per channel
+    for (int g = blockIdx.x; g < n_groups; g += gridDim.x) {
+      const int row0 = g * ROWS;
+      const int rows = min(ROWS, H * W - row0);
+      for (int ki = 0; ki < a.n_keys; ++ki) {
+        const KeyArgs& kc = a.keys[ki];
+        const int ke = kc.dtype == BA_BF16 ? 2 : 4;
+        const int n4 = rows * D / 4;  // 4-voxel chunks
+        for (int c = 0; c < kc.channels; ++c) {
+          const int64_t i0 = (b * kc.channels + c) * (int64_t)hwd + (int64_t)row0 * D;
+          for (int q = t; q < n4; q += PM_THREADS) {
+            if (ke == 2)
+              reinterpret_cast<uint2*>((uint16_t*)kc.dst + i0)[q] =
+                  __ldg(reinterpret_cast<const uint2*>((const uint16_t*)kc.src + i0) + q);
+            else
+              reinterpret_cast<float4*>((float*)kc.dst + i0)[q] =
+                  __ldg(reinterpret_cast<const float4*>((const float*)kc.src + i0) + q);
+          }
+        }
+      }
+    }
+    return;
+  }
+  if (t < 12) {
+    const int i = t / 4, j = t % 4;
+    const float* x = elem_xform(a, b);
+    if (a.xform_kind == BA_XFORM_AFFINE) {
+      // monai_affine_to_theta: theta = P S_norm A S_inv P, P swapping 0 and 2.
+      const int pi = 2 - i, pj = (j == 3) ? 3 : 2 - j;
+      const float s_j = (pj == 3) ? 1.0f : a.si[pj];
+      s_th[t] = (a.sn[pi] * x[pi * 4 + pj]) * s_j;
+    } else {
+      s_th[t] = x[i * 4 + j];
+    }
+  }
+  __syncthreads();
+  // the output axis (0: d, 1: w, 2: h) driving source axis r, and its sign
+  int col[3];
+  float sgn[3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    col[r] = s_th[r * 4] != 0.0f ? 0 : (s_th[r * 4 + 1] != 0.0f ? 1 : 2);
+    sgn[r] = s_th[r * 4 + col[r]];
+  }
+  for (int d = t; d < D; d += PM_THREADS)
+    s_x[d] = perm_axis<PAD>(perm_coord(d, D, sgn[0], s_th[3], D, ALIGN), D);
+  // the output index driving source y (r = 1, size W) and z (r = 2, size H)
+  const int yc = col[1], zc = col[2];
+  const float ys = sgn[1], zs = sgn[2], yt = s_th[7], zt = s_th[11];
+  const int wr = (t / 32) * R, lane = t % 32;  // the warp's first row in a group
+  for (int g = blockIdx.x; g < n_groups; g += gridDim.x) {
+    const int row0 = g * ROWS;
+    const int rows = min(ROWS, H * W - row0);
+    __syncthreads();  // the previous group's row tables are read
+    if (t < 2 * ROWS) {
+      const int j = t % ROWS, r = 1 + t / ROWS;
+      const int ri = min(row0 + j, H * W - 1);
+      const int w = ri % W, h = ri / W;
+      const int c = r == 1 ? yc : zc;
+      const int i = c == 1 ? w : h;
+      const int n = c == 1 ? W : H;
+      const int size = r == 1 ? W : H;
+      const PermAxis pa =
+          perm_axis<PAD>(perm_coord(i, n, r == 1 ? ys : zs, r == 1 ? yt : zt, size, ALIGN), size);
+      if (r == 1)
+        s_y[j] = pa;
+      else
+        s_z[j] = pa;
+    }
+    __syncthreads();
+    if (wr >= rows) continue;
+    const int nr = min(R, rows - wr);
+    // warp-uniform: every row of the warp on voxel centres along y and z
+    bool centre = spec_mode(S0) == BA_NEAREST;
+    if (!centre) {
+      centre = true;
+      for (int r = 0; r < nr; ++r)
+        centre = centre && s_y[wr + r].frac == 0.0f && s_z[wr + r].frac == 0.0f;
+    }
+    for (int d0 = 0; d0 < D; d0 += 128) {
+      const int d = d0 + 4 * lane;
+      const bool act = d < D;
+      const PermX px = perm_x(s_x + (act ? d : 0), D);
+      const bool xok = __all_sync(0xFFFFFFFFu, !act || px.base >= 0);
+      if (xok && centre)
+        perm_rows_fast<S0, S1, R>(a, b, H, W, D, row0 + wr, nr, d, act, px, s_y + wr, s_z + wr,
+                                  s_x + (act ? d : 0));
+      else
+        perm_rows_slow<S0, S1, R>(a, b, H, W, D, row0 + wr, nr, d, act, xok, px, s_y + wr,
+                                  s_z + wr, s_x + (act ? d : 0));
+    }
+  }
+}
+
 // Opt the staged kernel in to its dynamic shared memory once per process
 // (needed above 48 KB; idempotent, so concurrent first calls are harmless).
 template <int S0, int S1, bool FAST>
@@ -1443,6 +1903,60 @@ __global__ void __launch_bounds__(G4_THREADS, 8) resample3d_grid4_kernel(const _
 
 namespace ba {
 namespace {
+int sm_count_rs() {
+  static int cached = 0;
+  if (cached == 0) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+      cached = n;
+    else
+      cached = 148;
+  }
+  return cached;
+}
+
+// True when every active element of a host-parameter launch maps by a
+// signed permutation that resample3d_perm_kernel takes: theta's 3x3 part
+// (derived from the affine with the kernel's own arithmetic) one +-1 per row
+// and column, no translation, source x driven by output D, and a swapped
+// (H, W) plane square.
+bool perm_chunk(const ResampleArgs& a, int64_t nb) {
+  if (!a.inline_params || a.xform_kind == BA_XFORM_GRID) return false;
+  if (a.D % 4 != 0 || a.D > PM_MAX_D) return false;
+  for (int64_t i = 0; i < nb; ++i) {
+    if (!a.inl_mask[i]) continue;
+    const float* x = a.inl_xform + i * a.xform_stride;
+    float th[12];
+    for (int t = 0; t < 12; ++t) {
+      const int r = t / 4, j = t % 4;
+      if (a.xform_kind == BA_XFORM_AFFINE) {
+        const int pi = 2 - r, pj = (j == 3) ? 3 : 2 - j;
+        const float s_j = (pj == 3) ? 1.0f : a.si[pj];
+        th[t] = (a.sn[pi] * x[pi * 4 + pj]) * s_j;
+      } else {
+        th[t] = x[r * 4 + j];
+      }
+    }
+    int used = 0;
+    for (int r = 0; r < 3; ++r) {
+      int nz = 0, c = -1;
+      for (int j = 0; j < 3; ++j)
+        if (th[r * 4 + j] != 0.0f) {
+          ++nz;
+          c = j;
+        }
+      if (nz != 1 || (th[r * 4 + c] != 1.0f && th[r * 4 + c] != -1.0f) || th[r * 4 + 3] != 0.0f)
+        return false;
+      if (used & (1 << c)) return false;
+      used |= 1 << c;
+      if (r == 0 && c != 0) return false;        // x from d
+      if (r != 0 && c != r && a.H != a.W) return false;  // a swapped plane is square
+    }
+  }
+  return true;
+}
+
 // Launches of one resample over elements a.b0 .. a.b0 + nb - 1: the kernel
 // each key group takes (staged / fast for affine maps with a bilinear key,
 // grid kernel for grid maps, global-gather kernel otherwise).
@@ -1494,6 +2008,48 @@ ba_status launch_resample(const ba_resample_desc& d, ResampleArgs& a, int64_t nb
         return false;
     }
   };
+  // Signed permutations: the row-copy kernel, keys with zeros or border
+  // padding whose rows are vector-aligned.
+  auto perm_ok = [&](const KeyArgs& k) {
+    const uintptr_t align = k.dtype == BA_BF16 ? 8 : 16;
+    return k.padding != BA_PAD_REFLECTION && ((uintptr_t)k.src % align) == 0 &&
+           ((uintptr_t)k.dst % align) == 0;
+  };
+  // about four CTAs per SM over the launch's elements, each walking row
+  // groups; single-channel launches take 4 rows per warp
+  auto launch_perm = [&](const ResampleArgs& args, int s0, int s1) -> bool {
+    int nc = 0;
+    for (int i = 0; i < args.n_keys; ++i) nc = std::max(nc, args.keys[i].channels);
+    const int rpw = nc == 1 ? 4 : 1;
+    const int64_t rows = (int64_t)PM_WARPS * rpw;
+    const int64_t groups = (d.H * d.W + rows - 1) / rows;
+    const int64_t per_elem = std::max<int64_t>(1, (4 * (int64_t)sm_count_rs() + nb - 1) / nb);
+    const dim3 grid_pm((unsigned)std::min<int64_t>(groups, per_elem), (unsigned)nb);
+    switch (s0 * 16 + (s1 + 1)) {
+#define BA_PM(S0, S1)                                                                  \
+  case S0 * 16 + (S1 + 1):                                                             \
+    if (rpw == 4)                                                                      \
+      resample3d_perm_kernel<S0, S1, 4><<<grid_pm, PM_THREADS, 0, st>>>(args);         \
+    else                                                                               \
+      resample3d_perm_kernel<S0, S1, 1><<<grid_pm, PM_THREADS, 0, st>>>(args);         \
+    return true;
+#define BA_PM_PAD(P)                                                                \
+  BA_PM(spec_code(BA_BILINEAR, P, BA_F32), -1)                                      \
+  BA_PM(spec_code(BA_BILINEAR, P, BA_BF16), -1)                                     \
+  BA_PM(spec_code(BA_NEAREST, P, BA_F32), -1)                                       \
+  BA_PM(spec_code(BA_NEAREST, P, BA_BF16), -1)                                      \
+  BA_PM(spec_code(BA_BILINEAR, P, BA_F32), spec_code(BA_NEAREST, P, BA_F32))        \
+  BA_PM(spec_code(BA_BILINEAR, P, BA_F32), spec_code(BA_NEAREST, P, BA_BF16))       \
+  BA_PM(spec_code(BA_BILINEAR, P, BA_BF16), spec_code(BA_NEAREST, P, BA_F32))       \
+  BA_PM(spec_code(BA_BILINEAR, P, BA_BF16), spec_code(BA_NEAREST, P, BA_BF16))
+      BA_PM_PAD(BA_PAD_ZEROS)
+      BA_PM_PAD(BA_PAD_BORDER)
+#undef BA_PM_PAD
+#undef BA_PM
+      default:
+        return false;
+    }
+  };
   // Grid maps take the lane-per-voxel grid kernel.
   const bool grid4 = a.xform_kind == BA_XFORM_GRID;
   const dim3 g4_grid((unsigned)((hwd + G4_THREADS * G4_VOX - 1) / (G4_THREADS * G4_VOX)),
@@ -1507,6 +2063,9 @@ ba_status launch_resample(const ba_resample_desc& d, ResampleArgs& a, int64_t nb
       k0 = a.keys[0];
       k1 = a.keys[1];
     }
+    if (!exact && perm_ok(a.keys[0]) && perm_ok(a.keys[1]) && k1.mode == BA_NEAREST &&
+        k0.padding == k1.padding && perm_chunk(a, nb) && launch_perm(a, code(k0), code(k1)))
+      return check_launch("ba_resample3d");
     if (k0.mode == BA_BILINEAR && k1.mode == BA_NEAREST && k0.padding == k1.padding &&
         stageable(k0) && launch_staged(a, code(k0), code(k1)))
       return check_launch("ba_resample3d");
@@ -1537,8 +2096,17 @@ ba_status launch_resample(const ba_resample_desc& d, ResampleArgs& a, int64_t nb
   // otherwise one launch per key, each with its own compile-time spec
   ResampleArgs one = a;
   one.n_keys = 1;
+  // a nearest key reads the same voxels in both modes, so its permutations
+  // take the row-copy kernel in the exact mode too
+  const bool perm = perm_chunk(a, nb);
   for (int i = 0; i < a.n_keys; ++i) {
     one.keys[0] = a.keys[i];
+    if (perm && (!exact || one.keys[0].mode == BA_NEAREST) && perm_ok(one.keys[0]) &&
+        launch_perm(one, code(one.keys[0]), -1)) {
+      const ba_status s1 = check_launch("ba_resample3d");
+      if (s1 != BA_OK) return s1;
+      continue;
+    }
     if (stageable(one.keys[0]) && launch_staged(one, code(one.keys[0]), -1)) {
       const ba_status s1 = check_launch("ba_resample3d");
       if (s1 != BA_OK) return s1;

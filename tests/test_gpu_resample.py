@@ -277,3 +277,54 @@ def test_host_params_chunks_equal_device_params(ba, mode):
     assert torch.equal(host, dev)
     keep = ~torch.from_numpy(mask).cuda()
     assert torch.equal(host[keep], x[keep])  # masked-out elements copied
+
+
+def _signed_perm_affines(rng, B, square=True):
+    """Products of axis flips and (H, W)-plane rot90s (the maps a Compose of
+    RandAxisFlip / RandRotate90 accumulates), MONAI convention."""
+    out = np.zeros((B, 4, 4), np.float32)
+    for b in range(B):
+        a = np.eye(4, dtype=np.float32)
+        for ax in range(3):
+            if rng.random() < 0.5:
+                f = np.eye(4, dtype=np.float32)
+                f[ax, ax] = -1
+                a = a @ f
+        if square and rng.random() < 0.7:
+            k = int(rng.integers(1, 4))
+            c, s = [0.0, -1.0, 0.0][k - 1], [-1.0, 0.0, 1.0][k - 1]
+            r = np.eye(4, dtype=np.float32)
+            r[0, 0], r[0, 1], r[1, 0], r[1, 1] = c, -s, s, c
+            a = a @ r
+        out[b] = a
+    return out
+
+
+@pytest.mark.parametrize("shape", [(3, 2, 16, 16, 32), (2, 3, 12, 12, 20), (4, 1, 9, 9, 8),
+                                   (2, 2, 10, 14, 12), (2, 1, 8, 8, 13)])
+@pytest.mark.parametrize("dt", [np.float32, "bf16"])
+@pytest.mark.parametrize("pad", ["zeros", "border"])
+def test_signed_permutations_vs_oracle(ba, oracle_lib, shape, dt, pad):
+    """Flips and rot90s (the row-copy kernel in fast mode when D % 4 == 0
+    and the rotated plane is square; the general kernels otherwise): a
+    bilinear key with a nearest label key in one launch, masked elements,
+    against the oracle."""
+    from batchaug_b200 import ops
+    rng = np.random.default_rng(sum(shape))
+    B = shape[0]
+    x = rng.standard_normal(shape).astype(np.float32)
+    if dt == "bf16":
+        x = oracle_lib.to_bf16_bits(x)
+    seg = rng.integers(0, 7, shape).astype(np.float32)
+    A = _signed_perm_affines(rng, B, square=shape[2] == shape[3])
+    mask = rng.random(B) < 0.8
+    mask[0] = True
+    vo, so = ops.resample3d([to_dev(x), to_dev(seg)], affine=A, modes=["bilinear", "nearest"],
+                            paddings=pad, mask=mask)
+    ref = oracle_lib.resample3d(x, affine=A, mode="bilinear", padding=pad, mask=mask)
+    ref_seg = oracle_lib.resample3d(seg, affine=A, mode="nearest", padding=pad, mask=mask)
+    _check(to_np(vo), ref, False)
+    assert np.array_equal(to_np(so), ref_seg)
+    # nearest alone (an eager flip / rot90) is an exact voxel permutation
+    n1 = ops.resample3d(to_dev(seg), affine=A, modes="nearest", paddings=pad, mask=mask)
+    assert np.array_equal(to_np(n1), ref_seg)
