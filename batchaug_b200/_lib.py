@@ -114,6 +114,7 @@ SIGNATURES = {
     "ba_last_error": (ctypes.c_char_p, []),
     "ba_version": (_I32, []),
     "ba_kernel_launches": (ctypes.c_uint64, []),
+    "ba_wait_status": (_I32, [_P]),
 }
 
 
@@ -156,6 +157,13 @@ def dtype_code(t: torch.Tensor) -> int:
 def kernel_launches() -> int:
     """Kernels the library has enqueued in this process so far."""
     return int(lib.ba_kernel_launches())
+
+
+def wait_status(device: torch.device | None = None) -> None:
+    """Synchronise the current stream and raise if any bounded device wait
+    of the library (the TMA-staged resample's mbarrier waits) ran out."""
+    dev = torch.device("cuda") if device is None else device
+    check(lib.ba_wait_status(stream_ptr(dev)), "ba_wait_status")
 
 
 def stream_ptr(device: torch.device) -> int:

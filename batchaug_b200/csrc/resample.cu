@@ -28,10 +28,13 @@
 // unnormalise / clip / reflect / trilinear steps round exactly where torch's
 // scalar code rounds (this file is compiled with -fmad=false; fused or packed
 // operations appear only where written explicitly).
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <stdio.h>
 #include <string.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "ba_common.cuh"
 
@@ -1356,20 +1359,6 @@ __device__ __forceinline__ void perm_rows_fast(const ResampleArgs& a, int64_t b,
   }
 }
 
-// A voxel whose lane does not fill an aligned chunk: the fast kernel's lerps
-// over its 8 taps, bounds-checked, zero outside the volume.  Not reached by
-// the signed permutations the host selects; kept out of line.
-template <int DT>
-__device__ __noinline__ float perm_interp(const char* cs, PermAxis ax, PermAxis ay, PermAxis az,
-                                          int H, int W, int D) {
-  const int x0 = ax.lo, y0 = ay.lo, z0 = az.lo;
-  float va[8];
-  const bool interior = (unsigned)x0 < (unsigned)(D - 1) && (unsigned)y0 < (unsigned)(W - 1) &&
-                        (unsigned)z0 < (unsigned)(H - 1);
-  taps8<DT>(cs, x0, y0, z0, H, W, D, interior, va);
-  return trilerp2(va, va, f2(ax.frac), f2(ay.frac), f2(az.frac)).x;
-}
-
 // One key, one channel, one output row off voxel centres along y or z (a
 // coordinate a few ulp from an integer: a few rows per volume), or lanes
 // whose voxels do not fill aligned chunks: the 2 or 4 source rows around it
@@ -1565,6 +1554,424 @@ __global__ void __launch_bounds__(PM_THREADS, 2) resample3d_perm_kernel(const __
         perm_rows_slow<S0, S1, R>(a, b, H, W, D, row0 + wr, nr, d, act, xok, px, s_y + wr,
                                   s_z + wr, s_x + (act ? d : 0));
     }
+  }
+}
+
+// ===========================================================================
+// TMA-staged signed-permutation resample: the default for signed-permutation
+// launches whose H, W and D are at most PT_MAX_DIM (one tensor-map box spans
+// a whole D row).  The output is cut into tiles of PT_TR x PT_TR (h, w) rows
+// by the whole D extent.  A signed permutation maps a tile's rows onto a
+// PT_TR x PT_TR block of source rows, which one cp.async.bulk.tensor load per
+// (key, channel) copies into a shared-memory stage (zero-filled outside the
+// volume).  A producer warp keeps PT_STAGES loads in flight on mbarriers; four
+// consumer warps write the output rows from the stage as 16-byte (fp32) /
+// 8-byte (bf16) vectors, reversed for a flip along D.  Voxels off a voxel
+// centre take resample3d_perm_kernel's arithmetic: along x, a lerp with the
+// neighbouring voxel of the staged row; rows off a centre along y or z (a
+// plane or two per element) read their 2 or 4 source rows from global
+// memory.  Masked-out elements are the identity copy.  All keys of the launch
+// (any mix of modes and dtypes with one padding) go through one launch.
+// Every mbarrier wait is bounded (PT_WAIT_NS): a wait that runs out records
+// it in g_wait_timeouts (read by ba_wait_status) and the CTA stops, its
+// producer first waiting, again bounded, for the loads it issued.
+// ===========================================================================
+constexpr int PT_TR = 4;                          // tile rows along h and w
+constexpr int PT_ROWS = PT_TR * PT_TR;            // output rows per tile
+constexpr int PT_CWARPS = 4;                      // consumer warps
+constexpr int PT_THREADS = (PT_CWARPS + 1) * 32;  // + the producer warp
+constexpr int PT_STAGES = 4;
+constexpr int PT_MAX_DIM = 256;  // tensor-map box extent limit; also the tables
+constexpr unsigned long long PT_WAIT_NS = 2000000000ull;
+
+// Bounded device waits that ran out (any kernel of this file); read and
+// cleared by ba_wait_status.
+__device__ unsigned int g_wait_timeouts;
+
+struct PermTmaArgs {
+  CUtensorMap maps[BA_MAX_KEYS];  // key k's (B * C, H, W, D) source, box (1, PT_TR, PT_TR, D)
+  ResampleArgs r;
+  int32_t stage_bytes;  // one stage: the largest key's box
+};
+
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+  return (unsigned)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// true once the barrier's phase of parity `parity` has completed; the
+// thread may be suspended in the instruction until then, for at most
+// PT_SUSPEND_NS (so waiting warps do not spin through issue slots)
+constexpr unsigned PT_SUSPEND_NS = 1000000u;
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, unsigned parity) {
+  unsigned done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(PT_SUSPEND_NS)
+      : "memory");
+  return done != 0;
+}
+
+// mbar_test until it succeeds or PT_WAIT_NS pass; false when the time ran out
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+  if (mbar_test(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_test(bar, parity))
+    if (global_ns() - t0 > PT_WAIT_NS) return false;
+  return true;
+}
+
+// One box of a 4-D tensor map into shared memory, completing on `bar`.  The
+// innermost coordinate is always 0 here (16-byte aligned), the others may lie
+// outside the tensor (those elements read as zero).
+__device__ __forceinline__ void tma_load4(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                          int w, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <int DT>
+__device__ __forceinline__ void lds4(const unsigned char* row, int x, float* v) {
+  if (DT == BA_BF16) {
+    const uint2 u = *reinterpret_cast<const uint2*>(row + 2 * x);
+    v[0] = __uint_as_float(u.x << 16);
+    v[1] = __uint_as_float(u.x & 0xFFFF0000u);
+    v[2] = __uint_as_float(u.y << 16);
+    v[3] = __uint_as_float(u.y & 0xFFFF0000u);
+  } else {
+    const float4 f = *reinterpret_cast<const float4*>(row + 4 * x);
+    v[0] = f.x;
+    v[1] = f.y;
+    v[2] = f.z;
+    v[3] = f.w;
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ float lds1(const unsigned char* row, int x) {
+  if (DT == BA_BF16)
+    return __uint_as_float((uint32_t)(*reinterpret_cast<const uint16_t*>(row + 2 * x)) << 16);
+  return *reinterpret_cast<const float*>(row + 4 * x);
+}
+
+// Where a tile's source rows start along source axis y or z: the smaller of
+// the nearest indices of the tile's first and last rows along the output axis
+// driving it (the permutation is monotone along that axis).
+__device__ __forceinline__ int permt_box_start(const PermAxis* tab, int o0, int n) {
+  const int last = min(o0 + PT_TR - 1, n - 1);
+  return min(tab[o0].near, tab[last].near);
+}
+
+// Rows a consumer warp writes for each tile: rows r = warp + PT_CWARPS * i
+// of the tile, i < PT_RPW.
+constexpr int PT_RPW = PT_ROWS / PT_CWARPS;
+
+// A lane's 4 voxels d .. d+3 of one output row, copied from the staged
+// source row: the chunk's bits as they are (a copy keeps NaN payloads),
+// reversed for a flip along x.
+template <int DT>
+__device__ __forceinline__ void permt_chunk(const unsigned char* srow, char* cd, int o,
+                                            const PermX& x) {
+  if (DT == BA_BF16) {
+    uint2 u = *reinterpret_cast<const uint2*>(srow + 2 * x.base);
+    if (x.rev) u = make_uint2(__byte_perm(u.y, 0, 0x1032), __byte_perm(u.x, 0, 0x1032));
+    *reinterpret_cast<uint2*>(cd + 2 * (int64_t)o) = u;
+  } else {
+    uint4 u = *reinterpret_cast<const uint4*>(srow + 4 * x.base);
+    if (x.rev) u = make_uint4(u.w, u.z, u.y, u.x);
+    *reinterpret_cast<uint4*>(cd + 4 * (int64_t)o) = u;
+  }
+}
+
+// One consumer warp's rows of a tile, one key and channel, from the stage.
+// The warp writes output column ow = w0 + warp of the tile, rows
+// oh = h0 + i (i < PT_RPW), the i-th starting at orow0 + i * W * D.  srow[i]
+// packs the stage row for a nearest key (low byte) and for a bilinear key
+// (second byte): 0..PT_ROWS-1, PT_GLOBAL for the global-memory path, PT_NONE
+// where the tile has no output row.  PT_GLOBAL rows are left to
+// permt_fixups.
+constexpr int PT_GLOBAL = 0xFF, PT_NONE = 0xFE;
+
+template <int DT>
+__device__ __forceinline__ float permt_tap(const unsigned char* srow, int x, int D) {
+  return (unsigned)x < (unsigned)D ? lds1<DT>(srow, x) : 0.0f;
+}
+
+// A bilinear key's voxels of the chunk off a centre along x (one position
+// per row): the fast kernel's lerp fma(f, hi - lo, lo) over the two source
+// voxels of the staged row (zero outside the volume; trilerp2's lerps along y
+// and z at fraction 0 return it unchanged), stored over the copied value.
+template <int DT>
+__device__ __forceinline__ void permt_xfix(const unsigned char* srow, char* cd, int o, int D,
+                                           const PermAxis* sx) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const PermAxis ax = sx[j];
+    if (ax.frac != 0.0f) {
+      const float lo = permt_tap<DT>(srow, ax.lo, D), hi = permt_tap<DT>(srow, ax.lo + 1, D);
+      st<DT>(cd, o + j, __fmaf_rn(ax.frac, __fsub_rn(hi, lo), lo));
+    }
+  }
+}
+
+template <int MODE, int DT>
+__device__ __forceinline__ void permt_rows(const KeyArgs& k, int64_t b, int c, int H, int W,
+                                           int D, const unsigned char* stage, const int* srow,
+                                           int orow0, const PermX& x0, const PermX& x1,
+                                           const PermAxis* s_x, int lane) {
+  constexpr int esz = DT == BA_BF16 ? 2 : 4;
+  char* cd = (char*)k.dst + ((size_t)b * k.channels + c) * ((size_t)H * W * D) * esz;
+  const int d0 = 4 * lane, d1 = d0 + 128, plane = W * D;
+#pragma unroll
+  for (int i = 0; i < PT_RPW; ++i) {
+    const int sr = MODE == BA_NEAREST ? (srow[i] & 0xFF) : ((srow[i] >> 8) & 0xFF);
+    if (sr < PT_ROWS) {
+      const unsigned char* st = stage + sr * D * esz;
+      const int o = orow0 + i * plane;
+      if (d0 < D) {
+        permt_chunk<DT>(st, cd, o + d0, x0);
+        if (MODE != BA_NEAREST && x0.off) permt_xfix<DT>(st, cd, o + d0, D, s_x + d0);
+      }
+      if (d1 < D) {
+        permt_chunk<DT>(st, cd, o + d1, x1);
+        if (MODE != BA_NEAREST && x1.off) permt_xfix<DT>(st, cd, o + d1, D, s_x + d1);
+      }
+    }
+  }
+}
+
+// After a tile's staged items: the warp's rows and chunks the stage did not
+// serve, for every key and channel, by resample3d_perm_kernel's
+// global-memory path: PT_GLOBAL rows (a bilinear key's rows off a voxel
+// centre along y or z, a plane or two per element; rows outside the staged
+// block).  Out of line, so the staged loop keeps its registers.
+template <int PAD>
+__device__ __forceinline__ void permt_fixups(const ResampleArgs& a, int64_t b, const int* srow,
+                                          int orow0, int h0, int ow, int yc, int zc,
+                                          const PermAxis* s_x, const PermAxis* s_y,
+                                          const PermAxis* s_z, PermX x0, PermX x1, int lane) {
+  const int H = a.H, W = a.W, D = a.D, plane = W * D;
+  const int d0 = 4 * lane, d1 = d0 + 128;
+  for (int i = 0; i < PT_RPW; ++i) {
+    const int sn = srow[i] & 0xFF, sb = (srow[i] >> 8) & 0xFF;
+    if (sn == PT_NONE) continue;
+    const int oh = h0 + i, o = orow0 + i * plane;
+    const PermAxis ay = s_y[yc == 1 ? ow : oh], az = s_z[zc == 1 ? ow : oh];
+    for (int ki = 0; ki < a.n_keys; ++ki) {
+      const KeyArgs& k = a.keys[ki];
+      const bool nearest = k.mode == BA_NEAREST;
+      if ((nearest ? sn : sb) != PT_GLOBAL) continue;
+      const bool l0 = d0 < D, l1 = d1 < D;
+      const int esz = k.dtype == BA_BF16 ? 2 : 4;
+      for (int c = 0; c < k.channels; ++c) {
+        const size_t coff = ((size_t)b * k.channels + c) * ((size_t)H * W * D) * esz;
+        const char* cs = (const char*)k.src + coff;
+        char* cd = (char*)k.dst + coff;
+        switch (k.mode * 2 + k.dtype) {
+#define BA_PT_FIX(M, T)                                                                       \
+  case M * 2 + T:                                                                             \
+    if (l0) perm_row_slow<spec_code(M, PAD, T)>(cs, cd, H, W, D, o + d0, true, x0.base >= 0, \
+                                                x0, ay, az, s_x + d0);                        \
+    if (l1) perm_row_slow<spec_code(M, PAD, T)>(cs, cd, H, W, D, o + d1, true, x1.base >= 0, \
+                                                x1, ay, az, s_x + d1);                        \
+    break;
+          BA_PT_FIX(BA_BILINEAR, BA_F32)
+          BA_PT_FIX(BA_BILINEAR, BA_BF16)
+          BA_PT_FIX(BA_NEAREST, BA_F32)
+          BA_PT_FIX(BA_NEAREST, BA_BF16)
+#undef BA_PT_FIX
+          default:
+            break;
+        }
+      }
+    }
+  }
+}
+
+template <int PAD>
+__global__ void __launch_bounds__(PT_THREADS, 4)
+    resample3d_permt_kernel(const __grid_constant__ PermTmaArgs p) {
+  extern __shared__ __align__(128) unsigned char pt_stage[];
+  __shared__ PermAxis s_x[PT_MAX_DIM], s_y[PT_MAX_DIM], s_z[PT_MAX_DIM];
+  __shared__ __align__(8) uint64_t full[PT_STAGES], empty[PT_STAGES];
+  __shared__ float s_th[12];
+  const ResampleArgs& a = p.r;
+  const bool ALIGN = a.align_corners != 0;
+  const int H = a.H, W = a.W, D = a.D;
+  const int64_t b = a.b0 + blockIdx.y;
+  const bool act = elem_active(a, b);
+  const int t = threadIdx.x, warp = t / 32, lane = t % 32;
+  if (t < 12) {
+    const int i = t / 4, j = t % 4;
+    const float* x = elem_xform(a, b);
+    if (a.xform_kind == BA_XFORM_AFFINE) {
+      // monai_affine_to_theta: theta = P S_norm A S_inv P, P swapping 0 and 2.
+      const int pi = 2 - i, pj = (j == 3) ? 3 : 2 - j;
+      const float s_j = (pj == 3) ? 1.0f : a.si[pj];
+      s_th[t] = (a.sn[pi] * x[pi * 4 + pj]) * s_j;
+    } else {
+      s_th[t] = x[i * 4 + j];
+    }
+  } else if (t == 32) {
+    for (int i = 0; i < PT_STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], PT_CWARPS);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  // the output axis (0: d, 1: w, 2: h) driving source axis r, and its sign;
+  // a masked-out element is the identity copy
+  int col[3];
+  float sgn[3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    col[r] = s_th[r * 4] != 0.0f ? 0 : (s_th[r * 4 + 1] != 0.0f ? 1 : 2);
+    sgn[r] = s_th[r * 4 + col[r]];
+  }
+  const int yc = act ? col[1] : 1, zc = act ? col[2] : 2;
+  const int ny = yc == 1 ? W : H, nz = zc == 1 ? W : H;
+  for (int i = t; i < D; i += PT_THREADS)
+    s_x[i] = act ? perm_axis<PAD>(perm_coord(i, D, sgn[0], s_th[3], D, ALIGN), D)
+                 : PermAxis{i, 0.0f, i};
+  for (int i = t; i < ny; i += PT_THREADS)
+    s_y[i] = act ? perm_axis<PAD>(perm_coord(i, ny, sgn[1], s_th[7], W, ALIGN), W)
+                 : PermAxis{i, 0.0f, i};
+  for (int i = t; i < nz; i += PT_THREADS)
+    s_z[i] = act ? perm_axis<PAD>(perm_coord(i, nz, sgn[2], s_th[11], H, ALIGN), H)
+                 : PermAxis{i, 0.0f, i};
+  __syncthreads();
+  const int ntw = (W + PT_TR - 1) / PT_TR;
+  const int ntiles = ((H + PT_TR - 1) / PT_TR) * ntw;
+  if (warp == PT_CWARPS) {
+    // producer: one lane issues every load of the CTA's items in order
+    if (lane != 0) return;
+    int last_round[PT_STAGES];
+#pragma unroll
+    for (int s = 0; s < PT_STAGES; ++s) last_round[s] = -1;
+    bool ok = true;
+    int j = 0;
+    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+      const int h0 = (tile / ntw) * PT_TR, w0 = (tile % ntw) * PT_TR;
+      const int ys = permt_box_start(s_y, yc == 1 ? w0 : h0, ny);
+      const int zs = permt_box_start(s_z, zc == 1 ? w0 : h0, nz);
+      for (int ki = 0; ok && ki < a.n_keys; ++ki) {
+        const KeyArgs& k = a.keys[ki];
+        const unsigned bytes = (unsigned)(D * PT_ROWS * (k.dtype == BA_BF16 ? 2 : 4));
+        for (int c = 0; c < k.channels; ++c, ++j) {
+          const int s = j % PT_STAGES, round = j / PT_STAGES;
+          if (!mbar_wait(&empty[s], (unsigned)(round & 1) ^ 1u)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[s], bytes);
+          tma_load4(pt_stage + (size_t)s * p.stage_bytes, &p.maps[ki], 0, ys, zs,
+                    (int)(b * k.channels + c), &full[s]);
+          last_round[s] = round;
+        }
+      }
+    }
+    if (!ok) atomicOr(&g_wait_timeouts, 1u);
+    // every issued load lands before the CTA may exit
+    for (int s = 0; s < PT_STAGES; ++s)
+      if (last_round[s] >= 0 && !mbar_wait(&full[s], (unsigned)(last_round[s] & 1)))
+        atomicOr(&g_wait_timeouts, 1u);
+    return;
+  }
+  // consumers: the x side of the lane's chunks d = 4 lane and 4 lane + 128,
+  // fixed for the element
+  const int d0 = 4 * lane, d1 = d0 + 128;
+  const PermX x0 = perm_x(s_x + (d0 < D ? d0 : 0), D);
+  const PermX x1 = perm_x(s_x + (d1 < D ? d1 : 0), D);
+  const bool xok =
+      __all_sync(0xFFFFFFFFu, (d0 >= D || x0.base >= 0) && (d1 >= D || x1.base >= 0));
+  int j = 0;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int h0 = (tile / ntw) * PT_TR, w0 = (tile % ntw) * PT_TR;
+    const int ys = permt_box_start(s_y, yc == 1 ? w0 : h0, ny);
+    const int zs = permt_box_start(s_z, zc == 1 ? w0 : h0, nz);
+    // the warp's rows of this tile (column ow, rows h0 + i), for nearest and
+    // for bilinear keys
+    const int ow = w0 + warp;
+    const int orow0 = (h0 * W + ow) * D;
+    int srow[PT_RPW];
+    bool fix = false;  // a row for permt_fixups (warp-uniform)
+#pragma unroll
+    for (int i = 0; i < PT_RPW; ++i) {
+      const int oh = h0 + i;
+      srow[i] = PT_NONE | (PT_NONE << 8);
+      if (oh < H && ow < W) {
+        const PermAxis ay = s_y[yc == 1 ? ow : oh], az = s_z[zc == 1 ? ow : oh];
+        const int nyr = ay.near - ys, nzr = az.near - zs;
+        const int lyr = ay.lo - ys, lzr = az.lo - zs;
+        const int sn = xok && (unsigned)nyr < (unsigned)PT_TR && (unsigned)nzr < (unsigned)PT_TR
+                           ? nzr * PT_TR + nyr
+                           : PT_GLOBAL;
+        const int sb = xok && ay.frac == 0.0f && az.frac == 0.0f &&
+                               (unsigned)lyr < (unsigned)PT_TR && (unsigned)lzr < (unsigned)PT_TR
+                           ? lzr * PT_TR + lyr
+                           : PT_GLOBAL;
+        srow[i] = sn | (sb << 8);
+        fix = fix || sn == PT_GLOBAL || sb == PT_GLOBAL;
+      }
+    }
+    for (int ki = 0; ki < a.n_keys; ++ki) {
+      const KeyArgs& k = a.keys[ki];
+      for (int c = 0; c < k.channels; ++c, ++j) {
+        const int s = j % PT_STAGES, round = j / PT_STAGES;
+        const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&full[s], (unsigned)(round & 1)));
+        if (!ok) {
+          if (lane == 0) atomicOr(&g_wait_timeouts, 1u);
+          return;
+        }
+        const unsigned char* stage = pt_stage + (size_t)s * p.stage_bytes;
+        switch (k.mode * 2 + k.dtype) {
+          case BA_BILINEAR * 2 + BA_F32:
+            permt_rows<BA_BILINEAR, BA_F32>(k, b, c, H, W, D, stage, srow, orow0, x0, x1, s_x, lane);
+            break;
+          case BA_BILINEAR * 2 + BA_BF16:
+            permt_rows<BA_BILINEAR, BA_BF16>(k, b, c, H, W, D, stage, srow, orow0, x0, x1, s_x, lane);
+            break;
+          case BA_NEAREST * 2 + BA_F32:
+            permt_rows<BA_NEAREST, BA_F32>(k, b, c, H, W, D, stage, srow, orow0, x0, x1, s_x, lane);
+            break;
+          case BA_NEAREST * 2 + BA_BF16:
+            permt_rows<BA_NEAREST, BA_BF16>(k, b, c, H, W, D, stage, srow, orow0, x0, x1, s_x, lane);
+            break;
+          default:
+            break;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+    }
+    if (fix) permt_fixups<PAD>(a, b, srow, orow0, h0, ow, yc, zc, s_x, s_y, s_z, x0, x1, lane);
   }
 }
 
@@ -1957,9 +2364,143 @@ bool perm_chunk(const ResampleArgs& a, int64_t nb) {
   return true;
 }
 
+// cuTensorMapEncodeTiled from the driver the runtime loaded (no link-time
+// dependency on libcuda); null when the driver does not provide it.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+// Tensor maps of recent sources (a map depends only on the address, dtype
+// and shape, so a cached one stays valid for any buffer at that address and
+// shape): a Compose step resamples the same pipeline buffers every call, and
+// encoding costs a driver call per key.  `make` encodes a missing one.
+template <class F>
+bool cached_tensor_map(const void* src, int dtype, const cuuint64_t* dims, F make,
+                       CUtensorMap* out) {
+  struct Entry {
+    const void* src;
+    int dtype;
+    cuuint64_t dims[4];
+    int dev;
+    CUtensorMap map;
+  };
+  static std::mutex mu;
+  static Entry cache[16];
+  static int used = 0, next = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> g(mu);
+    for (int i = 0; i < used; ++i) {
+      const Entry& e = cache[i];
+      if (e.src == src && e.dtype == dtype && e.dev == dev &&
+          memcmp(e.dims, dims, sizeof(e.dims)) == 0) {
+        *out = e.map;
+        return true;
+      }
+    }
+  }
+  if (!make(out)) return false;
+  std::lock_guard<std::mutex> g(mu);
+  Entry& e = cache[next];
+  e.src = src;
+  e.dtype = dtype;
+  memcpy(e.dims, dims, sizeof(e.dims));
+  e.dev = dev;
+  e.map = *out;
+  next = (next + 1) % 16;
+  used = std::max(used, next == 0 ? 16 : next);
+  return true;
+}
+
+// The TMA-staged permutation kernel for a launch whose active elements are
+// all signed permutations (perm_chunk), when every key qualifies: one
+// padding (zeros or border) for all keys, bilinear keys only outside the
+// exact mode, H, W, D <= PT_MAX_DIM, rows a multiple of 16 bytes, 16-byte
+// aligned tensors.  Returns false (nothing launched) otherwise.
+bool launch_perm_tma(const ba_resample_desc& d, const ResampleArgs& a, int64_t nb, bool exact,
+                     cudaStream_t st) {
+  if (!a.inline_params || a.xform_kind == BA_XFORM_GRID) return false;
+  if (d.D > PT_MAX_DIM || d.H > PT_MAX_DIM || d.W > PT_MAX_DIM) return false;
+  const int pad = a.keys[0].padding;
+  if (pad == BA_PAD_REFLECTION) return false;
+  int stage_bytes = 0;
+  for (int i = 0; i < a.n_keys; ++i) {
+    const KeyArgs& k = a.keys[i];
+    const int esz = k.dtype == BA_BF16 ? 2 : 4;
+    if (k.padding != pad || (exact && k.mode != BA_NEAREST)) return false;
+    if ((d.D * esz) % 16 != 0 || ((uintptr_t)k.src % 16) != 0 || ((uintptr_t)k.dst % 16) != 0)
+      return false;
+    if (d.batch * k.channels > INT32_MAX) return false;
+    stage_bytes = std::max(stage_bytes, (int)d.D * PT_ROWS * esz);
+  }
+  if (!perm_chunk(a, nb)) return false;
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (encode == nullptr) return false;
+  PermTmaArgs p;
+  memset(&p, 0, sizeof(p));
+  for (int i = 0; i < a.n_keys; ++i) {
+    const KeyArgs& k = a.keys[i];
+    if (k.channels == 0) continue;  // no items: the map is never read
+    const cuuint64_t esz = k.dtype == BA_BF16 ? 2 : 4;
+    const cuuint64_t dims[4] = {(cuuint64_t)d.D, (cuuint64_t)d.W, (cuuint64_t)d.H,
+                                (cuuint64_t)(d.batch * k.channels)};
+    const cuuint64_t strides[3] = {(cuuint64_t)d.D * esz, (cuuint64_t)(d.W * d.D) * esz,
+                                   (cuuint64_t)(d.H * d.W * d.D) * esz};
+    const cuuint32_t box[4] = {(cuuint32_t)d.D, PT_TR, PT_TR, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    if (!cached_tensor_map(k.src, k.dtype, dims, [&](CUtensorMap* m) {
+          return encode(m,
+                        k.dtype == BA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                        4, const_cast<void*>(k.src), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        }, &p.maps[i]))
+      return false;
+  }
+  p.r = a;
+  p.stage_bytes = stage_bytes;
+  const int smem = PT_STAGES * stage_bytes;
+  const int64_t ntiles = ((d.H + PT_TR - 1) / PT_TR) * ((d.W + PT_TR - 1) / PT_TR);
+  // about four CTAs per SM over the launch's elements, each walking tiles
+  const int64_t per_elem = std::max<int64_t>(1, (4 * (int64_t)sm_count_rs() + nb - 1) / nb);
+  const dim3 grid((unsigned)std::min<int64_t>(ntiles, per_elem), (unsigned)nb);
+  static int opted[2] = {0, 0};  // dynamic shared memory each instantiation allows
+  int& o = opted[pad == BA_PAD_BORDER];
+  if (smem > 48 * 1024 && smem > o) {
+    if (pad == BA_PAD_BORDER)
+      cudaFuncSetAttribute(resample3d_permt_kernel<BA_PAD_BORDER>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    else
+      cudaFuncSetAttribute(resample3d_permt_kernel<BA_PAD_ZEROS>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    o = smem;
+  }
+  if (pad == BA_PAD_BORDER)
+    resample3d_permt_kernel<BA_PAD_BORDER><<<grid, PT_THREADS, smem, st>>>(p);
+  else
+    resample3d_permt_kernel<BA_PAD_ZEROS><<<grid, PT_THREADS, smem, st>>>(p);
+  return true;
+}
+
 // Launches of one resample over elements a.b0 .. a.b0 + nb - 1: the kernel
-// each key group takes (staged / fast for affine maps with a bilinear key,
-// grid kernel for grid maps, global-gather kernel otherwise).
+// each key group takes (TMA-staged row copies for signed permutations,
+// staged / fast for affine maps with a bilinear key, grid kernel for grid
+// maps, global-gather kernel otherwise).
 ba_status launch_resample(const ba_resample_desc& d, ResampleArgs& a, int64_t nb,
                           cudaStream_t st) {
   const int64_t hwd = d.H * d.W * d.D;
@@ -2050,6 +2591,8 @@ ba_status launch_resample(const ba_resample_desc& d, ResampleArgs& a, int64_t nb
         return false;
     }
   };
+  // Signed permutations of every key in one TMA-staged launch.
+  if (launch_perm_tma(d, a, nb, exact, st)) return check_launch("ba_resample3d");
   // Grid maps take the lane-per-voxel grid kernel.
   const bool grid4 = a.xform_kind == BA_XFORM_GRID;
   const dim3 g4_grid((unsigned)((hwd + G4_THREADS * G4_VOX - 1) / (G4_THREADS * G4_VOX)),
@@ -2245,4 +2788,26 @@ extern "C" ba_status ba_compose_field(const float* field, const float* theta,
   compose_field_kernel<<<g, 256, 0, (cudaStream_t)stream>>>(field, theta, mask_field, mask_affine,
                                                           (int)H, (int)W, (int)D, grid);
   return check_launch("ba_compose_field");
+}
+
+extern "C" ba_status ba_wait_status(ba_stream_t stream) {
+  using namespace ba;
+  clear_error();
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) {
+    set_error("ba_wait_status: %s", cudaGetErrorString(e));
+    return BA_ECUDA;
+  }
+  unsigned int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v));
+  if (e != cudaSuccess) {
+    set_error("ba_wait_status: %s", cudaGetErrorString(e));
+    return BA_ECUDA;
+  }
+  if (v == 0) return BA_OK;
+  const unsigned int zero = 0;
+  cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(zero));
+  set_error("ba_wait_status: a bounded device wait ran out of time; the output of the kernel "
+            "that recorded it is incomplete");
+  return BA_ETIMEOUT;
 }

@@ -252,7 +252,7 @@ class RandAxisFlip(BatchTransform):
     def apply(self, tensor, params):
         # An exact voxel permutation: the nearest resample of the flip affine.
         return ops.resample3d(tensor, affine=self.host_affine(params), modes="nearest",
-                              mask=params["mask"])
+                              mask=_host_mask(params))
 
 
 class RandFlip(BatchTransform):
@@ -282,7 +282,7 @@ class RandFlip(BatchTransform):
 
     def apply(self, tensor, params):
         return ops.resample3d(tensor, affine=self.host_affine(params), modes="nearest",
-                              mask=params["mask"])
+                              mask=_host_mask(params))
 
 
 class RandRotate90(BatchTransform):
@@ -330,10 +330,10 @@ class RandRotate90(BatchTransform):
         if tensor.shape[ax[0]] == tensor.shape[ax[1]]:
             # square plane: torch.rot90 is an exact voxel permutation
             return ops.resample3d(tensor, affine=self.host_affine(params), modes="nearest",
-                                  mask=params["mask"])
+                                  mask=_host_mask(params))
         # non-square plane: the reference's bilinear/zeros grid_sample fallback
         return ops.resample3d(tensor, affine=self.host_affine(params), modes="bilinear",
-                              paddings="zeros", mask=params["mask"])
+                              paddings="zeros", mask=_host_mask(params))
 
 
 class Rand3DElastic(BatchTransform):
@@ -388,6 +388,16 @@ class Rand3DElastic(BatchTransform):
         one launch reading the grid once."""
         return ops.resample3d(list(tensors), grid=params["grid"], mask=params["mask"],
                               modes=list(modes), paddings=list(paddings), align_corners=True)
+
+
+def _host_mask(params: dict) -> np.ndarray:
+    """The params' mask on the host: the copy sample_params keeps, else a
+    device read of an injected mask.  A host mask (with a host transform)
+    travels in the resample's kernel parameters."""
+    if "_host" in params and "mask" in params["_host"]:
+        return np.asarray(params["_host"]["mask"])
+    m = params["mask"]
+    return m.detach().cpu().numpy() if isinstance(m, torch.Tensor) else np.asarray(m)
 
 
 def _to_host(params: dict, keys) -> dict:

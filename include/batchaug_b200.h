@@ -419,6 +419,14 @@ BA_API int32_t ba_version(void);
  * host-side counter, incremented after each successful launch). */
 BA_API uint64_t ba_kernel_launches(void);
 
+/* Status of the library's bounded device waits (the mbarrier waits of the
+ * TMA-staged resample; each gives up after 2 s).  Synchronises `stream`,
+ * then returns BA_ETIMEOUT, and clears the record, if any wait of any
+ * earlier launch on this device ran out of time (that launch's output is
+ * incomplete), else BA_OK.  The only entry point that synchronises the host.
+ * No reference counterpart (library housekeeping). */
+BA_API ba_status ba_wait_status(ba_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -328,3 +328,55 @@ def test_signed_permutations_vs_oracle(ba, oracle_lib, shape, dt, pad):
     # nearest alone (an eager flip / rot90) is an exact voxel permutation
     n1 = ops.resample3d(to_dev(seg), affine=A, modes="nearest", paddings=pad, mask=mask)
     assert np.array_equal(to_np(n1), ref_seg)
+
+
+@pytest.mark.parametrize("shape", [(2, 2, 12, 12, 16), (3, 1, 8, 8, 256), (2, 1, 7, 7, 40),
+                                   (5, 2, 20, 20, 24)])
+@pytest.mark.parametrize("pad", ["zeros", "border"])
+def test_signed_permutations_tma_keys(ba, oracle_lib, shape, pad):
+    """The TMA-staged row copy (rows of 16-byte multiples, H, W, D <= 256):
+    three keys of mixed mode and dtype in one launch (an fp32 and a bf16
+    bilinear key, a bf16 label key), partial tiles, a D of 256 (two chunks
+    per lane), masked elements; then no bounded device wait ran out."""
+    from batchaug_b200 import _lib, ops
+    rng = np.random.default_rng(sum(shape) + 7)
+    B = shape[0]
+    x = rng.standard_normal(shape).astype(np.float32)
+    xb = oracle_lib.to_bf16_bits(rng.standard_normal(shape).astype(np.float32))
+    seg = oracle_lib.to_bf16_bits(rng.integers(0, 9, shape).astype(np.float32))
+    A = _signed_perm_affines(rng, B)
+    mask = rng.random(B) < 0.7
+    mask[0] = True
+    outs = ops.resample3d([to_dev(x), to_dev(xb), to_dev(seg)], affine=A,
+                          modes=["bilinear", "bilinear", "nearest"], paddings=pad, mask=mask)
+    _lib.wait_status()
+    for o, src, mode in zip(outs, (x, xb, seg), ("bilinear", "bilinear", "nearest")):
+        ref = oracle_lib.resample3d(src, affine=A, mode=mode, padding=pad, mask=mask)
+        _check(to_np(o), ref, mode == "nearest")
+
+
+def test_signed_permutation_copies_keep_bits(ba):
+    """Masked-out elements and nearest keys are bit copies: bf16 and fp32 NaN
+    payloads and negative zeros come through unchanged."""
+    from batchaug_b200 import ops
+    rng = np.random.default_rng(11)
+    B, C, H, W, D = 3, 2, 8, 8, 32
+    A = _signed_perm_affines(rng, B)
+    mask = np.array([True, False, True])
+    for dtype, nan_bits in ((torch.bfloat16, 0x7F85), (torch.float32, 0x7F800123)):
+        itype = np.int16 if dtype == torch.bfloat16 else np.int32
+        info = np.iinfo(itype)
+        nb = rng.integers(info.min, info.max, (B, C, H, W, D), dtype=itype, endpoint=True)
+        nb[..., 3] = nan_bits
+        nb[..., 5] = info.min  # -0.0
+        bits = torch.from_numpy(nb)
+        t = bits.view(dtype).cuda()
+        out = ops.resample3d(t, affine=A, modes="nearest", paddings="zeros", mask=mask)
+        got = out.view(bits.dtype).cpu()
+        assert torch.equal(got[1], bits[1])  # masked out: copied bit for bit
+        ref = ops.resample3d(t.float(), affine=A, modes="nearest", paddings="zeros", mask=mask)
+        fin = torch.isfinite(ref.cpu())
+        assert torch.equal(out.float().cpu()[fin], ref.cpu()[fin])
+        # every voxel of an active element is some source voxel's exact bits
+        for b in (0, 2):
+            assert torch.equal(torch.sort(got[b].flatten())[0], torch.sort(bits[b].flatten())[0])
