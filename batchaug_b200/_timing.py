@@ -10,6 +10,12 @@ kernels without a profiler::
         for _ in range(steps):
             pipeline(batch)
     per_entry = rec.summary()   # {name: {"launches", "ms_total", "ms_mean", "bytes"}}
+
+``lead_cycles`` > 0 puts a GPU busy-wait of that many clock cycles in front
+of every span's start event, so the host has enqueued the call's kernels
+before the device reaches the start event: the span then measures the
+kernels alone, not the host's launch latency (which a host-bound step would
+otherwise add to it).
 """
 from __future__ import annotations
 
@@ -19,8 +25,9 @@ _active = None
 
 
 class Recorder:
-    def __init__(self):
+    def __init__(self, lead_cycles: int = 0):
         self.spans = []  # (name, algorithmic bytes, start event, end event)
+        self.lead_cycles = int(lead_cycles)
 
     def __enter__(self):
         global _active
@@ -55,6 +62,9 @@ def begin(name: str, nbytes: int, device):
     if rec is None:
         return None
     stream = torch.cuda.current_stream(device)
+    if rec.lead_cycles > 0:
+        with torch.cuda.device(device):
+            torch.cuda._sleep(rec.lead_cycles)
     e0 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     return rec, name, nbytes, e0, stream

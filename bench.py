@@ -24,7 +24,8 @@ alternate between 2 distinct batches of 671 MB each (larger than the 126 MB
 L2).  ``value`` = voxels of all keys and ranks / max-over-ranks time.  Every
 library call is also bracketed by CUDA events
 (``batchaug_b200._timing``) in a second run of the same steps after the
-timed one; ``roofline`` is the dominant entry point's
+timed one, each span behind a short device busy-wait so that it holds the
+kernels alone and not the host's launch latency; ``roofline`` is the dominant entry point's
 algorithmic bytes per launch over its mean event-timed duration, and
 ``roofline_step`` the whole step's algorithmic bytes over the step time.
 ``e2e`` is the same step through the public API from pinned host memory:
@@ -499,9 +500,10 @@ def run_b200(args, wl: Workload):
     total_ms = start.elapsed_time(end)
     # attribution: the same steps again with every library call bracketed by
     # CUDA events (kept out of the timed loop above: recording events costs
-    # host time between launches)
+    # host time between launches), each span behind a ~75 us device busy-wait
+    # so it times the kernels, not the host's launch of them
     n_attr = max(1, min(args.steps, 20))
-    with _timing.Recorder() as rec:
+    with _timing.Recorder(lead_cycles=150_000) as rec:
         for i in range(n_attr):
             step(sets[i % len(sets)])
     barrier()

@@ -380,3 +380,25 @@ def test_signed_permutation_copies_keep_bits(ba):
         # every voxel of an active element is some source voxel's exact bits
         for b in (0, 2):
             assert torch.equal(torch.sort(got[b].flatten())[0], torch.sort(bits[b].flatten())[0])
+
+
+@pytest.mark.parametrize("zoom", [1.5, 1.7, 2.2])
+@pytest.mark.parametrize("pad", ["zeros", "border"])
+def test_large_footprints_vs_oracle(ba, oracle_lib, zoom, pad):
+    """Source footprints around and over the staging limit (a zoom-out of
+    1.5-2.2 with a rotation and shear): some tiles stage their box, the others
+    gather from global memory; partial tiles along every axis, two channels,
+    a label key in the same launch."""
+    from batchaug_b200 import ops
+    rng = np.random.default_rng(int(zoom * 10))
+    shape = (2, 2, 37, 48, 60)
+    x = rng.standard_normal(shape).astype(np.float32)
+    seg = rng.integers(0, 5, (2, 1) + shape[2:]).astype(np.float32)
+    A = _rand_affine(rng, 2, scale=False)
+    A[:, :3, :3] *= zoom
+    outs = ops.resample3d([to_dev(x), to_dev(seg)], affine=A, modes=["bilinear", "nearest"],
+                          paddings=pad)
+    ref = oracle_lib.resample3d(x, affine=A, mode="bilinear", padding=pad)
+    ref_seg = oracle_lib.resample3d(seg, affine=A, mode="nearest", padding=pad)
+    _check(to_np(outs[0]), ref, False)
+    assert np.array_equal(to_np(outs[1]), ref_seg)
