@@ -1580,7 +1580,10 @@ constexpr int PT_TR = 4;                          // tile rows along h and w
 constexpr int PT_ROWS = PT_TR * PT_TR;            // output rows per tile
 constexpr int PT_CWARPS = 4;                      // consumer warps
 constexpr int PT_THREADS = (PT_CWARPS + 1) * 32;  // + the producer warp
-constexpr int PT_STAGES = 4;
+#ifndef BA_PT_STAGES
+#define BA_PT_STAGES 4
+#endif
+constexpr int PT_STAGES = BA_PT_STAGES;
 constexpr int PT_MAX_DIM = 256;  // tensor-map box extent limit; also the tables
 constexpr unsigned long long PT_WAIT_NS = 2000000000ull;
 
@@ -1636,11 +1639,16 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, unsigned parity) {
 }
 
 // mbar_test until it succeeds or PT_WAIT_NS pass; false when the time ran out
+#ifndef BA_PT_BACKOFF_NS
+#define BA_PT_BACKOFF_NS 0
+#endif
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
   if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = global_ns();
-  while (!mbar_test(bar, parity))
+  while (!mbar_test(bar, parity)) {
+    if (BA_PT_BACKOFF_NS > 0) __nanosleep(BA_PT_BACKOFF_NS);
     if (global_ns() - t0 > PT_WAIT_NS) return false;
+  }
   return true;
 }
 
@@ -1776,10 +1784,13 @@ __device__ __forceinline__ void permt_fixups(const ResampleArgs& a, int64_t b, c
                                           int orow0, int h0, int ow, int yc, int zc,
                                           const PermAxis* s_x, const PermAxis* s_y,
                                           const PermAxis* s_z, PermX x0, PermX x1, int lane) {
+  static_assert(PT_RPW == 4, "four rows per warp");
   const int H = a.H, W = a.W, D = a.D, plane = W * D;
   const int d0 = 4 * lane, d1 = d0 + 128;
   for (int i = 0; i < PT_RPW; ++i) {
-    const int sn = srow[i] & 0xFF, sb = (srow[i] >> 8) & 0xFF;
+    // selects, not indexing, so the rows' codes stay in registers
+    const int sv = (i & 2) ? ((i & 1) ? srow[3] : srow[2]) : ((i & 1) ? srow[1] : srow[0]);
+    const int sn = sv & 0xFF, sb = (sv >> 8) & 0xFF;
     if (sn == PT_NONE) continue;
     const int oh = h0 + i, o = orow0 + i * plane;
     const PermAxis ay = s_y[yc == 1 ? ow : oh], az = s_z[zc == 1 ? ow : oh];
@@ -1815,7 +1826,10 @@ __device__ __forceinline__ void permt_fixups(const ResampleArgs& a, int64_t b, c
 }
 
 template <int PAD>
-__global__ void __launch_bounds__(PT_THREADS, 4)
+#ifndef BA_PT_MINBLOCKS
+#define BA_PT_MINBLOCKS 4
+#endif
+__global__ void __launch_bounds__(PT_THREADS, BA_PT_MINBLOCKS)
     resample3d_permt_kernel(const __grid_constant__ PermTmaArgs p) {
   extern __shared__ __align__(128) unsigned char pt_stage[];
   __shared__ PermAxis s_x[PT_MAX_DIM], s_y[PT_MAX_DIM], s_z[PT_MAX_DIM];
@@ -1872,9 +1886,6 @@ __global__ void __launch_bounds__(PT_THREADS, 4)
   if (warp == PT_CWARPS) {
     // producer: one lane issues every load of the CTA's items in order
     if (lane != 0) return;
-    int last_round[PT_STAGES];
-#pragma unroll
-    for (int s = 0; s < PT_STAGES; ++s) last_round[s] = -1;
     bool ok = true;
     int j = 0;
     for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
@@ -1893,15 +1904,16 @@ __global__ void __launch_bounds__(PT_THREADS, 4)
           mbar_expect_tx(&full[s], bytes);
           tma_load4(pt_stage + (size_t)s * p.stage_bytes, &p.maps[ki], 0, ys, zs,
                     (int)(b * k.channels + c), &full[s]);
-          last_round[s] = round;
         }
       }
     }
     if (!ok) atomicOr(&g_wait_timeouts, 1u);
-    // every issued load lands before the CTA may exit
-    for (int s = 0; s < PT_STAGES; ++s)
-      if (last_round[s] >= 0 && !mbar_wait(&full[s], (unsigned)(last_round[s] & 1)))
-        atomicOr(&g_wait_timeouts, 1u);
+    // every issued load (items 0 .. j-1) lands before the CTA may exit: the
+    // last one of stage s is item s + PT_STAGES * ((j - 1 - s) / PT_STAGES)
+    for (int s = 0; s < PT_STAGES && s < j; ++s) {
+      const int round = (s + PT_STAGES * ((j - 1 - s) / PT_STAGES)) / PT_STAGES;
+      if (!mbar_wait(&full[s], (unsigned)(round & 1))) atomicOr(&g_wait_timeouts, 1u);
+    }
     return;
   }
   // consumers: the x side of the lane's chunks d = 4 lane and 4 lane + 128,
@@ -2481,7 +2493,7 @@ bool launch_perm_tma(const ba_resample_desc& d, const ResampleArgs& a, int64_t n
   const dim3 grid((unsigned)std::min<int64_t>(ntiles, per_elem), (unsigned)nb);
   static int opted[2] = {0, 0};  // dynamic shared memory each instantiation allows
   int& o = opted[pad == BA_PAD_BORDER];
-  if (smem > 48 * 1024 && smem > o) {
+  if (smem > o) {  // with the 9 KB of static tables, even 48 KB of stages needs the opt-in
     if (pad == BA_PAD_BORDER)
       cudaFuncSetAttribute(resample3d_permt_kernel<BA_PAD_BORDER>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

@@ -59,10 +59,16 @@ UNIT = "voxel/s"
 HEADLINE = "config4"
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
-# dominant entry point's kernel, from one ncu capture of that kernel on the
-# workload's shapes.  config2: resample3d_staged_kernel on 8x1x128^3 fp32
-# (RandAffine, border), one launch.
-DRAM_BYTES_PER_LAUNCH = {"config2": 96078080}
+# dominant entry point's kernels, from ncu captures of those kernels.
+#   config2: resample3d_fast_kernel<2,-1> on 8x1x128^3 fp32 (RandAffine,
+#     border), one launch: 62,467,840 + 33,467,392 B.
+#   config4: the step's two ba_resample3d launches, captured on a 2-element
+#     slice of the workload (2x4x128^3 vol + seg) and scaled to the 5
+#     elements of a launch (traffic grows with the elements): the permutation
+#     kernel resample3d_permt_kernel<0> 135,690,496 + 90,970,880 B and the
+#     affine kernel resample3d_fast_kernel<0,6> 130,048,512 + 102,385,152 B,
+#     mean 229,547,520 B x 5 / 2.
+DRAM_BYTES_PER_LAUNCH = {"config2": 95935232, "config4": 573868800}
 
 
 def _peaks():
@@ -433,6 +439,13 @@ WORKLOADS = {
     "rot90": Workload("rot90", "RandRotate90(prob=1, max_k 3, axes (0,1)) eager apply, B=8 C=1 "
                       "128^3 fp32", "f32", {"vol": (1, 4)}, 8, (128, 128, 128), _ROT,
                       _build_single(_mk_eager("RandRotate90"))),
+    "affine-reflection": Workload("affine-reflection", "config 2's RandAffine with reflection "
+                                  "padding (the global-gather resample kernel), B=8 C=1 128^3 "
+                                  "fp32", "f32", {"vol": (1, 4)}, 8, (128, 128, 128), _ROT,
+                                  _build_single(_mk_eager(
+                                      "RandAffine", rotate_range=0.785, shear_range=0.3,
+                                      translate_range=5, scale_range=0.1,
+                                      padding_mode="reflection"))),
     "minmax": Workload("minmax", "per-(element, channel) min/max (ba_minmax) of 16x4x128^3 bf16",
                        "bf16", {"v": (4, 1)}, 16, (128, 128, 128), _ROT,
                        _build_single(_mk_minmax), e2e=False),
