@@ -350,6 +350,63 @@ __device__ __forceinline__ void sample_pair(const KeyArgs& k, int64_t b, int H, 
   }
 }
 
+// A nearest key's first (up to) four channels at a pair of output voxels,
+// split into the gathers (nearest_begin) and the stores (nearest_end) so a
+// kernel can issue the gathers, do other work while they are in flight, and
+// store afterwards; channels past the fourth are gathered and stored in
+// nearest_begin.  Coordinates, rounding and bounds are sample_pair's.
+struct NearestPair {
+  float va[4], vb[4];
+};
+
+template <int PAD, int DT, bool ALIGN>
+__device__ __forceinline__ void nearest_begin(const KeyArgs& k, int64_t b, int H, int W, int D,
+                                              int hwd, float2 ix, float2 iy, float2 iz, int sa,
+                                              int sb, bool has_b, NearestPair& q) {
+  const float2 px = pad2<PAD, ALIGN>(ix, D);
+  const float2 py = pad2<PAD, ALIGN>(iy, W);
+  const float2 pz = pad2<PAD, ALIGN>(iz, H);
+  const size_t esz = DT == BA_BF16 ? 2 : 4;
+  const char* src_e = (const char*)k.src + (size_t)b * k.channels * hwd * esz;
+  const int xa = __float2int_rn(px.x), ya = __float2int_rn(py.x), za = __float2int_rn(pz.x);
+  const int xb = __float2int_rn(px.y), yb = __float2int_rn(py.y), zb = __float2int_rn(pz.y);
+  const bool oka =
+      (unsigned)xa < (unsigned)D && (unsigned)ya < (unsigned)W && (unsigned)za < (unsigned)H;
+  const bool okb = has_b && (unsigned)xb < (unsigned)D && (unsigned)yb < (unsigned)W &&
+                   (unsigned)zb < (unsigned)H;
+  const int oa = oka ? (za * W + ya) * D + xa : 0;
+  const int ob = okb ? (zb * W + yb) * D + xb : 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const void* cs = src_e + (size_t)j * hwd * esz;
+    q.va[j] = (j < k.channels && oka) ? ld<DT>(cs, oa) : 0.0f;
+    q.vb[j] = (j < k.channels && okb) ? ld<DT>(cs, ob) : 0.0f;
+  }
+  char* dst_e = (char*)k.dst + (size_t)b * k.channels * hwd * esz;
+  for (int c = 4; c < k.channels; ++c) {
+    const void* cs = src_e + (size_t)c * hwd * esz;
+    void* cd = dst_e + (size_t)c * hwd * esz;
+    const float va = oka ? ld<DT>(cs, oa) : 0.0f;
+    const float vb = okb ? ld<DT>(cs, ob) : 0.0f;
+    st<DT>(cd, sa, va);
+    if (has_b) st<DT>(cd, sb, vb);
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void nearest_end(const KeyArgs& k, int64_t b, int hwd, int sa, int sb,
+                                            bool has_b, const NearestPair& q) {
+  const size_t esz = DT == BA_BF16 ? 2 : 4;
+  char* dst_e = (char*)k.dst + (size_t)b * k.channels * hwd * esz;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (j >= k.channels) break;
+    void* cd = dst_e + (size_t)j * hwd * esz;
+    st<DT>(cd, sa, q.va[j]);
+    if (has_b) st<DT>(cd, sb, q.vb[j]);
+  }
+}
+
 // A key's sampling spec as one compile-time code: (mode*3 + padding)*2 + dtype.
 __host__ __device__ constexpr int spec_code(int mode, int pad, int dt) { return (mode * 3 + pad) * 2 + dt; }
 __host__ __device__ constexpr int spec_mode(int s) { return s / 6; }
@@ -964,6 +1021,9 @@ __device__ __forceinline__ void stage_box_pitched(float4* s_dyn4, const char* sr
 #ifndef BA_FS_MINBLOCKS
 #define BA_FS_MINBLOCKS 4
 #endif
+#ifndef BA_FS_SEG_OVERLAP
+#define BA_FS_SEG_OVERLAP 1
+#endif
 
 template <int S0, int S1>
 __global__ void __launch_bounds__(ST_THREADS, BA_FS_MINBLOCKS)
@@ -1044,13 +1104,26 @@ __global__ void __launch_bounds__(ST_THREADS, BA_FS_MINBLOCKS)
         iz = pH ? unnormalize2_pow2(g[2], fH) : unnormalize2<false>(g[2], fH);
       }
       const int row = (h * W + w) * D;
-      if (S1 >= 0 && c0 == 0 && valid) {
-        if (ALIGN)
-          sample_spec<(S1 < 0 ? 0 : S1), true>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da,
-                                               row + db, has_b);
-        else
-          sample_spec<(S1 < 0 ? 0 : S1), false>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da,
-                                                row + db, has_b);
+      // the paired nearest key (S1): its gathers issued now, stored after
+      // this pair's interpolation, so their latency overlaps it
+      constexpr int S1K = S1 < 0 ? 0 : S1;
+      const bool seg = S1 >= 0 && c0 == 0 && valid;
+      NearestPair nq;
+      if (seg) {
+        if (BA_FS_SEG_OVERLAP) {
+          if (ALIGN)
+            nearest_begin<spec_pad(S1K), spec_dt(S1K), true>(a.keys[1], b, H, W, D, hwd, ix, iy,
+                                                             iz, row + da, row + db, has_b, nq);
+          else
+            nearest_begin<spec_pad(S1K), spec_dt(S1K), false>(a.keys[1], b, H, W, D, hwd, ix, iy,
+                                                              iz, row + da, row + db, has_b, nq);
+        } else if (ALIGN) {
+          sample_spec<S1K, true>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da, row + db,
+                                 has_b);
+        } else {
+          sample_spec<S1K, false>(a.keys[1], b, H, W, D, hwd, ix, iy, iz, row + da, row + db,
+                                  has_b);
+        }
       }
       const float2 px = f2(fast_pad<PAD>(ix.x, fD), fast_pad<PAD>(ix.y, fD));
       const float2 py = f2(fast_pad<PAD>(iy.x, fW), fast_pad<PAD>(iy.y, fW));
@@ -1106,6 +1179,8 @@ __global__ void __launch_bounds__(ST_THREADS, BA_FS_MINBLOCKS)
         st<DT>(dst_c, row + da, r.x);
         if (has_b) st<DT>(dst_c, row + db, r.y);
       }
+      if (BA_FS_SEG_OVERLAP && seg)
+        nearest_end<spec_dt(S1K)>(a.keys[1], b, hwd, row + da, row + db, has_b, nq);
     }
     if (staged) __syncthreads();
   }
@@ -1748,7 +1823,7 @@ __device__ __forceinline__ void permt_xfix(const unsigned char* srow, char* cd, 
   }
 }
 
-template <int MODE, int DT>
+template <int MODE, int DT, int NQ>
 __device__ __forceinline__ void permt_rows(const KeyArgs& k, int64_t b, int c, int H, int W,
                                            int D, const unsigned char* stage, const int* srow,
                                            int orow0, const PermX& x0, const PermX& x1,
@@ -1766,7 +1841,7 @@ __device__ __forceinline__ void permt_rows(const KeyArgs& k, int64_t b, int c, i
         permt_chunk<DT>(st, cd, o + d0, x0);
         if (MODE != BA_NEAREST && x0.off) permt_xfix<DT>(st, cd, o + d0, D, s_x + d0);
       }
-      if (d1 < D) {
+      if (NQ > 1 && d1 < D) {
         permt_chunk<DT>(st, cd, o + d1, x1);
         if (MODE != BA_NEAREST && x1.off) permt_xfix<DT>(st, cd, o + d1, D, s_x + d1);
       }
@@ -1779,7 +1854,7 @@ __device__ __forceinline__ void permt_rows(const KeyArgs& k, int64_t b, int c, i
 // global-memory path: PT_GLOBAL rows (a bilinear key's rows off a voxel
 // centre along y or z, a plane or two per element; rows outside the staged
 // block).  Out of line, so the staged loop keeps its registers.
-template <int PAD>
+template <int PAD, int NQ>
 __device__ __forceinline__ void permt_fixups(const ResampleArgs& a, int64_t b, const int* srow,
                                           int orow0, int h0, int ow, int yc, int zc,
                                           const PermAxis* s_x, const PermAxis* s_y,
@@ -1798,7 +1873,7 @@ __device__ __forceinline__ void permt_fixups(const ResampleArgs& a, int64_t b, c
       const KeyArgs& k = a.keys[ki];
       const bool nearest = k.mode == BA_NEAREST;
       if ((nearest ? sn : sb) != PT_GLOBAL) continue;
-      const bool l0 = d0 < D, l1 = d1 < D;
+      const bool l0 = d0 < D, l1 = NQ > 1 && d1 < D;
       const int esz = k.dtype == BA_BF16 ? 2 : 4;
       for (int c = 0; c < k.channels; ++c) {
         const size_t coff = ((size_t)b * k.channels + c) * ((size_t)H * W * D) * esz;
@@ -1825,10 +1900,11 @@ __device__ __forceinline__ void permt_fixups(const ResampleArgs& a, int64_t b, c
   }
 }
 
-template <int PAD>
 #ifndef BA_PT_MINBLOCKS
 #define BA_PT_MINBLOCKS 4
 #endif
+// NQ: 16-byte chunks per lane and row (1 for D <= 128, 2 up to PT_MAX_DIM)
+template <int PAD, int NQ>
 __global__ void __launch_bounds__(PT_THREADS, BA_PT_MINBLOCKS)
     resample3d_permt_kernel(const __grid_constant__ PermTmaArgs p) {
   extern __shared__ __align__(128) unsigned char pt_stage[];
@@ -1920,9 +1996,9 @@ __global__ void __launch_bounds__(PT_THREADS, BA_PT_MINBLOCKS)
   // fixed for the element
   const int d0 = 4 * lane, d1 = d0 + 128;
   const PermX x0 = perm_x(s_x + (d0 < D ? d0 : 0), D);
-  const PermX x1 = perm_x(s_x + (d1 < D ? d1 : 0), D);
+  const PermX x1 = NQ > 1 ? perm_x(s_x + (d1 < D ? d1 : 0), D) : x0;
   const bool xok =
-      __all_sync(0xFFFFFFFFu, (d0 >= D || x0.base >= 0) && (d1 >= D || x1.base >= 0));
+      __all_sync(0xFFFFFFFFu, (d0 >= D || x0.base >= 0) && (NQ == 1 || d1 >= D || x1.base >= 0));
   int j = 0;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const int h0 = (tile / ntw) * PT_TR, w0 = (tile % ntw) * PT_TR;
@@ -1965,16 +2041,20 @@ __global__ void __launch_bounds__(PT_THREADS, BA_PT_MINBLOCKS)
         const unsigned char* stage = pt_stage + (size_t)s * p.stage_bytes;
         switch (k.mode * 2 + k.dtype) {
           case BA_BILINEAR * 2 + BA_F32:
-            permt_rows<BA_BILINEAR, BA_F32>(k, b, c, H, W, D, stage, srow, orow0, x0, x1, s_x, lane);
+            permt_rows<BA_BILINEAR, BA_F32, NQ>(k, b, c, H, W, D, stage, srow, orow0, x0, x1, s_x,
+                                            lane);
             break;
           case BA_BILINEAR * 2 + BA_BF16:
-            permt_rows<BA_BILINEAR, BA_BF16>(k, b, c, H, W, D, stage, srow, orow0, x0, x1, s_x, lane);
+            permt_rows<BA_BILINEAR, BA_BF16, NQ>(k, b, c, H, W, D, stage, srow, orow0, x0, x1, s_x,
+                                            lane);
             break;
           case BA_NEAREST * 2 + BA_F32:
-            permt_rows<BA_NEAREST, BA_F32>(k, b, c, H, W, D, stage, srow, orow0, x0, x1, s_x, lane);
+            permt_rows<BA_NEAREST, BA_F32, NQ>(k, b, c, H, W, D, stage, srow, orow0, x0, x1, s_x,
+                                            lane);
             break;
           case BA_NEAREST * 2 + BA_BF16:
-            permt_rows<BA_NEAREST, BA_BF16>(k, b, c, H, W, D, stage, srow, orow0, x0, x1, s_x, lane);
+            permt_rows<BA_NEAREST, BA_BF16, NQ>(k, b, c, H, W, D, stage, srow, orow0, x0, x1, s_x,
+                                            lane);
             break;
           default:
             break;
@@ -1983,7 +2063,7 @@ __global__ void __launch_bounds__(PT_THREADS, BA_PT_MINBLOCKS)
         if (lane == 0) mbar_arrive(&empty[s]);
       }
     }
-    if (fix) permt_fixups<PAD>(a, b, srow, orow0, h0, ow, yc, zc, s_x, s_y, s_z, x0, x1, lane);
+    if (fix) permt_fixups<PAD, NQ>(a, b, srow, orow0, h0, ow, yc, zc, s_x, s_y, s_z, x0, x1, lane);
   }
 }
 
@@ -2491,21 +2571,29 @@ bool launch_perm_tma(const ba_resample_desc& d, const ResampleArgs& a, int64_t n
   // about four CTAs per SM over the launch's elements, each walking tiles
   const int64_t per_elem = std::max<int64_t>(1, (4 * (int64_t)sm_count_rs() + nb - 1) / nb);
   const dim3 grid((unsigned)std::min<int64_t>(ntiles, per_elem), (unsigned)nb);
-  static int opted[2] = {0, 0};  // dynamic shared memory each instantiation allows
-  int& o = opted[pad == BA_PAD_BORDER];
-  if (smem > o) {  // with the 9 KB of static tables, even 48 KB of stages needs the opt-in
-    if (pad == BA_PAD_BORDER)
-      cudaFuncSetAttribute(resample3d_permt_kernel<BA_PAD_BORDER>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    else
-      cudaFuncSetAttribute(resample3d_permt_kernel<BA_PAD_ZEROS>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    o = smem;
+  // dynamic shared memory each instantiation allows (with the 9 KB of
+  // static tables, even 48 KB of stages needs the opt-in)
+  static int opted[4] = {0, 0, 0, 0};
+  const int nq = d.D <= 128 ? 1 : 2;
+  const int which = (pad == BA_PAD_BORDER ? 2 : 0) + (nq - 1);
+  switch (which) {
+#define BA_PT_LAUNCH(I, P, Q)                                                         \
+  case I:                                                                             \
+    if (smem > opted[I]) {                                                            \
+      cudaFuncSetAttribute(resample3d_permt_kernel<P, Q>,                             \
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);        \
+      opted[I] = smem;                                                                \
+    }                                                                                 \
+    resample3d_permt_kernel<P, Q><<<grid, PT_THREADS, smem, st>>>(p);                 \
+    break;
+    BA_PT_LAUNCH(0, BA_PAD_ZEROS, 1)
+    BA_PT_LAUNCH(1, BA_PAD_ZEROS, 2)
+    BA_PT_LAUNCH(2, BA_PAD_BORDER, 1)
+    BA_PT_LAUNCH(3, BA_PAD_BORDER, 2)
+#undef BA_PT_LAUNCH
+    default:
+      return false;
   }
-  if (pad == BA_PAD_BORDER)
-    resample3d_permt_kernel<BA_PAD_BORDER><<<grid, PT_THREADS, smem, st>>>(p);
-  else
-    resample3d_permt_kernel<BA_PAD_ZEROS><<<grid, PT_THREADS, smem, st>>>(p);
   return true;
 }
 
@@ -2610,7 +2698,10 @@ ba_status launch_resample(const ba_resample_desc& d, ResampleArgs& a, int64_t nb
   const dim3 g4_grid((unsigned)((hwd + G4_THREADS * G4_VOX - 1) / (G4_THREADS * G4_VOX)),
                      (unsigned)nb);
   // vol (bilinear) + seg (nearest) with one padding: one fused launch
-  if (a.n_keys == 2) {
+#ifndef BA_RS_FUSE_PAIR
+#define BA_RS_FUSE_PAIR 1
+#endif
+  if (BA_RS_FUSE_PAIR && a.n_keys == 2) {
     KeyArgs k0 = a.keys[0], k1 = a.keys[1];
     if (k0.mode == BA_NEAREST && k1.mode == BA_BILINEAR) {
       a.keys[0] = k1;

@@ -61,14 +61,14 @@ HEADLINE = "config4"
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
 # dominant entry point's kernels, from ncu captures of those kernels.
 #   config2: resample3d_fast_kernel<2,-1> on 8x1x128^3 fp32 (RandAffine,
-#     border), one launch: 62,467,840 + 33,467,392 B.
+#     border), one launch: 63,000,576 + 34,108,928 B.
 #   config4: the step's two ba_resample3d launches, captured on a 2-element
 #     slice of the workload (2x4x128^3 vol + seg) and scaled to the 5
 #     elements of a launch (traffic grows with the elements): the permutation
 #     kernel resample3d_permt_kernel<0> 135,690,496 + 90,970,880 B and the
 #     affine kernel resample3d_fast_kernel<0,6> 130,048,512 + 102,385,152 B,
 #     mean 229,547,520 B x 5 / 2.
-DRAM_BYTES_PER_LAUNCH = {"config2": 95935232, "config4": 573868800}
+DRAM_BYTES_PER_LAUNCH = {"config2": 97109504, "config4": 573868800}
 
 
 def _peaks():
@@ -357,10 +357,9 @@ def _mk_elastic(D):
     return mk
 
 
-def _mk_eager(cls, **kw):
+def _mk_eager(cls, shape=(8, 1, 128, 128, 128), **kw):
     def mk(torch, ba, device, g):
-        sets = [{"vol": torch.rand(8, 1, 128, 128, 128, device=device, generator=g)}
-                for _ in range(4)]
+        sets = [{"vol": torch.rand(*shape, device=device, generator=g)} for _ in range(4)]
         t = getattr(ba, cls)(prob=1.0, **kw)
         return sets, lambda d: {"vol": t(d["vol"])}
     return mk
@@ -436,6 +435,10 @@ WORKLOADS = {
     "flip": Workload("flip", "RandAxisFlip(prob=1) eager apply, B=8 C=1 128^3 fp32", "f32",
                      {"vol": (1, 4)}, 8, (128, 128, 128), _ROT,
                      _build_single(_mk_eager("RandAxisFlip"))),
+    "flip-d260": Workload("flip-d260", "RandAxisFlip(prob=1) eager apply on rows longer than one "
+                          "tensor-map box (D=260: the per-lane row-copy kernel), B=8 C=1 "
+                          "128x128x260 fp32", "f32", {"vol": (1, 4)}, 8, (128, 128, 260), _ROT,
+                          _build_single(_mk_eager("RandAxisFlip", shape=(8, 1, 128, 128, 260)))),
     "rot90": Workload("rot90", "RandRotate90(prob=1, max_k 3, axes (0,1)) eager apply, B=8 C=1 "
                       "128^3 fp32", "f32", {"vol": (1, 4)}, 8, (128, 128, 128), _ROT,
                       _build_single(_mk_eager("RandRotate90"))),
