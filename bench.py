@@ -372,6 +372,35 @@ def _mk_minmax(torch, ba, device, g):
     return sets, lambda d: dict(zip(("min", "max"), ops.minmax(d["v"], 64)))
 
 
+def _mk_fallbacks(torch, ba, device, g):
+    """One launch of each kernel that only fallback cases reach: the exact
+    trilinear mode (resample3d_staged_kernel), an elastic field whose taps
+    exceed the wide passes' 63 (elastic_draw4, axis passes, elastic grid),
+    a smoothing with more than 63 taps (axis passes), and a smoothing whose
+    H line is too long to stage (roll_axis)."""
+    from batchaug_b200 import ops
+    vol = torch.rand(8, 1, 128, 128, 128, device=device, generator=g)
+    aff = ba.RandAffine(prob=1.0, rotate_range=0.785, shear_range=0.3, translate_range=5,
+                        scale_range=0.1, padding_mode="border")
+    pa = aff.sample_params(8, vol.shape, device)
+    el = ba.Rand3DElastic(prob=1.0, sigma_range=(11.0, 12.0), magnitude_range=(50, 150))
+    v2 = torch.rand(2, 1, 96, 96, 96, device=device, generator=g)
+    big = ba.RandGaussianSmooth(prob=1.0, sigma_x=(8.5, 9.0), sigma_y=(8.5, 9.0),
+                                sigma_z=(8.5, 9.0))
+    pb = big.sample_params(2, v2.shape, device)
+    v3 = torch.rand(1, 1, 800, 64, 48, device=device, generator=g)
+    long_h = ba.RandGaussianSmooth(prob=1.0, sigma_x=(5.0, 5.0), sigma_y=(5.0, 5.0),
+                                   sigma_z=(5.0, 5.0))
+    pl = long_h.sample_params(1, v3.shape, device)
+
+    def step(d):
+        with ops.resample_exact(True):
+            a = aff.apply(d["vol"], pa)
+        grid = el.sample_params(2, (2, 1, 96, 96, 96), device)["grid"]
+        return {"a": a, "grid": grid, "b": big.apply(d["v2"], pb), "c": long_h.apply(d["v3"], pl)}
+    return [{"vol": vol, "v2": v2, "v3": v3}], step
+
+
 def _mk_compose_field(torch, ba, device, g):
     from batchaug_b200 import ops
     el = ba.Rand3DElastic(prob=1.0, sigma_range=(5, 7), magnitude_range=(50, 150))
@@ -449,6 +478,12 @@ WORKLOADS = {
                                       "RandAffine", rotate_range=0.785, shear_range=0.3,
                                       translate_range=5, scale_range=0.1,
                                       padding_mode="reflection"))),
+    "fallbacks": Workload("fallbacks", "one launch of each fallback-only kernel: exact-mode "
+                          "RandAffine (8x1x128^3), elastic field sigma 11..12 (2x96^3), smoothing "
+                          "sigma 8.5..9 (2x1x96^3) and sigma 5 on an 800-long H line (1x1x800x64x48);"
+                          " for ncu summaries, not a throughput line", "f32", {"vol": (1, 4)}, 8,
+                          (128, 128, 128), "inputs larger than L2", _build_single(_mk_fallbacks),
+                          e2e=False),
     "minmax": Workload("minmax", "per-(element, channel) min/max (ba_minmax) of 16x4x128^3 bf16",
                        "bf16", {"v": (4, 1)}, 16, (128, 128, 128), _ROT,
                        _build_single(_mk_minmax), e2e=False),

@@ -402,3 +402,24 @@ def test_large_footprints_vs_oracle(ba, oracle_lib, zoom, pad):
     ref_seg = oracle_lib.resample3d(seg, affine=A, mode="nearest", padding=pad)
     _check(to_np(outs[0]), ref, False)
     assert np.array_equal(to_np(outs[1]), ref_seg)
+
+
+def test_tensor_map_cache_follows_shape(ba, oracle_lib):
+    """The TMA kernel caches tensor maps by address, dtype and shape: two
+    volumes of different shapes starting at the same address (views of one
+    buffer) each resample correctly, in either order, twice."""
+    from batchaug_b200 import _lib, ops
+    rng = np.random.default_rng(5)
+    buf = torch.empty(2 * 12 * 16 * 20 * 8, device="cuda")
+    shapes = [(2, 2, 16, 16, 24), (3, 1, 12, 12, 32)]
+    for _ in range(2):
+        for shape in shapes + shapes[::-1]:
+            n = int(np.prod(shape))
+            x = rng.standard_normal(shape).astype(np.float32)
+            src = buf[:n].view(shape)
+            src.copy_(torch.from_numpy(x))
+            A = _signed_perm_affines(rng, shape[0])
+            out = ops.resample3d(src, affine=A, modes="nearest", paddings="zeros")
+            ref = oracle_lib.resample3d(x, affine=A, mode="nearest", padding="zeros")
+            assert np.array_equal(to_np(out), ref), shape
+    _lib.wait_status()
