@@ -1854,8 +1854,16 @@ __device__ __forceinline__ void permt_rows(const KeyArgs& k, int64_t b, int c, i
 // global-memory path: PT_GLOBAL rows (a bilinear key's rows off a voxel
 // centre along y or z, a plane or two per element; rows outside the staged
 // block).  Out of line, so the staged loop keeps its registers.
+#ifndef BA_PT_FIXUPS_INLINE
+#define BA_PT_FIXUPS_INLINE 1
+#endif
+#if BA_PT_FIXUPS_INLINE
+#define BA_PT_FIXUPS_ATTR __forceinline__
+#else
+#define BA_PT_FIXUPS_ATTR __noinline__
+#endif
 template <int PAD, int NQ>
-__device__ __forceinline__ void permt_fixups(const ResampleArgs& a, int64_t b, const int* srow,
+__device__ BA_PT_FIXUPS_ATTR void permt_fixups(const ResampleArgs& a, int64_t b, const int* srow,
                                           int orow0, int h0, int ow, int yc, int zc,
                                           const PermAxis* s_x, const PermAxis* s_y,
                                           const PermAxis* s_z, PermX x0, PermX x1, int lane) {
@@ -2568,14 +2576,32 @@ bool launch_perm_tma(const ba_resample_desc& d, const ResampleArgs& a, int64_t n
   p.stage_bytes = stage_bytes;
   const int smem = PT_STAGES * stage_bytes;
   const int64_t ntiles = ((d.H + PT_TR - 1) / PT_TR) * ((d.W + PT_TR - 1) / PT_TR);
-  // about four CTAs per SM over the launch's elements, each walking tiles
-  const int64_t per_elem = std::max<int64_t>(1, (4 * (int64_t)sm_count_rs() + nb - 1) / nb);
-  const dim3 grid((unsigned)std::min<int64_t>(ntiles, per_elem), (unsigned)nb);
+  // one wave: as many CTAs as fit on the SMs at once (registers and this
+  // stage size decide how many per SM), spread over the launch's elements,
+  // each walking tiles
   // dynamic shared memory each instantiation allows (with the 9 KB of
   // static tables, even 48 KB of stages needs the opt-in)
   static int opted[4] = {0, 0, 0, 0};
   const int nq = d.D <= 128 ? 1 : 2;
   const int which = (pad == BA_PAD_BORDER ? 2 : 0) + (nq - 1);
+  static int occ_smem[4] = {-1, -1, -1, -1}, occ[4] = {1, 1, 1, 1};  // last query per kernel
+  auto grid_for = [&](const void* fn) {
+    if (occ_smem[which] != smem) {
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, PT_THREADS, smem) !=
+              cudaSuccess ||
+          per_sm < 1) {
+        cudaGetLastError();
+        per_sm = 1;
+      }
+      occ[which] = per_sm;
+      occ_smem[which] = smem;
+    }
+    const int per_sm = occ[which];
+    const int64_t ctas = (int64_t)per_sm * sm_count_rs();
+    const int64_t per_elem = std::max<int64_t>(1, ctas / nb);
+    return dim3((unsigned)std::min<int64_t>(ntiles, per_elem), (unsigned)nb);
+  };
   switch (which) {
 #define BA_PT_LAUNCH(I, P, Q)                                                         \
   case I:                                                                             \
@@ -2584,7 +2610,8 @@ bool launch_perm_tma(const ba_resample_desc& d, const ResampleArgs& a, int64_t n
                            cudaFuncAttributeMaxDynamicSharedMemorySize, smem);        \
       opted[I] = smem;                                                                \
     }                                                                                 \
-    resample3d_permt_kernel<P, Q><<<grid, PT_THREADS, smem, st>>>(p);                 \
+    resample3d_permt_kernel<P, Q><<<grid_for((const void*)resample3d_permt_kernel<P, Q>), \
+                                    PT_THREADS, smem, st>>>(p);                       \
     break;
     BA_PT_LAUNCH(0, BA_PAD_ZEROS, 1)
     BA_PT_LAUNCH(1, BA_PAD_ZEROS, 2)
