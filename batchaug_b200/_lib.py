@@ -32,6 +32,7 @@ BA_RICIAN_PHILOX, BA_RICIAN_RELATIVE = 0x1, 0x2
 BA_STD_NONZERO, BA_STAT_CHANNEL = 0x2, 0x4
 BA_SHIFT_SAFE = 0x1
 BA_RESCALE_MINV, BA_RESCALE_MAXV, BA_RESCALE_CHANNEL, BA_RESCALE_FACTOR = 0x1, 0x2, 0x4, 0x8
+BA_RESCALE_GIVEN = 0x10
 
 BA_SMOOTH_ZEROS, BA_SMOOTH_REFLECT, BA_SMOOTH_REPLICATE = 0, 1, 2
 
@@ -48,7 +49,7 @@ _U64 = ctypes.c_uint64
 
 class ResampleKey(ctypes.Structure):
     _fields_ = [("src", _P), ("dst", _P), ("channels", _I64), ("dtype", _I32), ("mode", _I32),
-                ("padding", _I32), ("reserved", _I32)]
+                ("padding", _I32), ("reserved", _I32), ("minmax", _P)]
 
 
 class ResampleDesc(ctypes.Structure):
@@ -61,7 +62,8 @@ class ResampleDesc(ctypes.Structure):
 class Op(ctypes.Structure):
     _fields_ = [("kind", _I32), ("flags", _I32), ("mask", _P), ("param", _P), ("param2", _P),
                 ("noise", _P), ("seed", _U64), ("elem_offset", _U64), ("degree", _I32),
-                ("reserved", _I32), ("c0", ctypes.c_double), ("c1", ctypes.c_double)]
+                ("reserved", _I32), ("stats", _P), ("c0", ctypes.c_double),
+                ("c1", ctypes.c_double)]
 
 
 class ChainDesc(ctypes.Structure):

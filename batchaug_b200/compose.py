@@ -51,7 +51,7 @@ import torch
 from . import _lib as L
 from . import ops
 from .base import to_device
-from .intensity import _FusibleIntensity
+from .intensity import ScaleIntensity, _FusibleIntensity
 
 
 def compose_affines(a: np.ndarray, b: np.ndarray) -> np.ndarray:
@@ -111,6 +111,16 @@ class Compose:
     def _is_fusible(t) -> bool:
         inner = getattr(t, "transform", None)
         return isinstance(inner, _FusibleIntensity) and hasattr(t, "keys")
+
+    @staticmethod
+    def _stats_keys(t) -> set:
+        """Keys whose materialisation can hand their min/max straight to the
+        transform ``t`` that follows it: a ScaleIntensity(d) that rescales
+        with per-(element, channel) statistics."""
+        inner = getattr(t, "transform", None)
+        if isinstance(inner, ScaleIntensity) and inner.takes_stats() and hasattr(t, "keys"):
+            return set(t.keys)
+        return set()
 
     def _get_mode(self, key: str) -> str:
         if isinstance(self._mode, dict):
@@ -211,8 +221,10 @@ class Compose:
 
     # -- intensity fusion ---------------------------------------------------
     def _run_intensity(self, d: dict, run: list, inputs: set | None = None,
-                       injected: list | None = None) -> dict:
-        """Apply consecutive fusible dict transforms as one chain per key."""
+                       injected: list | None = None, stats: dict | None = None) -> dict:
+        """Apply consecutive fusible dict transforms as one chain per key.
+        ``stats`` (key -> the min/max the preceding materialisation folded)
+        serves a ScaleIntensity that opens the run on the full batch."""
         d = dict(d)
         sampled = []
         for i, t in enumerate(run):
@@ -240,21 +252,29 @@ class Compose:
                     sub = [(t, _slice_params(p, b, n)) for t, p in sampled]
                     self._chain_keys({k: d[k][b:b + n] for k in keys}, sub, inplace=True)
                 return d
-        out = self._chain_keys({k: d[k] for k in keys}, sampled, inplace=owned)
+        out = self._chain_keys({k: d[k] for k in keys}, sampled, inplace=owned, stats=stats)
         d.update(out)
         return d
 
     @staticmethod
-    def _chain_keys(views: dict, sampled: list, inplace: bool) -> dict:
+    def _chain_keys(views: dict, sampled: list, inplace: bool,
+                    stats: dict | None = None) -> dict:
         """One ba_intensity_chain per key over the ops that list it; an op
-        that selects no element is the identity and is left out."""
+        that selects no element is the identity and is left out.  A key's
+        first op takes ``stats[key]`` when it is a ScaleIntensity that can
+        (the statistics describe the chain's input)."""
         per_key: dict[str, list] = {}
         for t, params in sampled:
             if not np.asarray(params["_host"]["mask"]).any():
                 continue
             for key in t.keys:
                 if key in views:
-                    per_key.setdefault(key, []).append(t.transform.chain_op(params, views[key]))
+                    chain = per_key.setdefault(key, [])
+                    st = stats.get(key) if stats and not chain else None
+                    if st is not None and isinstance(t.transform, ScaleIntensity):
+                        chain.append(t.transform.chain_op(params, views[key], stats=st))
+                    else:
+                        chain.append(t.transform.chain_op(params, views[key]))
         out = {}
         for key, chain in per_key.items():
             x = views[key]
@@ -316,7 +336,12 @@ class Compose:
 
     # -- lazy materialisation (compose.py:71-110) ---------------------------
     def _materialize(self, d: dict, pending: dict, fields: dict | None = None,
-                     inputs: set | None = None) -> dict:
+                     inputs: set | None = None, want_stats: set | None = None,
+                     stats_out: dict | None = None) -> dict:
+        """Resample every pending key (one launch per key group).  Keys in
+        ``want_stats`` that a full-batch launch writes also get their output's
+        per-(element, channel) min/max in ``stats_out`` (folded by the
+        resample as it writes, for the ScaleIntensity that follows)."""
         d = dict(d)
         if fields:
             d = self._materialize_fields(d, pending, fields)
@@ -347,10 +372,17 @@ class Compose:
                         for k, o in zip(chunk, outs):
                             self._scatter(d[k], idx, o)
                         continue
+                    mm = None
+                    if want_stats and stats_out is not None:
+                        mm = [torch.empty((d[k].shape[0], d[k].shape[1], 2), dtype=torch.int32,
+                                          device=d[k].device) if k in want_stats else None
+                              for k in chunk]
                     outs = ops.resample3d([d[k] for k in chunk], affine=affine, mask=mask,
-                                          modes=modes, paddings=paddings)
-                    for k, o in zip(chunk, outs):
+                                          modes=modes, paddings=paddings, minmax=mm)
+                    for i_k, (k, o) in enumerate(zip(chunk, outs)):
                         d[k] = o
+                        if mm is not None and mm[i_k] is not None:
+                            stats_out[k] = mm[i_k]
         return d
 
     def __call__(self, data: dict[str, torch.Tensor],
@@ -426,15 +458,17 @@ class Compose:
                     pending[key] = new
                 i += 1
                 continue
+            stats: dict = {}
             if pending or fields:
-                d = self._materialize(d, pending, fields, inputs)
+                want = self._stats_keys(t) if inputs is not None else set()
+                d = self._materialize(d, pending, fields, inputs, want, stats)
                 pending.clear()
                 fields.clear()
             if self._is_fusible(t):
                 j = i
                 while j < len(ts) and self._is_fusible(ts[j]):
                     j += 1
-                d = self._run_intensity(d, ts[i:j], inputs, injected[i:j])
+                d = self._run_intensity(d, ts[i:j], inputs, injected[i:j], stats)
                 i = j
             else:
                 d = self._apply_dict(d, t, inputs, injected[i])

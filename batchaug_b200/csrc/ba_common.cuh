@@ -26,6 +26,13 @@ ba_status check_launch(const char* what);
 // defined in intensity.cu.
 ba_status validate_chain(const ba_chain_desc* d);
 
+// Per-group min/max keys (the chain's statistics format) for
+// ba_resample3d's minmax output: reset, and fold a tensor's groups of
+// group_size consecutive values into them; defined in intensity.cu.
+ba_status minmax_keys_init(int32_t* keys, int64_t groups, cudaStream_t st);
+ba_status minmax_keys_fold(const void* x, int dtype, int64_t groups, int64_t group_size,
+                           int32_t* keys, cudaStream_t st);
+
 #define BA_REQUIRE(cond, ...)        \
   do {                               \
     if (!(cond)) {                   \

@@ -998,10 +998,17 @@ bool needs_moments(const ba_op& op) {
          (op.kind == BA_OP_RICIAN && (op.flags & BA_RICIAN_RELATIVE));
 }
 
+// RESCALE with its min/max given (BA_RESCALE_GIVEN, ba_op.stats)
+bool stats_given(const ba_op& op) {
+  return op.kind == BA_OP_RESCALE && (op.flags & BA_RESCALE_GIVEN) &&
+         !(op.flags & BA_RESCALE_FACTOR) && (op.flags & (BA_RESCALE_MINV | BA_RESCALE_MAXV));
+}
+
 bool needs_stats(const ba_op& op) {
   if (op.kind == BA_OP_CONTRAST || needs_moments(op)) return true;
   if (op.kind == BA_OP_RESCALE)
-    return !(op.flags & BA_RESCALE_FACTOR) && (op.flags & (BA_RESCALE_MINV | BA_RESCALE_MAXV));
+    return !(op.flags & BA_RESCALE_FACTOR) && (op.flags & (BA_RESCALE_MINV | BA_RESCALE_MAXV)) &&
+           !(op.flags & BA_RESCALE_GIVEN);
   return false;
 }
 
@@ -1061,6 +1068,37 @@ ba_status launch_segment(ChainArgs& a, int64_t nb, bool write, cudaStream_t st) 
 
 }  // namespace
 
+// Per-group min/max keys for ba_resample3d's minmax output: set them to the
+// empty fold, and fold a tensor's groups into them (a group: group_size
+// consecutive values; the same keys and kernel as a chain's statistics).
+ba_status minmax_keys_init(int32_t* keys, int64_t groups, cudaStream_t st) {
+  if (groups <= 0) return BA_OK;
+  init_keys_kernel<<<(unsigned)std::min<int64_t>((groups + 255) / 256, 1024), 256, 0, st>>>(
+      keys, groups);
+  return check_launch("ba_resample3d minmax");
+}
+
+ba_status minmax_keys_fold(const void* x, int dtype, int64_t groups, int64_t group_size,
+                           int32_t* keys, cudaStream_t st) {
+  if (groups <= 0 || group_size <= 0) return BA_OK;
+  const int vec = dtype == BA_BF16 ? 8 : 4;
+  const bool vec_ok = (group_size % vec) == 0 && ((uintptr_t)x % 16) == 0;
+  const int64_t tile = pick_tile(group_size, groups, vec_ok ? vec : 1);
+  dim3 grid((unsigned)((group_size + tile - 1) / tile), (unsigned)groups);
+  if (dtype == BA_BF16) {
+    if (vec_ok)
+      minmax_kernel<BA_BF16, 8><<<grid, CHAIN_THREADS, 0, st>>>(x, group_size, tile, keys);
+    else
+      minmax_kernel<BA_BF16, 1><<<grid, CHAIN_THREADS, 0, st>>>(x, group_size, tile, keys);
+  } else {
+    if (vec_ok)
+      minmax_kernel<BA_F32, 4><<<grid, CHAIN_THREADS, 0, st>>>(x, group_size, tile, keys);
+    else
+      minmax_kernel<BA_F32, 1><<<grid, CHAIN_THREADS, 0, st>>>(x, group_size, tile, keys);
+  }
+  return check_launch("ba_resample3d minmax");
+}
+
 // Shape, dtype, op and pointer checks of a chain descriptor, shared with
 // ba_intensity_chain_noalloc (noalloc.cu).
 ba_status validate_chain(const ba_chain_desc* d) {
@@ -1100,6 +1138,14 @@ ba_status validate_chain(const ba_chain_desc* d) {
       case BA_OP_STD_SHIFT:
       case BA_OP_FIXED_MEAN:
         BA_REQUIRE(op.param, "ba_intensity_chain: op %d needs its per-element factor", i);
+        break;
+      case BA_OP_RESCALE:
+        if (op.flags & BA_RESCALE_GIVEN)
+          BA_REQUIRE(op.stats && (op.flags & BA_RESCALE_CHANNEL) &&
+                         !(op.flags & BA_RESCALE_FACTOR),
+                     "ba_intensity_chain: op %d RESCALE with BA_RESCALE_GIVEN needs stats and "
+                     "BA_RESCALE_CHANNEL",
+                     i);
         break;
       case BA_OP_BIAS_FIELD:
         BA_REQUIRE(op.param, "ba_intensity_chain: op %d BIAS_FIELD needs coefficients", i);
@@ -1234,7 +1280,11 @@ extern "C" ba_status ba_intensity_chain(const ba_chain_desc* desc, void* workspa
         o.span = (float)(op.c1 - op.c0);
         o.factor1p = (float)(1.0 + op.c0);
         o.mean = (float)op.c0;
-        if (needs_stats(op)) {
+        if (stats_given(op)) {
+          // min/max per (element, channel) from the resample that wrote src
+          o.stats_per_channel = 1;
+          o.stats_in = op.stats;
+        } else if (needs_stats(op)) {
           // Stats come from the previous segment.
           const Segment& prev = segs[si - 1];
           o.stats_per_channel = stats_per_channel(op) ? 1 : 0;

@@ -76,6 +76,7 @@ struct KeyArgs {
   int32_t dtype;
   int32_t mode;
   int32_t padding;
+  int32_t* minmax;  // (B, channels, 2) min/max keys the fast kernel folds (or NULL)
 };
 
 // Elements per launch whose transform and mask ride in the kernel's
@@ -935,6 +936,156 @@ __global__ void __launch_bounds__(ST_THREADS, BA_ST_MINBLOCKS)
 }
 
 
+// NaN-propagating min/max (PTX min.NaN / max.NaN): a NaN anywhere makes the
+// running value NaN, as torch.min / torch.max propagate it.
+__device__ __forceinline__ float rs_min_nan(float a, float b) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float rs_max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+// three-input forms (sm_100): one instruction folds a voxel pair
+__device__ __forceinline__ float rs_min3_nan(float a, float b, float c) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float rs_max3_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Block-wide min/max of the 128 threads' running (mn[i], mx[i]) for up to
+// FS_FOLD_CH channels i < n, committed to channel i's (min, max) key pair at
+// keys + 2 i with one atomic each (order-preserving int32 keys, NaN winning
+// both: the intensity chain's statistics format).  One block exchange serves
+// all n channels; every thread of the CTA calls it.
+__device__ __forceinline__ void rs_commit_minmax_n(const float* mn, const float* mx, int n,
+                                                   int32_t* keys) {
+  constexpr int G = 4;  // FS_FOLD_CH
+  __shared__ int32_t s_k[ST_THREADS / 32][2 * G];
+  int32_t k[2 * G];
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    const bool nan = (mn[i] != mn[i]) || (mx[i] != mx[i]);
+    k[2 * i] = nan ? KEY_MIN_NAN : fkey(mn[i]);
+    k[2 * i + 1] = nan ? KEY_MAX_NAN : fkey(mx[i]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int i = 0; i < G; ++i) {
+      k[2 * i] = min(k[2 * i], __shfl_xor_sync(0xFFFFFFFFu, k[2 * i], o));
+      k[2 * i + 1] = max(k[2 * i + 1], __shfl_xor_sync(0xFFFFFFFFu, k[2 * i + 1], o));
+    }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  __syncthreads();  // an earlier commit's reads of s_k are done
+  if (lane == 0)
+#pragma unroll
+    for (int i = 0; i < 2 * G; ++i) s_k[warp][i] = k[i];
+  __syncthreads();
+  if (threadIdx.x < 2 * n) {
+    const int i = threadIdx.x;  // (group i / 2, min or max)
+    int32_t v = s_k[0][i];
+    for (int w = 1; w < ST_THREADS / 32; ++w) v = (i & 1) ? max(v, s_k[w][i]) : min(v, s_k[w][i]);
+    if ((i & 1) == 0 && v != fkey(INFINITY)) atomicMin(keys + i, v);
+    if ((i & 1) == 1 && v != fkey(-INFINITY)) atomicMax(keys + i, v);
+  }
+}
+
+// A masked-out element's tile when key 0 folds its min/max: the copy of
+// staged_copy_masked (16-byte vectors where the row is whole and aligned),
+// channel by channel, key 0's channels committed one at a time.
+__device__ __forceinline__ void staged_copy_masked_fold(const ResampleArgs& a, int64_t b, int d0,
+                                                        int w0, int h0, int hwd, int t) {
+  const int H = a.H, W = a.W, D = a.D;
+  const int w = w0 + t % ST_TW, h = h0 + t / ST_TW;
+  const bool in = w < W && h < H;
+  const int n = min(ST_TD, D - d0);
+  for (int ki = 0; ki < a.n_keys; ++ki) {
+    const KeyArgs& kc = a.keys[ki];
+    const int ke = kc.dtype == BA_BF16 ? 2 : 4;
+    const bool fold = ki == 0 && kc.minmax != nullptr;
+    float gmn[4], gmx[4];  // the current group of 4 channels
+    for (int c = 0; c < kc.channels; ++c) {
+      float mn = INFINITY, mx = -INFINITY;
+      if (in) {
+        const int64_t i0 = (b * kc.channels + c) * (int64_t)hwd + ((int64_t)h * W + w) * D + d0;
+        const char* sp = (const char*)kc.src + i0 * ke;
+        char* dp = (char*)kc.dst + i0 * ke;
+        if (n == ST_TD && ((uintptr_t)sp % 16) == 0 && ((uintptr_t)dp % 16) == 0) {
+          uint4 v[4];
+          const int nv = ST_TD * ke / 16;  // 4 (fp32) or 2 (bf16)
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (q < nv) v[q] = __ldg(reinterpret_cast<const uint4*>(sp) + q);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (q < nv) reinterpret_cast<uint4*>(dp)[q] = v[q];
+          if (fold) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              if (q >= nv) break;
+              const uint32_t u[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+              for (int j = 0; j < 4; j += 2) {
+                if (ke == 2) {
+#pragma unroll
+                  for (int e = j; e < j + 2; ++e) {
+                    const float lo = __uint_as_float(u[e] << 16);
+                    const float hi = __uint_as_float(u[e] & 0xFFFF0000u);
+                    mn = rs_min3_nan(mn, lo, hi);
+                    mx = rs_max3_nan(mx, lo, hi);
+                  }
+                } else {
+                  const float x0 = __uint_as_float(u[j]), x1 = __uint_as_float(u[j + 1]);
+                  mn = rs_min3_nan(mn, x0, x1);
+                  mx = rs_max3_nan(mx, x0, x1);
+                }
+              }
+            }
+          }
+        } else {
+          for (int q = 0; q < n; ++q) {
+            float v;
+            if (ke == 2) {
+              const uint16_t u = __ldg((const uint16_t*)sp + q);
+              ((uint16_t*)dp)[q] = u;
+              v = __uint_as_float((uint32_t)u << 16);
+            } else {
+              v = __ldg((const float*)sp + q);
+              ((float*)dp)[q] = v;
+            }
+            mn = rs_min_nan(mn, v);
+            mx = rs_max_nan(mx, v);
+          }
+        }
+      }
+      if (fold) {
+        const int slot = c % 4;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (slot == 0) {
+            gmn[i] = INFINITY;
+            gmx[i] = -INFINITY;
+          }
+          if (i == slot) {
+            gmn[i] = mn;
+            gmx[i] = mx;
+          }
+        }
+        if (slot == 3 || c + 1 == kc.channels)
+          rs_commit_minmax_n(gmn, gmx, slot + 1, kc.minmax + 2 * (b * kc.channels + c - slot));
+      }
+    }
+  }
+}
+
 // ===========================================================================
 // Fast affine resample: the default for a bilinear key (zeros or border
 // padding) of an affine map; BA_RESAMPLE_EXACT selects the kernels above.
@@ -1024,8 +1175,11 @@ __device__ __forceinline__ void stage_box_pitched(float4* s_dyn4, const char* sr
 #ifndef BA_FS_SEG_OVERLAP
 #define BA_FS_SEG_OVERLAP 1
 #endif
+// channels staged side by side at most, when key 0 folds its min/max
+constexpr int FS_FOLD_CH = 4;
 
-template <int S0, int S1>
+// FOLD: key 0's minmax output is folded (only set for launches that ask)
+template <int S0, int S1, bool FOLD>
 __global__ void __launch_bounds__(ST_THREADS, BA_FS_MINBLOCKS)
     resample3d_fast_kernel(const __grid_constant__ ResampleArgs a) {
   extern __shared__ float4 s_dyn4[];
@@ -1046,8 +1200,13 @@ __global__ void __launch_bounds__(ST_THREADS, BA_FS_MINBLOCKS)
   const int tx = t & 7, ty = (t >> 3) & 1, tz = (t >> 4) & 1, wp = t >> 5;
   const KeyArgs& k = a.keys[0];
   const size_t esz = DT == BA_BF16 ? 2 : 4;
+  // key 0's per-(element, channel) min/max folded as the outputs are written
+  const bool fold = FOLD && k.minmax != nullptr;
   if (!elem_active(a, b)) {
-    staged_copy_masked(a, b, d0, w0, h0, hwd, t);
+    if (fold)
+      staged_copy_masked_fold(a, b, d0, w0, h0, hwd, t);
+    else
+      staged_copy_masked(a, b, d0, w0, h0, hwd, t);
     return;
   }
   staged_setup<PAD, true>(a, b, d0, w0, h0, ALIGN, t, sh);
@@ -1056,8 +1215,11 @@ __global__ void __launch_bounds__(ST_THREADS, BA_FS_MINBLOCKS)
   const int exp = nx4 * 4, plp = ey * exp, box = ez * plp;
   const bool staged = nx4 > 0 && box <= FS_MAX_FLOATS;
   // channels staged together: all of them when their boxes fit side by
-  // side, so each voxel's coordinates serve every channel
-  const int cstack = staged && (int64_t)box * k.channels <= FS_MAX_FLOATS ? k.channels : 1;
+  // side, so each voxel's coordinates serve every channel (at most
+  // FS_FOLD_CH of them when folding min/max)
+  int cstack = staged && (int64_t)box * k.channels <= FS_MAX_FLOATS ? k.channels : 1;
+  // folding: at most FS_FOLD_CH channels a pass, each with its own registers
+  if (fold) cstack = min(cstack, FS_FOLD_CH);
   // a voxel's first tap, relative to the box: (z0 - lz) * plp + (y0 - ly) * exp
   // + x0 - lx4; clamped to [0, smax] so that even a wrong index stays inside
   const int s_off = -(lz * plp + ly * exp + lx4);
@@ -1072,13 +1234,27 @@ __global__ void __launch_bounds__(ST_THREADS, BA_FS_MINBLOCKS)
   const float fD = (float)D, fW = (float)W, fH = (float)H;
   const bool pD = (D & (D - 1)) == 0, pW = (W & (W - 1)) == 0, pH = (H & (H - 1)) == 0;
   const size_t cstride = (size_t)hwd * esz;
+  // key 0's running min/max of this pass's channels, as stored (folding
+  // only; indexed by compile-time channel numbers, so they stay in registers)
+  float fmn[FS_FOLD_CH], fmx[FS_FOLD_CH];
   for (int c0 = 0; c0 < k.channels; c0 += cstack) {
+#pragma unroll
+    for (int i = 0; i < FS_FOLD_CH; ++i) {
+      fmn[i] = INFINITY;
+      fmx[i] = -INFINITY;
+    }
     const int nch = min(cstack, k.channels - c0);
     const char* src_c = (const char*)k.src + ((size_t)b * k.channels + c0) * cstride;
     char* dst_c = (char*)k.dst + ((size_t)b * k.channels + c0) * cstride;
     if (staged)
       stage_box_pitched<DT>(s_dyn4, src_c, cstride, nch, box, lx4, ly, lz, nx4, ey, ez, exp, plp,
                             H, W, D, t);
+    // channel ci's pair as stored, into its running min/max (ci a constant)
+    auto fold_pair = [&](int ci, float2 r, bool has_b) {
+      const float va = round_dt<DT>(r.x), vb = has_b ? round_dt<DT>(r.y) : va;
+      fmn[ci] = rs_min3_nan(fmn[ci], va, vb);
+      fmx[ci] = rs_max3_nan(fmx[ci], va, vb);
+    };
     for (int pw = 0; pw < ST_PW; ++pw) {
       const int h = h0 + tz + 2 * wp;
       const int w = w0 + ty + 2 * pw;
@@ -1141,7 +1317,8 @@ __global__ void __launch_bounds__(ST_THREADS, BA_FS_MINBLOCKS)
         const bool centre = !valid || ((wx.x == 0.0f && wy.x == 0.0f && wz.x == 0.0f) &&
                                        (!has_b || (wx.y == 0.0f && wy.y == 0.0f && wz.y == 0.0f)));
         const bool one_tap = __all_sync(0xFFFFFFFFu, centre);
-        for (int ci = 0; valid && ci < nch; ++ci) {
+        // channel ci of the pass: interpolated from its staged box, stored
+        auto chan = [&](int ci) -> float2 {
           const float* sc = s_src + ci * box;
           char* dst = dst_c + ci * cstride;
           float2 r;
@@ -1166,6 +1343,14 @@ __global__ void __launch_bounds__(ST_THREADS, BA_FS_MINBLOCKS)
           }
           st<DT>(dst, row + da, r.x);
           if (has_b) st<DT>(dst, row + db, r.y);
+          return r;
+        };
+        if (FOLD && fold) {
+#pragma unroll
+          for (int ci = 0; ci < FS_FOLD_CH; ++ci)
+            if (valid && ci < nch) fold_pair(ci, chan(ci), has_b);
+        } else {
+          for (int ci = 0; valid && ci < nch; ++ci) chan(ci);
         }
       } else if (valid) {
         const bool ia = (unsigned)fx.lo < (unsigned)(D - 1) && (unsigned)fy.lo < (unsigned)(W - 1) &&
@@ -1178,10 +1363,13 @@ __global__ void __launch_bounds__(ST_THREADS, BA_FS_MINBLOCKS)
         const float2 r = trilerp2(va, vb, wx, wy, wz);
         st<DT>(dst_c, row + da, r.x);
         if (has_b) st<DT>(dst_c, row + db, r.y);
+        if (fold) fold_pair(0, r, has_b);
       }
       if (BA_FS_SEG_OVERLAP && seg)
         nearest_end<spec_dt(S1K)>(a.keys[1], b, hwd, row + da, row + db, has_b, nq);
     }
+    // the pass's channels complete: one block exchange commits them all
+    if (fold) rs_commit_minmax_n(fmn, fmx, nch, k.minmax + 2 * (b * k.channels + c0));
     if (staged) __syncthreads();
   }
 }
@@ -2081,10 +2269,12 @@ template <int S0, int S1, bool FAST>
 void allow_staged_smem(int bytes) {
   static bool done = false;
   if (!done) {
-    if (FAST)
-      cudaFuncSetAttribute(resample3d_fast_kernel<S0, S1>,
+    if (FAST) {
+      cudaFuncSetAttribute(resample3d_fast_kernel<S0, S1, false>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    else
+      cudaFuncSetAttribute(resample3d_fast_kernel<S0, S1, true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    } else
       cudaFuncSetAttribute(resample3d_staged_kernel<S0, S1>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     done = true;
@@ -2628,8 +2818,23 @@ bool launch_perm_tma(const ba_resample_desc& d, const ResampleArgs& a, int64_t n
 // each key group takes (TMA-staged row copies for signed permutations,
 // staged / fast for affine maps with a bilinear key, grid kernel for grid
 // maps, global-gather kernel otherwise).
+// Keys whose min/max the staged affine kernel folded in one launch_resample
+// call (by output pointer).
+struct FoldLog {
+  const void* dst[BA_MAX_KEYS];
+  int n = 0;
+  void add(const void* p) {
+    if (n < BA_MAX_KEYS) dst[n++] = p;
+  }
+  bool has(const void* p) const {
+    for (int i = 0; i < n; ++i)
+      if (dst[i] == p) return true;
+    return false;
+  }
+};
+
 ba_status launch_resample(const ba_resample_desc& d, ResampleArgs& a, int64_t nb,
-                          cudaStream_t st) {
+                          cudaStream_t st, FoldLog& folded) {
   const int64_t hwd = d.H * d.W * d.D;
   const int tiles_d = (int)((d.D + BD - 1) / BD);
   const int64_t gx = (int64_t)tiles_d * ((d.W + TY - 1) / TY);
@@ -2651,6 +2856,7 @@ ba_status launch_resample(const ba_resample_desc& d, ResampleArgs& a, int64_t nb
   // returns false when (s0, s1) has no staged instantiation
   const bool exact = (d.flags & BA_RESAMPLE_EXACT) != 0;
   auto launch_staged = [&](const ResampleArgs& args, int s0, int s1) -> bool {
+    if (!exact && args.keys[0].minmax != nullptr) folded.add(args.keys[0].dst);
     switch (s0 * 16 + (s1 + 1)) {
 #define BA_ST(S0, S1)                                                                \
   case S0 * 16 + (S1 + 1):                                                           \
@@ -2659,7 +2865,10 @@ ba_status launch_resample(const ba_resample_desc& d, ResampleArgs& a, int64_t nb
       resample3d_staged_kernel<S0, S1><<<st_grid, ST_THREADS, st_smem, st>>>(args);  \
     } else {                                                                         \
       allow_staged_smem<S0, S1, true>(fs_smem);                                      \
-      resample3d_fast_kernel<S0, S1><<<st_grid, ST_THREADS, fs_smem, st>>>(args);    \
+      if (args.keys[0].minmax != nullptr)                                            \
+        resample3d_fast_kernel<S0, S1, true><<<st_grid, ST_THREADS, fs_smem, st>>>(args); \
+      else                                                                           \
+        resample3d_fast_kernel<S0, S1, false><<<st_grid, ST_THREADS, fs_smem, st>>>(args); \
     }                                                                                \
     return true;
 #define BA_ST_KEY(P, T0)                                                               \
@@ -2878,10 +3087,42 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
     a.keys[i].dtype = k.dtype;
     a.keys[i].mode = k.mode;
     a.keys[i].padding = k.padding;
+    a.keys[i].minmax = k.minmax;
+    if (k.minmax != nullptr)
+      BA_REQUIRE(((uintptr_t)k.minmax % 4) == 0, "ba_resample3d: key %d minmax not 4-byte aligned",
+                 i);
   }
   if (d.batch == 0) return BA_OK;
   const cudaStream_t st = (cudaStream_t)stream;
-  if (!(d.flags & BA_RESAMPLE_HOST_PARAMS)) return launch_resample(d, a, d.batch, st);
+  // min/max outputs: reset, folded by the staged affine kernel as it writes,
+  // reduced from the output by the other paths
+  for (int i = 0; i < d.n_keys; ++i)
+    if (a.keys[i].minmax != nullptr && a.keys[i].channels > 0) {
+      const ba_status s = minmax_keys_init(a.keys[i].minmax, d.batch * a.keys[i].channels, st);
+      if (s != BA_OK) return s;
+    }
+  int launches = 0, fold_count[BA_MAX_KEYS] = {0};
+  auto run = [&](int64_t nb) -> ba_status {
+    FoldLog folded;
+    const ba_status s = launch_resample(d, a, nb, st, folded);
+    ++launches;
+    for (int i = 0; i < d.n_keys; ++i)
+      if (folded.has(d.keys[i].dst)) ++fold_count[i];
+    return s;
+  };
+  auto finish = [&]() -> ba_status {
+    for (int i = 0; i < d.n_keys; ++i) {
+      const ba_resample_key& k = d.keys[i];
+      if (k.minmax == nullptr || k.channels == 0 || fold_count[i] == launches) continue;
+      const ba_status s = minmax_keys_fold(k.dst, k.dtype, d.batch * k.channels, hwd, k.minmax, st);
+      if (s != BA_OK) return s;
+    }
+    return BA_OK;
+  };
+  if (!(d.flags & BA_RESAMPLE_HOST_PARAMS)) {
+    const ba_status s = run(d.batch);
+    return s != BA_OK ? s : finish();
+  }
   // host parameters: each launch of up to RS_INLINE_B elements carries their
   // transform and mask in its kernel parameters (read here, before return)
   BA_REQUIRE(d.xform_kind == BA_XFORM_GRID || d.xform_stride <= 16,
@@ -2896,10 +3137,10 @@ extern "C" ba_status ba_resample3d(const ba_resample_desc* desc, ba_stream_t str
         memcpy(a.inl_xform + i * d.xform_stride, d.xform + (b0 + i) * d.xform_stride,
                (size_t)d.xform_stride * sizeof(float));
     }
-    const ba_status s = launch_resample(d, a, nb, st);
+    const ba_status s = run(nb);
     if (s != BA_OK) return s;
   }
-  return BA_OK;
+  return finish();
 }
 
 extern "C" ba_status ba_compose_field(const float* field, const float* theta,

@@ -355,7 +355,14 @@ class ScaleIntensity(_FusibleIntensity):
         self.factor = factor
         self.channel_wise = channel_wise
 
-    def chain_op(self, params, tensor):
+    def takes_stats(self) -> bool:
+        """True when the rescale can use per-(element, channel) min/max made
+        elsewhere (``ops.resample3d(..., minmax=...)``) instead of reducing
+        its input itself."""
+        return self.factor is None and self.channel_wise and (
+            self.minv is not None or self.maxv is not None)
+
+    def chain_op(self, params, tensor, stats=None):
         if self.factor is not None:
             return ops.ChainOp(L.BA_OP_RESCALE, flags=L.BA_RESCALE_FACTOR, c0=self.factor)
         flags = 0
@@ -365,8 +372,12 @@ class ScaleIntensity(_FusibleIntensity):
             flags |= L.BA_RESCALE_MAXV
         if self.channel_wise:
             flags |= L.BA_RESCALE_CHANNEL
+        if stats is not None and self.takes_stats():
+            flags |= L.BA_RESCALE_GIVEN
+        else:
+            stats = None
         return ops.ChainOp(L.BA_OP_RESCALE, flags=flags, c0=self.minv or 0.0,
-                           c1=self.maxv or 0.0)
+                           c1=self.maxv or 0.0, stats=stats)
 
     def chain_params(self, batch_size, shape, device):
         # chain_op reads no params: nothing to upload

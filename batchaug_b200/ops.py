@@ -76,15 +76,19 @@ def resample_exact(flag: bool = True):
 
 
 def resample3d(tensors, *, affine=None, theta=None, grid=None, modes="bilinear",
-               paddings="zeros", align_corners=False, mask=None, out=None, exact=None):
+               paddings="zeros", align_corners=False, mask=None, out=None, exact=None,
+               minmax=None):
     """Resample one or more (B,C,H,W,D) tensors through one shared map.
 
     Exactly one of ``affine`` (MONAI (B,4,4)), ``theta`` (affine_grid
     (B,3|4,4)) or ``grid`` (grid_sample (B,H,W,D,3)) gives the map.  ``modes``
     and ``paddings`` are a string or one entry per tensor.  Masked-out
     elements are copied.  ``exact`` overrides the default trilinear
-    arithmetic (``set_resample_exact``).  Returns a list of new tensors (or
-    fills ``out``).
+    arithmetic (``set_resample_exact``).  ``minmax`` (one entry per tensor,
+    None or an int32 (B, C, 2) device tensor) receives each output's
+    per-(element, channel) min/max as statistics for a following
+    ScaleIntensity (``ChainOp(stats=...)``).  Returns a list of new tensors
+    (or fills ``out``).
     """
     single = isinstance(tensors, torch.Tensor)
     ts = [tensors] if single else list(tensors)
@@ -150,9 +154,19 @@ def resample3d(tensors, *, affine=None, theta=None, grid=None, modes="bilinear",
         d.xform = xf.data_ptr()
         d.mask = L.ptr(m)
     d.xform_stride = stride
+    mms = list(minmax) if minmax is not None else [None] * len(ts)
+    if len(mms) != len(ts):
+        raise ValueError("resample3d: minmax needs one entry per tensor")
     for i, (t, o) in enumerate(zip(ts, outs)):
         k = d.keys[i]
         k.src, k.dst = t.data_ptr(), o.data_ptr()
+        mm = mms[i]
+        if mm is not None:
+            if (mm.dtype != torch.int32 or tuple(mm.shape) != (B, t.shape[1], 2)
+                    or not mm.is_contiguous() or mm.device != device):
+                raise ValueError(f"resample3d: minmax[{i}] must be a contiguous int32 "
+                                 f"{(B, t.shape[1], 2)} tensor on {device}")
+            k.minmax = mm.data_ptr()
         k.channels = t.shape[1]
         k.dtype = L.dtype_code(t)
         k.mode = L.MODES[modes[i]]
@@ -172,14 +186,15 @@ class ChainOp:
     """One op of a fused intensity chain (device tensors for its params)."""
 
     __slots__ = ("kind", "flags", "mask", "param", "param2", "noise", "seed", "elem_offset",
-                 "degree", "c0", "c1")
+                 "degree", "c0", "c1", "stats")
 
     def __init__(self, kind, flags=0, mask=None, param=None, param2=None, noise=None, seed=0,
-                 elem_offset=0, degree=0, c0=0.0, c1=0.0):
+                 elem_offset=0, degree=0, c0=0.0, c1=0.0, stats=None):
         self.kind, self.flags, self.mask = kind, flags, mask
         self.param, self.param2, self.noise = param, param2, noise
         self.seed, self.elem_offset, self.degree = seed, elem_offset, degree
         self.c0, self.c1 = c0, c1
+        self.stats = stats  # RESCALE with BA_RESCALE_GIVEN: resample3d's minmax
 
 
 def intensity_chain(x: torch.Tensor, ops, out: torch.Tensor | None = None,
@@ -202,7 +217,7 @@ def intensity_chain(x: torch.Tensor, ops, out: torch.Tensor | None = None,
     for i, op in enumerate(ops):
         o = d.ops[i]
         o.kind, o.flags = op.kind, op.flags
-        for name in ("mask", "param", "param2", "noise"):
+        for name in ("mask", "param", "param2", "noise", "stats"):
             t = getattr(op, name)
             if t is not None:
                 if t.device != x.device:

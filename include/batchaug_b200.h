@@ -72,6 +72,13 @@ typedef struct ba_resample_key {
   int32_t mode;    /* ba_interp */
   int32_t padding; /* ba_padding */
   int32_t reserved;
+  int32_t* minmax; /* optional (NULL: none): (B, channels, 2) int32 that the call
+                      fills with the per-(element, channel) minimum and maximum
+                      of this key's output, as statistics for a following
+                      RESCALE with BA_RESCALE_GIVEN (ba_op.stats); order-
+                      preserving keys, opaque to the caller.  The staged affine
+                      kernel folds them as it writes; other paths reduce the
+                      output after the resample. */
 } ba_resample_key;
 
 /* ba_resample_desc.flags */
@@ -159,6 +166,10 @@ typedef enum ba_op_kind {
 #define BA_RESCALE_MAXV 0x2    /* RESCALE: maxv given */
 #define BA_RESCALE_CHANNEL 0x4 /* RESCALE: min/max per (element, channel) */
 #define BA_RESCALE_FACTOR 0x8  /* RESCALE: x * (1 + c0) instead of min/max */
+#define BA_RESCALE_GIVEN 0x10  /* RESCALE (with BA_RESCALE_CHANNEL): the min/max of its
+                                  input are ba_op.stats, as ba_resample3d's minmax
+                                  produced them for the tensor the chain reads,
+                                  instead of a reduction pass of the chain's own */
 #define BA_RICIAN_PHILOX 0x1   /* RICIAN: generate u1, u2 ~ N(0,1) in-kernel */
 #define BA_RICIAN_RELATIVE 0x2 /* RICIAN: std * std(x) over the element */
 #define BA_STD_NONZERO 0x2     /* STD_SHIFT: std of the nonzero values (if > 1 of them) */
@@ -182,6 +193,8 @@ typedef struct ba_op {
   uint64_t elem_offset; /* ... and the global index of element 0 */
   int32_t degree;       /* BIAS_FIELD: Legendre degree 1..6 */
   int32_t reserved;
+  const int32_t* stats; /* RESCALE with BA_RESCALE_GIVEN: (B, C, 2) statistics from
+                           ba_resample_key.minmax */
   double c0, c1; /* RESCALE: minv, maxv (or factor in c0 with BA_RESCALE_FACTOR);
                     RICIAN: the noise mean in c0 */
 } ba_op;

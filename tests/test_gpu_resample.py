@@ -423,3 +423,54 @@ def test_tensor_map_cache_follows_shape(ba, oracle_lib):
             ref = oracle_lib.resample3d(x, affine=A, mode="nearest", padding="zeros")
             assert np.array_equal(to_np(out), ref), shape
     _lib.wait_status()
+
+
+def _decode_keys(keys: np.ndarray) -> np.ndarray:
+    """The order-preserving int32 min/max keys as floats."""
+    k = keys.astype(np.int64)
+    bits = np.where(k >= 0, k, k ^ 0x7FFFFFFF) & 0xFFFFFFFF
+    return bits.astype(np.uint32).view(np.float32)
+
+
+@pytest.mark.parametrize("case", ["affine_pair", "affine_bf16", "perm", "exact", "grid_like"])
+def test_resample_minmax_matches_output(ba, case):
+    """minmax holds each output's per-(element, channel) min and max: folded
+    by the staged affine kernel (masked-out copies included, 4 channels per
+    pass), reduced from the output on every other path."""
+    from batchaug_b200 import ops
+    rng = np.random.default_rng(17)
+    B, C, H, W, D = 5, 4, 24, 20, 32
+    vol = torch.from_numpy(rng.standard_normal((B, C, H, W, D)).astype(np.float32)).cuda()
+    seg = torch.from_numpy(rng.integers(0, 3, (B, 2, H, W, D)).astype(np.float32)).cuda()
+    if case == "affine_bf16":
+        vol = vol.bfloat16()
+    A = _signed_perm_affines(rng, B, square=False) if case == "perm" else _rand_affine(rng, B)
+    mask = np.array([True, False, True, True, False])
+    mm = [torch.empty(B, C, 2, dtype=torch.int32, device="cuda"),
+          torch.empty(B, 2, 2, dtype=torch.int32, device="cuda")]
+    kw = dict(affine=A, modes=["bilinear", "nearest"], paddings="zeros", mask=mask, minmax=mm)
+    if case == "exact":
+        kw["exact"] = True
+    if case == "grid_like":
+        kw["paddings"] = "reflection"  # the global-gather kernel
+    outs = ops.resample3d([vol, seg], **kw)
+    for o, m in zip(outs, mm):
+        got = _decode_keys(m.cpu().numpy())
+        of = o.float()
+        assert np.array_equal(got[..., 0], of.amin(dim=(2, 3, 4)).cpu().numpy()), case
+        assert np.array_equal(got[..., 1], of.amax(dim=(2, 3, 4)).cpu().numpy()), case
+
+
+def test_scale_intensity_with_given_stats(ba):
+    """A ScaleIntensity chain fed the resample's min/max gives the result of
+    the chain that reduces its input itself, bit for bit."""
+    from batchaug_b200 import ops
+    rng = np.random.default_rng(23)
+    B, C = 4, 3
+    x = torch.from_numpy(rng.standard_normal((B, C, 16, 16, 32)).astype(np.float32)).cuda()
+    mm = torch.empty(B, C, 2, dtype=torch.int32, device="cuda")
+    y = ops.resample3d(x, affine=_rand_affine(rng, B), paddings="border", minmax=[mm])
+    si = ba.ScaleIntensity(minv=0.0, maxv=1.0)
+    ref = ops.intensity_chain(y, [si.chain_op(None, y)])
+    got = ops.intensity_chain(y, [si.chain_op(None, y, stats=mm)])
+    assert torch.equal(ref, got)
