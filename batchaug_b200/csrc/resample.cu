@@ -607,8 +607,18 @@ constexpr int ST_MAX_FLOATS = BA_ST_MAX_FLOATS;
 #ifndef BA_FS_MAX_FLOATS
 #define BA_FS_MAX_FLOATS 11264
 #endif
+// the largest box of one channel the fast kernel stages; a tile with a
+// larger box gathers its taps from global memory.  Measured on B200: 8192,
+// 6144 and 4096 floats are slower than 11264 on both a single-channel
+// affine (more tiles gather) and a four-channel one, and so is a 14208-float
+// limit with the shared memory a four-CTA instantiation leaves (staging
+// 44-56 KB boxes costs more than gathering those tiles' taps)
+#ifndef BA_FS_STAGE_FLOATS
+#define BA_FS_STAGE_FLOATS BA_FS_MAX_FLOATS
+#endif
+static_assert(BA_FS_STAGE_FLOATS <= BA_FS_MAX_FLOATS, "a staged box must fit");
 // the fast kernel re-checks its box with the padded pitches
-constexpr int FS_MAX_SETUP_FLOATS = BA_FS_MAX_FLOATS;
+constexpr int FS_MAX_SETUP_FLOATS = BA_FS_STAGE_FLOATS;
 constexpr int ST_PW = ST_TW / 2, ST_PH = ST_TH / 8;
 static_assert(ST_TW % 2 == 0 && ST_TH % 8 == 0, "tile covered by the thread layout");
 
@@ -1124,7 +1134,7 @@ __device__ __forceinline__ float2 trilerp2(const float* va, const float* vb, flo
   return lerp2(lerp2(c00, c10, fy), lerp2(c01, c11, fy), fz);
 }
 
-constexpr int FS_MAX_FLOATS = BA_FS_MAX_FLOATS;
+constexpr int FS_MAX_FLOATS = BA_FS_MAX_FLOATS, FS_STAGE_FLOATS = BA_FS_STAGE_FLOATS;
 
 // Copy the boxes of channels src_c, src_c + cstride, ... (nch of them) into
 // shared memory, channel i at float offset i * box, rows of exp and planes of
@@ -1213,11 +1223,11 @@ __global__ void __launch_bounds__(ST_THREADS, BA_FS_MINBLOCKS)
   const int lx4 = sh.box[0], ly = sh.box[1], lz = sh.box[2], ey = sh.box[4], ez = sh.box[5];
   const int nx4 = sh.box[3];
   const int exp = nx4 * 4, plp = ey * exp, box = ez * plp;
-  const bool staged = nx4 > 0 && box <= FS_MAX_FLOATS;
-  // channels staged together: all of them when their boxes fit side by
-  // side, so each voxel's coordinates serve every channel (at most
-  // FS_FOLD_CH of them when folding min/max)
-  int cstack = staged && (int64_t)box * k.channels <= FS_MAX_FLOATS ? k.channels : 1;
+  const bool staged = nx4 > 0 && box <= FS_STAGE_FLOATS;
+  // channels staged together: as many as fit side by side, so each voxel's
+  // coordinates serve every channel of a pass (at most FS_FOLD_CH of them
+  // when folding min/max)
+  int cstack = staged ? min(k.channels, FS_MAX_FLOATS / box) : 1;
   // folding: at most FS_FOLD_CH channels a pass, each with its own registers
   if (fold) cstack = min(cstack, FS_FOLD_CH);
   // a voxel's first tap, relative to the box: (z0 - lz) * plp + (y0 - ly) * exp
