@@ -278,13 +278,15 @@ __device__ __forceinline__ void resolve_op(const ChainArgs& a, int oi, int64_t b
 
 // Apply op oi to n consecutive values of one channel (positions
 // s0..s0+n-1), rounding its result to the tensor dtype as torch does.
-template <int DT, int VEC>
+// KIND >= 0: the op is known to be of that kind (a one-op segment), so the
+// dispatch folds away at compile time.
+template <int DT, int VEC, int KIND = -1>
 __device__ __forceinline__ void apply_one(const ChainArgs& a, int oi, const OpConst& k, int64_t b,
                                           int64_t c, int64_t s0, int n, float* v) {
   {
     const OpArgs& op = a.ops[oi];
     const bool on = k.on != 0;
-    switch (op.kind) {
+    switch (KIND >= 0 ? KIND : op.kind) {
       case BA_OP_NOISE: {
         // x + dt(noise) * dt(mask).  A masked-out element with generated noise
         // adds a zero; injected noise keeps the product (its sign of zero).
@@ -479,10 +481,13 @@ __device__ __forceinline__ void apply_one(const ChainArgs& a, int oi, const OpCo
 }
 
 // The segment's ops, in order, on n consecutive values of one channel.
-template <int DT, int VEC>
+template <int DT, int VEC, int KIND = -1>
 __device__ __forceinline__ void apply_ops(const ChainArgs& a, const OpConst* oc, int64_t b,
                                           int64_t c, int64_t s0, int n, float* v) {
-  for (int oi = 0; oi < a.n_ops; ++oi) apply_one<DT, VEC>(a, oi, oc[oi], b, c, s0, n, v);
+  if (KIND >= 0)
+    apply_one<DT, VEC, KIND>(a, 0, oc[0], b, c, s0, n, v);
+  else
+    for (int oi = 0; oi < a.n_ops; ++oi) apply_one<DT, VEC>(a, oi, oc[oi], b, c, s0, n, v);
 }
 
 // ---------------------------------------------------------------------------
@@ -514,14 +519,16 @@ __device__ __forceinline__ void pack_words(const float* v, uint32_t* w) {
     w[j] = __byte_perm(__float_as_uint(v[2 * j]), __float_as_uint(v[2 * j + 1]), 0x7632);
 }
 
+template <int KIND = -1>
 __device__ __forceinline__ void apply_ops_bf16x8(const ChainArgs& a, const OpConst* oc,
                                                  int64_t b, int64_t c, int64_t s0, uint32_t* w) {
-  for (int oi = 0; oi < a.n_ops; ++oi) {
+  const int n_ops = KIND >= 0 ? 1 : a.n_ops;
+  for (int oi = 0; oi < n_ops; ++oi) {
     const OpArgs& op = a.ops[oi];
     const OpConst& k = oc[oi];
     const bool on = k.on != 0;
     bool done = true;
-    switch (op.kind) {
+    switch (KIND >= 0 ? KIND : op.kind) {
       case BA_OP_NOISE:
         if (op.flags & BA_NOISE_PHILOX) {
           if (!on) {
@@ -622,7 +629,7 @@ __device__ __forceinline__ void apply_ops_bf16x8(const ChainArgs& a, const OpCon
     if (!done) {
       float v[8];
       unpack_words(w, v);
-      apply_one<BA_BF16, 8>(a, oi, k, b, c, s0, 8, v);
+      apply_one<BA_BF16, 8, KIND>(a, oi, k, b, c, s0, 8, v);
       pack_words(v, w);
     }
   }
@@ -777,7 +784,7 @@ __device__ __forceinline__ uint4 pack16(const float* v) {
 // a private ring of PIPE slots in shared memory with cp.async, so PIPE chunks
 // per thread are in flight without holding registers.  A thread only reads
 // the slots it filled itself, so cp.async.wait_group alone orders the data.
-template <int DT, int VEC, bool WRITE>
+template <int DT, int VEC, bool WRITE, int KIND>
 __device__ __forceinline__ void run_range_vec(const ChainArgs& a, const OpConst* oc, int64_t b,
                                               int64_t c, int64_t s_begin, int64_t s_end,
                                               bool stats, float& mn, float& mx, Moments& mo,
@@ -806,7 +813,7 @@ __device__ __forceinline__ void run_range_vec(const ChainArgs& a, const OpConst*
     if constexpr (DT == BA_BF16) {
       const uint4 t = ring[slot * CHAIN_THREADS + tid];
       uint32_t w[4] = {t.x, t.y, t.z, t.w};
-      apply_ops_bf16x8(a, oc, b, c, s_begin + j * VEC, w);
+      apply_ops_bf16x8<KIND>(a, oc, b, c, s_begin + j * VEC, w);
       if (WRITE) dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
       if (stats) {
         if (a.stats_moments) {
@@ -820,7 +827,7 @@ __device__ __forceinline__ void run_range_vec(const ChainArgs& a, const OpConst*
     } else {
       float v[VEC];
       unpack16<DT, VEC>(ring[slot * CHAIN_THREADS + tid], v);
-      apply_ops<DT, VEC>(a, oc, b, c, s_begin + j * VEC, VEC, v);
+      apply_ops<DT, VEC, KIND>(a, oc, b, c, s_begin + j * VEC, VEC, v);
       if (WRITE) dst[j] = pack16<DT, VEC>(v);
       if (stats) {
         if (a.stats_moments)
@@ -863,8 +870,9 @@ __device__ __forceinline__ void run_range_scalar(const ChainArgs& a, const OpCon
 // One segment of the chain.  CTA (x, y) handles spatial positions
 // [x * tile, +tile) of channel y % C of element b0 + y / C, so the cp.async
 // ring runs uninterrupted over the whole range and the op constants are
-// resolved once per CTA.
-template <int DT, int VEC, bool WRITE>
+// resolved once per CTA.  KIND >= 0: the segment is that one op (its
+// dispatch resolved at compile time), -1: any ops.
+template <int DT, int VEC, bool WRITE, int KIND = -1>
 __global__ void __launch_bounds__(CHAIN_THREADS, chain_minblocks<DT>())
     chain_kernel(const __grid_constant__ ChainArgs a) {
   __shared__ OpConst s_oc[BA_MAX_OPS];
@@ -878,8 +886,8 @@ __global__ void __launch_bounds__(CHAIN_THREADS, chain_minblocks<DT>())
   float mn = INFINITY, mx = -INFINITY;
   Moments mo = {0.0, 0.0, 0.0};
   if (VEC > 1)
-    run_range_vec<DT, VEC, WRITE>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx, mo,
-                                  s_ring);
+    run_range_vec<DT, VEC, WRITE, KIND>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx,
+                                        mo, s_ring);
   else
     run_range_scalar<DT, WRITE>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx, mo);
   if (a.stats_mode != 0) {
@@ -1059,6 +1067,14 @@ ba_status launch_segment(ChainArgs& a, int64_t nb, bool write, cudaStream_t st) 
   const int64_t tile = pick_tile(a.HWD, nb * a.C, VEC);
   a.tile = tile;
   dim3 grid((unsigned)((a.HWD + tile - 1) / tile), (unsigned)(nb * a.C));
+  // a lone rescale (ScaleIntensity on given statistics, the usual last
+  // segment) runs without the op loop and kind dispatch
+  if constexpr (VEC > 1) {
+    if (write && a.n_ops == 1 && a.ops[0].kind == BA_OP_RESCALE) {
+      chain_kernel<DT, VEC, true, BA_OP_RESCALE><<<grid, CHAIN_THREADS, 0, st>>>(a);
+      return check_launch("ba_intensity_chain");
+    }
+  }
   if (write)
     chain_kernel<DT, VEC, true><<<grid, CHAIN_THREADS, 0, st>>>(a);
   else
