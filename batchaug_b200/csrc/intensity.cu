@@ -1068,10 +1068,14 @@ ba_status launch_segment(ChainArgs& a, int64_t nb, bool write, cudaStream_t st) 
   a.tile = tile;
   dim3 grid((unsigned)((a.HWD + tile - 1) / tile), (unsigned)(nb * a.C));
   // a lone rescale (ScaleIntensity on given statistics, the usual last
-  // segment) runs without the op loop and kind dispatch
+  // segment) or a lone noise op runs without the op loop and kind dispatch
   if constexpr (VEC > 1) {
     if (write && a.n_ops == 1 && a.ops[0].kind == BA_OP_RESCALE) {
       chain_kernel<DT, VEC, true, BA_OP_RESCALE><<<grid, CHAIN_THREADS, 0, st>>>(a);
+      return check_launch("ba_intensity_chain");
+    }
+    if (write && a.n_ops == 1 && a.ops[0].kind == BA_OP_NOISE) {
+      chain_kernel<DT, VEC, true, BA_OP_NOISE><<<grid, CHAIN_THREADS, 0, st>>>(a);
       return check_launch("ba_intensity_chain");
     }
   }
