@@ -278,8 +278,8 @@ __device__ __forceinline__ void resolve_op(const ChainArgs& a, int oi, int64_t b
 
 // Apply op oi to n consecutive values of one channel (positions
 // s0..s0+n-1), rounding its result to the tensor dtype as torch does.
-// KIND >= 0: the op is known to be of that kind (a one-op segment), so the
-// dispatch folds away at compile time.
+// KIND >= 0: the op is known to be of that kind (an op of a sequence given
+// at compile time), so the dispatch folds away.
 template <int DT, int VEC, int KIND = -1>
 __device__ __forceinline__ void apply_one(const ChainArgs& a, int oi, const OpConst& k, int64_t b,
                                           int64_t c, int64_t s0, int n, float* v) {
@@ -481,11 +481,22 @@ __device__ __forceinline__ void apply_one(const ChainArgs& a, int oi, const OpCo
 }
 
 // The segment's ops, in order, on n consecutive values of one channel.
-template <int DT, int VEC, int KIND = -1>
+// SEQ >= 0: the ops' kinds in compile-time form, four bits each, the first
+// op in the lowest bits (0 ends the sequence); -1: any ops.
+template <int DT, int VEC, int SEQ>
+__device__ __forceinline__ void apply_seq(const ChainArgs& a, const OpConst* oc, int oi,
+                                          int64_t b, int64_t c, int64_t s0, int n, float* v) {
+  if constexpr (SEQ != 0) {
+    apply_one<DT, VEC, (SEQ & 15)>(a, oi, oc[oi], b, c, s0, n, v);
+    apply_seq<DT, VEC, (SEQ >> 4)>(a, oc, oi + 1, b, c, s0, n, v);
+  }
+}
+
+template <int DT, int VEC, int SEQ = -1>
 __device__ __forceinline__ void apply_ops(const ChainArgs& a, const OpConst* oc, int64_t b,
                                           int64_t c, int64_t s0, int n, float* v) {
-  if (KIND >= 0)
-    apply_one<DT, VEC, KIND>(a, 0, oc[0], b, c, s0, n, v);
+  if constexpr (SEQ >= 0)
+    apply_seq<DT, VEC, SEQ>(a, oc, 0, b, c, s0, n, v);
   else
     for (int oi = 0; oi < a.n_ops; ++oi) apply_one<DT, VEC>(a, oi, oc[oi], b, c, s0, n, v);
 }
@@ -519,13 +530,13 @@ __device__ __forceinline__ void pack_words(const float* v, uint32_t* w) {
     w[j] = __byte_perm(__float_as_uint(v[2 * j]), __float_as_uint(v[2 * j + 1]), 0x7632);
 }
 
-template <int KIND = -1>
-__device__ __forceinline__ void apply_ops_bf16x8(const ChainArgs& a, const OpConst* oc,
+// Op oi of the segment on one chunk of 8 bf16 values (four bf16x2 words);
+// KIND >= 0: the op's kind, known at compile time.
+template <int KIND>
+__device__ __forceinline__ void apply_one_bf16x8(const ChainArgs& a, int oi, const OpConst& k,
                                                  int64_t b, int64_t c, int64_t s0, uint32_t* w) {
-  const int n_ops = KIND >= 0 ? 1 : a.n_ops;
-  for (int oi = 0; oi < n_ops; ++oi) {
+  {
     const OpArgs& op = a.ops[oi];
-    const OpConst& k = oc[oi];
     const bool on = k.on != 0;
     bool done = true;
     switch (KIND >= 0 ? KIND : op.kind) {
@@ -633,6 +644,28 @@ __device__ __forceinline__ void apply_ops_bf16x8(const ChainArgs& a, const OpCon
       pack_words(v, w);
     }
   }
+}
+
+// A segment's ops given at compile time: SEQ holds their kinds, four bits
+// each, the first op in the lowest bits (0 ends the sequence).
+template <int SEQ>
+__device__ __forceinline__ void apply_seq_bf16x8(const ChainArgs& a, const OpConst* oc, int oi,
+                                                 int64_t b, int64_t c, int64_t s0, uint32_t* w) {
+  if constexpr (SEQ != 0) {
+    apply_one_bf16x8<(SEQ & 15)>(a, oi, oc[oi], b, c, s0, w);
+    apply_seq_bf16x8<(SEQ >> 4)>(a, oc, oi + 1, b, c, s0, w);
+  }
+}
+
+// The segment's ops on one chunk of 8 bf16 values.  SEQ >= 0: the ops'
+// kinds in compile-time form (apply_seq_bf16x8), -1: any ops.
+template <int SEQ = -1>
+__device__ __forceinline__ void apply_ops_bf16x8(const ChainArgs& a, const OpConst* oc,
+                                                 int64_t b, int64_t c, int64_t s0, uint32_t* w) {
+  if constexpr (SEQ >= 0)
+    apply_seq_bf16x8<SEQ>(a, oc, 0, b, c, s0, w);
+  else
+    for (int oi = 0; oi < a.n_ops; ++oi) apply_one_bf16x8<-1>(a, oi, oc[oi], b, c, s0, w);
 }
 
 __device__ __forceinline__ void fold_minmax_bf16x8(const uint32_t* w, __nv_bfloat162& mn,
@@ -784,7 +817,7 @@ __device__ __forceinline__ uint4 pack16(const float* v) {
 // a private ring of PIPE slots in shared memory with cp.async, so PIPE chunks
 // per thread are in flight without holding registers.  A thread only reads
 // the slots it filled itself, so cp.async.wait_group alone orders the data.
-template <int DT, int VEC, bool WRITE, int KIND>
+template <int DT, int VEC, bool WRITE, int SEQ>
 __device__ __forceinline__ void run_range_vec(const ChainArgs& a, const OpConst* oc, int64_t b,
                                               int64_t c, int64_t s_begin, int64_t s_end,
                                               bool stats, float& mn, float& mx, Moments& mo,
@@ -813,7 +846,7 @@ __device__ __forceinline__ void run_range_vec(const ChainArgs& a, const OpConst*
     if constexpr (DT == BA_BF16) {
       const uint4 t = ring[slot * CHAIN_THREADS + tid];
       uint32_t w[4] = {t.x, t.y, t.z, t.w};
-      apply_ops_bf16x8<KIND>(a, oc, b, c, s_begin + j * VEC, w);
+      apply_ops_bf16x8<SEQ>(a, oc, b, c, s_begin + j * VEC, w);
       if (WRITE) dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
       if (stats) {
         if (a.stats_moments) {
@@ -827,7 +860,7 @@ __device__ __forceinline__ void run_range_vec(const ChainArgs& a, const OpConst*
     } else {
       float v[VEC];
       unpack16<DT, VEC>(ring[slot * CHAIN_THREADS + tid], v);
-      apply_ops<DT, VEC, KIND>(a, oc, b, c, s_begin + j * VEC, VEC, v);
+      apply_ops<DT, VEC, SEQ>(a, oc, b, c, s_begin + j * VEC, VEC, v);
       if (WRITE) dst[j] = pack16<DT, VEC>(v);
       if (stats) {
         if (a.stats_moments)
@@ -870,9 +903,10 @@ __device__ __forceinline__ void run_range_scalar(const ChainArgs& a, const OpCon
 // One segment of the chain.  CTA (x, y) handles spatial positions
 // [x * tile, +tile) of channel y % C of element b0 + y / C, so the cp.async
 // ring runs uninterrupted over the whole range and the op constants are
-// resolved once per CTA.  KIND >= 0: the segment is that one op (its
-// dispatch resolved at compile time), -1: any ops.
-template <int DT, int VEC, bool WRITE, int KIND = -1>
+// resolved once per CTA.  SEQ >= 0: the segment's op kinds, four bits each
+// (first op lowest), so their dispatch is resolved at compile time; -1: any
+// ops.
+template <int DT, int VEC, bool WRITE, int SEQ = -1>
 __global__ void __launch_bounds__(CHAIN_THREADS, chain_minblocks<DT>())
     chain_kernel(const __grid_constant__ ChainArgs a) {
   __shared__ OpConst s_oc[BA_MAX_OPS];
@@ -886,8 +920,8 @@ __global__ void __launch_bounds__(CHAIN_THREADS, chain_minblocks<DT>())
   float mn = INFINITY, mx = -INFINITY;
   Moments mo = {0.0, 0.0, 0.0};
   if (VEC > 1)
-    run_range_vec<DT, VEC, WRITE, KIND>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx,
-                                        mo, s_ring);
+    run_range_vec<DT, VEC, WRITE, SEQ>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx,
+                                       mo, s_ring);
   else
     run_range_scalar<DT, WRITE>(a, s_oc, b, c, s_begin, s_end, a.stats_mode != 0, mn, mx, mo);
   if (a.stats_mode != 0) {
@@ -1067,16 +1101,26 @@ ba_status launch_segment(ChainArgs& a, int64_t nb, bool write, cudaStream_t st) 
   const int64_t tile = pick_tile(a.HWD, nb * a.C, VEC);
   a.tile = tile;
   dim3 grid((unsigned)((a.HWD + tile - 1) / tile), (unsigned)(nb * a.C));
-  // a lone rescale (ScaleIntensity on given statistics, the usual last
-  // segment) or a lone noise op runs without the op loop and kind dispatch
+  // segments of common op sequences run without the op loop and kind
+  // dispatch: a lone noise, bias field or rescale (ScaleIntensity on given
+  // statistics, the usual last segment), and contrast -> scale -> shift
   if constexpr (VEC > 1) {
-    if (write && a.n_ops == 1 && a.ops[0].kind == BA_OP_RESCALE) {
-      chain_kernel<DT, VEC, true, BA_OP_RESCALE><<<grid, CHAIN_THREADS, 0, st>>>(a);
-      return check_launch("ba_intensity_chain");
-    }
-    if (write && a.n_ops == 1 && a.ops[0].kind == BA_OP_NOISE) {
-      chain_kernel<DT, VEC, true, BA_OP_NOISE><<<grid, CHAIN_THREADS, 0, st>>>(a);
-      return check_launch("ba_intensity_chain");
+    int seq = 0;
+    for (int i = a.n_ops - 1; i >= 0 && a.n_ops <= 3; --i) seq = (seq << 4) | a.ops[i].kind;
+    if (write) {
+      switch (a.n_ops <= 3 ? seq : -1) {
+#define BA_SEQ(S)                                                        \
+  case S:                                                                \
+    chain_kernel<DT, VEC, true, (S)><<<grid, CHAIN_THREADS, 0, st>>>(a); \
+    return check_launch("ba_intensity_chain");
+        BA_SEQ(BA_OP_NOISE)
+        BA_SEQ(BA_OP_BIAS_FIELD)
+        BA_SEQ(BA_OP_RESCALE)
+        BA_SEQ(BA_OP_CONTRAST | BA_OP_SCALE << 4 | BA_OP_SHIFT << 8)
+#undef BA_SEQ
+        default:
+          break;
+      }
     }
   }
   if (write)
