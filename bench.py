@@ -65,10 +65,10 @@ HEADLINE = "config4"
 #   config4: the step's two ba_resample3d launches, captured on a 2-element
 #     slice of the workload (2x4x128^3 vol + seg) and scaled to the 5
 #     elements of a launch (traffic grows with the elements): the permutation
-#     kernel resample3d_permt_kernel<0> 135,690,496 + 90,970,880 B and the
-#     affine kernel resample3d_fast_kernel<0,6> 130,048,512 + 102,385,152 B,
-#     mean 229,547,520 B x 5 / 2.
-DRAM_BYTES_PER_LAUNCH = {"config2": 97109504, "config4": 573868800}
+#     kernel resample3d_permt_kernel<0,1> 136,066,816 + 89,412,352 B and the
+#     affine kernel resample3d_fast_kernel<0,6,1> (min/max folded)
+#     130,400,256 + 102,155,520 B, mean 229,017,472 B x 5 / 2.
+DRAM_BYTES_PER_LAUNCH = {"config2": 97109504, "config4": 572543680}
 
 
 def _peaks():
