@@ -1102,8 +1102,9 @@ ba_status launch_segment(ChainArgs& a, int64_t nb, bool write, cudaStream_t st) 
   a.tile = tile;
   dim3 grid((unsigned)((a.HWD + tile - 1) / tile), (unsigned)(nb * a.C));
   // segments of common op sequences run without the op loop and kind
-  // dispatch: a lone noise, bias field or rescale (ScaleIntensity on given
-  // statistics, the usual last segment), and contrast -> scale -> shift
+  // dispatch: any lone op (a rescale on given statistics is the usual last
+  // segment; ops that read their input's statistics cut the chain into
+  // one-op segments), and contrast -> scale -> shift
   if constexpr (VEC > 1) {
     int seq = 0;
     for (int i = a.n_ops - 1; i >= 0 && a.n_ops <= 3; --i) seq = (seq << 4) | a.ops[i].kind;
@@ -1114,8 +1115,14 @@ ba_status launch_segment(ChainArgs& a, int64_t nb, bool write, cudaStream_t st) 
     chain_kernel<DT, VEC, true, (S)><<<grid, CHAIN_THREADS, 0, st>>>(a); \
     return check_launch("ba_intensity_chain");
         BA_SEQ(BA_OP_NOISE)
+        BA_SEQ(BA_OP_CONTRAST)
+        BA_SEQ(BA_OP_SCALE)
+        BA_SEQ(BA_OP_SHIFT)
         BA_SEQ(BA_OP_BIAS_FIELD)
         BA_SEQ(BA_OP_RESCALE)
+        BA_SEQ(BA_OP_RICIAN)
+        BA_SEQ(BA_OP_STD_SHIFT)
+        BA_SEQ(BA_OP_FIXED_MEAN)
         BA_SEQ(BA_OP_CONTRAST | BA_OP_SCALE << 4 | BA_OP_SHIFT << 8)
 #undef BA_SEQ
         default:
