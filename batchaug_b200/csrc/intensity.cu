@@ -1128,6 +1128,10 @@ ba_status launch_segment(ChainArgs& a, int64_t nb, bool write, cudaStream_t st) 
         default:
           break;
       }
+    } else if (a.n_ops == 0) {
+      // a statistics pass over the input alone (no ops, no write)
+      chain_kernel<DT, VEC, false, 0><<<grid, CHAIN_THREADS, 0, st>>>(a);
+      return check_launch("ba_intensity_chain");
     }
   }
   if (write)
