@@ -1179,6 +1179,10 @@ __device__ __forceinline__ void stage_box_pitched(float4* s_dyn4, const char* sr
   __syncthreads();
 }
 
+// CTAs per SM the fast kernel's registers are bounded for.  Measured on
+// B200: 5 (96 registers, a paired key's variants spilling) made a four-
+// channel vol + seg affine 12 % slower than 4 (128) and left a one-channel
+// one unchanged.
 #ifndef BA_FS_MINBLOCKS
 #define BA_FS_MINBLOCKS 4
 #endif
