@@ -69,6 +69,8 @@ class _Recorder:
     def __init__(self, oracle):
         self.O = oracle
         self.calls = []
+        self.minmax = []     # each resample call's minmax argument
+        self.chain_ops = []  # each chain call's ops
 
     def resample3d(self, tensors, *, affine=None, modes="bilinear", paddings="zeros",
                    mask=None, **kw):
@@ -77,6 +79,7 @@ class _Recorder:
         modes = [modes] * len(ts) if isinstance(modes, str) else modes
         paddings = [paddings] * len(ts) if isinstance(paddings, str) else paddings
         self.calls.append(("resample", len(ts), np.array(mask)))
+        self.minmax.append(kw.get("minmax"))
         outs = [torch.from_numpy(self.O.resample3d(t.numpy(), affine=affine, mode=m, padding=p,
                                                    mask=mask)) for t, m, p in zip(ts, modes,
                                                                                   paddings)]
@@ -84,6 +87,7 @@ class _Recorder:
 
     def intensity_chain(self, x, ops_, **kw):
         self.calls.append(("chain", len(ops_), [o.kind for o in ops_]))
+        self.chain_ops.append(list(ops_))
         return x + 0  # values are not checked here, only the plan
 
 
@@ -128,6 +132,38 @@ def test_compose_plan_config4(ba, rec, oracle_lib):
     assert rec.calls[3][2] == [6, 4]  # ScaleIntensity then shift, one chain
     # nearest keeps binary labels
     assert set(np.unique(out["seg"].numpy())) <= {0.0, 1.0}
+
+
+def test_compose_hands_resample_stats_to_scale_intensity(ba, rec, oracle_lib):
+    """A materialisation followed by a channel-wise ScaleIntensity(d) asks
+    the resample for the rescaled keys' per-(element, channel) min/max, and
+    the rescale takes them as given statistics; a factor rescale, a
+    per-element one and keys the rescale does not list get none."""
+    from batchaug_b200 import _lib as L
+    torch.manual_seed(0)
+    vol = torch.randn(3, 2, 8, 8, 8)
+    seg = (torch.rand(3, 1, 8, 8, 8) > 0.5).float()
+    mode = {"vol": "bilinear", "seg": "nearest"}
+    c = ba.Compose([ba.RandAffined(["vol", "seg"], prob=1.0, rotate_range=0.5),
+                    ba.ScaleIntensityd(["vol"])], lazy=True, mode=mode)
+    c({"vol": vol, "seg": seg})
+    mm = rec.minmax[-1]
+    assert mm is not None
+    given = [m for m in mm if m is not None]
+    assert len(given) == 1 and tuple(given[0].shape) == (3, 2, 2)  # vol's (B, C, 2) only
+    assert given[0].dtype == torch.int32
+    (op,) = rec.chain_ops[-1]
+    assert op.kind == L.BA_OP_RESCALE and op.stats is given[0]
+    assert op.flags & L.BA_RESCALE_GIVEN
+    for last in (ba.ScaleIntensityd(["vol"], factor=0.1),
+                 ba.ScaleIntensityd(["vol"], channel_wise=False),
+                 ba.ScaleIntensityd(["seg"], minv=None, maxv=None)):
+        rec.minmax.clear()
+        rec.chain_ops.clear()
+        ba.Compose([ba.RandAffined(["vol", "seg"], prob=1.0, rotate_range=0.5), last],
+                   lazy=True, mode=mode)({"vol": vol, "seg": seg})
+        assert all(m is None for m in (rec.minmax[-1] or []))
+        assert all(getattr(o, "stats", None) is None for ops_ in rec.chain_ops for o in ops_)
 
 
 def test_owned_key_chain_runs_on_selected_elements_only(ba, rec, oracle_lib):
